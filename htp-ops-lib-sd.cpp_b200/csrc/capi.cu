@@ -1,0 +1,708 @@
+// Device-pointer C ABI of libhtp_ops_b200.so (include/htp_ops_b200.h): device
+// context, TMA tensor maps, prepared-weight cache, workspace, plans, and the
+// reference's kernel-level entry points (include/dsp/ops.h:20-31 of the
+// reference) on top of them.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/htp_ops_b200.h"
+#include "../../include/op_reg.h"
+#include "kernels.h"
+
+using namespace htpg;
+
+// ------------------------------------------------------------------ state
+namespace {
+
+__device__ uint32_t g_watchdog;  // bits set by bounded device waits that expired
+
+thread_local std::string t_last_cuda_error;
+thread_local float t_phase_ms[3] = {0, 0, 0};
+std::mutex g_mu;
+int g_profiling = 0;
+
+// benchmark phase timing: event triples recorded by runs, read back later
+struct PhaseEvents {
+  cudaEvent_t e[3];
+};
+bool g_phase_on = false;
+std::vector<PhaseEvents> g_phase_pending, g_phase_free;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct Workspace {
+  void *base = nullptr;
+  size_t bytes = 0;
+};
+
+struct Device {
+  bool ready = false;
+  int ordinal = -1;
+  int sms = 148;
+  cudaStream_t stream = nullptr;
+  uint32_t *watchdog = nullptr;
+  std::map<cudaStream_t, Workspace> ws;
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+};
+
+Device g_dev[16];
+EncodeTiledFn g_encode = nullptr;
+
+int record_cuda(cudaError_t e, int code = HTPG_ELAUNCH) {
+  if (e == cudaSuccess) return HTPG_OK;
+  t_last_cuda_error = cudaGetErrorString(e);
+  if (std::getenv("HTPG_LOG")) std::fprintf(stderr, "htpg: CUDA error: %s\n", cudaGetErrorString(e));
+  return code;
+}
+
+int current_device(Device **out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) return HTPG_ELAUNCH;
+  Device &d = g_dev[dev];
+  if (!d.ready) {
+    const int rc = htpg_init(dev);
+    if (rc != HTPG_OK) return rc;
+  }
+  *out = &d;
+  return HTPG_OK;
+}
+
+cudaStream_t pick_stream(Device *d, void *stream) {
+  return stream ? static_cast<cudaStream_t>(stream) : d->stream;
+}
+
+// Stream-private scratch: activation codes / FP16 activations, row scales,
+// split-K accumulators.  Grows (after a stream synchronisation) when a larger
+// shape arrives; kept for the life of the library otherwise.
+int workspace(Device *d, cudaStream_t st, size_t bytes, void **out) {
+  Workspace &w = d->ws[st];
+  if (w.bytes < bytes) {
+    if (w.base) {
+      cudaStreamSynchronize(st);
+      cudaFree(w.base);
+      w.base = nullptr;
+      w.bytes = 0;
+    }
+    size_t want = bytes + bytes / 4 + (1u << 20);
+    if (cudaMalloc(&w.base, want) != cudaSuccess) {
+      cudaGetLastError();
+      return HTPG_ENOMEM;
+    }
+    // split-K accumulators and counters must start (and are left) at zero
+    if (cudaMemsetAsync(w.base, 0, want, st) != cudaSuccess) return HTPG_ELAUNCH;
+    w.bytes = want;
+  }
+  *out = w.base;
+  return HTPG_OK;
+}
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Largest split-K footprint: 128 weight tiles x 128 rows x 32 activation rows
+// of INT32, plus one counter per tile.
+constexpr size_t kSplitKRegion = 128u * 128u * 32u * 4u + 4096u;
+
+// 2-D K-major tensor map: `rows` rows of `k` elements, row pitch `pitch`
+// bytes, box = 128 bytes of K x box_rows rows, 128-byte swizzle, zero fill.
+int make_map(CUtensorMap *map, const void *base, Kind kind, int k, int rows, size_t pitch,
+             int box_rows) {
+  if (!g_encode) return HTPG_ELAUNCH;
+  const int esize = kind == Kind::I8 ? 1 : 2;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esize), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(map, kind == Kind::I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              2, const_cast<void *>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    t_last_cuda_error = "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")";
+    return HTPG_ELAUNCH;
+  }
+  return HTPG_OK;
+}
+
+}  // namespace
+
+// Prepared weight: K-major rows in HBM plus the per-column epilogue data.
+struct htpg_weights {
+  Kind kind = Kind::I8;
+  int k = 0, ncols = 0, n0 = 0, n_total = 0;
+  int device = 0;
+  void *wk = nullptr;          // [ncols][k] int8 / fp16
+  float *sw = nullptr;         // I8: [ncols] column scales
+  int32_t *corr = nullptr;     // I8: [ncols] zero-point correction differences
+  float *inverse = nullptr;    // I8: [k], nullptr when every entry is 1.0
+  std::map<int, CUtensorMap> maps;  // by box rows
+};
+
+namespace {
+
+int weight_map(htpg_weights *w, int box_rows, const CUtensorMap **out) {
+  auto it = w->maps.find(box_rows);
+  if (it == w->maps.end()) {
+    CUtensorMap m;
+    const size_t pitch = static_cast<size_t>(w->k) * (w->kind == Kind::I8 ? 1 : 2);
+    const int rc = make_map(&m, w->wk, w->kind, w->k, w->ncols, pitch, box_rows);
+    if (rc != HTPG_OK) return rc;
+    it = w->maps.emplace(box_rows, m).first;
+  }
+  *out = &it->second;
+  return HTPG_OK;
+}
+
+// pointer-keyed cache of prepared weights for the one-call entry points
+typedef std::tuple<const void *, int, int, int, int> CacheKey;  // ptr, kind, k, n, device
+std::map<CacheKey, htpg_weights *> g_cache;
+
+}  // namespace
+
+// ================================================================ library
+extern "C" int htpg_version(void) { return 1; }
+
+extern "C" const char *htpg_strerror(int code) {
+  switch (code) {
+    case HTPG_OK: return "ok";
+    case HTPG_EPAYLOAD: return "bad payload size or shape";
+    case HTPG_EUNMAPPED: return "buffer not registered or too small";
+    case HTPG_EHEADER: return "constants header or alignment mismatch";
+    case HTPG_EARGS: return "null pointer or shape out of range";
+    case HTPG_ECAPACITY: return "shape constraint violated";
+    case HTPG_ECONTROL: return "alignment or control block error";
+    case HTPG_ELAUNCH: return "CUDA launch or stream error";
+    case HTPG_ENOPLAN: return "no tile plan for this shape";
+    case HTPG_EWATCHDOG: return "device wait expired";
+    case HTPG_ENOMEM: return "device allocation failed";
+    case HTPG_EARCH: return "device is not sm_100";
+    default: return "unknown error";
+  }
+}
+
+extern "C" const char *htpg_last_cuda_error(void) { return t_last_cuda_error.c_str(); }
+
+extern "C" int htpg_init(int device) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (device < 0 || device >= 16) return HTPG_EARGS;
+  Device &d = g_dev[device];
+  if (cudaSetDevice(device) != cudaSuccess) {
+    cudaGetLastError();
+    return HTPG_ELAUNCH;
+  }
+  if (d.ready) return HTPG_OK;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return record_cuda(cudaGetLastError());
+  if (prop.major != 10 || prop.minor != 0) return HTPG_EARCH;
+  if (!g_encode) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return record_cuda(cudaErrorNotSupported);
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  d.ordinal = device;
+  d.sms = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking) != cudaSuccess)
+    return record_cuda(cudaGetLastError());
+  if (cudaGetSymbolAddress(reinterpret_cast<void **>(&d.watchdog), g_watchdog) != cudaSuccess)
+    return record_cuda(cudaGetLastError());
+  for (auto &e : d.ev)
+    if (cudaEventCreate(&e) != cudaSuccess) return record_cuda(cudaGetLastError());
+  d.ready = true;
+  return HTPG_OK;
+}
+
+extern "C" int htpg_check_device(void *stream, uint32_t *flags) {
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t st = pick_stream(d, stream);
+  if (cudaStreamSynchronize(st) != cudaSuccess) return record_cuda(cudaGetLastError());
+  uint32_t v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_watchdog, sizeof(v)) != cudaSuccess) return record_cuda(cudaGetLastError());
+  if (v) {
+    const uint32_t zero = 0;
+    cudaMemcpyToSymbol(g_watchdog, &zero, sizeof(zero));
+    // a launch that gave up may have left split-K partials behind
+    for (auto &kv : d->ws)
+      if (kv.second.base) cudaMemset(kv.second.base, 0, kv.second.bytes);
+  }
+  if (flags) *flags = v;
+  return v ? HTPG_EWATCHDOG : HTPG_OK;
+}
+
+extern "C" uint64_t htpg_launch_count(void) { return htpg::launches(); }
+
+extern "C" int htpg_phase_timing(int on) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_phase_on = on != 0;
+  return HTPG_OK;
+}
+
+extern "C" int htpg_phase_timing_read(double *act_ms, double *gemm_ms, int *runs) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  double a = 0, g = 0;
+  int n = 0;
+  for (auto &pe : g_phase_pending) {
+    float t01 = 0, t12 = 0;
+    if (cudaEventSynchronize(pe.e[2]) != cudaSuccess) return record_cuda(cudaGetLastError());
+    cudaEventElapsedTime(&t01, pe.e[0], pe.e[1]);
+    cudaEventElapsedTime(&t12, pe.e[1], pe.e[2]);
+    a += t01;
+    g += t12;
+    ++n;
+    g_phase_free.push_back(pe);
+  }
+  g_phase_pending.clear();
+  if (act_ms) *act_ms = a;
+  if (gemm_ms) *gemm_ms = g;
+  if (runs) *runs = n;
+  return HTPG_OK;
+}
+
+extern "C" int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]) {
+  if (!out || m < 1 || n < 1 || k < 1 || sms < 1 || (kind != 0 && kind != 1)) return HTPG_EARGS;
+  const GemmPlan p = plan_gemm(kind == 0 ? Kind::I8 : Kind::F16, m, n, k, sms);
+  const int64_t v[10] = {p.swap ? 1 : 0, p.bn, p.splits, p.tiles_a, p.tiles_b, p.kb_total,
+                         p.kb_per_split, p.units, p.grid, static_cast<int64_t>(p.smem)};
+  for (int i = 0; i < 10; ++i) out[i] = v[i];
+  return HTPG_OK;
+}
+
+extern "C" int htpg_set_profiling(int on) {
+  g_profiling = on ? 1 : 0;
+  return HTPG_OK;
+}
+
+extern "C" int htpg_last_phase_ms(float *quant_ms, float *gemm_ms, float *total_ms) {
+  if (quant_ms) *quant_ms = t_phase_ms[0];
+  if (gemm_ms) *gemm_ms = t_phase_ms[1];
+  if (total_ms) *total_ms = t_phase_ms[2];
+  return HTPG_OK;
+}
+
+// ================================================================ quantise
+extern "C" int htpg_quantize_rows(int8_t *codes, float *row_scales, const float *x,
+                                  const float *inverse, int m, int k, void *stream) {
+  if (!codes || !row_scales || !x || m < 1 || k < 32 || k % 32) return HTPG_EARGS;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(codes)) & 15u) return HTPG_ECONTROL;
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  return record_cuda(launch_quantize_rows(codes, row_scales, x, inverse, m, k, pick_stream(d, stream)));
+}
+
+// ================================================================ weights
+extern "C" int htpg_weights_cols(const htpg_weights *w) { return w ? w->ncols : 0; }
+
+extern "C" void htpg_weights_destroy(htpg_weights *w) {
+  if (!w) return;
+  cudaFree(w->wk);
+  cudaFree(w->sw);
+  cudaFree(w->corr);
+  cudaFree(w->inverse);
+  delete w;
+}
+
+extern "C" int htpg_w8a8_weights_create(const void *constants, int k, int n, int n0, int n_cols,
+                                        void *stream, htpg_weights **out) {
+  if (!out) return HTPG_EARGS;
+  *out = nullptr;
+  if (!constants || k < 32 || k > HTPG_W8A8_MAX_K || n < 64 || n > HTPG_W8A8_MAX_N) return HTPG_EARGS;
+  if (k % 32 || n % 64) return HTPG_ECAPACITY;
+  if (n_cols == 0) n_cols = n - n0;
+  if (n0 < 0 || n0 % 64 || n_cols < 64 || n_cols % 64 || n0 + n_cols > n) return HTPG_ECAPACITY;
+  if (reinterpret_cast<uintptr_t>(constants) & 15u) return HTPG_ECONTROL;
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t st = pick_stream(d, stream);
+  W8A8Header h;
+  if (cudaMemcpyAsync(&h, constants, sizeof(h), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return record_cuda(cudaGetLastError());
+  const size_t kn = static_cast<size_t>(k) * n;
+  const size_t bytes = 128u + kn + 8u * n + 4u * static_cast<size_t>(k);
+  // same acceptance rules as the reference executor (op_executor.cc:331-335)
+  if (h.magic != W8A8_HEADER_MAGIC || h.version != W8A8_HEADER_VERSION || h.k != static_cast<uint32_t>(k) ||
+      h.n != static_cast<uint32_t>(n) || h.weight_offset != 128 || h.scale_offset != 128u + kn ||
+      h.sum_offset != h.scale_offset + 4u * n || h.inverse_offset != h.sum_offset + 4u * n ||
+      h.bytes != bytes)
+    return HTPG_EHEADER;
+  const uint8_t *blob = static_cast<const uint8_t *>(constants);
+  htpg_weights *w = new htpg_weights;
+  w->kind = Kind::I8;
+  w->k = k;
+  w->ncols = n_cols;
+  w->n0 = n0;
+  w->n_total = n;
+  w->device = d->ordinal;
+  uint32_t *flag = nullptr;
+  bool ok = cudaMalloc(&w->wk, static_cast<size_t>(n_cols) * k) == cudaSuccess &&
+            cudaMalloc(&w->sw, 4u * n_cols) == cudaSuccess &&
+            cudaMalloc(&w->corr, 4u * n_cols) == cudaSuccess &&
+            cudaMalloc(&w->inverse, 4u * k) == cudaSuccess && cudaMalloc(&flag, 4) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    cudaFree(flag);
+    htpg_weights_destroy(w);
+    return HTPG_ENOMEM;
+  }
+  cudaError_t e = launch_repack_w8(static_cast<int8_t *>(w->wk), blob + h.weight_offset, k, n0, n_cols, st);
+  if (e == cudaSuccess)
+    e = launch_colsum_corr(w->corr, static_cast<const int8_t *>(w->wk),
+                           reinterpret_cast<const int32_t *>(blob + h.sum_offset), k, n0, n_cols, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(w->sw, blob + h.scale_offset + 4u * n0, 4u * n_cols, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(w->inverse, blob + h.inverse_offset, 4u * k, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(flag, 0, 4, st);
+  if (e == cudaSuccess) e = launch_check_ones(flag, w->inverse, k, st);
+  uint32_t not_ones = 1;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&not_ones, flag, 4, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  cudaFree(flag);
+  if (e != cudaSuccess) {
+    htpg_weights_destroy(w);
+    return record_cuda(e);
+  }
+  if (!not_ones) {  // x*1.0f == x exactly: skip the multiply
+    cudaFree(w->inverse);
+    w->inverse = nullptr;
+  }
+  *out = w;
+  return HTPG_OK;
+}
+
+extern "C" int htpg_f16_weights_create(const uint16_t *permuted_weight, int k, int n, int n0,
+                                       int n_cols, void *stream, htpg_weights **out) {
+  if (!out) return HTPG_EARGS;
+  *out = nullptr;
+  if (!permuted_weight || k < 32 || n < 32) return HTPG_EARGS;
+  if (k % 32 || n % 32) return HTPG_ECAPACITY;
+  if (n_cols == 0) n_cols = n - n0;
+  if (n0 < 0 || n0 % 32 || n_cols < 32 || n_cols % 32 || n0 + n_cols > n) return HTPG_ECAPACITY;
+  if (reinterpret_cast<uintptr_t>(permuted_weight) & 3u) return HTPG_ECONTROL;
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t st = pick_stream(d, stream);
+  htpg_weights *w = new htpg_weights;
+  w->kind = Kind::F16;
+  w->k = k;
+  w->ncols = n_cols;
+  w->n0 = n0;
+  w->n_total = n;
+  w->device = d->ordinal;
+  if (cudaMalloc(&w->wk, static_cast<size_t>(n_cols) * k * 2) != cudaSuccess) {
+    cudaGetLastError();
+    delete w;
+    return HTPG_ENOMEM;
+  }
+  cudaError_t e = launch_repack_f16(static_cast<uint16_t *>(w->wk), permuted_weight, k, n0, n_cols, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    htpg_weights_destroy(w);
+    return record_cuda(e);
+  }
+  *out = w;
+  return HTPG_OK;
+}
+
+// ================================================================ run
+namespace {
+
+int run_common(htpg_weights *w, float *out, int ldo, const float *x, const float *bias, int m,
+               int channels, int mode, void *stream) {
+  if (!w || !out || !x) return HTPG_EARGS;
+  const int n = w->ncols, k = w->k;
+  if (m < 1 || m > HTPG_W8A8_MAX_M) return HTPG_EARGS;
+  if (mode < 0 || mode > HTPG_MODE_RAW) return HTPG_ECAPACITY;
+  if (channels == 0) channels = n;
+  if (channels < 1 || channels > n || (mode != 3 && channels != n)) return HTPG_ECAPACITY;
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return HTPG_ECONTROL;
+  if (reinterpret_cast<uintptr_t>(out) & 3u) return HTPG_ECONTROL;
+  if (ldo == 0) ldo = mode == 3 ? m : n;
+  if ((mode == 3 && ldo < m) || (mode != 3 && ldo < n)) return HTPG_EARGS;
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t st = pick_stream(d, stream);
+  std::lock_guard<std::mutex> lk(g_mu);
+
+  const GemmPlan plan = plan_gemm(w->kind, m, n, k, d->sms);
+  // Workspace: [split-K accumulators + counters | activation codes / FP16 | row scales].
+  // The split-K region sits at a fixed offset and is kept all-zero (zeroed at
+  // allocation, left zeroed by every launch), so no per-call clear is needed.
+  const size_t wsk_bytes = kSplitKRegion;
+  if (splitk_ws_bytes(plan) + splitk_count_bytes(plan) > wsk_bytes) return HTPG_ENOPLAN;
+  const size_t act_elem = w->kind == Kind::I8 ? 1 : 2;
+  const size_t act_bytes = align_up(static_cast<size_t>(m) * k * act_elem, 1024);
+  const size_t scale_bytes = align_up(4u * static_cast<size_t>(m), 1024);
+  void *base = nullptr;
+  rc = workspace(d, st, wsk_bytes + act_bytes + scale_bytes, &base);
+  if (rc) return rc;
+  int32_t *wsk = static_cast<int32_t *>(base);
+  uint32_t *cnt = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(base) + splitk_ws_bytes(plan));
+  uint8_t *act = static_cast<uint8_t *>(base) + wsk_bytes;
+  float *scales = reinterpret_cast<float *>(act + act_bytes);
+
+  const bool prof = g_profiling != 0;
+  PhaseEvents pe;
+  const bool phase = g_phase_on;
+  if (phase) {
+    if (g_phase_free.empty()) {
+      for (auto &e : pe.e) cudaEventCreate(&e);
+    } else {
+      pe = g_phase_free.back();
+      g_phase_free.pop_back();
+    }
+    cudaEventRecord(pe.e[0], st);
+  }
+  if (prof) cudaEventRecord(d->ev[0], st);
+  cudaError_t e;
+  if (w->kind == Kind::I8)
+    e = launch_quantize_rows(reinterpret_cast<int8_t *>(act), scales, x, w->inverse, m, k, st);
+  else
+    e = launch_to_f16(reinterpret_cast<uint16_t *>(act), x, static_cast<long long>(m) * k, st);
+  if (e != cudaSuccess) return record_cuda(e);
+  if (prof) cudaEventRecord(d->ev[1], st);
+  if (phase) cudaEventRecord(pe.e[1], st);
+
+  CUtensorMap act_map;
+  const CUtensorMap *wmap = nullptr;
+  rc = make_map(&act_map, act, w->kind, k, m, static_cast<size_t>(k) * act_elem,
+                plan.swap ? plan.bn : 128);
+  if (rc) return rc;
+  rc = weight_map(w, plan.swap ? 128 : plan.bn, &wmap);
+  if (rc) return rc;
+
+  GemmArgs a;
+  a.M = m;
+  a.N = n;
+  a.K = k;
+  a.out = out;
+  a.ldo = ldo;
+  a.mode = mode;
+  a.channels = channels;
+  a.row_scale = scales;
+  a.col_scale = w->sw;
+  a.col_corr = w->corr;
+  a.bias = bias;
+  a.ws = wsk;
+  a.ws_count = cnt;
+  a.watchdog = d->watchdog;
+  e = plan.swap ? launch_gemm(plan, *wmap, act_map, a, st) : launch_gemm(plan, act_map, *wmap, a, st);
+  if (e != cudaSuccess) return record_cuda(e);
+  if (phase) {
+    cudaEventRecord(pe.e[2], st);
+    g_phase_pending.push_back(pe);
+  }
+  if (prof) {
+    cudaEventRecord(d->ev[2], st);
+    cudaEventSynchronize(d->ev[2]);
+    cudaEventElapsedTime(&t_phase_ms[0], d->ev[0], d->ev[1]);
+    cudaEventElapsedTime(&t_phase_ms[1], d->ev[1], d->ev[2]);
+    cudaEventElapsedTime(&t_phase_ms[2], d->ev[0], d->ev[2]);
+  }
+  return HTPG_OK;
+}
+
+}  // namespace
+
+extern "C" int htpg_w8a8_run(const htpg_weights *w, float *out, int ldo, const float *x,
+                             const float *bias, int m, int channels, int mode, void *stream) {
+  if (!w || w->kind != Kind::I8) return HTPG_EARGS;
+  return run_common(const_cast<htpg_weights *>(w), out, ldo, x, bias, m, channels, mode, stream);
+}
+
+extern "C" int htpg_f16_run(const htpg_weights *w, float *out, int ldo, const float *x,
+                            const float *bias, int m, int channels, int mode, void *stream) {
+  if (!w || w->kind != Kind::F16) return HTPG_EARGS;
+  return run_common(const_cast<htpg_weights *>(w), out, ldo, x, bias, m, channels, mode, stream);
+}
+
+// ================================================================ one-call
+namespace {
+
+int cached_weights(Kind kind, const void *ptr, int k, int n, void *stream, htpg_weights **out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const CacheKey key(ptr, static_cast<int>(kind), k, n, dev);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_cache.find(key);
+    if (it != g_cache.end()) {
+      *out = it->second;
+      return HTPG_OK;
+    }
+  }
+  htpg_weights *w = nullptr;
+  const int rc = kind == Kind::I8
+                     ? htpg_w8a8_weights_create(ptr, k, n, 0, 0, stream, &w)
+                     : htpg_f16_weights_create(static_cast<const uint16_t *>(ptr), k, n, 0, 0, stream, &w);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_cache[key] = w;
+  *out = w;
+  return HTPG_OK;
+}
+
+}  // namespace
+
+extern "C" void htpg_weight_cache_drop(const void *weights) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (auto it = g_cache.begin(); it != g_cache.end();) {
+    if (std::get<0>(it->first) == weights) {
+      htpg_weights_destroy(it->second);
+      it = g_cache.erase(it);
+    } else {
+      ++it;
+    }
+  }
+}
+
+extern "C" void htpg_weight_cache_clear(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (auto &kv : g_cache) htpg_weights_destroy(kv.second);
+  g_cache.clear();
+}
+
+extern "C" int htpg_w8a8_linear(float *out, const float *x, const void *constants, const float *bias,
+                                int m, int k, int n, int channels, int mode, void *stream) {
+  if (!out || !x || !constants || m < 1 || m > HTPG_W8A8_MAX_M || k < 32 || k > HTPG_W8A8_MAX_K ||
+      n < 64 || n > HTPG_W8A8_MAX_N)
+    return HTPG_EARGS;
+  if (k % 32 || n % 64) return HTPG_EARGS;
+  htpg_weights *w = nullptr;
+  int rc = cached_weights(Kind::I8, constants, k, n, stream, &w);
+  if (rc) return rc;
+  return run_common(w, out, 0, x, bias, m, channels, mode, stream);
+}
+
+extern "C" int htpg_f16_linear(float *out, const float *x, const uint16_t *permuted_weight,
+                               const float *bias, int m, int k, int n, int channels, int mode,
+                               void *stream) {
+  // argument checks in the reference's order and codes (mat_mul.c:939-951)
+  if (!out || !x || !permuted_weight || !m || !n || !k) return HTPG_EARGS;
+  if (m < 1 || k < 1 || n < 1 || channels < 1 || channels > n || mode < 0 || mode > 3 ||
+      (mode != 3 && channels != n) || k % 32 || n % 32)
+    return HTPG_ECAPACITY;
+  if (m > HTPG_W8A8_MAX_M) return HTPG_ENOPLAN;
+  htpg_weights *w = nullptr;
+  int rc = cached_weights(Kind::F16, permuted_weight, k, n, stream, &w);
+  if (rc) return rc;
+  return run_common(w, out, 0, x, bias, m, channels, mode, stream);
+}
+
+// ================================================================ reference kernel names
+// Synchronous like the reference kernels: return once the output is written.
+namespace {
+
+int finish_sync(int rc) {
+  if (rc) return rc;
+  return htpg_check_device(nullptr, nullptr);
+}
+
+}  // namespace
+
+extern "C" int hmx_mat_mul_native_w8a8_profiled(float *dst, const float *activation,
+                                                const uint8_t *constants, int m, int k, int n,
+                                                struct NativeW8A8Profile *profile) {
+  // reference admission (linear_w8a8.c:337-338) with the widened M/K limits
+  if (!dst || !activation || !constants || m < 1 || m > HTPG_W8A8_MAX_M || k < 32 ||
+      k > HTPG_W8A8_MAX_K || k % 32 || n < 64 || n > HTPG_W8A8_MAX_N || n % 64)
+    return HTPG_EARGS;
+  uint32_t mode = 0;
+  if (profile) {
+    mode = profile->mode;
+    std::memset(profile, 0, sizeof(*profile));
+    profile->mode = mode;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  htpg_weights *w = nullptr;
+  int rc = cached_weights(Kind::I8, constants, k, n, nullptr, &w);
+  if (rc) return rc;
+  const auto t1 = std::chrono::steady_clock::now();
+  const int prev = g_profiling;
+  if (profile) g_profiling = 1;
+  rc = finish_sync(run_common(w, dst, 0, activation, nullptr, m, 0, 0, nullptr));
+  g_profiling = prev;
+  if (profile && rc == HTPG_OK) {
+    const double tick_per_ms = 19200.0;  // the reference reports 19.2 MHz qtimer ticks
+    profile->setup_ticks =
+        static_cast<uint64_t>(std::chrono::duration<double, std::milli>(t1 - t0).count() * tick_per_ms);
+    profile->activation_ticks = static_cast<uint64_t>(t_phase_ms[0] * tick_per_ms);
+    profile->hmx_ticks = static_cast<uint64_t>(t_phase_ms[1] * tick_per_ms);
+    profile->output_ticks = 0;  // the epilogue is fused into the GEMM
+    if (mode == 2) profile->mac_ticks = profile->hmx_ticks;
+    if (mode == 3) {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      const GemmPlan p = plan_gemm(Kind::I8, m, n, k, g_dev[dev].sms);
+      const uint32_t rows64 = p.swap ? 2u : 2u;
+      const uint32_t cols64 = static_cast<uint32_t>(p.swap ? 2 : (p.bn >= 64 ? p.bn / 64 : 1));
+      profile->reserved = rows64 | (cols64 << 16) | (p.swap ? 0x80000000u : 0u);
+      profile->mac_ticks = static_cast<uint64_t>(p.units);  // weight tiles streamed
+      profile->readout_ticks = static_cast<uint64_t>(p.units) *
+                               static_cast<uint64_t>(p.swap ? 128 : p.bn) *
+                               static_cast<uint64_t>(p.kb_per_split) * 128u;  // weight bytes streamed
+    }
+  }
+  return rc;
+}
+
+extern "C" int hmx_mat_mul_native_w8a8(float *dst, const float *activation, const uint8_t *constants,
+                                       int m, int k, int n) {
+  return hmx_mat_mul_native_w8a8_profiled(dst, activation, constants, m, k, n, nullptr);
+}
+
+// The raw INT32 byte-plane export of the reference (linear_w8a8.c:205-227,
+// 512-526) is a property of the Hexagon HMX readout; this device has no byte
+// planes, so the request is answered like the reference answers it on a DSP
+// without the feature (-75).
+extern "C" int hmx_mat_mul_native_w8a8_cpu(float *dst, const float *activation,
+                                           const uint8_t *constants, int m, int k, int n,
+                                           struct W8A8CpuControl *control) {
+  (void)dst;
+  (void)activation;
+  (void)constants;
+  (void)m;
+  (void)k;
+  (void)n;
+  if (!control) return HTPG_ECONTROL;
+  return HTPG_EARCH;
+}
+
+extern "C" int hmx_mat_mul_f16_epilogue(float *dst, const float *activation, const uint16_t *weight,
+                                        const float *bias, int m, int k, int n, int channels,
+                                        int mode) {
+  if (!dst || !activation || !weight || !m || !n || !k) return HTPG_EARGS;
+  if (m < 1 || k < 1 || n < 1 || channels < 1 || channels > n || mode < 0 || mode > 3 ||
+      (mode != 3 && channels != n) || k % 32 || n % 32)
+    return HTPG_ECAPACITY;
+  // the reference requires 128-byte aligned tensors (mat_mul.c:946-948)
+  if ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(activation) |
+       reinterpret_cast<uintptr_t>(weight)) & 127u)
+    return HTPG_ECONTROL;
+  return finish_sync(htpg_f16_linear(dst, activation, weight, bias, m, k, n, channels, mode, nullptr));
+}
+
+extern "C" int hmx_mat_mul_permuted_w16a32(float *dst, const float *activation,
+                                           const uint16_t *permuted_weight, int m, int k, int n) {
+  return hmx_mat_mul_f16_epilogue(dst, activation, permuted_weight, nullptr, m, k, n, n, 0);
+}

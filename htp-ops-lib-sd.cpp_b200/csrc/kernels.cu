@@ -1,0 +1,745 @@
+// Device kernels of the B200 linear-operator path.
+//
+//  * quantize_rows_*     per-row INT8 activation quantisation, bit-exact with
+//                        the reference's IEEE restatement (linear_w8a8.c:34-128)
+//  * to_f16_kernel       FP32 -> FP16 activation conversion (mat_mul.c:114-148)
+//  * repack_*            one-time weight repacks from the reference layouts
+//                        (HMX deep INT8, permuted FP16 tiles) to K-major rows
+//  * gemm_kernel         warp-specialised persistent GEMM: TMA producer warp,
+//                        single-thread tcgen05.mma issuer with double-buffered
+//                        TMEM accumulators, four epilogue warps that apply the
+//                        dequantisation / bias / activation / layout before
+//                        the first HBM store.
+#include <cuda_fp16.h>
+
+#include <atomic>
+#include <cstdio>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace htpg {
+
+static std::atomic<uint64_t> g_launches{0};
+uint64_t launches() { return g_launches.load(); }
+static inline cudaError_t counted(cudaError_t e) {
+  if (e == cudaSuccess) g_launches.fetch_add(1);
+  return e;
+}
+
+// ===================================================================== quant
+// Shared per-element steps.  Every FP32 operation is an explicit IEEE
+// round-to-nearest intrinsic so the compiler cannot contract or reorder.
+__device__ __forceinline__ float scaled_input(float x, const float *inverse, int c) {
+  return inverse ? __fmul_rn(x, __ldg(inverse + c)) : x;
+}
+// u = x'*s + 128 (two roundings), clamped to [1,255] by integer max/min on the
+// IEEE bits (linear_w8a8.c:44-49), then rounded half to even; returned as the
+// signed code u-128 in [-127, 127].
+__device__ __forceinline__ int quant_code(float xs, float s) {
+  const float u = __fadd_rn(__fmul_rn(xs, s), 128.0f);
+  int b = __float_as_int(u);
+  b = max(b, 0x3f800000);
+  b = min(b, 0x437f0000);
+  return __float2int_rn(__int_as_float(b)) - 128;
+}
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
+         ((static_cast<uint32_t>(c) & 0xffu) << 16) | ((static_cast<uint32_t>(d) & 0xffu) << 24);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Rows are split over `TPR` threads (a warp or a whole block); each thread
+// handles 8 consecutive elements per step (two float4 loads).
+template <int TPR, int ROWS>
+__global__ void __launch_bounds__(TPR *ROWS) quantize_rows_kernel(int8_t *__restrict__ codes,
+                                                                 float *__restrict__ scales,
+                                                                 const float *__restrict__ x,
+                                                                 const float *__restrict__ inverse,
+                                                                 int m, int k) {
+  constexpr int kWarps = TPR / 32;
+  __shared__ float red[ROWS][kWarps > 0 ? kWarps : 1];
+  const int local_row = threadIdx.x / TPR;
+  const int t = threadIdx.x % TPR;
+  const int row = blockIdx.x * ROWS + local_row;
+  const bool valid = row < m;
+  const float *xr = x + static_cast<size_t>(valid ? row : 0) * k;
+
+  float amax = 0.0f;
+  if (valid) {
+    for (int c = t * 8; c < k; c += TPR * 8) {
+      const float4 a = __ldg(reinterpret_cast<const float4 *>(xr + c));
+      const float4 b = __ldg(reinterpret_cast<const float4 *>(xr + c + 4));
+      const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(scaled_input(v[i], inverse, c + i)));
+    }
+  }
+  amax = warp_max(amax);
+  if (kWarps > 1) {
+    if ((t & 31) == 0) red[local_row][t >> 5] = amax;
+    __syncthreads();
+    amax = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) amax = fmaxf(amax, red[local_row][w]);
+  }
+  if (!valid) return;
+  const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+  const float s = __fdiv_rn(1.0f, scale);
+  if (t == 0) scales[row] = scale;
+  int8_t *cr = codes + static_cast<size_t>(row) * k;
+  for (int c = t * 8; c < k; c += TPR * 8) {
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(xr + c));
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(xr + c + 4));
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    int q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = quant_code(scaled_input(v[i], inverse, c + i), s);
+    *reinterpret_cast<uint2 *>(cr + c) =
+        make_uint2(pack4(q[0], q[1], q[2], q[3]), pack4(q[4], q[5], q[6], q[7]));
+  }
+}
+
+cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
+                                 const float *inverse, int m, int k, cudaStream_t st) {
+  // Long rows or few rows: a 256-thread block per row; otherwise a warp per row.
+  if (k >= 4096 || m < 1184) {
+    quantize_rows_kernel<256, 1><<<m, 256, 0, st>>>(codes, scales, x, inverse, m, k);
+  } else {
+    quantize_rows_kernel<32, 8><<<(m + 7) / 8, 256, 0, st>>>(codes, scales, x, inverse, m, k);
+  }
+  return counted(cudaGetLastError());
+}
+
+__global__ void to_f16_kernel(uint16_t *__restrict__ dst, const float *__restrict__ x,
+                              long long count) {
+  const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (i >= count) return;
+  const float4 a = __ldg(reinterpret_cast<const float4 *>(x + i));
+  const float4 b = __ldg(reinterpret_cast<const float4 *>(x + i + 4));
+  const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t lo = __half_as_ushort(__float2half_rn(v[2 * j]));
+    const uint32_t hi = __half_as_ushort(__float2half_rn(v[2 * j + 1]));
+    w[j] = lo | (hi << 16);
+  }
+  *reinterpret_cast<uint4 *>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+cudaError_t launch_to_f16(uint16_t *dst, const float *x, long long count, cudaStream_t st) {
+  const long long threads = (count + 7) / 8;
+  to_f16_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(dst, x, count);
+  return counted(cudaGetLastError());
+}
+
+// ==================================================================== repack
+// HMX deep N64 layout -> K-major rows dst[c][k] for columns n0+c.
+__device__ __forceinline__ size_t deep_offset(int k_total, int n, int k) {
+  return static_cast<size_t>(n / 64) * 64u * static_cast<size_t>(k_total) +
+         static_cast<size_t>(k / 32) * 2048u + static_cast<size_t>((n % 64) / 32) * 1024u +
+         static_cast<size_t>((k % 32) / 4) * 128u + static_cast<size_t>(n % 32) * 4u +
+         static_cast<size_t>(k % 4);
+}
+
+__global__ void repack_w8_kernel(int8_t *__restrict__ dst, const uint8_t *__restrict__ deep, int k,
+                                 int n0, int ncols) {
+  const long long words = static_cast<long long>(ncols) * (k / 4);
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= words) return;
+  const int c = static_cast<int>(i / (k / 4));
+  const int kk = static_cast<int>(i % (k / 4)) * 4;
+  const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(deep + deep_offset(k, n0 + c, kk)));
+  *reinterpret_cast<uint32_t *>(dst + static_cast<size_t>(c) * k + kk) = v;
+}
+
+cudaError_t launch_repack_w8(int8_t *dst, const uint8_t *deep, int k, int n0, int ncols,
+                             cudaStream_t st) {
+  const long long words = static_cast<long long>(ncols) * (k / 4);
+  repack_w8_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0, st>>>(dst, deep, k, n0,
+                                                                               ncols);
+  return counted(cudaGetLastError());
+}
+
+// corr[c] = (sum_k w[c][k] - sums[n0+c]) << 7 in wrapping INT32: the
+// difference between the reference's zero-point correction, which uses the
+// blob's stored column sums (linear_w8a8.c:159, 168), and the signed
+// accumulation done here.  Zero for every blob whose sums are consistent.
+__global__ void colsum_corr_kernel(int32_t *__restrict__ corr, const int8_t *__restrict__ wk,
+                                   const int32_t *__restrict__ sums, int k, int n0, int ncols) {
+  const int c = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (c >= ncols) return;
+  const int8_t *row = wk + static_cast<size_t>(c) * k;
+  int s = 0;
+  for (int i = lane * 4; i < k; i += 128) {
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(row + i);
+    s += static_cast<int8_t>(w & 0xff) + static_cast<int8_t>((w >> 8) & 0xff) +
+         static_cast<int8_t>((w >> 16) & 0xff) + static_cast<int8_t>(w >> 24);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) {
+    const uint32_t diff = static_cast<uint32_t>(s) - static_cast<uint32_t>(sums[n0 + c]);
+    corr[c] = static_cast<int32_t>(diff << 7);
+  }
+}
+
+cudaError_t launch_colsum_corr(int32_t *corr, const int8_t *wk, const int32_t *sums, int k, int n0,
+                               int ncols, cudaStream_t st) {
+  colsum_corr_kernel<<<(ncols + 7) / 8, 256, 0, st>>>(corr, wk, sums, k, n0, ncols);
+  return counted(cudaGetLastError());
+}
+
+__global__ void check_ones_kernel(uint32_t *flag, const float *v, int count) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < count && __float_as_uint(v[i]) != 0x3f800000u) atomicOr(flag, 1u);
+}
+
+cudaError_t launch_check_ones(uint32_t *flag, const float *v, int count, cudaStream_t st) {
+  check_ones_kernel<<<(count + 255) / 256, 256, 0, st>>>(flag, v, count);
+  return counted(cudaGetLastError());
+}
+
+// Permuted FP16 tiles (element (k,n) at tile (n/32)*(K/32)+k/32, offset
+// ((k%32)&~1)*32 + (n%32)*2 + (k&1)) -> K-major rows dst[c][k].  Elements k
+// and k+1 (k even) are adjacent, so one 32-bit word moves a pair.
+__global__ void repack_f16_kernel(uint16_t *__restrict__ dst, const uint16_t *__restrict__ perm,
+                                  int k, int n0, int ncols) {
+  const long long pairs = static_cast<long long>(ncols) * (k / 2);
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= pairs) return;
+  const int c = static_cast<int>(i / (k / 2));
+  const int kk = static_cast<int>(i % (k / 2)) * 2;
+  const int n = n0 + c;
+  const size_t tile = static_cast<size_t>(n / 32) * static_cast<size_t>(k / 32) + kk / 32;
+  const size_t off = tile * 1024u + static_cast<size_t>(kk % 32) * 32u + static_cast<size_t>(n % 32) * 2u;
+  const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(perm + off));
+  *reinterpret_cast<uint32_t *>(dst + static_cast<size_t>(c) * k + kk) = v;
+}
+
+cudaError_t launch_repack_f16(uint16_t *dst, const uint16_t *perm, int k, int n0, int ncols,
+                              cudaStream_t st) {
+  const long long pairs = static_cast<long long>(ncols) * (k / 2);
+  repack_f16_kernel<<<static_cast<unsigned>((pairs + 255) / 256), 256, 0, st>>>(dst, perm, k, n0,
+                                                                                ncols);
+  return counted(cudaGetLastError());
+}
+
+// ====================================================================== GEMM
+// Optional epilogue activation (mat_mul.c:788-826): GELU(tanh) written as
+// x*sigmoid(1.5957691216057308*(x + 0.044715 x^3)), QuickGELU as
+// x*sigmoid(1.702 x); the sigmoid keeps the reference's stable form
+// e = 2^max(-|z| log2(e), -126), inv = 1/(1+e), sigma = z<0 ? e*inv : inv,
+// with CUDA's exp2f and a correctly rounded reciprocal.
+__device__ __forceinline__ float epilogue_act(float x, int mode) {
+  if (mode != 1 && mode != 2) return x;
+  float z;
+  if (mode == 1) {
+    const float cubic = __fmul_rn(__fmul_rn(x, x), x);
+    z = __fmul_rn(__fadd_rn(x, __fmul_rn(cubic, 0.044715f)), 1.5957691216057308f);
+  } else {
+    z = __fmul_rn(x, 1.702f);
+  }
+  const float arg = fmaxf(__fmul_rn(fabsf(z), -1.4426950408889634f), -126.0f);
+  const float e = exp2f(arg);
+  const float inv = __frcp_rn(__fadd_rn(e, 1.0f));
+  const float sig = z < 0.0f ? __fmul_rn(e, inv) : inv;
+  return __fmul_rn(x, sig);
+}
+
+// I8: v = fl(fl(float(acc + corr) * sw) * rs) (linear_w8a8.c:168-179), then bias, act.
+__device__ __forceinline__ float finish_i8(int32_t acc, int32_t corr, float sw, float rs,
+                                           float bias, bool has_bias, int mode) {
+  const int32_t y = static_cast<int32_t>(static_cast<uint32_t>(acc) + static_cast<uint32_t>(corr));
+  if (mode == 4) return __int_as_float(y);  // diagnostic: raw INT32 accumulator
+  float v = __fmul_rn(__fmul_rn(__int2float_rn(y), sw), rs);
+  if (has_bias) v = __fadd_rn(v, bias);
+  return epilogue_act(v, mode);
+}
+// F16: v = acc (FP32 accumulate), then bias, act (mat_mul.c:864-882).
+__device__ __forceinline__ float finish_f16(float acc, float bias, bool has_bias, int mode) {
+  if (mode == 4) return acc;  // diagnostic: raw FP32 accumulator
+  float v = acc;
+  if (has_bias) v = __fadd_rn(v, bias);
+  return epilogue_act(v, mode);
+}
+
+constexpr int kThreads = 192;      // warp 0 TMA, warp 1 MMA/TMEM, warps 2..5 epilogue
+constexpr int kEpiThreads = 128;
+constexpr int kRowBytes = 128;     // one K block = one 128-byte swizzle row
+constexpr int kTransposeStride = 33;
+
+__host__ __device__ constexpr int stages_for(int bn) {
+  return bn >= 256 ? 4 : bn >= 128 ? 6 : bn >= 64 ? 8 : 10;
+}
+__host__ __device__ constexpr int tmem_cols_for(int bn) {
+  return 2 * bn <= 32 ? 32 : 2 * bn <= 64 ? 64 : 2 * bn <= 128 ? 128 : 2 * bn <= 256 ? 256 : 512;
+}
+__host__ __device__ constexpr size_t smem_bytes_for(int bn) {
+  return 1024 /* alignment slack */ + static_cast<size_t>(stages_for(bn)) * (128 + bn) * kRowBytes +
+         4u * 32u * kTransposeStride * 4u + 256 /* barriers, tmem slot, flags */;
+}
+
+struct SmemLayout {
+  uint8_t *a;          // STAGES x 128 rows x 128 B
+  uint8_t *b;          // STAGES x BN rows x 128 B
+  float *transpose;    // 4 warps x 32 x 33
+  uint64_t *full, *empty, *tfull, *tempty, *mma_done;
+  uint32_t *tmem_slot;
+  uint32_t *flag;            // split-K "this CTA finishes the tile"
+  volatile uint32_t *abort;  // sticky: some wait of this CTA gave up
+};
+
+template <int BN, int STAGES>
+__device__ __forceinline__ SmemLayout carve(uint8_t *raw) {
+  SmemLayout L;
+  uint8_t *p = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  L.a = p;
+  p += STAGES * 128 * kRowBytes;
+  L.b = p;
+  p += STAGES * BN * kRowBytes;
+  L.transpose = reinterpret_cast<float *>(p);
+  p += 4 * 32 * kTransposeStride * 4;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(p);
+  L.full = bars;
+  L.empty = bars + STAGES;
+  L.tfull = bars + 2 * STAGES;
+  L.tempty = bars + 2 * STAGES + 2;
+  L.mma_done = bars + 2 * STAGES + 4;
+  L.tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
+  L.flag = L.tmem_slot + 1;
+  L.abort = L.tmem_slot + 2;
+  return L;
+}
+
+struct Unit {
+  int ta, tb, ks;
+};
+__device__ __forceinline__ Unit decode_unit(int u, int tiles_b, int splits) {
+  Unit w;
+  w.ta = u / (tiles_b * splits);
+  const int r = u % (tiles_b * splits);
+  w.tb = r / splits;
+  w.ks = r % splits;
+  return w;
+}
+
+struct KernelParams {
+  GemmArgs a;
+  int tiles_a, tiles_b, splits, kb_total, kb_per_split, units;
+};
+
+template <Kind KIND, int BN, bool SWAP>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const KernelParams P) {
+  constexpr int STAGES = stages_for(BN);
+  constexpr int TCOLS = tmem_cols_for(BN);
+  constexpr uint32_t kStageBytes = (128 + BN) * kRowBytes;
+  constexpr int kElemsPerRow = KIND == Kind::I8 ? 128 : 64;
+  constexpr uint32_t kIdesc = KIND == Kind::I8 ? idesc_i8(128, BN) : idesc_f16(128, BN);
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(!SWAP || BN <= 32, "swapped tiles hold at most 32 activation rows");
+
+  extern __shared__ uint8_t smem_raw[];
+  const SmemLayout L = carve<BN, STAGES>(smem_raw);
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const GemmArgs &g = P.a;
+  uint32_t *wd = g.watchdog;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&L.full[s]), 1);
+      mbar_init(smem_u32(&L.empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&L.tfull[b]), 1);
+      mbar_init(smem_u32(&L.tempty[b]), kEpiThreads / 32);
+    }
+    mbar_init(smem_u32(L.mma_done), 1);
+    *L.abort = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(L.tmem_slot), TCOLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *L.tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int s = 0;
+      uint32_t ph = 0;
+      int last_phase[STAGES];
+#pragma unroll
+      for (int i = 0; i < STAGES; ++i) last_phase[i] = -1;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < P.units; u += gridDim.x) {
+        const Unit w = decode_unit(u, P.tiles_b, P.splits);
+        const int kb0 = w.ks * P.kb_per_split;
+        const int kb1 = min(kb0 + P.kb_per_split, P.kb_total);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(smem_u32(&L.empty[s]), ph ^ 1u, wd, kWatchProducer, L.abort)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&L.full[s]);
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          tma_load_2d(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, kb * kElemsPerRow, w.ta * 128);
+          tma_load_2d(smem_u32(L.b + s * BN * kRowBytes), &tmB, fb, kb * kElemsPerRow, w.tb * BN);
+          last_phase[s] = static_cast<int>(ph);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Never leave the CTA with a TMA copy still landing in its shared memory.
+      for (int i = 0; i < STAGES; ++i)
+        if (last_phase[i] >= 0)
+          mbar_wait(smem_u32(&L.full[i]), static_cast<uint32_t>(last_phase[i]), wd, kWatchProducer,
+                    L.abort);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t iter = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < P.units; u += gridDim.x, ++iter) {
+        const Unit w = decode_unit(u, P.tiles_b, P.splits);
+        const int kb0 = w.ks * P.kb_per_split;
+        const int kb1 = min(kb0 + P.kb_per_split, P.kb_total);
+        const uint32_t buf = iter & 1u;
+        const uint32_t acc_ph = (iter >> 1) & 1u;
+        if (!mbar_wait(smem_u32(&L.tempty[buf]), acc_ph ^ 1u, wd, kWatchMma, L.abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(smem_u32(&L.full[s]), ph, wd, kWatchMma, L.abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(L.a + s * 128 * kRowBytes);
+          const uint32_t b_addr = smem_u32(L.b + s * BN * kRowBytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t da = umma_desc_sw128(a_addr + kk * 32);
+            const uint64_t db = umma_desc_sw128(b_addr + kk * 32);
+            const uint32_t accumulate = (kb > kb0 || kk > 0) ? 1u : 0u;
+            if (KIND == Kind::I8)
+              umma_i8(d_tmem, da, db, kIdesc, accumulate);
+            else
+              umma_f16(d_tmem, da, db, kIdesc, accumulate);
+          }
+          tc_commit(smem_u32(&L.empty[s]));
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (ok) tc_commit(smem_u32(&L.tfull[buf]));
+      }
+      // All MMAs of this thread complete before TMEM can be released.
+      tc_commit(smem_u32(L.mma_done));
+      mbar_wait(smem_u32(L.mma_done), 0, wd, kWatchMma, L.abort);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;                      // TMEM lane quadrant of this warp
+    const int epi_t = threadIdx.x - 64;          // 0..127
+    float *tr = L.transpose + (warp - 2) * 32 * kTransposeStride;
+    const bool has_bias = g.bias != nullptr;
+    uint32_t iter = 0;
+    for (int u = blockIdx.x; u < P.units; u += gridDim.x, ++iter) {
+      const Unit w = decode_unit(u, P.tiles_b, P.splits);
+      const uint32_t buf = iter & 1u;
+      const uint32_t acc_ph = (iter >> 1) & 1u;
+      // No early exit: all four epilogue warps run the same iterations so
+      // their named barriers always match; after a failed wait the unit's
+      // work is skipped (the watchdog word reports the failure).
+      const bool ok = mbar_wait(smem_u32(&L.tfull[buf]), acc_ph, wd, kWatchEpilogue, L.abort);
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+
+      if (!SWAP) {
+        if (!ok) continue;
+        // rows of D = activation rows m, columns = weight columns n
+        const int m = w.ta * 128 + q * 32 + lane;
+        const bool m_ok = m < g.M;
+        const float rs = (KIND == Kind::I8 && m_ok) ? __ldg(g.row_scale + m) : 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c * 32, r);
+          tmem_ld_wait();
+          const int n0 = w.tb * BN + c * 32;
+          const int nl = n0 + lane;
+          const bool nl_ok = nl < g.N;
+          float sw_l = 0.0f, b_l = 0.0f;
+          int32_t cr_l = 0;
+          if (nl_ok) {
+            if (KIND == Kind::I8) {
+              sw_l = __ldg(g.col_scale + nl);
+              cr_l = __ldg(g.col_corr + nl);
+            }
+            if (has_bias) b_l = __ldg(g.bias + nl);
+          }
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float bj = __shfl_sync(0xffffffffu, b_l, j);
+            if (KIND == Kind::I8) {
+              const float swj = __shfl_sync(0xffffffffu, sw_l, j);
+              const int32_t crj = __shfl_sync(0xffffffffu, cr_l, j);
+              v[j] = finish_i8(static_cast<int32_t>(r[j]), crj, swj, rs, bj, has_bias, g.mode);
+            } else {
+              v[j] = finish_f16(__uint_as_float(r[j]), bj, has_bias, g.mode);
+            }
+          }
+          if (g.mode == 3) {
+            // channel-major: out[n*ldo + m]; lanes hold consecutive m -> coalesced
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = n0 + j;
+              if (m_ok && n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = v[j];
+            }
+          } else {
+            // row-major: transpose through shared memory so each store is one
+            // 128-byte row segment
+#pragma unroll
+            for (int j = 0; j < 32; ++j) tr[lane * kTransposeStride + j] = v[j];
+            __syncwarp();
+            const int mbase = w.ta * 128 + q * 32;
+#pragma unroll 4
+            for (int rr = 0; rr < 32; ++rr) {
+              const int mr = mbase + rr;
+              if (mr < g.M && nl_ok)
+                g.out[static_cast<long long>(mr) * g.ldo + nl] = tr[rr * kTransposeStride + lane];
+            }
+            __syncwarp();
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&L.tempty[buf]));
+      } else {
+        // rows of D = weight columns n, columns = activation rows m (BN <= 32)
+        const int n = w.ta * 128 + q * 32 + lane;
+        const bool n_ok = n < g.N;
+        uint32_t r[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+        if (ok) {
+          if (BN == 16) {
+            uint32_t r16[16];
+            tmem_ld16(t_row, r16);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) r[j] = r16[j];
+          } else {
+            tmem_ld32(t_row, r);
+            tmem_ld_wait();
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&L.tempty[buf]));
+        }
+
+        bool finish = ok;
+        if (P.splits > 1) {
+          // exact INT32 split-K: accumulate partials in HBM; the last CTA of the
+          // tile finishes it and leaves the workspace zeroed for the next call
+          const int tile = w.ta * P.tiles_b + w.tb;
+          int32_t *ws = g.ws + (static_cast<size_t>(tile) * 128 + q * 32 + lane) * BN;
+          if (ok) {
+#pragma unroll
+            for (int j = 0; j < BN; ++j) atomicAdd(ws + j, static_cast<int32_t>(r[j]));
+            __threadfence();
+          }
+          named_bar_sync(1, kEpiThreads);
+          if (epi_t == 0) {
+            uint32_t last = 0u;
+            if (!*L.abort) {
+              const uint32_t prev = atomicAdd(g.ws_count + tile, 1u);
+              last = (prev == static_cast<uint32_t>(P.splits - 1)) ? 1u : 0u;
+            }
+            *L.flag = last;
+          }
+          named_bar_sync(1, kEpiThreads);
+          finish = ok && *L.flag != 0u;
+          if (finish) {
+            __threadfence();
+#pragma unroll
+            for (int j = 0; j < BN; ++j) {
+              r[j] = static_cast<uint32_t>(__ldcg(ws + j));
+              ws[j] = 0;
+            }
+            if (epi_t == 0) g.ws_count[tile] = 0u;
+          }
+          named_bar_sync(1, kEpiThreads);
+        }
+        if (finish) {
+          const int mrow = w.tb * BN + lane;
+          const float rs_l = (KIND == Kind::I8 && mrow < g.M) ? __ldg(g.row_scale + mrow) : 0.0f;
+          float rsj[BN];
+#pragma unroll
+          for (int j = 0; j < BN; ++j) rsj[j] = __shfl_sync(0xffffffffu, rs_l, j);
+          if (n_ok) {
+            float sw = 0.0f, bn_ = 0.0f;
+            int32_t cr = 0;
+            if (KIND == Kind::I8) {
+              sw = __ldg(g.col_scale + n);
+              cr = __ldg(g.col_corr + n);
+            }
+            if (has_bias) bn_ = __ldg(g.bias + n);
+#pragma unroll
+            for (int j = 0; j < BN; ++j) {
+              const int m = w.tb * BN + j;
+              if (m >= g.M) continue;
+              const float v = KIND == Kind::I8 ? finish_i8(static_cast<int32_t>(r[j]), cr, sw, rsj[j],
+                                                           bn_, has_bias, g.mode)
+                                               : finish_f16(__uint_as_float(r[j]), bn_, has_bias, g.mode);
+              if (g.mode == 3) {
+                if (n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = v;
+              } else {
+                g.out[static_cast<long long>(m) * g.ldo + n] = v;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TCOLS);
+  }
+}
+
+// --------------------------------------------------------------- planning
+// Tile plan keyed on M:
+//  * I8 and M <= 32: swapped orientation (weights fill the 128-row MMA
+//    dimension, the activation rows are the MMA N = 16 or 32); the K range is
+//    split over CTAs until the grid covers the SMs, with an exact INT32
+//    reduction.  These shapes stream the weight once and are HBM-bound.
+//  * otherwise: activation rows in 128-row tiles and the widest weight tile
+//    N in {256, 128, 64, 32} that still gives one CTA per SM; K stays whole
+//    inside a CTA (no split), so the FP16 accumulation order never depends on
+//    the plan.
+GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms) {
+  GemmPlan p;
+  p.kind = kind;
+  const int elems = kind == Kind::I8 ? 128 : 64;
+  p.kb_total = (K + elems - 1) / elems;
+  if (kind == Kind::I8 && M <= 32) {
+    p.swap = true;
+    p.bn = M <= 16 ? 16 : 32;
+    p.tiles_a = (N + 127) / 128;
+    p.tiles_b = (M + p.bn - 1) / p.bn;
+    int splits = num_sms / (p.tiles_a * p.tiles_b);
+    splits = splits < 1 ? 1 : splits;
+    const int max_splits = p.kb_total / 8 > 0 ? p.kb_total / 8 : 1;
+    splits = splits > max_splits ? max_splits : splits;
+    p.kb_per_split = (p.kb_total + splits - 1) / splits;
+    p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
+  } else {
+    p.swap = false;
+    p.tiles_a = (M + 127) / 128;
+    const int cands[4] = {256, 128, 64, 32};
+    p.bn = 32;
+    for (int c : cands) {
+      // accept one wave that leaves at most ~15% of the SMs idle
+      if (static_cast<long long>(p.tiles_a) * ((N + c - 1) / c) * 20 >= 17LL * num_sms) {
+        p.bn = c;
+        break;
+      }
+    }
+    p.tiles_b = (N + p.bn - 1) / p.bn;
+    p.splits = 1;
+    p.kb_per_split = p.kb_total;
+  }
+  p.units = p.tiles_a * p.tiles_b * p.splits;
+  p.grid = p.units < num_sms ? p.units : num_sms;
+  p.smem = smem_bytes_for(p.bn);
+  return p;
+}
+
+size_t splitk_ws_bytes(const GemmPlan &p) {
+  return p.splits > 1 ? static_cast<size_t>(p.tiles_a) * p.tiles_b * 128 * p.bn * 4 : 0;
+}
+size_t splitk_count_bytes(const GemmPlan &p) {
+  return p.splits > 1 ? static_cast<size_t>(p.tiles_a) * p.tiles_b * 4 : 0;
+}
+
+template <Kind KIND, int BN, bool SWAP>
+static cudaError_t launch_one(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
+                              const GemmArgs &a, cudaStream_t st) {
+  auto fn = gemm_kernel<KIND, BN, SWAP>;
+  static bool configured = false;  // per instantiation; first call happens before any capture
+  const size_t smem = smem_bytes_for(BN);
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  KernelParams P;
+  P.a = a;
+  P.tiles_a = p.tiles_a;
+  P.tiles_b = p.tiles_b;
+  P.splits = p.splits;
+  P.kb_total = p.kb_total;
+  P.kb_per_split = p.kb_per_split;
+  P.units = p.units;
+  fn<<<p.grid, kThreads, smem, st>>>(tmA, tmB, P);
+  return counted(cudaGetLastError());
+}
+
+cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
+                        const GemmArgs &a, cudaStream_t st) {
+  if (p.kind == Kind::I8) {
+    if (p.swap) {
+      if (p.bn == 16) return launch_one<Kind::I8, 16, true>(p, tmA, tmB, a, st);
+      if (p.bn == 32) return launch_one<Kind::I8, 32, true>(p, tmA, tmB, a, st);
+    } else {
+      switch (p.bn) {
+        case 256: return launch_one<Kind::I8, 256, false>(p, tmA, tmB, a, st);
+        case 128: return launch_one<Kind::I8, 128, false>(p, tmA, tmB, a, st);
+        case 64: return launch_one<Kind::I8, 64, false>(p, tmA, tmB, a, st);
+        case 32: return launch_one<Kind::I8, 32, false>(p, tmA, tmB, a, st);
+        default: break;
+      }
+    }
+  } else if (!p.swap) {
+    switch (p.bn) {
+      case 256: return launch_one<Kind::F16, 256, false>(p, tmA, tmB, a, st);
+      case 128: return launch_one<Kind::F16, 128, false>(p, tmA, tmB, a, st);
+      case 64: return launch_one<Kind::F16, 64, false>(p, tmA, tmB, a, st);
+      case 32: return launch_one<Kind::F16, 32, false>(p, tmA, tmB, a, st);
+      default: break;
+    }
+  }
+  return cudaErrorInvalidConfiguration;
+}
+
+}  // namespace htpg

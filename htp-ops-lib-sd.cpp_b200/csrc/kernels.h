@@ -1,0 +1,69 @@
+// Host-side launchers of the device kernels (kernels.cu).  Internal to
+// libhtp_ops_b200.so; the public surface is include/htp_ops_b200.h.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace htpg {
+
+enum class Kind : int { I8 = 0, F16 = 1 };
+
+// One GEMM launch: D[rows_a x rows_b] = A[rows_a x K] * B[rows_b x K]^T, both
+// operands K-major in HBM and fetched by TMA.  Normal orientation: A = the
+// activation (M rows), B = the weight (N rows).  Swapped (small M): A = the
+// weight, B = the activation, so the 128-row MMA dimension runs over N.
+struct GemmPlan {
+  Kind kind = Kind::I8;
+  bool swap = false;
+  int bn = 256;          // MMA N (rows of B per tile)
+  int splits = 1;        // K splits (I8 swapped only; exact INT32 reduction)
+  int tiles_a = 0, tiles_b = 0;
+  int kb_total = 0, kb_per_split = 0;
+  int units = 0;         // tiles_a * tiles_b * splits
+  int grid = 0;          // persistent CTAs
+  size_t smem = 0;       // dynamic shared memory bytes
+};
+
+struct GemmArgs {
+  int M = 0, N = 0, K = 0;        // logical problem (N = columns of this weight)
+  float *out = nullptr;
+  long long ldo = 0;              // elements between output rows
+  int mode = 0, channels = 0;
+  const float *row_scale = nullptr;  // I8: [M]
+  const float *col_scale = nullptr;  // I8: [N]
+  const int32_t *col_corr = nullptr; // I8: [N]
+  const float *bias = nullptr;       // [N] or null
+  int32_t *ws = nullptr;             // split-K accumulators
+  uint32_t *ws_count = nullptr;      // split-K arrival counters (self-resetting)
+  uint32_t *watchdog = nullptr;
+};
+
+// Plan for an M x N x K problem (see plan_gemm in kernels.cu for the rules).
+GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms);
+// Bytes of split-K workspace (ws) and counters the plan needs.
+size_t splitk_ws_bytes(const GemmPlan &p);
+size_t splitk_count_bytes(const GemmPlan &p);
+// Box rows of the A and B tensor maps for this plan.
+inline int box_rows_a(const GemmPlan &) { return 128; }
+inline int box_rows_b(const GemmPlan &p) { return p.bn; }
+
+cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
+                        const GemmArgs &a, cudaStream_t st);
+
+cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
+                                 const float *inverse, int m, int k, cudaStream_t st);
+cudaError_t launch_to_f16(uint16_t *dst, const float *x, long long count, cudaStream_t st);
+cudaError_t launch_repack_w8(int8_t *dst, const uint8_t *deep, int k, int n0, int ncols,
+                             cudaStream_t st);
+cudaError_t launch_colsum_corr(int32_t *corr, const int8_t *wk, const int32_t *sums, int k,
+                               int n0, int ncols, cudaStream_t st);
+cudaError_t launch_check_ones(uint32_t *flag, const float *v, int count, cudaStream_t st);
+cudaError_t launch_repack_f16(uint16_t *dst, const uint16_t *perm, int k, int n0, int ncols,
+                              cudaStream_t st);
+
+// Kernel launches issued since load (all launchers above count themselves).
+uint64_t launches();
+
+}  // namespace htpg

@@ -1,0 +1,231 @@
+"""ctypes binding of libhtp_ops_b200.so for the Python harness (tests, bench,
+smoke).  The library is plain C: every call passes raw device pointers, sizes
+and a cudaStream_t; torch is used by the harness only to own device memory and
+streams.  Loading fails loudly when the compiled library is missing: there is
+no fallback implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "libhtp_ops_b200.so")
+INCLUDE = os.path.join(REPO, "include")
+
+# error codes (include/htp_ops_b200.h)
+OK, EPAYLOAD, EUNMAPPED, EHEADER = 0, -1, -2, -3
+EARGS, ECAPACITY, ECONTROL, ELAUNCH, ENOPLAN = -10, -11, -12, -13, -14
+EWATCHDOG, ENOMEM, EARCH = -16, -17, -75
+BUF_DEVICE, BUF_HOST = 0, 1
+
+_lib = None
+
+
+def build(jobs: int = 8) -> str:
+    subprocess.run(["make", "-s", "-C", HERE, f"-j{jobs}"], check=True)
+    return LIB_PATH
+
+
+def declared_symbols() -> list[str]:
+    """Function names declared in include/*.h and include/host/*.h."""
+    names = []
+    for root, _, files in os.walk(INCLUDE):
+        for f in files:
+            if not f.endswith(".h"):
+                continue
+            text = open(os.path.join(root, f)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            text = re.sub(r"#define[^\n]*\n", "\n", text)
+            text = re.sub(r"static inline[^{]*\{.*?\n\}", "", text, flags=re.S)
+            for m in re.finditer(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(([^;{]*)\)\s*;", text):
+                name = m.group(1)
+                if name in ("sizeof", "if", "return", "HTPB_STATIC_ASSERT", "__attribute__"):
+                    continue
+                names.append(name)
+    return sorted(set(names))
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is not built (run __graft_entry__.build()); "
+                           "this library has no CPU fallback")
+    L = ctypes.CDLL(LIB_PATH)
+    P, I, S, U32, U64, I64 = (ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_uint32,
+                              ctypes.c_uint64, ctypes.c_int64)
+    sig = {
+        "htpg_init": (I, [I]),
+        "htpg_version": (I, []),
+        "htpg_strerror": (ctypes.c_char_p, [I]),
+        "htpg_last_cuda_error": (ctypes.c_char_p, []),
+        "htpg_check_device": (I, [P, ctypes.POINTER(U32)]),
+        "htpg_quantize_rows": (I, [P, P, P, P, I, I, P]),
+        "htpg_w8a8_weights_create": (I, [P, I, I, I, I, P, ctypes.POINTER(P)]),
+        "htpg_f16_weights_create": (I, [P, I, I, I, I, P, ctypes.POINTER(P)]),
+        "htpg_weights_destroy": (None, [P]),
+        "htpg_weights_cols": (I, [P]),
+        "htpg_w8a8_run": (I, [P, P, I, P, P, I, I, I, P]),
+        "htpg_f16_run": (I, [P, P, I, P, P, I, I, I, P]),
+        "htpg_w8a8_linear": (I, [P, P, P, P, I, I, I, I, I, P]),
+        "htpg_f16_linear": (I, [P, P, P, P, I, I, I, I, I, P]),
+        "htpg_weight_cache_drop": (None, [P]),
+        "htpg_weight_cache_clear": (None, []),
+        "htpg_set_profiling": (I, [I]),
+        "htpg_last_phase_ms": (I, [ctypes.POINTER(ctypes.c_float)] * 3),
+        "htpg_launch_count": (U64, []),
+        "htpg_plan_info": (I, [I, I, I, I, I, ctypes.POINTER(I64)]),
+        "htpg_phase_timing": (I, [I]),
+        "htpg_phase_timing_read": (I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                                       ctypes.POINTER(I)]),
+        "htpg_buffer_alloc": (I, [S, I, ctypes.POINTER(I), ctypes.POINTER(P)]),
+        "htpg_buffer_register": (I, [I, P, S, I]),
+        "htpg_buffer_release": (I, [I]),
+        "htpg_buffer_touch": (I, [I]),
+        "htpg_buffer_resolve": (P, [I, I64, S, ctypes.POINTER(I)]),
+        "execute_op_simple": (I, [P, S]),
+        "hmx_mat_mul_native_w8a8": (I, [P, P, P, I, I, I]),
+        "hmx_mat_mul_native_w8a8_profiled": (I, [P, P, P, I, I, I, P]),
+        "hmx_mat_mul_native_w8a8_cpu": (I, [P, P, P, I, I, I, P]),
+        "hmx_mat_mul_f16_epilogue": (I, [P, P, P, P, I, I, I, I, I]),
+        "hmx_mat_mul_permuted_w16a32": (I, [P, P, P, I, I, I]),
+        "htp_ops_open": (I, [ctypes.c_char_p, ctypes.POINTER(U64)]),
+        "htp_ops_close": (I, [U64]),
+        "htp_ops_init_backend": (I, [U64]),
+        "htp_ops_init_backend_fraction": (I, [U64, U32, U32]),
+        "htp_ops_init_mapping_backend": (I, [U64]),
+        "htp_ops_release_backend": (I, [U64]),
+        "htp_ops_create_channel": (I, [U64, ctypes.c_int32, U32]),
+        "htp_ops_create_channel_with_token": (I, [U64, U64, ctypes.c_int32, U32]),
+        "htp_ops_destroy_channel": (I, [U64]),
+        "htp_ops_rms_norm_f32": (I, [U64, I, I, I, I, I, I]),
+        "htp_ops_mat_mul_permuted_w16a32": (I, [U64, I, I, I, I, I, I, I, I, I]),
+        "htp_ops_mat_mul_permuted_w16a32_trace": (I, [U64, I, I, I, I, I, I, I, I, I] + [ctypes.POINTER(U64)] * 3),
+        "htp_ops_test_ops": (I, [U64, ctypes.POINTER(ctypes.c_int32)]),
+        "htp_ops_session_open": (I, [ctypes.POINTER(P), I, ctypes.c_char_p, I]),
+        "htp_ops_default_session": (P, []),
+        "htp_ops_session_init_backend": (I, [P]),
+        "htp_ops_session_acquire_backend": (I, [P]),
+        "htp_ops_session_release_backend": (I, [P]),
+        "htp_ops_session_create_channel": (I, [P, I, ctypes.c_uint]),
+        "htp_ops_session_create_channel_with_token": (I, [P, I, ctypes.c_uint]),
+        "htp_ops_session_destroy_channel": (I, [P]),
+        "htp_ops_session_handle": (U64, [P]),
+        "htp_ops_set_active_session": (I, [P]),
+        "htp_ops_set_default_session": (I, []),
+        "htp_ops_session_id": (U32, [P]),
+        "htp_ops_session_domain": (U32, [P]),
+        "htp_ops_session_is_reserved": (I, [P]),
+        "htp_ops_session_is_initialized": (I, [P]),
+        "htp_ops_session_has_channel": (I, [P]),
+        "htp_ops_session_close": (None, [P]),
+        "open_dsp_session": (I, [I, I]),
+        "close_dsp_session": (None, []),
+        "get_global_handle": (U64, []),
+        "init_htp_backend": (None, []),
+        "release_htp_backend": (I, []),
+        "create_htp_message_channel": (I, [I, ctypes.c_uint]),
+        "destroy_htp_message_channel": (I, []),
+        "htp_ops_rpc_rms_norm_f32": (I, [I] * 6),
+        "htp_ops_rpc_mat_mul_permuted_w16a32": (I, [I] * 9),
+        "htp_ops_f16_epilogue_version": (I, []),
+        "htp_ops_native_model_version": (I, []),
+        "htp_ops_dit_aux_version": (I, []),
+        "htp_ops_dit_concat_version": (I, []),
+        "htp_ops_w8a8_epilogue_version": (I, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        L = lib()
+        raise RuntimeError(f"{what}: {rc} ({L.htpg_strerror(rc).decode()}) "
+                           f"{L.htpg_last_cuda_error().decode()}")
+
+
+def ptr(t) -> int | None:
+    """Device (or host) address of a torch tensor / numpy array, None for None."""
+    if t is None:
+        return None
+    if hasattr(t, "data_ptr"):
+        return t.data_ptr()
+    return t.ctypes.data
+
+
+def stream_ptr(stream=None) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+
+
+class Weights:
+    """A prepared (repacked) weight owned by the library."""
+
+    def __init__(self, handle: int, cols: int):
+        self.handle = handle
+        self.cols = cols
+
+    def __del__(self):
+        if self.handle and _lib is not None:
+            _lib.htpg_weights_destroy(self.handle)
+            self.handle = None
+
+
+def w8a8_weights(blob_dev, k: int, n: int, n0: int = 0, n_cols: int = 0, stream=None) -> Weights:
+    h = ctypes.c_void_p()
+    check(lib().htpg_w8a8_weights_create(ptr(blob_dev), k, n, n0, n_cols, stream_ptr(stream),
+                                         ctypes.byref(h)), "htpg_w8a8_weights_create")
+    return Weights(h.value, lib().htpg_weights_cols(h.value))
+
+
+def f16_weights(wperm_dev, k: int, n: int, n0: int = 0, n_cols: int = 0, stream=None) -> Weights:
+    h = ctypes.c_void_p()
+    check(lib().htpg_f16_weights_create(ptr(wperm_dev), k, n, n0, n_cols, stream_ptr(stream),
+                                        ctypes.byref(h)), "htpg_f16_weights_create")
+    return Weights(h.value, lib().htpg_weights_cols(h.value))
+
+
+def w8a8_run(w: Weights, out, x, bias=None, m=None, channels=0, mode=0, ldo=0, stream=None) -> int:
+    m = x.shape[0] if m is None else m
+    return lib().htpg_w8a8_run(w.handle, ptr(out), ldo, ptr(x), ptr(bias), m, channels, mode,
+                               stream_ptr(stream))
+
+
+def f16_run(w: Weights, out, x, bias=None, m=None, channels=0, mode=0, ldo=0, stream=None) -> int:
+    m = x.shape[0] if m is None else m
+    return lib().htpg_f16_run(w.handle, ptr(out), ldo, ptr(x), ptr(bias), m, channels, mode,
+                              stream_ptr(stream))
+
+
+PLAN_FIELDS = ("swap", "bn", "splits", "tiles_a", "tiles_b", "kb_total", "kb_per_split",
+               "units", "grid", "smem")
+
+
+def plan_info(kind: int, m: int, n: int, k: int, sms: int = 148) -> dict:
+    out = (ctypes.c_int64 * 10)()
+    check(lib().htpg_plan_info(kind, m, n, k, sms, out), "htpg_plan_info")
+    return dict(zip(PLAN_FIELDS, list(out)))
+
+
+def phase_timing_read() -> tuple[float, float, int]:
+    a, g, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+    check(lib().htpg_phase_timing_read(ctypes.byref(a), ctypes.byref(g), ctypes.byref(n)),
+          "htpg_phase_timing_read")
+    return a.value, g.value, n.value
+
+
+def check_device(stream=None) -> int:
+    flags = ctypes.c_uint32(0)
+    return lib().htpg_check_device(stream_ptr(stream), ctypes.byref(flags))

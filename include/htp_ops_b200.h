@@ -1,0 +1,195 @@
+/*
+ * libhtp_ops_b200.so — C ABI of the B200 (sm_100a) linear-operator library.
+ *
+ * Two layers, both plain C (no torch types, plain pointers and sizes):
+ *
+ *  1. Device-pointer kernel API (htpg_* and the reference kernel names).
+ *     Tensors live in HBM; work is enqueued on a CUDA stream (`stream` is a
+ *     cudaStream_t passed as void*; NULL = the library's per-device stream).
+ *     Calls return 0 or a negative error code and never synchronise unless
+ *     stated.  These replace the DSP kernel entry points of the reference
+ *     (include/dsp/ops.h:20-31).
+ *
+ *  2. The reference-facing host API (message channel, sessions, IDL names):
+ *     declared in htp_ops.h, host/session.h and host/op_export.h of this
+ *     include directory; it resolves {fd, offset} buffer references through the
+ *     buffer registry below and calls layer 1.
+ *
+ * Error codes are the reference's (src/dsp/op_executor.cc:316-335,
+ * src/dsp/ops/linear_w8a8.c:337-392, src/dsp/ops/mat_mul.c:939-955).
+ */
+#ifndef HTP_OPS_B200_H
+#define HTP_OPS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- error codes ------------------------------------------------------ */
+#define HTPG_OK 0
+#define HTPG_EPAYLOAD (-1)   /* executor: bad payload size or shape */
+#define HTPG_EUNMAPPED (-2)  /* executor: {fd,offset} not registered or too small */
+#define HTPG_EHEADER (-3)    /* executor: constants header / alignment mismatch */
+#define HTPG_EARGS (-10)     /* kernel: null pointer or shape out of range */
+#define HTPG_ECAPACITY (-11) /* kernel: shape constraint (k%32, n%32/64, channels) */
+#define HTPG_ECONTROL (-12)  /* kernel: alignment / control block */
+#define HTPG_ELAUNCH (-13)   /* kernel: CUDA launch or stream error (worker submit in the reference) */
+#define HTPG_ENOPLAN (-14)   /* kernel: no tile plan for this shape */
+#define HTPG_EWATCHDOG (-16) /* device wait gave up (bounded spin expired); context stays usable */
+#define HTPG_ENOMEM (-17)    /* device allocation failed */
+#define HTPG_EARCH (-75)     /* device is not sm_100 */
+
+/* Shape limits.  The reference admits M<=4096, K<=6144, N<=16384
+ * (src/dsp/op_executor.cc:320); this build widens M and K (documented
+ * extension) so the M=16384 and K=14336 configurations run. */
+#define HTPG_W8A8_MAX_M 65536
+#define HTPG_W8A8_MAX_K 16384
+#define HTPG_W8A8_MAX_N 16384
+
+/* Epilogue modes (include/op_reg.h F16EpilogueParams).  */
+#define HTPG_MODE_BIAS 0
+#define HTPG_MODE_GELU 1
+#define HTPG_MODE_QUICK_GELU 2
+#define HTPG_MODE_NCHW 3
+/* Diagnostic mode of htpg_*_run / htpg_*_linear only (not on the wire): the
+ * raw accumulators, row-major -- W8A8: the signed INT32 sum
+ * sum_k (code-128)*w[n][k] (equal to the reference's acc - (colsum << 7)),
+ * stored as int32; FP16: the FP32 accumulator. */
+#define HTPG_MODE_RAW 4
+
+/* ---- library / device ------------------------------------------------- */
+/* Select `device` for this thread, check it is sm_100, create the library stream.
+ * Returns 0, HTPG_EARCH (not sm_100) or HTPG_ELAUNCH (no CUDA device). */
+int htpg_init(int device);
+/* Library version (1). */
+int htpg_version(void);
+/* Text for an error code. */
+const char *htpg_strerror(int code);
+/* Last CUDA error text recorded by the library on this thread ("" if none). */
+const char *htpg_last_cuda_error(void);
+/* Synchronise `stream`, then read and clear the device watchdog word.  Returns 0
+ * when no device wait expired, HTPG_EWATCHDOG otherwise; *flags (optional)
+ * receives the raw bits (bit 0: producer, 1: MMA, 2: epilogue wait expired). */
+int htpg_check_device(void *stream, uint32_t *flags);
+
+/* ---- activation quantisation (reference: linear_w8a8.c:34-128) --------- */
+/* Per row m: x' = x*inverse[k]; scale = max(absmax(x')/127, 1e-12);
+ * code = RNE(clamp(x'*(1/scale) + 128, 1, 255)) - 128 (int8, in [-127,127]).
+ * inverse may be NULL (all ones).  codes: [m][k] int8; row_scales: [m]. */
+int htpg_quantize_rows(int8_t *codes, float *row_scales, const float *x, const float *inverse,
+                       int m, int k, void *stream);
+
+/* ---- prepared weights ------------------------------------------------- */
+typedef struct htpg_weights htpg_weights;
+
+/* Repack a W8A8 constants blob (device memory, reference layout:
+ * include/op_reg.h W8A8Header) into the tensor-core layout; columns
+ * [n0, n0+n_cols) only (n0, n_cols multiples of 64; n_cols = 0 means all).
+ * Reads the 128-byte header once (synchronous).  Header errors: HTPG_EHEADER. */
+int htpg_w8a8_weights_create(const void *constants, int k, int n, int n0, int n_cols,
+                             void *stream, htpg_weights **out);
+/* Repack a permuted FP16 weight (device memory, 32x32 tile layout of
+ * src/host/test.c:552-556) into the tensor-core layout, columns [n0, n0+n_cols). */
+int htpg_f16_weights_create(const uint16_t *permuted_weight, int k, int n, int n0, int n_cols,
+                            void *stream, htpg_weights **out);
+void htpg_weights_destroy(htpg_weights *w);
+/* Columns held by a prepared weight. */
+int htpg_weights_cols(const htpg_weights *w);
+
+/* ---- linear operators on prepared weights ----------------------------- */
+/* out = epilogue(dequant(quant(x) * W^T)) for the W8A8 path; see
+ * htpg_w8a8_linear.  x: [m][k] FP32; out: [m][cols] (mode 0-2, row stride
+ * ldo >= cols) or [channels][m] (mode 3, row stride ldo >= m); ldo = 0 means
+ * dense.  bias: [cols] FP32 or NULL. */
+int htpg_w8a8_run(const htpg_weights *w, float *out, int ldo, const float *x, const float *bias,
+                  int m, int channels, int mode, void *stream);
+int htpg_f16_run(const htpg_weights *w, float *out, int ldo, const float *x, const float *bias,
+                 int m, int channels, int mode, void *stream);
+
+/* ---- one-call linear operators (weights cached by pointer) ------------- */
+/* W8A8 linear, opcode 15 (reference: linear_w8a8.c:327-530) plus the
+ * optional opcode-16 epilogue (extension).  constants: device copy of the
+ * blob.  The repacked weight is cached keyed by (constants, k, n); a caller
+ * that rewrites a blob in place calls htpg_weight_cache_drop(constants). */
+int htpg_w8a8_linear(float *out, const float *x, const void *constants, const float *bias,
+                     int m, int k, int n, int channels, int mode, void *stream);
+/* Packed FP16 GEMM with fused epilogue, opcodes 1 and 16
+ * (reference: mat_mul.c:937-1049).  FP32 accumulate. */
+int htpg_f16_linear(float *out, const float *x, const uint16_t *permuted_weight, const float *bias,
+                    int m, int k, int n, int channels, int mode, void *stream);
+void htpg_weight_cache_drop(const void *weights);
+void htpg_weight_cache_clear(void);
+
+/* Per-phase device times (ms) of the last htpg_*_linear / run call on this
+ * thread when profiling is on (htpg_set_profiling(1)); used for the opcode-15
+ * profile trailer. */
+int htpg_set_profiling(int on);
+int htpg_last_phase_ms(float *quant_ms, float *gemm_ms, float *total_ms);
+
+/* Phase timing for benchmarks: while on, every run records CUDA events on its
+ * stream before the activation pass, between it and the GEMM, and after the
+ * GEMM, without synchronising.  htpg_phase_timing_read synchronises those
+ * events, returns the summed device milliseconds of both phases and the
+ * number of runs since the last read, and resets the sums. */
+int htpg_phase_timing(int on);
+int htpg_phase_timing_read(double *act_ms, double *gemm_ms, int *runs);
+
+/* Kernel launches issued by this library since load (for launch accounting). */
+uint64_t htpg_launch_count(void);
+
+/* Tile plan the library uses for an m x n x k problem (kind 0 = W8A8,
+ * 1 = FP16) on a device with `sms` SMs.  out[0..9] = swap, bn, splits,
+ * tiles_a, tiles_b, kb_total, kb_per_split, units, grid, smem bytes. */
+int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]);
+
+/* ---- reference kernel-level names (reference: include/dsp/ops.h:20-31) ---
+ * Same arguments and return codes as the DSP kernels, on device pointers;
+ * synchronous (they return once the output is written).  The FP16 weight
+ * type __fp16 of the reference is passed as its 16-bit pattern. */
+struct NativeW8A8Profile;
+struct W8A8CpuControl;
+int hmx_mat_mul_native_w8a8(float *dst, const float *activation, const uint8_t *constants, int m,
+                            int k, int n);
+int hmx_mat_mul_native_w8a8_profiled(float *dst, const float *activation, const uint8_t *constants,
+                                     int m, int k, int n, struct NativeW8A8Profile *profile);
+/* Raw byte-plane export of the HMX readout: not available on this device (-75;
+ * -12 when control is NULL), as on a DSP without the feature. */
+int hmx_mat_mul_native_w8a8_cpu(float *dst, const float *activation, const uint8_t *constants,
+                                int m, int k, int n, struct W8A8CpuControl *control);
+int hmx_mat_mul_f16_epilogue(float *dst, const float *activation, const uint16_t *weight,
+                             const float *bias, int m, int k, int n, int channels, int mode);
+int hmx_mat_mul_permuted_w16a32(float *dst, const float *activation,
+                                const uint16_t *permuted_weight, int m, int k, int n);
+
+/* ---- buffer registry (replaces the DSP fd->pointer map cache,
+ *      src/dsp/mmap_mgr.cc:10-139) ----------------------------------------- */
+#define HTPG_BUF_DEVICE 0 /* HBM; ops read/write it directly */
+#define HTPG_BUF_HOST 1   /* pinned host memory; ops stage through HBM */
+
+/* Allocate a buffer of `bytes` (kind DEVICE: cudaMalloc; HOST: pinned host)
+ * and register it; *fd receives a new descriptor, *ptr the address. */
+int htpg_buffer_alloc(size_t bytes, int kind, int *fd, void **ptr);
+/* Register caller-owned memory under a caller-chosen fd (>= 0). */
+int htpg_buffer_register(int fd, void *ptr, size_t bytes, int kind);
+/* Forget fd (frees it if the library allocated it); drops cached repacks. */
+int htpg_buffer_release(int fd);
+/* Mark fd's contents as rewritten: cached weight repacks taken from it are dropped. */
+int htpg_buffer_touch(int fd);
+/* Resolve {fd, offset} with `size` bytes needed; NULL if unknown / too small. */
+void *htpg_buffer_resolve(int fd, int64_t offset, size_t size, int *kind);
+
+/* Execute one OpComputeRequest (reference: src/dsp/op_executor.cc:274).
+ * `req` points at the OpComputeRequest; req_size includes its payload.
+ * Synchronous: returns after the device work finished (output visible to
+ * host-kind buffers).  Returns the RequestHeader.state value. */
+struct OpComputeRequest;
+int execute_op_simple(struct OpComputeRequest *req, size_t req_size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HTP_OPS_B200_H */

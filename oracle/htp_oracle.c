@@ -1,0 +1,349 @@
+/*
+ * htp_oracle.c — CPU restatement of the reference linear-operator arithmetic.
+ * TEST INFRASTRUCTURE ONLY (see htp_oracle.h).  Build with -ffp-contract=off.
+ *
+ * Reference files cited below are paths inside destined555/htp-ops-lib-sd.cpp.
+ */
+#include "htp_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+int orc_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+/* ------------------------------------------------------------------------ */
+/* Seeded generators                                                        */
+/* ------------------------------------------------------------------------ */
+
+uint64_t orc_splitmix64(uint64_t *state) {
+  uint64_t z = (*state += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+/* uniform double in [0, 1) with 53 random bits */
+static double unit_double(uint64_t *s) { return (double)(orc_splitmix64(s) >> 11) * 0x1.0p-53; }
+
+void orc_fill_normal(float *dst, size_t count, double sigma, double outlier_p, double outlier_scale,
+                     uint64_t seed) {
+  uint64_t s = seed;
+  for (size_t i = 0; i < count; i += 2) {
+    /* Box-Muller on FP64: u1 in (0,1], u2 in [0,1) */
+    const double u1 = 1.0 - unit_double(&s);
+    const double u2 = unit_double(&s);
+    const double r = sqrt(-2.0 * log(u1));
+    const double z[2] = {r * cos(2.0 * M_PI * u2), r * sin(2.0 * M_PI * u2)};
+    for (int j = 0; j < 2 && i + j < count; ++j) {
+      double v = sigma * z[j];
+      if (outlier_p > 0.0 && unit_double(&s) < outlier_p) v *= outlier_scale;
+      dst[i + j] = (float)v;
+    }
+  }
+}
+
+void orc_fill_uniform(float *dst, size_t count, double lo, double hi, uint64_t seed) {
+  uint64_t s = seed;
+  for (size_t i = 0; i < count; ++i) dst[i] = (float)(lo + (hi - lo) * unit_double(&s));
+}
+
+void orc_fill_int8(int8_t *dst, size_t count, uint64_t seed) {
+  uint64_t s = seed;
+  for (size_t i = 0; i < count; ++i) dst[i] = (int8_t)((int)(orc_splitmix64(&s) % 255u) - 127);
+}
+
+void orc_fill_f16_normal(uint16_t *dst, size_t count, double sigma, uint64_t seed) {
+  float *tmp = (float *)malloc(count * sizeof(float));
+  orc_fill_normal(tmp, count, sigma, 0.0, 1.0, seed);
+  for (size_t i = 0; i < count; ++i) dst[i] = orc_f32_to_f16(tmp[i]);
+  free(tmp);
+}
+
+/* ------------------------------------------------------------------------ */
+/* FP16 conversion (IEEE binary16, round to nearest even)                   */
+/* ------------------------------------------------------------------------ */
+
+uint16_t orc_f32_to_f16(float x) {
+  _Float16 h = (_Float16)x;
+  uint16_t bits;
+  memcpy(&bits, &h, 2);
+  return bits;
+}
+
+float orc_f16_to_f32(uint16_t bits) {
+  _Float16 h;
+  memcpy(&h, &bits, 2);
+  return (float)h;
+}
+
+static inline uint32_t f32_bits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+static inline float bits_f32(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Layouts                                                                  */
+/* ------------------------------------------------------------------------ */
+
+/* Weight region of the constants blob: groups of 64 output columns, each a
+ * run of K/32 slices of 2048 bytes; a slice holds two 32-column halves of
+ * 1024 bytes; inside a half, byte (n%32)*4 + k%4 of row (k%32)/4 (128 bytes).
+ * linear_w8a8.c:453 (group base n0*k), :487 (slice t*2048, "weight.b ... :deep"),
+ * study_dsp.c:79-84 (tile (t*banks+h)*1024, (k/4)*128 + n*4 + k%4). */
+size_t orc_deep_offset(int k_total, int n, int k) {
+  return (size_t)(n / 64) * 64u * (size_t)k_total + (size_t)(k / 32) * 2048u +
+         (size_t)((n % 64) / 32) * 1024u + (size_t)((k % 32) / 4) * 128u + (size_t)(n % 32) * 4u +
+         (size_t)(k % 4);
+}
+
+size_t orc_w8a8_blob_bytes(int k, int n) {
+  return 128u + (size_t)k * n + (size_t)n * 8u + (size_t)k * 4u;
+}
+
+void orc_w8a8_pack(uint8_t *blob, const int8_t *w_nk, const float *sw, const float *inverse,
+                   int k, int n, uint64_t signature) {
+  const size_t bytes = orc_w8a8_blob_bytes(k, n);
+  memset(blob, 0, 128);
+  uint32_t *h = (uint32_t *)blob;
+  h[0] = 0x38574d48u; /* magic "HMW8" */
+  h[1] = 1;           /* version */
+  h[2] = (uint32_t)k;
+  h[3] = (uint32_t)n;
+  h[4] = 128;                                 /* weight_offset */
+  h[5] = 128u + (uint32_t)((size_t)k * n);    /* scale_offset */
+  h[6] = h[5] + 4u * (uint32_t)n;             /* sum_offset */
+  h[7] = h[6] + 4u * (uint32_t)n;             /* inverse_offset */
+  h[8] = (uint32_t)bytes;                     /* bytes */
+  memcpy(blob + 40, &signature, 8);           /* original_f16_signature */
+  uint8_t *weights = blob + 128;
+  float *scales = (float *)(blob + h[5]);
+  int32_t *sums = (int32_t *)(blob + h[6]);
+  float *inv = (float *)(blob + h[7]);
+  for (int c = 0; c < n; ++c) {
+    int32_t sum = 0;
+    for (int r = 0; r < k; ++r) {
+      const int8_t v = w_nk[(size_t)c * k + r];
+      weights[orc_deep_offset(k, c, r)] = (uint8_t)v;
+      sum += v;
+    }
+    sums[c] = sum;
+    scales[c] = sw[c];
+  }
+  for (int r = 0; r < k; ++r) inv[r] = inverse ? inverse[r] : 1.0f;
+}
+
+void orc_w8a8_unpack_weight(int8_t *w_nk, const uint8_t *blob, int k, int n) {
+  const uint32_t *h = (const uint32_t *)blob;
+  const uint8_t *weights = blob + h[4];
+#pragma omp parallel for schedule(static)
+  for (int c = 0; c < n; ++c)
+    for (int r = 0; r < k; ++r) w_nk[(size_t)c * k + r] = (int8_t)weights[orc_deep_offset(k, c, r)];
+}
+
+/* FP16 permuted weight: 32x32 tiles, tile (n/32)*(K/32) + k/32 of 1024
+ * elements; inside, element ((k%32) & ~1)*32 + (n%32)*2 + (k & 1)
+ * (src/host/test.c:548-556, mat_mul.c:994 chunk base nc*K). */
+size_t orc_f16_perm_offset(int k_total, int k, int n) {
+  const size_t tile = (size_t)(n / 32) * (size_t)(k_total / 32) + (size_t)(k / 32);
+  return tile * 1024u + (size_t)((k % 32) & ~1) * 32u + (size_t)(n % 32) * 2u + (size_t)(k & 1);
+}
+
+void orc_f16_pack_permuted(uint16_t *dst, const uint16_t *w_kn, int k, int n) {
+  for (int r = 0; r < k; ++r)
+    for (int c = 0; c < n; ++c) dst[orc_f16_perm_offset(k, r, c)] = w_kn[(size_t)r * n + c];
+}
+
+/* Compact CM activation tiles: tile (m/64)*64*K + (k/32)*2048, row-major
+ * 64 x 32 bytes inside (linear_w8a8.c:117, 281). */
+size_t orc_cm_offset(int k_total, int m, int k) {
+  return (size_t)(m / 64) * 64u * (size_t)k_total + (size_t)(k / 32) * 2048u +
+         (size_t)(m % 64) * 32u + (size_t)(k % 32);
+}
+
+/* ------------------------------------------------------------------------ */
+/* W8A8                                                                     */
+/* ------------------------------------------------------------------------ */
+
+/* One row of linear_w8a8.c:65-118 (prepare_tile_impl): x' = x*inverse,
+ * absmax, scale = fmaxf(absmax/127, 1e-12f) (row_scale :34-40), s = 1/scale
+ * (:106), then quantize_scaled (:42-59): u = x'*s + 128 (two IEEE roundings),
+ * clamp to [1,255] by integer max/min on the IEEE bits, round half to even. */
+static float quantize_row(uint8_t *codes, const float *x, const float *inverse, int k,
+                          float *scratch) {
+  float absmax = 0.0f;
+  for (int c = 0; c < k; ++c) {
+    const float v = inverse ? x[c] * inverse[c] : x[c];
+    scratch[c] = v;
+    const float a = fabsf(v);
+    absmax = fmaxf(absmax, a);
+  }
+  const float scale = fmaxf(absmax / 127.0f, 1e-12f);
+  const float s = 1.0f / scale;
+  for (int c = 0; c < k; ++c) {
+    const float t = scratch[c] * s;
+    const float u = t + 128.0f;
+    int32_t b = (int32_t)f32_bits(u);
+    if (b < (int32_t)0x3f800000) b = (int32_t)0x3f800000; /* 1.0f */
+    if (b > (int32_t)0x437f0000) b = (int32_t)0x437f0000; /* 255.0f */
+    codes[c] = (uint8_t)rintf(bits_f32((uint32_t)b));     /* RNE in default mode */
+  }
+  return scale;
+}
+
+void orc_quantize_rows(uint8_t *codes, float *scales, const float *x, const float *inverse,
+                       int m, int k) {
+#pragma omp parallel
+  {
+    float *scratch = (float *)malloc((size_t)k * sizeof(float));
+#pragma omp for schedule(static)
+    for (int r = 0; r < m; ++r)
+      scales[r] = quantize_row(codes + (size_t)r * k, x + (size_t)r * k, inverse, k, scratch);
+    free(scratch);
+  }
+}
+
+static inline int32_t dot_u8_s8(const uint8_t *a, const int8_t *b, int k) {
+  int32_t acc = 0;
+  for (int i = 0; i < k; ++i) acc += (int32_t)a[i] * (int32_t)b[i];
+  return acc;
+}
+
+void orc_w8a8_accumulate(int32_t *acc, const uint8_t *codes, const int8_t *w_nk, int m, int k,
+                         int n) {
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int r = 0; r < m; ++r)
+    for (int c = 0; c < n; ++c)
+      acc[(size_t)r * n + c] = dot_u8_s8(codes + (size_t)r * k, w_nk + (size_t)c * k, k);
+}
+
+/* Optional epilogue shared by both operators (mat_mul.c:788-826 and
+ * :864-882): GELU(tanh) as x*sigmoid(1.5957691216057308*(x + 0.044715 x^3)),
+ * QuickGELU as x*sigmoid(1.702 x).  The sigmoid keeps the reference's stable
+ * structure e = 2^max(-|z|*log2(e), -126), inv = 1/(1+e),
+ * sigma = z < 0 ? e*inv : inv, with libm exp2f and an exact division in place
+ * of the HVX polynomial and Newton steps. */
+float orc_epilogue_activation(float x, int mode) {
+  if (mode != 1 && mode != 2) return x;
+  float z;
+  if (mode == 1) {
+    const float cubic = (x * x) * x;
+    z = x + cubic * 0.044715f;
+    z = z * 1.5957691216057308f;
+  } else {
+    z = x * 1.702f;
+  }
+  float arg = fabsf(z) * -1.4426950408889634f;
+  arg = fmaxf(arg, -126.0f);
+  const float e = exp2f(arg);
+  const float inv = 1.0f / (e + 1.0f);
+  const float sig = z < 0.0f ? e * inv : inv;
+  return x * sig;
+}
+
+static inline void store_out(float *out, int mode, int channels, int nrows, int r, int c, int n,
+                             float v) {
+  if (mode == 3) {
+    if (c < channels) out[(size_t)c * nrows + r] = v; /* mat_mul.c:847-858 */
+  } else {
+    out[(size_t)r * n + c] = v;
+  }
+}
+
+void orc_w8a8_linear_rows(float *out, const float *x, const uint8_t *blob, const float *bias,
+                          int m, int k, int n, int channels, int mode, const int32_t *rows,
+                          int nrows, uint8_t *codes_out, float *scales_out,
+                          int32_t *signed_acc_out) {
+  (void)m;
+  const uint32_t *h = (const uint32_t *)blob;
+  const float *sw = (const float *)(blob + h[5]);
+  const int32_t *sums = (const int32_t *)(blob + h[6]);
+  const float *inverse = (const float *)(blob + h[7]);
+  int8_t *w = (int8_t *)malloc((size_t)k * n);
+  orc_w8a8_unpack_weight(w, blob, k, n);
+#pragma omp parallel
+  {
+    float *scratch = (float *)malloc((size_t)k * sizeof(float));
+    uint8_t *codes = (uint8_t *)malloc((size_t)k);
+#pragma omp for schedule(dynamic, 1)
+    for (int i = 0; i < nrows; ++i) {
+      const int row = rows ? rows[i] : i;
+      const float rs = quantize_row(codes, x + (size_t)row * k, inverse, k, scratch);
+      if (codes_out) memcpy(codes_out + (size_t)i * k, codes, (size_t)k);
+      if (scales_out) scales_out[i] = rs;
+      for (int c = 0; c < n; ++c) {
+        const int32_t acc = dot_u8_s8(codes, w + (size_t)c * k, k);
+        /* zero-point correction acc - (sum << 7) (linear_w8a8.c:159, 168),
+         * done in wrapping 32-bit arithmetic like the HVX word ops */
+        const int32_t y = (int32_t)((uint32_t)acc - ((uint32_t)sums[c] << 7));
+        if (signed_acc_out) signed_acc_out[(size_t)i * n + c] = y;
+        float v = (float)y;   /* Q6_Vsf_equals_Vw: nearest even */
+        v = v * sw[c];        /* column scale first (:174) */
+        v = v * rs;           /* then the row scale (:176) */
+        if (bias) v = v + bias[c];
+        v = orc_epilogue_activation(v, mode);
+        store_out(out, mode, channels, nrows, i, c, n, v);
+      }
+    }
+    free(codes);
+    free(scratch);
+  }
+  free(w);
+}
+
+/* ------------------------------------------------------------------------ */
+/* FP16 GEMM + epilogue                                                     */
+/* ------------------------------------------------------------------------ */
+
+/* mat_mul.c:937-1044: activation rounded to FP16 (:114-148), FP16 x FP16
+ * products accumulated over the whole K (:724-748; K is never split,
+ * f16_gemm_plan.h:11-12), optional bias then activation (:864-882) or the
+ * cropped channel-major store (:830-862). */
+void orc_f16_linear_rows(float *out, const float *x, const uint16_t *wperm, const float *bias,
+                         int m, int k, int n, int channels, int mode, int round_acc_f16,
+                         const int32_t *rows, int nrows) {
+  (void)m;
+  /* weights as FP32 [n][k] */
+  float *w = (float *)malloc((size_t)k * n * sizeof(float));
+#pragma omp parallel for schedule(static)
+  for (int c = 0; c < n; ++c)
+    for (int r = 0; r < k; ++r)
+      w[(size_t)c * k + r] = orc_f16_to_f32(wperm[orc_f16_perm_offset(k, r, c)]);
+#pragma omp parallel
+  {
+    float *a = (float *)malloc((size_t)k * sizeof(float));
+#pragma omp for schedule(dynamic, 1)
+    for (int i = 0; i < nrows; ++i) {
+      const int row = rows ? rows[i] : i;
+      for (int r = 0; r < k; ++r) a[r] = orc_f16_to_f32(orc_f32_to_f16(x[(size_t)row * k + r]));
+      for (int c = 0; c < n; ++c) {
+        const float *wc = w + (size_t)c * k;
+        float acc = 0.0f;
+        for (int r = 0; r < k; ++r) acc += a[r] * wc[r]; /* products exact in FP32 */
+        if (round_acc_f16) acc = orc_f16_to_f32(orc_f32_to_f16(acc));
+        float v = acc;
+        if (bias) v = v + bias[c];
+        v = orc_epilogue_activation(v, mode);
+        store_out(out, mode, channels, nrows, i, c, n, v);
+      }
+    }
+    free(a);
+  }
+  free(w);
+}

@@ -1,0 +1,99 @@
+/*
+ * htp_oracle — CPU restatement of the reference library's linear-operator
+ * arithmetic (W8A8 opcode 15, packed FP16 GEMM + epilogue opcodes 1/16).
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in libhtp_ops_b200.so links or calls this
+ * code; only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg
+ * use it, as the checker.
+ *
+ * Parity pinning (what this restatement is checked against):
+ *  - integer semantics (UINT8 x INT8 -> exact INT32, zero-point-128
+ *    correction, HMX "deep" N64 weight layout, CM activation tiles, FP16
+ *    crouton layout) against the known-answer cases of the reference's HMX
+ *    probe (tests/hmx-probe/integer_tests.c:79-134, study_data.h:1-21,
+ *    study_dsp.c:70-86) and its host layout demo (src/host/test.c:545-556);
+ *  - the wire ABI and the planner against the reference headers/test compiled
+ *    here (oracle/_ref);
+ *  - FP32 arithmetic: IEEE single precision with no contraction
+ *    (-ffp-contract=off, as the reference builds linear_w8a8.c,
+ *    CMakeLists.txt:97-98).  The reference executes these steps in HVX QFloat,
+ *    whose ulp-level rounding is undocumented and cannot run here, so the FP32
+ *    steps are pinned only by this restatement ("parity unpinned" at the ulp
+ *    level of QFloat; within the BASELINE tolerances otherwise).
+ */
+#ifndef HTP_ORACLE_H
+#define HTP_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- seeded synthetic inputs (splitmix64; Box-Muller on FP64) ---------- */
+uint64_t orc_splitmix64(uint64_t *state);
+/* N(0, sigma) rounded to FP32; each element independently multiplied by
+ * outlier_scale with probability outlier_p. */
+void orc_fill_normal(float *dst, size_t count, double sigma, double outlier_p,
+                     double outlier_scale, uint64_t seed);
+void orc_fill_uniform(float *dst, size_t count, double lo, double hi, uint64_t seed);
+/* uniform integers in [-127, 127] */
+void orc_fill_int8(int8_t *dst, size_t count, uint64_t seed);
+/* FP16 bit patterns of N(0, sigma) */
+void orc_fill_f16_normal(uint16_t *dst, size_t count, double sigma, uint64_t seed);
+
+/* ---- FP16 helpers ------------------------------------------------------ */
+uint16_t orc_f32_to_f16(float x); /* round to nearest even */
+float orc_f16_to_f32(uint16_t h);
+
+/* ---- layouts ------------------------------------------------------------ */
+/* Byte offset of W[n][k] inside the weight region of a constants blob
+ * (HMX deep N64 layout; linear_w8a8.c:453,482,487; study_dsp.c:79-84). */
+size_t orc_deep_offset(int k_total, int n, int k);
+size_t orc_w8a8_blob_bytes(int k, int n);
+/* Build a constants blob from row-major w[n][k], sw[n], inverse[k] (NULL = 1).
+ * sums[n] = sum_k w[n][k]. */
+void orc_w8a8_pack(uint8_t *blob, const int8_t *w_nk, const float *sw, const float *inverse,
+                   int k, int n, uint64_t signature);
+void orc_w8a8_unpack_weight(int8_t *w_nk, const uint8_t *blob, int k, int n);
+/* Offset (in FP16 elements) of W16[k][n] in the permuted layout
+ * (src/host/test.c:548-556). */
+size_t orc_f16_perm_offset(int k_total, int k, int n);
+void orc_f16_pack_permuted(uint16_t *dst, const uint16_t *w_kn, int k, int n);
+/* Offset of activation code (m,k) in the compact CM tiles (linear_w8a8.c:117,281). */
+size_t orc_cm_offset(int k_total, int m, int k);
+
+/* ---- W8A8 (reference: linear_w8a8.c) ------------------------------------ */
+/* Per-row quantisation (linear_w8a8.c:34-128).  codes: UINT8 [m][k] in [1,255]
+ * (zero point 128); scales: [m]. */
+void orc_quantize_rows(uint8_t *codes, float *scales, const float *x, const float *inverse,
+                       int m, int k);
+/* acc[m][n] = sum_k code[m][k] * w[n][k]  (UINT8 x INT8 -> INT32, a4). */
+void orc_w8a8_accumulate(int32_t *acc, const uint8_t *codes, const int8_t *w_nk,
+                         int m, int k, int n);
+/* Full operator on a subset of rows.  rows: `nrows` row indices of x (NULL =
+ * rows 0..m-1 with nrows = m).  out: [nrows][n] for mode 0-2; for mode 3
+ * [channels][nrows].  bias may be NULL.  Also returns codes/scales/signed
+ * accumulators of those rows when the pointers are non-NULL. */
+void orc_w8a8_linear_rows(float *out, const float *x, const uint8_t *blob, const float *bias,
+                          int m, int k, int n, int channels, int mode,
+                          const int32_t *rows, int nrows,
+                          uint8_t *codes_out, float *scales_out, int32_t *signed_acc_out);
+
+/* ---- FP16 GEMM + epilogue (reference: mat_mul.c:724-1049) --------------- */
+float orc_epilogue_activation(float x, int mode);
+/* out rows as above.  round_acc_f16 != 0 rounds each accumulator to FP16
+ * before the epilogue (HMX "cvt.hf = acc", hmx_utils.h:34-40). */
+void orc_f16_linear_rows(float *out, const float *x, const uint16_t *wperm, const float *bias,
+                         int m, int k, int n, int channels, int mode, int round_acc_f16,
+                         const int32_t *rows, int nrows);
+
+/* Number of OpenMP threads this build uses (1 without OpenMP). */
+int orc_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

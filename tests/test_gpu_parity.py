@@ -1,0 +1,173 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
+
+Bars: INT8 activation codes, row scales and INT32
+accumulators bit-exact; W8A8 FP32 outputs within max-abs-rel 2e-3 (achieved
+bit-exact without an activation); FP16-weight GEMM outputs within
+max-abs-rel 1e-2 of the oracle with FP32 accumulation.
+"""
+import numpy as np
+import pytest
+
+import htpg
+import oracle as O
+
+W8A8_TOL = 2e-3
+F16_TOL = 1e-2
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _quant_case(m, k, seed, kind="normal"):
+    x = O.normal(m * k, 1.0, 0.01, 20.0, seed).reshape(m, k)
+    if kind == "edges" and m >= 4:
+        x[0, :] = 0.0                       # all-zero row: scale clamps to 1e-12
+        x[1, :] = 1e-30                     # subnormal-scale row
+        x[2, ::7] = 1.0e38                  # huge outliers (finite after x*inverse)
+        x[3, :] = np.float32(-0.0)
+    return x
+
+
+@pytest.mark.parametrize("m,k", [(1, 32), (3, 64), (77, 768), (256, 1152), (1000, 1536),
+                                 (2048, 1536), (16, 14336), (5, 4096), (9, 6144)])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_quantize_rows_bitexact(gpu, lib, m, k, inverse):
+    import torch
+    x = _quant_case(m, k, 1000 + m + k, "edges")
+    inv = O.uniform(k, 0.5, 2.0, 77) if inverse else None
+    codes_ref, scales_ref = O.quantize_rows(x, inv)
+    codes = torch.empty(m, k, dtype=torch.int8, device=gpu)
+    scales = torch.empty(m, dtype=torch.float32, device=gpu)
+    htpg.check(lib.htpg_quantize_rows(htpg.ptr(codes), htpg.ptr(scales), htpg.ptr(_t(x, gpu)),
+                                      htpg.ptr(_t(inv, gpu)) if inverse else None, m, k,
+                                      htpg.stream_ptr()), "quantize")
+    torch.cuda.synchronize()
+    got_codes = codes.cpu().numpy().astype(np.int16) + 128
+    np.testing.assert_array_equal(got_codes, codes_ref.astype(np.int16))
+    np.testing.assert_array_equal(scales.cpu().numpy().view(np.uint32), scales_ref.view(np.uint32))
+
+
+W8A8_SHAPES = [  # (m, k, n): swapped (m<=32) incl. split-K, and normal tiles with ragged edges
+    (1, 128, 64), (4, 256, 128), (16, 512, 192), (32, 1152, 256), (33, 256, 192),
+    (77, 768, 640), (128, 128, 128), (200, 1152, 640), (256, 1152, 4608), (300, 2048, 1024),
+    (4, 14336, 4096), (16, 4096, 1024),
+]
+
+
+def _w8a8_case(m, k, n, seed=0, outliers=0.01, inverse=False, bias=False, mode=0):
+    c = O.make_w8a8(seed, f"t{m}x{k}x{n}", m, k, n, outliers, bias, mode,
+                    inverse_range=(0.5, 2.0) if inverse else None)
+    return c
+
+
+def _run_w8a8(lib, gpu, c, mode, bias=None, channels=None, raw=False):
+    import torch
+    channels = c.n if channels is None else channels
+    blob = _t(c.blob, gpu)
+    x = _t(c.x, gpu)
+    if raw:
+        out = torch.empty(c.m, c.n, dtype=torch.int32, device=gpu)
+        mode = htpg_mode_raw = 4
+    elif mode == 3:
+        out = torch.full((channels, c.m), float("nan"), dtype=torch.float32, device=gpu)
+    else:
+        out = torch.full((c.m, c.n), float("nan"), dtype=torch.float32, device=gpu)
+    b = _t(bias, gpu) if bias is not None else None
+    rc = lib.htpg_w8a8_linear(htpg.ptr(out), htpg.ptr(x), htpg.ptr(blob), htpg.ptr(b), c.m, c.k, c.n,
+                              channels, mode, htpg.stream_ptr())
+    htpg.check(rc, "htpg_w8a8_linear")
+    htpg.check(htpg.check_device(), "device watchdog")
+    lib.htpg_weight_cache_drop(htpg.ptr(blob))
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("m,k,n", W8A8_SHAPES)
+def test_w8a8_int32_accumulators_bitexact(gpu, lib, m, k, n):
+    c = _w8a8_case(m, k, n, seed=m)
+    _, codes, scales, acc = O.w8a8_linear(c.x, c.blob, k, n, want_intermediates=True)
+    got = _run_w8a8(lib, gpu, c, 0, raw=True)
+    np.testing.assert_array_equal(got, acc)
+
+
+@pytest.mark.parametrize("m,k,n", W8A8_SHAPES)
+def test_w8a8_output_bitexact_mode0(gpu, lib, m, k, n):
+    c = _w8a8_case(m, k, n, seed=m + 1, inverse=(m % 2 == 1))
+    ref = O.w8a8_linear(c.x, c.blob, k, n)
+    got = _run_w8a8(lib, gpu, c, 0)
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("m,k,n", [(4, 256, 192), (77, 768, 640), (300, 512, 256), (16, 4096, 1024)])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_w8a8_epilogue_modes(gpu, lib, m, k, n, mode, with_bias):
+    c = _w8a8_case(m, k, n, seed=7 * m + mode, outliers=0.005)
+    bias = O.normal(n, 0.01, 0, 1, 99 + n) if with_bias else None
+    channels = n - 64 + 5 if mode == 3 else n   # cropped channel-major store
+    ref = O.w8a8_linear(c.x, c.blob, k, n, bias=bias, channels=channels, mode=mode)
+    got = _run_w8a8(lib, gpu, c, mode, bias=bias, channels=channels)
+    assert not np.isnan(got).any()
+    err = O.max_abs_rel(got, ref)
+    assert err <= W8A8_TOL, err
+    if mode in (0, 3):
+        np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def _f16_case(m, k, n, seed):
+    x = O.normal(m * k, 1.0, 0, 1, seed).reshape(m, k)
+    w = O.f16_normal(k * n, 0.02, seed + 1).reshape(k, n)
+    return x, w, O.f16_pack_permuted(w)
+
+
+def _run_f16(lib, gpu, x, wperm, m, k, n, bias=None, channels=None, mode=0, raw=False):
+    import torch
+    channels = n if channels is None else channels
+    if mode == 3:
+        out = torch.full((channels, m), float("nan"), dtype=torch.float32, device=gpu)
+    else:
+        out = torch.full((m, n), float("nan"), dtype=torch.float32, device=gpu)
+    wdev = _t(wperm.view(np.int16), gpu)
+    b = _t(bias, gpu) if bias is not None else None
+    rc = lib.htpg_f16_linear(htpg.ptr(out), htpg.ptr(_t(x, gpu)), htpg.ptr(wdev), htpg.ptr(b), m, k, n,
+                             channels, 4 if raw else mode, htpg.stream_ptr())
+    htpg.check(rc, "htpg_f16_linear")
+    htpg.check(htpg.check_device(), "device watchdog")
+    lib.htpg_weight_cache_drop(htpg.ptr(wdev))
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 32, 32), (77, 768, 3072), (128, 256, 96), (300, 1024, 512),
+                                   (512, 512, 1024)])
+def test_f16_accumulator_close_to_fp64(gpu, lib, m, k, n):
+    x, w, wperm = _f16_case(m, k, n, 5 + m)
+    got = _run_f16(lib, gpu, x, wperm, m, k, n, raw=True)
+    x16 = x.astype(np.float16).astype(np.float64)
+    w64 = w.view(np.float16).astype(np.float64)
+    ref = x16 @ w64
+    # FP32 accumulation of exact FP16 products over K terms
+    assert O.max_abs_rel(got, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("m,k,n", [(77, 768, 3072), (5, 64, 96), (256, 512, 256)])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_f16_epilogue_modes(gpu, lib, m, k, n, mode, with_bias):
+    x, w, wperm = _f16_case(m, k, n, 17 + mode)
+    bias = O.normal(n, 0.01, 0, 1, 3 + n) if with_bias else None
+    channels = n - 32 + 7 if mode == 3 else n
+    got = _run_f16(lib, gpu, x, wperm, m, k, n, bias=bias, channels=channels, mode=mode)
+    assert not np.isnan(got).any()
+    for round_acc in (False, True):   # FP32 accumulator, and the HMX FP16-rounded one
+        ref = O.f16_linear(x, wperm, k, n, bias=bias, channels=channels, mode=mode,
+                           round_acc_f16=round_acc)
+        assert O.max_abs_rel(got, ref) <= F16_TOL
+    ref = O.f16_linear(x, wperm, k, n, bias=bias, channels=channels, mode=mode)
+    assert O.max_abs_rel(got, ref) <= 1e-5
+
+
+def test_watchdog_clear(gpu, lib):
+    assert htpg.check_device() == 0
