@@ -1,0 +1,422 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 linear-operator path (the driver's contract).
+
+Workload (default, every N): BASELINE config C4 — W8A8 MLP fc1 with bias +
+GELU(tanh) epilogue, M=16384 tokens, K=1536, N=6144, column-sharded over the
+N GPUs (N/world columns per GPU); for N > 1 each step ends with an NCCL
+all-gather of the output slices over NVLink and the reassembly of the
+row-major [M][N] output.  One step = quantise the activation rows, the tcgen05
+INT8 GEMM with the fused dequant/bias/GELU epilogue, (gather).  Metric: whole-
+job INT8 TOPS (2*M*N*K per step / device time, max over ranks).
+
+* value        device-resident inputs; per-step CUDA-event time (L2 flushed
+               between steps by a 256 MiB write outside the timed events).
+* e2e          the same operator through the reference-facing API: an opcode-15
+               request (56-byte epilogue payload) posted on the shared-memory
+               message channel with host (pinned) buffers; the receiver copies
+               the activation in and the output out every step.
+* roofline     the GEMM kernel's algorithmic bytes / ops per launch over its
+               average event-timed duration inside the timed region.
+* cpu_baseline the CPU oracle (restatement of the reference arithmetic; the
+               reference itself only builds for a Hexagon DSP) on a bounded row
+               sample of the same workload, all host threads.
+
+`--impl reference` times that CPU implementation alone (rank 0), as the
+reference arm.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import faulthandler
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "htp-ops-lib-sd.cpp_b200")
+sys.path.insert(0, PKG)
+
+M_C4, K_C4, N_C4 = 16384, 1536, 6144
+FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", 0)), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ inputs
+def make_c4_inputs(torch, dev, m, k, n, seed=0x5EED0003):
+    """Seeded synthetic C4 tensors with BASELINE's distributions (config index 2
+    values): X ~ N(0,1) with 0.5% of entries x20, W int8 uniform [-127,127],
+    column scales U[1e-3,1e-2], bias N(0,0.01)."""
+    import numpy as np
+    import htpg
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    x = torch.randn(m, k, device=dev, generator=g)
+    x = torch.where(torch.rand(m, k, device=dev, generator=g) < 0.005, x * 20.0, x).contiguous()
+    gc = torch.Generator()
+    gc.manual_seed(seed + 1)
+    w = torch.randint(-127, 128, (n, k), generator=gc, dtype=torch.int16).to(torch.int8).numpy()
+    sw = (torch.rand(n, generator=gc) * 9e-3 + 1e-3).numpy().astype(np.float32)
+    bias = (torch.randn(n, generator=gc) * 0.01).to(dev)
+    blob = htpg.pack_w8a8_constants(w, sw, None, signature=seed)
+    return x, torch.from_numpy(blob).to(dev), bias, blob
+
+
+# ------------------------------------------------------------------ CPU leg
+def cpu_sample(k, n, rows, reps=1):
+    """Time the OpenMP CPU oracle on `rows` rows of a C4-shaped problem.
+    Returns (TOPS, threads, seconds)."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+    import numpy as np
+    kind = "native"
+    try:
+        O.lib("native")
+    except Exception:
+        kind = "omp"
+    c = O.make_w8a8(3, "C4-sample", rows, k, n, 0.005, True, 1)
+    O.w8a8_linear(c.x[:8], c.blob, k, n, bias=c.bias, mode=1, kind=kind)  # warm
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.w8a8_linear(c.x, c.blob, k, n, bias=c.bias, mode=1, kind=kind)
+    dt = (time.perf_counter() - t0) / reps
+    return 2.0 * rows * n * k / dt / 1e12, O.lib(kind).orc_threads(), dt
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return
+    rows = args.cpu_rows
+    vals = []
+    threads = 1
+    for i in range(args.warmup + args.steps):
+        tops, threads, _ = cpu_sample(K_C4, N_C4, rows)
+        if i >= args.warmup:
+            vals.append(tops)
+    v = statistics.median(vals)
+    line = {
+        "impl": "reference",
+        "metric": "W8A8 linear INT8 TOPS (C4 fc1 M=16384 K=1536 N=6144 bias+GELU)",
+        "value": v, "unit": "TOPS", "higher_is_better": True, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "dtype": "u8xs8->s32, f32 io",
+        "data": "synthetic (seeded; BASELINE C4 distributions)",
+        "config": {"workload": "C4", "M": M_C4, "K": K_C4, "N": N_C4, "epilogue": "bias+gelu_tanh"},
+        "cpu_baseline": {"value": v, "unit": "TOPS", "cores": threads, "kind": "port",
+                         "sample": f"{rows} of {M_C4} rows per step, all {N_C4} columns"},
+        "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ e2e
+def e2e_channel(torch, L, htpg, m, k, n, x_dev, blob_host, bias_dev, steps, warmup):
+    """Opcode-15 (56-byte epilogue payload) through the message channel with
+    host buffers.  Returns (seconds per step, h2d bytes, d2h bytes)."""
+    import numpy as np
+    msg_bytes = 4096
+    fds, ptrs = {}, {}
+
+    def alloc(name, nbytes):
+        fd, p = ctypes.c_int(), ctypes.c_void_p()
+        htpg.check(L.htpg_buffer_alloc(nbytes, htpg.BUF_HOST, ctypes.byref(fd), ctypes.byref(p)), name)
+        fds[name], ptrs[name] = fd.value, p.value
+
+    alloc("chan", msg_bytes)
+    alloc("x", m * k * 4)
+    alloc("out", m * n * 4)
+    alloc("blob", blob_host.nbytes)
+    alloc("bias", n * 4)
+    # host copies are held in variables: a temporary's memory may be returned
+    # to the OS before memmove reads it
+    x_host = np.ascontiguousarray(x_dev.cpu().numpy())
+    bias_host = np.ascontiguousarray(bias_dev.cpu().numpy())
+    ctypes.memmove(ptrs["x"], x_host.ctypes.data, m * k * 4)
+    ctypes.memmove(ptrs["blob"], blob_host.ctypes.data, blob_host.nbytes)
+    ctypes.memmove(ptrs["bias"], bias_host.ctypes.data, n * 4)
+
+    sess = ctypes.c_void_p()
+    htpg.check(L.htp_ops_session_open(ctypes.byref(sess), 3, None, 0), "session_open")
+    htpg.check(L.htp_ops_session_init_backend(sess), "init_backend")
+    htpg.check(L.htp_ops_session_create_channel(sess, fds["chan"], msg_bytes), "create_channel")
+    chan = ptrs["chan"]
+    # MessageHeader(16) + 2 offsets, RequestHeader(8) + OpComputeRequest(4) + payload(56)
+    hdr = 16 + 8
+    payload = np.zeros(14, np.int32)
+    payload[0:2] = (fds["out"], 0)
+    payload[2:4] = (fds["x"], 0)
+    payload[4:6] = (fds["blob"], 0)
+    payload[6:10] = (m, k, n, 0)
+    payload[10:12] = (fds["bias"], 0)
+    payload[12:14] = (n, 1)          # channels, mode 1 = bias + GELU
+    req = np.concatenate([np.array([0, 2], np.int32), np.array([15], np.int32), payload])
+    state = (ctypes.c_uint8 * 8).from_address(chan)
+
+    def post():
+        ctypes.memset(chan, 0, 8)
+        head = np.array([0, 0, 0, 1, hdr, hdr + req.nbytes], np.int32)  # state(8) checksum n_reqs offs
+        ctypes.memmove(chan + 8, head[2:].ctypes.data, 16)
+        ctypes.memmove(chan + hdr, req.ctypes.data, req.nbytes)
+        state[0] = 1
+        while state[1] != 1:
+            pass
+        rc = ctypes.c_int32.from_address(chan + hdr).value
+        htpg.check(rc, "opcode 15 via channel")
+
+    for _ in range(warmup):
+        post()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        post()
+    dt = (time.perf_counter() - t0) / steps
+    L.htp_ops_session_destroy_channel(sess)
+    L.htp_ops_session_close(sess)
+    for name in fds:
+        L.htpg_buffer_release(fds[name])
+    return dt, m * k * 4 + n * 4, m * n * 4
+
+
+# ------------------------------------------------------------------ main arm
+def main():
+    faulthandler.enable()
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-rows", type=int, default=256)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+
+    import torch
+    import htpg
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    L = htpg.lib()
+    htpg.check(L.htpg_init(local), "htpg_init")
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+
+    m, k, n = M_C4, K_C4, N_C4
+    assert n % (64 * world) == 0
+    n_loc = n // world
+    n0 = rank * n_loc
+    x, blob_dev, bias, blob_host = make_c4_inputs(torch, dev, m, k, n)
+    w = htpg.w8a8_weights(blob_dev, k, n, n0=n0, n_cols=n_loc)
+    bias_loc = bias[n0:n0 + n_loc].contiguous()
+    out_loc = torch.empty(m, n_loc, dtype=torch.float32, device=dev)
+    gathered = torch.empty(world, m, n_loc, dtype=torch.float32, device=dev) if world > 1 else None
+    full = torch.empty(m, n, dtype=torch.float32, device=dev) if world > 1 else None
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        htpg.check(L.htpg_w8a8_run(w.handle, htpg.ptr(out_loc), 0, htpg.ptr(x), htpg.ptr(bias_loc), m, n_loc,
+                                   1, sp), "htpg_w8a8_run")
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out_loc)
+            full.view(m, world, n_loc).copy_(gathered.permute(1, 0, 2))
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    htpg.check(htpg.check_device(), "watchdog")
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    L.htpg_phase_timing(1)
+    htpg.phase_timing_read()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    # settle steps: keep the GPU under this load for ~1.5 s before timing so the
+    # 200 ms clock samples describe the timed steps; every rank runs the same count
+    t0 = time.perf_counter()
+    for _ in range(5):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    per = max((time.perf_counter() - t0) / 5, 1e-5)
+    cnt = torch.tensor([min(int(1.5 / per) + 1, 20000)], dtype=torch.int64, device=dev)
+    if dist:
+        dist.all_reduce(cnt, op=dist.ReduceOp.MAX)
+    settle = int(cnt.item())
+    with ClockSampler(local) as clocks:
+        for i in range(settle):
+            flush.zero_()
+            step()
+            if i % 64 == 63:
+                htpg.phase_timing_read()   # keeps the pending event list short
+        torch.cuda.synchronize()
+        htpg.phase_timing_read()
+        launches0 = L.htpg_launch_count()
+        for i in range(args.steps):
+            flush.zero_()                      # L2 flush outside the timed events
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    launches = L.htpg_launch_count() - launches0
+    if dist:
+        dist.barrier()
+    L.htpg_phase_timing(0)
+    act_ms, gemm_ms, runs = htpg.phase_timing_read()
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    htpg.check(htpg.check_device(), "watchdog")
+
+    ms_per_step = total_ms / args.steps
+    ops = 2.0 * m * n * k
+    value = ops / (ms_per_step * 1e-3) / 1e12
+
+    hbm, bf16, bf16_sus, peak_kind = peaks()
+    int8_peak = 2.0 * bf16  # no measured INT8 GEMM: 2x the measured dense BF16 (B200: INT8 = 2x BF16 rate)
+    gemm_avg_ms = gemm_ms / max(runs, 1)
+    act_avg_ms = act_ms / max(runs, 1)
+    gemm_bytes = m * k + k * n_loc + 4 * n_loc * 2 + 4 * m + 4 * m * n_loc
+    gemm_ops = 2.0 * m * n_loc * k
+    t_hbm = gemm_bytes / (hbm * 1e9)
+    t_tc = gemm_ops / (int8_peak * 1e12)
+    if t_tc >= t_hbm:
+        roof = {"bound": "tensor", "achieved": gemm_ops / (gemm_avg_ms * 1e-3) / 1e12, "peak": int8_peak,
+                "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": gemm_bytes / (gemm_avg_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = None
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            tr = json.load(f).get(f"C4_w{world}")
+            roof["traffic"] = tr
+    except Exception:
+        pass
+    roof["kernel"] = "gemm_kernel<I8,256,false> (tcgen05 kind::i8 + fused dequant/bias/GELU)"
+    roof["peak_source"] = f"hbm {peak_kind} burst copy; tensor = 2 x {peak_kind} dense BF16 burst"
+    roof["hbm_frac"] = gemm_bytes / (gemm_avg_ms * 1e-3) / 1e9 / hbm
+    roof["tensor_frac"] = gemm_ops / (gemm_avg_ms * 1e-3) / 1e12 / int8_peak
+    roof["gemm_us"] = gemm_avg_ms * 1e3
+    roof["quant_us"] = act_avg_ms * 1e3
+    roof["algorithmic_bytes"] = gemm_bytes
+
+    line = {
+        "metric": "W8A8 linear INT8 TOPS (C4 fc1 M=16384 K=1536 N=6144 bias+GELU)",
+        "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "u8xs8->s32 (int8 tensor cores), f32 io",
+        "data": "synthetic (seeded; BASELINE C4 distributions)",
+        "config": {"workload": "C4", "M": m, "K": k, "N": n, "N_per_gpu": n_loc,
+                   "epilogue": "bias+gelu_tanh", "parallelism": f"tp{world} (columns)" if world > 1 else "single",
+                   "exchange": "nccl all_gather + reassembly" if world > 1 else None,
+                   "l2": "256 MiB flush write between steps (outside the timed events)"},
+        "roofline": roof,
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+    }
+
+    if rank == 0 and world == 1 and not args.no_e2e:
+        dt, h2d, d2h = e2e_channel(torch, L, htpg, m, k, n, x, blob_host, bias, max(3, args.steps // 4), 2)
+        line["e2e"] = {"value": ops / dt / 1e12, "unit": "TOPS", "h2d_bytes_per_step": h2d,
+                       "d2h_bytes_per_step": d2h, "path": "message channel, opcode 15 (56-byte payload), "
+                       "pinned host buffers"}
+    elif world > 1:
+        line["e2e"] = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tops, threads, secs = cpu_sample(k, n, args.cpu_rows)
+        line["cpu_baseline"] = {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port",
+                                "sample": f"{args.cpu_rows} of {m} rows, all {n} columns ({secs:.2f} s)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

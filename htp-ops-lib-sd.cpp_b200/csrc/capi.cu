@@ -52,7 +52,6 @@ struct Device {
   bool ready = false;
   int ordinal = -1;
   int sms = 148;
-  cudaStream_t stream = nullptr;
   uint32_t *watchdog = nullptr;
   std::map<cudaStream_t, Workspace> ws;
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -80,9 +79,9 @@ int current_device(Device **out) {
   return HTPG_OK;
 }
 
-cudaStream_t pick_stream(Device *d, void *stream) {
-  return stream ? static_cast<cudaStream_t>(stream) : d->stream;
-}
+// NULL is the CUDA default stream (the stream torch and most callers use
+// unless they create their own).
+cudaStream_t pick_stream(Device *, void *stream) { return static_cast<cudaStream_t>(stream); }
 
 // Stream-private scratch: activation codes / FP16 activations, row scales,
 // split-K accumulators.  Grows (after a stream synchronisation) when a larger
@@ -216,8 +215,6 @@ extern "C" int htpg_init(int device) {
   }
   d.ordinal = device;
   d.sms = prop.multiProcessorCount;
-  if (cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking) != cudaSuccess)
-    return record_cuda(cudaGetLastError());
   if (cudaGetSymbolAddress(reinterpret_cast<void **>(&d.watchdog), g_watchdog) != cudaSuccess)
     return record_cuda(cudaGetLastError());
   for (auto &e : d.ev)
@@ -597,9 +594,10 @@ extern "C" int htpg_w8a8_linear(float *out, const float *x, const void *constant
 extern "C" int htpg_f16_linear(float *out, const float *x, const uint16_t *permuted_weight,
                                const float *bias, int m, int k, int n, int channels, int mode,
                                void *stream) {
-  // argument checks in the reference's order and codes (mat_mul.c:939-951)
+  // argument checks in the reference's order and codes (mat_mul.c:939-951);
+  // the diagnostic raw-accumulator mode is accepted here as well
   if (!out || !x || !permuted_weight || !m || !n || !k) return HTPG_EARGS;
-  if (m < 1 || k < 1 || n < 1 || channels < 1 || channels > n || mode < 0 || mode > 3 ||
+  if (m < 1 || k < 1 || n < 1 || channels < 1 || channels > n || mode < 0 || mode > HTPG_MODE_RAW ||
       (mode != 3 && channels != n) || k % 32 || n % 32)
     return HTPG_ECAPACITY;
   if (m > HTPG_W8A8_MAX_M) return HTPG_ENOPLAN;

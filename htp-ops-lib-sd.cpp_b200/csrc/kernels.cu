@@ -237,60 +237,78 @@ cudaError_t launch_repack_f16(uint16_t *dst, const uint16_t *perm, int k, int n0
 // x*sigmoid(1.5957691216057308*(x + 0.044715 x^3)), QuickGELU as
 // x*sigmoid(1.702 x); the sigmoid keeps the reference's stable form
 // e = 2^max(-|z| log2(e), -126), inv = 1/(1+e), sigma = z<0 ? e*inv : inv,
-// with CUDA's exp2f and a correctly rounded reciprocal.
-__device__ __forceinline__ float epilogue_act(float x, int mode) {
-  if (mode != 1 && mode != 2) return x;
-  float z;
-  if (mode == 1) {
-    const float cubic = __fmul_rn(__fmul_rn(x, x), x);
-    z = __fmul_rn(__fadd_rn(x, __fmul_rn(cubic, 0.044715f)), 1.5957691216057308f);
+// with CUDA's exp2f and the hardware reciprocal (e+1 lies in [1,2]).
+// MODE is a template parameter so the per-element code is branch-free and the
+// 32 elements of a TMEM chunk interleave.
+template <int MODE>
+__device__ __forceinline__ float epilogue_act(float x) {
+  if constexpr (MODE != 1 && MODE != 2) {
+    return x;
   } else {
-    z = __fmul_rn(x, 1.702f);
+    float z;
+    if constexpr (MODE == 1) {
+      const float cubic = __fmul_rn(__fmul_rn(x, x), x);
+      z = __fmul_rn(__fadd_rn(x, __fmul_rn(cubic, 0.044715f)), 1.5957691216057308f);
+    } else {
+      z = __fmul_rn(x, 1.702f);
+    }
+    const float arg = fmaxf(__fmul_rn(fabsf(z), -1.4426950408889634f), -126.0f);
+    const float e = exp2f(arg);
+    const float inv = __fdividef(1.0f, __fadd_rn(e, 1.0f));
+    const float sig = z < 0.0f ? __fmul_rn(e, inv) : inv;
+    return __fmul_rn(x, sig);
   }
-  const float arg = fmaxf(__fmul_rn(fabsf(z), -1.4426950408889634f), -126.0f);
-  const float e = exp2f(arg);
-  const float inv = __frcp_rn(__fadd_rn(e, 1.0f));
-  const float sig = z < 0.0f ? __fmul_rn(e, inv) : inv;
-  return __fmul_rn(x, sig);
 }
 
-// I8: v = fl(fl(float(acc + corr) * sw) * rs) (linear_w8a8.c:168-179), then bias, act.
-__device__ __forceinline__ float finish_i8(int32_t acc, int32_t corr, float sw, float rs,
-                                           float bias, bool has_bias, int mode) {
-  const int32_t y = static_cast<int32_t>(static_cast<uint32_t>(acc) + static_cast<uint32_t>(corr));
-  if (mode == 4) return __int_as_float(y);  // diagnostic: raw INT32 accumulator
-  float v = __fmul_rn(__fmul_rn(__int2float_rn(y), sw), rs);
-  if (has_bias) v = __fadd_rn(v, bias);
-  return epilogue_act(v, mode);
-}
-// F16: v = acc (FP32 accumulate), then bias, act (mat_mul.c:864-882).
-__device__ __forceinline__ float finish_f16(float acc, float bias, bool has_bias, int mode) {
-  if (mode == 4) return acc;  // diagnostic: raw FP32 accumulator
-  float v = acc;
-  if (has_bias) v = __fadd_rn(v, bias);
-  return epilogue_act(v, mode);
+// One accumulator element -> output value.
+//  I8:  v = fl(fl(float(acc + corr) * sw) * rs) (linear_w8a8.c:168-179), bias, act
+//  F16: v = acc (FP32 accumulate), bias, act (mat_mul.c:864-882)
+//  MODE 4 (diagnostic): the raw accumulator bits.
+template <Kind KIND, int MODE, bool BIAS>
+__device__ __forceinline__ float finish(uint32_t acc, int32_t corr, float sw, float rs, float bias) {
+  float v;
+  if constexpr (KIND == Kind::I8) {
+    const int32_t y = static_cast<int32_t>(acc + static_cast<uint32_t>(corr));
+    if constexpr (MODE == 4) return __int_as_float(y);
+    v = __fmul_rn(__fmul_rn(__int2float_rn(y), sw), rs);
+  } else {
+    v = __uint_as_float(acc);
+    if constexpr (MODE == 4) return v;
+  }
+  if constexpr (BIAS) v = __fadd_rn(v, bias);
+  return epilogue_act<MODE>(v);
 }
 
-constexpr int kThreads = 192;      // warp 0 TMA, warp 1 MMA/TMEM, warps 2..5 epilogue
-constexpr int kEpiThreads = 128;
-constexpr int kRowBytes = 128;     // one K block = one 128-byte swizzle row
+constexpr int kEpiWarps = 8;                       // two per TMEM lane quadrant
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;         // warp 0 TMA, warp 1 MMA/TMEM, 2..9 epilogue
+constexpr int kRowBytes = 128;                     // one K block = one 128-byte swizzle row
 constexpr int kTransposeStride = 33;
+constexpr int kWarpScratch = 32 * kTransposeStride;  // floats per epilogue warp
 
+constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block on sm_100
+// As many pipeline stages as fit beside the epilogue scratch (at most 10).
 __host__ __device__ constexpr int stages_for(int bn) {
-  return bn >= 256 ? 4 : bn >= 128 ? 6 : bn >= 64 ? 8 : 10;
+  return (kSmemLimit - 1024 - 256 - kEpiWarps * kWarpScratch * 4) / ((128 + bn) * kRowBytes) < 10
+             ? (kSmemLimit - 1024 - 256 - kEpiWarps * kWarpScratch * 4) / ((128 + bn) * kRowBytes)
+             : 10;
 }
 __host__ __device__ constexpr int tmem_cols_for(int bn) {
   return 2 * bn <= 32 ? 32 : 2 * bn <= 64 ? 64 : 2 * bn <= 128 ? 128 : 2 * bn <= 256 ? 256 : 512;
 }
 __host__ __device__ constexpr size_t smem_bytes_for(int bn) {
   return 1024 /* alignment slack */ + static_cast<size_t>(stages_for(bn)) * (128 + bn) * kRowBytes +
-         4u * 32u * kTransposeStride * 4u + 256 /* barriers, tmem slot, flags */;
+         static_cast<size_t>(kEpiWarps) * kWarpScratch * 4u + 256 /* barriers, tmem slot, flags */;
 }
+static_assert(smem_bytes_for(256) <= kSmemLimit && smem_bytes_for(128) <= kSmemLimit &&
+                  smem_bytes_for(64) <= kSmemLimit && smem_bytes_for(32) <= kSmemLimit &&
+                  smem_bytes_for(16) <= kSmemLimit,
+              "shared memory budget");
 
 struct SmemLayout {
   uint8_t *a;          // STAGES x 128 rows x 128 B
   uint8_t *b;          // STAGES x BN rows x 128 B
-  float *transpose;    // 4 warps x 32 x 33
+  float *scratch;      // per epilogue warp: column parameters, then the 32x33 transpose
   uint64_t *full, *empty, *tfull, *tempty, *mma_done;
   uint32_t *tmem_slot;
   uint32_t *flag;            // split-K "this CTA finishes the tile"
@@ -305,8 +323,8 @@ __device__ __forceinline__ SmemLayout carve(uint8_t *raw) {
   p += STAGES * 128 * kRowBytes;
   L.b = p;
   p += STAGES * BN * kRowBytes;
-  L.transpose = reinterpret_cast<float *>(p);
-  p += 4 * 32 * kTransposeStride * 4;
+  L.scratch = reinterpret_cast<float *>(p);
+  p += kEpiWarps * kWarpScratch * 4;
   uint64_t *bars = reinterpret_cast<uint64_t *>(p);
   L.full = bars;
   L.empty = bars + STAGES;
@@ -336,6 +354,190 @@ struct KernelParams {
   int tiles_a, tiles_b, splits, kb_total, kb_per_split, units;
 };
 
+// Everything an epilogue warp needs for one unit.
+struct EpiCtx {
+  const GemmArgs *g;
+  const KernelParams *P;
+  SmemLayout L;
+  float *scr;        // this warp's scratch
+  uint32_t t_row;    // TMEM address of lane quadrant q, accumulator buffer
+  Unit w;
+  int q, half, lane, epi_t;
+  bool ok;           // the accumulator-full wait succeeded
+};
+
+// Normal orientation: TMEM lane = activation row m, column = weight column n.
+// Each warp takes every other 32-column chunk of its lane quadrant.
+template <Kind KIND, int BN, int MODE, bool BIAS>
+__device__ __forceinline__ void epilogue_normal(const EpiCtx &c) {
+  const GemmArgs &g = *c.g;
+  const int m = c.w.ta * 128 + c.q * 32 + c.lane;
+  const bool m_ok = m < g.M;
+  const float rs = (KIND == Kind::I8 && m_ok) ? __ldg(g.row_scale + m) : 0.0f;
+  float *scr = c.scr;
+#pragma unroll 1
+  for (int ch = c.half; ch < BN / 32; ch += 2) {
+    uint32_t r[32];
+    tmem_ld32(c.t_row + ch * 32, r);
+    const int n0 = c.w.tb * BN + ch * 32;
+    const int nl = n0 + c.lane;
+    const bool nl_ok = nl < g.N;
+    // per-column parameters of this chunk -> scratch[0..95], read back as broadcasts
+    if (KIND == Kind::I8) {
+      scr[c.lane] = nl_ok ? __ldg(g.col_scale + nl) : 0.0f;
+      scr[32 + c.lane] = __int_as_float(nl_ok ? __ldg(g.col_corr + nl) : 0);
+    }
+    if (BIAS) scr[64 + c.lane] = nl_ok ? __ldg(g.bias + nl) : 0.0f;
+    tmem_ld_wait();
+    __syncwarp();
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f), c4 = s4, b4 = s4;
+      if (KIND == Kind::I8) {
+        s4 = *reinterpret_cast<const float4 *>(scr + j);
+        c4 = *reinterpret_cast<const float4 *>(scr + 32 + j);
+      }
+      if (BIAS) b4 = *reinterpret_cast<const float4 *>(scr + 64 + j);
+      v[j + 0] = finish<KIND, MODE, BIAS>(r[j + 0], __float_as_int(c4.x), s4.x, rs, b4.x);
+      v[j + 1] = finish<KIND, MODE, BIAS>(r[j + 1], __float_as_int(c4.y), s4.y, rs, b4.y);
+      v[j + 2] = finish<KIND, MODE, BIAS>(r[j + 2], __float_as_int(c4.z), s4.z, rs, b4.z);
+      v[j + 3] = finish<KIND, MODE, BIAS>(r[j + 3], __float_as_int(c4.w), s4.w, rs, b4.w);
+    }
+    __syncwarp();
+    if (MODE == 3) {
+      // channel-major out[n*ldo + m]: lanes hold consecutive m -> coalesced
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = n0 + j;
+        if (m_ok && n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = v[j];
+      }
+    } else {
+      // row-major: transpose through shared memory so each store is one
+      // 128-byte row segment
+#pragma unroll
+      for (int j = 0; j < 32; ++j) scr[c.lane * kTransposeStride + j] = v[j];
+      __syncwarp();
+      const int mbase = c.w.ta * 128 + c.q * 32;
+#pragma unroll 8
+      for (int rr = 0; rr < 32; ++rr) {
+        const int mr = mbase + rr;
+        if (mr < g.M && nl_ok)
+          g.out[static_cast<long long>(mr) * g.ldo + nl] = scr[rr * kTransposeStride + c.lane];
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// Swapped orientation (small M): TMEM lane = weight column n, column = activation
+// row m (BN <= 32).  The first four warps hold the data; all eight take part in
+// the split-K barriers.
+template <Kind KIND, int BN, int MODE, bool BIAS>
+__device__ __forceinline__ void epilogue_swap(const EpiCtx &c) {
+  const GemmArgs &g = *c.g;
+  const KernelParams &P = *c.P;
+  const bool owner = c.half == 0;
+  const int n = c.w.ta * 128 + c.q * 32 + c.lane;
+  const bool n_ok = n < g.N;
+  uint32_t r[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) r[j] = 0u;
+  if (c.ok && owner) {
+    if (BN == 16) {
+      uint32_t r16[16];
+      tmem_ld16(c.t_row, r16);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) r[j] = r16[j];
+    } else {
+      tmem_ld32(c.t_row, r);
+      tmem_ld_wait();
+    }
+  }
+  bool fin = c.ok;
+  if (P.splits > 1) {
+    // exact INT32 split-K: partials meet in HBM; the last CTA of the tile
+    // finishes it and leaves the accumulators and counter zeroed
+    const int tile = c.w.ta * P.tiles_b + c.w.tb;
+    int32_t *ws = g.ws + (static_cast<size_t>(tile) * 128 + c.q * 32 + c.lane) * BN;
+    if (c.ok && owner) {
+#pragma unroll
+      for (int j = 0; j < BN; ++j) atomicAdd(ws + j, static_cast<int32_t>(r[j]));
+      __threadfence();
+    }
+    named_bar_sync(1, kEpiThreads);
+    if (c.epi_t == 0) {
+      uint32_t last = 0u;
+      if (!*c.L.abort) {
+        const uint32_t prev = atomicAdd(g.ws_count + tile, 1u);
+        last = (prev == static_cast<uint32_t>(P.splits - 1)) ? 1u : 0u;
+      }
+      *c.L.flag = last;
+    }
+    named_bar_sync(1, kEpiThreads);
+    fin = c.ok && *c.L.flag != 0u;
+    if (fin && owner) {
+      __threadfence();
+#pragma unroll
+      for (int j = 0; j < BN; ++j) {
+        r[j] = static_cast<uint32_t>(__ldcg(ws + j));
+        ws[j] = 0;
+      }
+      if (c.epi_t == 0) g.ws_count[tile] = 0u;
+    }
+    named_bar_sync(1, kEpiThreads);
+  }
+  if (!fin || !owner) return;
+  float *scr = c.scr;
+  const int mrow = c.w.tb * BN + c.lane;
+  scr[c.lane] = (KIND == Kind::I8 && mrow < g.M) ? __ldg(g.row_scale + mrow) : 0.0f;
+  __syncwarp();
+  if (!n_ok) return;
+  float sw = 0.0f, bn_ = 0.0f;
+  int32_t cr = 0;
+  if (KIND == Kind::I8) {
+    sw = __ldg(g.col_scale + n);
+    cr = __ldg(g.col_corr + n);
+  }
+  if (BIAS) bn_ = __ldg(g.bias + n);
+#pragma unroll
+  for (int j = 0; j < BN; ++j) {
+    const int m = c.w.tb * BN + j;
+    if (m >= g.M) break;
+    const float v = finish<KIND, MODE, BIAS>(r[j], cr, sw, scr[j], bn_);
+    if (MODE == 3) {
+      if (n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = v;
+    } else {
+      g.out[static_cast<long long>(m) * g.ldo + n] = v;
+    }
+  }
+}
+
+template <Kind KIND, int BN, bool SWAP, int MODE, bool BIAS>
+__device__ __forceinline__ void epilogue_unit(const EpiCtx &c) {
+  if constexpr (SWAP) {
+    epilogue_swap<KIND, BN, MODE, BIAS>(c);
+  } else {
+    if (c.ok) epilogue_normal<KIND, BN, MODE, BIAS>(c);
+  }
+}
+
+template <Kind KIND, int BN, bool SWAP>
+__device__ __forceinline__ void epilogue_dispatch(const EpiCtx &c, int mode, bool bias) {
+  switch (mode * 2 + (bias ? 1 : 0)) {
+    case 0: epilogue_unit<KIND, BN, SWAP, 0, false>(c); break;
+    case 1: epilogue_unit<KIND, BN, SWAP, 0, true>(c); break;
+    case 2: epilogue_unit<KIND, BN, SWAP, 1, false>(c); break;
+    case 3: epilogue_unit<KIND, BN, SWAP, 1, true>(c); break;
+    case 4: epilogue_unit<KIND, BN, SWAP, 2, false>(c); break;
+    case 5: epilogue_unit<KIND, BN, SWAP, 2, true>(c); break;
+    case 6: epilogue_unit<KIND, BN, SWAP, 3, false>(c); break;
+    case 7: epilogue_unit<KIND, BN, SWAP, 3, true>(c); break;
+    default: epilogue_unit<KIND, BN, SWAP, 4, false>(c); break;
+  }
+}
+
 template <Kind KIND, int BN, bool SWAP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -362,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&L.tfull[b]), 1);
-      mbar_init(smem_u32(&L.tempty[b]), kEpiThreads / 32);
+      mbar_init(smem_u32(&L.tempty[b]), kEpiWarps);
     }
     mbar_init(smem_u32(L.mma_done), 1);
     *L.abort = 0u;
@@ -462,169 +664,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;                      // TMEM lane quadrant of this warp
-    const int epi_t = threadIdx.x - 64;          // 0..127
-    float *tr = L.transpose + (warp - 2) * 32 * kTransposeStride;
+    EpiCtx c;
+    c.g = &g;
+    c.P = &P;
+    c.L = L;
+    c.q = warp & 3;                            // TMEM lane quadrant of this warp
+    c.half = (warp - 2) / 4;                   // which of the two warps of the quadrant
+    c.lane = lane;
+    c.epi_t = threadIdx.x - 64;
+    c.scr = L.scratch + (warp - 2) * kWarpScratch;
     const bool has_bias = g.bias != nullptr;
     uint32_t iter = 0;
+    // No early exit: all epilogue warps run the same iterations so their
+    // named barriers always match; after a failed wait the unit's work is
+    // skipped (the watchdog word reports the failure).
     for (int u = blockIdx.x; u < P.units; u += gridDim.x, ++iter) {
-      const Unit w = decode_unit(u, P.tiles_b, P.splits);
+      c.w = decode_unit(u, P.tiles_b, P.splits);
       const uint32_t buf = iter & 1u;
       const uint32_t acc_ph = (iter >> 1) & 1u;
-      // No early exit: all four epilogue warps run the same iterations so
-      // their named barriers always match; after a failed wait the unit's
-      // work is skipped (the watchdog word reports the failure).
-      const bool ok = mbar_wait(smem_u32(&L.tfull[buf]), acc_ph, wd, kWatchEpilogue, L.abort);
+      c.ok = mbar_wait(smem_u32(&L.tfull[buf]), acc_ph, wd, kWatchEpilogue, L.abort);
       tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-
-      if (!SWAP) {
-        if (!ok) continue;
-        // rows of D = activation rows m, columns = weight columns n
-        const int m = w.ta * 128 + q * 32 + lane;
-        const bool m_ok = m < g.M;
-        const float rs = (KIND == Kind::I8 && m_ok) ? __ldg(g.row_scale + m) : 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c * 32, r);
-          tmem_ld_wait();
-          const int n0 = w.tb * BN + c * 32;
-          const int nl = n0 + lane;
-          const bool nl_ok = nl < g.N;
-          float sw_l = 0.0f, b_l = 0.0f;
-          int32_t cr_l = 0;
-          if (nl_ok) {
-            if (KIND == Kind::I8) {
-              sw_l = __ldg(g.col_scale + nl);
-              cr_l = __ldg(g.col_corr + nl);
-            }
-            if (has_bias) b_l = __ldg(g.bias + nl);
-          }
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float bj = __shfl_sync(0xffffffffu, b_l, j);
-            if (KIND == Kind::I8) {
-              const float swj = __shfl_sync(0xffffffffu, sw_l, j);
-              const int32_t crj = __shfl_sync(0xffffffffu, cr_l, j);
-              v[j] = finish_i8(static_cast<int32_t>(r[j]), crj, swj, rs, bj, has_bias, g.mode);
-            } else {
-              v[j] = finish_f16(__uint_as_float(r[j]), bj, has_bias, g.mode);
-            }
-          }
-          if (g.mode == 3) {
-            // channel-major: out[n*ldo + m]; lanes hold consecutive m -> coalesced
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = n0 + j;
-              if (m_ok && n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = v[j];
-            }
-          } else {
-            // row-major: transpose through shared memory so each store is one
-            // 128-byte row segment
-#pragma unroll
-            for (int j = 0; j < 32; ++j) tr[lane * kTransposeStride + j] = v[j];
-            __syncwarp();
-            const int mbase = w.ta * 128 + q * 32;
-#pragma unroll 4
-            for (int rr = 0; rr < 32; ++rr) {
-              const int mr = mbase + rr;
-              if (mr < g.M && nl_ok)
-                g.out[static_cast<long long>(mr) * g.ldo + nl] = tr[rr * kTransposeStride + lane];
-            }
-            __syncwarp();
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&L.tempty[buf]));
-      } else {
-        // rows of D = weight columns n, columns = activation rows m (BN <= 32)
-        const int n = w.ta * 128 + q * 32 + lane;
-        const bool n_ok = n < g.N;
-        uint32_t r[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = 0u;
-        if (ok) {
-          if (BN == 16) {
-            uint32_t r16[16];
-            tmem_ld16(t_row, r16);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) r[j] = r16[j];
-          } else {
-            tmem_ld32(t_row, r);
-            tmem_ld_wait();
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&L.tempty[buf]));
-        }
-
-        bool finish = ok;
-        if (P.splits > 1) {
-          // exact INT32 split-K: accumulate partials in HBM; the last CTA of the
-          // tile finishes it and leaves the workspace zeroed for the next call
-          const int tile = w.ta * P.tiles_b + w.tb;
-          int32_t *ws = g.ws + (static_cast<size_t>(tile) * 128 + q * 32 + lane) * BN;
-          if (ok) {
-#pragma unroll
-            for (int j = 0; j < BN; ++j) atomicAdd(ws + j, static_cast<int32_t>(r[j]));
-            __threadfence();
-          }
-          named_bar_sync(1, kEpiThreads);
-          if (epi_t == 0) {
-            uint32_t last = 0u;
-            if (!*L.abort) {
-              const uint32_t prev = atomicAdd(g.ws_count + tile, 1u);
-              last = (prev == static_cast<uint32_t>(P.splits - 1)) ? 1u : 0u;
-            }
-            *L.flag = last;
-          }
-          named_bar_sync(1, kEpiThreads);
-          finish = ok && *L.flag != 0u;
-          if (finish) {
-            __threadfence();
-#pragma unroll
-            for (int j = 0; j < BN; ++j) {
-              r[j] = static_cast<uint32_t>(__ldcg(ws + j));
-              ws[j] = 0;
-            }
-            if (epi_t == 0) g.ws_count[tile] = 0u;
-          }
-          named_bar_sync(1, kEpiThreads);
-        }
-        if (finish) {
-          const int mrow = w.tb * BN + lane;
-          const float rs_l = (KIND == Kind::I8 && mrow < g.M) ? __ldg(g.row_scale + mrow) : 0.0f;
-          float rsj[BN];
-#pragma unroll
-          for (int j = 0; j < BN; ++j) rsj[j] = __shfl_sync(0xffffffffu, rs_l, j);
-          if (n_ok) {
-            float sw = 0.0f, bn_ = 0.0f;
-            int32_t cr = 0;
-            if (KIND == Kind::I8) {
-              sw = __ldg(g.col_scale + n);
-              cr = __ldg(g.col_corr + n);
-            }
-            if (has_bias) bn_ = __ldg(g.bias + n);
-#pragma unroll
-            for (int j = 0; j < BN; ++j) {
-              const int m = w.tb * BN + j;
-              if (m >= g.M) continue;
-              const float v = KIND == Kind::I8 ? finish_i8(static_cast<int32_t>(r[j]), cr, sw, rsj[j],
-                                                           bn_, has_bias, g.mode)
-                                               : finish_f16(__uint_as_float(r[j]), bn_, has_bias, g.mode);
-              if (g.mode == 3) {
-                if (n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = v;
-              } else {
-                g.out[static_cast<long long>(m) * g.ldo + n] = v;
-              }
-            }
-          }
-        }
-      }
+      c.t_row = tmem_base + (static_cast<uint32_t>(c.q * 32) << 16) + buf * BN;
+      epilogue_dispatch<KIND, BN, SWAP>(c, g.mode, has_bias);
+      // this warp's TMEM reads of the buffer are complete (tcgen05.wait::ld)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && c.ok) mbar_arrive(smem_u32(&L.tempty[buf]));
     }
   }
 

@@ -229,3 +229,43 @@ def phase_timing_read() -> tuple[float, float, int]:
 def check_device(stream=None) -> int:
     flags = ctypes.c_uint32(0)
     return lib().htpg_check_device(stream_ptr(stream), ctypes.byref(flags))
+
+
+# ------------------------------------------------------------------ formats
+# Host-side packers of the reference's weight formats (what the caller's
+# offline packer produces): the W8A8 constants blob (include/op_reg.h
+# W8A8Header; INT8 weights in the HMX deep N64 layout of
+# src/dsp/ops/linear_w8a8.c:453-487) and the permuted FP16 tile layout
+# (src/host/test.c:548-556).
+def pack_w8a8_constants(w_nk, sw, inverse=None, signature: int = 0):
+    """w_nk: [N][K] int8, sw: [N] float32, inverse: [K] float32 or None (ones)."""
+    import numpy as np
+    w_nk = np.ascontiguousarray(w_nk, np.int8)
+    n, k = w_nk.shape
+    assert n % 64 == 0 and k % 32 == 0
+    kn = k * n
+    bytes_ = 128 + kn + 8 * n + 4 * k
+    blob = np.zeros(bytes_, np.uint8)
+    hdr = np.zeros(10, np.uint32)
+    hdr[:] = [0x38574D48, 1, k, n, 128, 128 + kn, 128 + kn + 4 * n, 128 + kn + 8 * n, bytes_, 0]
+    blob[:40] = hdr.view(np.uint8)
+    blob[40:48] = np.array([signature], np.uint64).view(np.uint8)
+    # n = g*64 + h*32 + j, k = t*32 + q*4 + r  ->  [g][t][h][q][j][r]
+    deep = w_nk.reshape(n // 64, 2, 32, k // 32, 8, 4).transpose(0, 3, 1, 4, 2, 5)
+    blob[128:128 + kn] = deep.reshape(-1).view(np.uint8)
+    blob[128 + kn:128 + kn + 4 * n] = np.ascontiguousarray(sw, np.float32).view(np.uint8)
+    sums = w_nk.astype(np.int32).sum(axis=1).astype(np.int32)
+    blob[128 + kn + 4 * n:128 + kn + 8 * n] = sums.view(np.uint8)
+    inv = np.ones(k, np.float32) if inverse is None else np.ascontiguousarray(inverse, np.float32)
+    blob[128 + kn + 8 * n:] = inv.view(np.uint8)
+    return blob
+
+
+def pack_f16_permuted(w_kn_bits):
+    """w_kn_bits: [K][N] FP16 bit patterns (uint16) -> permuted 32x32 tiles."""
+    import numpy as np
+    w = np.ascontiguousarray(w_kn_bits, np.uint16)
+    k, n = w.shape
+    assert k % 32 == 0 and n % 32 == 0
+    # k = t*32 + p*2 + b, n = s*32 + j  ->  [s][t][p][j][b]
+    return w.reshape(k // 32, 16, 2, n // 32, 32).transpose(3, 0, 1, 4, 2).reshape(-1).copy()

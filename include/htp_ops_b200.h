@@ -5,7 +5,7 @@
  *
  *  1. Device-pointer kernel API (htpg_* and the reference kernel names).
  *     Tensors live in HBM; work is enqueued on a CUDA stream (`stream` is a
- *     cudaStream_t passed as void*; NULL = the library's per-device stream).
+ *     cudaStream_t passed as void*; NULL = the CUDA default stream).
  *     Calls return 0 or a negative error code and never synchronise unless
  *     stated.  These replace the DSP kernel entry points of the reference
  *     (include/dsp/ops.h:20-31).
@@ -61,7 +61,7 @@ extern "C" {
 #define HTPG_MODE_RAW 4
 
 /* ---- library / device ------------------------------------------------- */
-/* Select `device` for this thread, check it is sm_100, create the library stream.
+/* Select `device` for this thread and check it is sm_100.
  * Returns 0, HTPG_EARCH (not sm_100) or HTPG_ELAUNCH (no CUDA device). */
 int htpg_init(int device);
 /* Library version (1). */

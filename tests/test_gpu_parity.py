@@ -42,9 +42,10 @@ def test_quantize_rows_bitexact(gpu, lib, m, k, inverse):
     codes_ref, scales_ref = O.quantize_rows(x, inv)
     codes = torch.empty(m, k, dtype=torch.int8, device=gpu)
     scales = torch.empty(m, dtype=torch.float32, device=gpu)
-    htpg.check(lib.htpg_quantize_rows(htpg.ptr(codes), htpg.ptr(scales), htpg.ptr(_t(x, gpu)),
-                                      htpg.ptr(_t(inv, gpu)) if inverse else None, m, k,
-                                      htpg.stream_ptr()), "quantize")
+    xd = _t(x, gpu)                       # keep device copies alive until the kernel ran
+    invd = _t(inv, gpu) if inverse else None
+    htpg.check(lib.htpg_quantize_rows(htpg.ptr(codes), htpg.ptr(scales), htpg.ptr(xd), htpg.ptr(invd),
+                                      m, k, htpg.stream_ptr()), "quantize")
     torch.cuda.synchronize()
     got_codes = codes.cpu().numpy().astype(np.int16) + 128
     np.testing.assert_array_equal(got_codes, codes_ref.astype(np.int16))
@@ -132,7 +133,8 @@ def _run_f16(lib, gpu, x, wperm, m, k, n, bias=None, channels=None, mode=0, raw=
         out = torch.full((m, n), float("nan"), dtype=torch.float32, device=gpu)
     wdev = _t(wperm.view(np.int16), gpu)
     b = _t(bias, gpu) if bias is not None else None
-    rc = lib.htpg_f16_linear(htpg.ptr(out), htpg.ptr(_t(x, gpu)), htpg.ptr(wdev), htpg.ptr(b), m, k, n,
+    xd = _t(x, gpu)
+    rc = lib.htpg_f16_linear(htpg.ptr(out), htpg.ptr(xd), htpg.ptr(wdev), htpg.ptr(b), m, k, n,
                              channels, 4 if raw else mode, htpg.stream_ptr())
     htpg.check(rc, "htpg_f16_linear")
     htpg.check(htpg.check_device(), "device watchdog")
