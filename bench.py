@@ -134,6 +134,9 @@ def make_c4_inputs(torch, dev, m, k, n, seed=0x5EED0003):
 
 
 # ------------------------------------------------------------------ CPU leg
+_CPU_CASES = {}
+
+
 def cpu_sample(k, n, rows, reps=1):
     """Time the OpenMP CPU oracle on `rows` rows of a C4-shaped problem.
     Returns (TOPS, threads, seconds)."""
@@ -145,7 +148,10 @@ def cpu_sample(k, n, rows, reps=1):
         O.lib("native")
     except Exception:
         kind = "omp"
-    c = O.make_w8a8(3, "C4-sample", rows, k, n, 0.005, True, 1)
+    key = (rows, k, n)
+    if key not in _CPU_CASES:
+        _CPU_CASES[key] = O.make_w8a8(3, "C4-sample", rows, k, n, 0.005, True, 1)
+    c = _CPU_CASES[key]
     O.w8a8_linear(c.x[:8], c.blob, k, n, bias=c.bias, mode=1, kind=kind)  # warm
     t0 = time.perf_counter()
     for _ in range(reps):
@@ -254,9 +260,14 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-rows", type=int, default=256)
+    ap.add_argument("--cpu-rows", type=int, default=M_C4,
+                    help="rows of the C4 problem the CPU baseline computes per sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--m", type=int, default=M_C4,
+                    help="token rows; smaller values only for profiling captures (workload C4-M<m>)")
+    ap.add_argument("--settle", type=float, default=1.5,
+                    help="seconds of untimed load before timing (clock sampling); 0 under ncu")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -280,7 +291,8 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
 
-    m, k, n = M_C4, K_C4, N_C4
+    m, k, n = args.m, K_C4, N_C4
+    workload = "C4" if m == M_C4 else f"C4-M{m}"
     assert n % (64 * world) == 0
     n_loc = n // world
     n0 = rank * n_loc
@@ -322,7 +334,7 @@ def main():
         step()
     torch.cuda.synchronize()
     per = max((time.perf_counter() - t0) / 5, 1e-5)
-    cnt = torch.tensor([min(int(1.5 / per) + 1, 20000)], dtype=torch.int64, device=dev)
+    cnt = torch.tensor([min(int(args.settle / per), 20000)], dtype=torch.int64, device=dev)
     if dist:
         dist.all_reduce(cnt, op=dist.ReduceOp.MAX)
     settle = int(cnt.item())
@@ -392,7 +404,7 @@ def main():
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "u8xs8->s32 (int8 tensor cores), f32 io",
         "data": "synthetic (seeded; BASELINE C4 distributions)",
-        "config": {"workload": "C4", "M": m, "K": k, "N": n, "N_per_gpu": n_loc,
+        "config": {"workload": workload, "M": m, "K": k, "N": n, "N_per_gpu": n_loc,
                    "epilogue": "bias+gelu_tanh", "parallelism": f"tp{world} (columns)" if world > 1 else "single",
                    "exchange": "nccl all_gather + reassembly" if world > 1 else None,
                    "l2": "256 MiB flush write between steps (outside the timed events)"},

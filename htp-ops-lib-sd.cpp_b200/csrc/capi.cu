@@ -135,6 +135,24 @@ int make_map(CUtensorMap *map, const void *base, Kind kind, int k, int rows, siz
   return HTPG_OK;
 }
 
+// Row-major FP32 output [rows][cols] with row pitch ldo floats: 32 x 32 boxes,
+// 128-byte swizzle (the epilogue's staging layout).
+int make_out_map(CUtensorMap *map, float *out, int rows, int cols, long long ldo) {
+  if (!g_encode) return HTPG_ELAUNCH;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldo) * 4u};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    t_last_cuda_error = "cuTensorMapEncodeTiled(out) failed (" + std::to_string(static_cast<int>(r)) + ")";
+    return HTPG_ELAUNCH;
+  }
+  return HTPG_OK;
+}
+
 }  // namespace
 
 // Prepared weight: K-major rows in HBM plus the per-column epilogue data.
@@ -485,7 +503,7 @@ int run_common(htpg_weights *w, float *out, int ldo, const float *x, const float
   rc = make_map(&act_map, act, w->kind, k, m, static_cast<size_t>(k) * act_elem,
                 plan.swap ? plan.bn : 128);
   if (rc) return rc;
-  rc = weight_map(w, plan.swap ? 128 : plan.bn, &wmap);
+  rc = weight_map(w, plan.swap ? 128 : box_rows_b(plan), &wmap);
   if (rc) return rc;
 
   GemmArgs a;
@@ -503,7 +521,15 @@ int run_common(htpg_weights *w, float *out, int ldo, const float *x, const float
   a.ws = wsk;
   a.ws_count = cnt;
   a.watchdog = d->watchdog;
-  e = plan.swap ? launch_gemm(plan, *wmap, act_map, a, st) : launch_gemm(plan, act_map, *wmap, a, st);
+  // row-major outputs of the normal orientation leave the SM through TMA stores
+  CUtensorMap out_map = act_map;  // placeholder when unused
+  if (!plan.swap && mode != 3 && tma_store_ok(out, ldo)) {
+    rc = make_out_map(&out_map, out, m, n, ldo);
+    if (rc) return rc;
+    a.tma_store = 1;
+  }
+  e = plan.swap ? launch_gemm(plan, *wmap, act_map, out_map, a, st)
+                : launch_gemm(plan, act_map, *wmap, out_map, a, st);
   if (e != cudaSuccess) return record_cuda(e);
   if (phase) {
     cudaEventRecord(pe.e[2], st);

@@ -105,10 +105,84 @@ __global__ void __launch_bounds__(TPR *ROWS) quantize_rows_kernel(int8_t *__rest
   }
 }
 
+// Rows of at most STEPS*256 elements: a warp per row that keeps the whole row
+// in registers, so the row is read from HBM once and all of a lane's loads
+// are in flight before the first use.
+template <int STEPS>
+__global__ void __launch_bounds__(256) quantize_rows_reg_kernel(int8_t *__restrict__ codes,
+                                                                float *__restrict__ scales,
+                                                                const float *__restrict__ x,
+                                                                const float *__restrict__ inverse,
+                                                                int m, int k) {
+  const int row = blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= m) return;
+  const float *xr = x + static_cast<size_t>(row) * k;
+  float v[STEPS][8];
+#pragma unroll
+  for (int s = 0; s < STEPS; ++s) {
+    const int c = s * 256 + lane * 8;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (c < k) {
+      a = __ldg(reinterpret_cast<const float4 *>(xr + c));
+      b = __ldg(reinterpret_cast<const float4 *>(xr + c + 4));
+    }
+    v[s][0] = a.x; v[s][1] = a.y; v[s][2] = a.z; v[s][3] = a.w;
+    v[s][4] = b.x; v[s][5] = b.y; v[s][6] = b.z; v[s][7] = b.w;
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int s = 0; s < STEPS; ++s) {
+    const int c = s * 256 + lane * 8;
+    if (c < k) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[s][i] = scaled_input(v[s][i], inverse, c + i);
+        amax = fmaxf(amax, fabsf(v[s][i]));
+      }
+    }
+  }
+  amax = warp_max(amax);
+  const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+  const float inv_scale = __fdiv_rn(1.0f, scale);
+  if (lane == 0) scales[row] = scale;
+  int8_t *cr = codes + static_cast<size_t>(row) * k;
+#pragma unroll
+  for (int s = 0; s < STEPS; ++s) {
+    const int c = s * 256 + lane * 8;
+    if (c < k) {
+      int q[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[i] = quant_code(v[s][i], inv_scale);
+      *reinterpret_cast<uint2 *>(cr + c) =
+          make_uint2(pack4(q[0], q[1], q[2], q[3]), pack4(q[4], q[5], q[6], q[7]));
+    }
+  }
+}
+
+template <int STEPS>
+static void launch_reg(int8_t *codes, float *scales, const float *x, const float *inverse, int m,
+                       int k, cudaStream_t st) {
+  quantize_rows_reg_kernel<STEPS><<<(m + 7) / 8, 256, 0, st>>>(codes, scales, x, inverse, m, k);
+}
+
 cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
                                  const float *inverse, int m, int k, cudaStream_t st) {
-  // Long rows or few rows: a 256-thread block per row; otherwise a warp per row.
-  if (k >= 4096 || m < 1184) {
+  // Many rows of at most 2048 elements: a register-resident warp per row.
+  // Long rows or few rows: a 256-thread block per row (two passes, the
+  // second from L1/L2).
+  if (k <= 2048 && m >= 1184) {
+    switch ((k + 255) / 256) {
+      case 1: launch_reg<1>(codes, scales, x, inverse, m, k, st); break;
+      case 2: launch_reg<2>(codes, scales, x, inverse, m, k, st); break;
+      case 3: launch_reg<3>(codes, scales, x, inverse, m, k, st); break;
+      case 4: launch_reg<4>(codes, scales, x, inverse, m, k, st); break;
+      case 5: launch_reg<5>(codes, scales, x, inverse, m, k, st); break;
+      case 6: launch_reg<6>(codes, scales, x, inverse, m, k, st); break;
+      case 7: launch_reg<7>(codes, scales, x, inverse, m, k, st); break;
+      default: launch_reg<8>(codes, scales, x, inverse, m, k, st); break;
+    }
+  } else if (k >= 4096 || m < 1184) {
     quantize_rows_kernel<256, 1><<<m, 256, 0, st>>>(codes, scales, x, inverse, m, k);
   } else {
     quantize_rows_kernel<32, 8><<<(m + 7) / 8, 256, 0, st>>>(codes, scales, x, inverse, m, k);
@@ -233,13 +307,14 @@ cudaError_t launch_repack_f16(uint16_t *dst, const uint16_t *perm, int k, int n0
 }
 
 // ====================================================================== GEMM
-// Optional epilogue activation (mat_mul.c:788-826): GELU(tanh) written as
-// x*sigmoid(1.5957691216057308*(x + 0.044715 x^3)), QuickGELU as
-// x*sigmoid(1.702 x); the sigmoid keeps the reference's stable form
-// e = 2^max(-|z| log2(e), -126), inv = 1/(1+e), sigma = z<0 ? e*inv : inv,
-// with CUDA's exp2f and the hardware reciprocal (e+1 lies in [1,2]).
-// MODE is a template parameter so the per-element code is branch-free and the
-// 32 elements of a TMEM chunk interleave.
+// Optional epilogue activation (mat_mul.c:788-826): GELU(tanh) as
+// x*sigmoid(z), z = 1.5957691216057308*(x + 0.044715 x^3), QuickGELU as
+// x*sigmoid(1.702 x).  The sigmoid is evaluated as 1/(1 + 2^(-z log2 e)) with
+// the hardware 2^x and reciprocal (each within 2 ulp).  Neither step cancels,
+// so this matches the reference's sign-split form e = 2^-|z|, e*inv or inv
+// to a few ulp for every z: large -z overflows 2^x to +inf and 1/inf = 0,
+// large +z gives 1/(1+0) = 1.  MODE is a template parameter so the
+// per-element code is branch-free and the 32 elements of a chunk interleave.
 template <int MODE>
 __device__ __forceinline__ float epilogue_act(float x) {
   if constexpr (MODE != 1 && MODE != 2) {
@@ -247,16 +322,13 @@ __device__ __forceinline__ float epilogue_act(float x) {
   } else {
     float z;
     if constexpr (MODE == 1) {
-      const float cubic = __fmul_rn(__fmul_rn(x, x), x);
-      z = __fmul_rn(__fadd_rn(x, __fmul_rn(cubic, 0.044715f)), 1.5957691216057308f);
+      constexpr float c1 = 1.5957691216057308f, c3 = 1.5957691216057308f * 0.044715f;
+      z = x * fmaf(x * x, c3, c1);
     } else {
-      z = __fmul_rn(x, 1.702f);
+      z = x * 1.702f;
     }
-    const float arg = fmaxf(__fmul_rn(fabsf(z), -1.4426950408889634f), -126.0f);
-    const float e = exp2f(arg);
-    const float inv = __fdividef(1.0f, __fadd_rn(e, 1.0f));
-    const float sig = z < 0.0f ? __fmul_rn(e, inv) : inv;
-    return __fmul_rn(x, sig);
+    const float e = ex2_approx(z * -1.4426950408889634f);
+    return x * rcp_approx(1.0f + e);
   }
 }
 
@@ -279,18 +351,26 @@ __device__ __forceinline__ float finish(uint32_t acc, int32_t corr, float sw, fl
   return epilogue_act<MODE>(v);
 }
 
-constexpr int kEpiWarps = 8;                       // two per TMEM lane quadrant
+// Sixteen epilogue warps: four per TMEM lane quadrant, so each SM sub-partition
+// interleaves four independent chunk pipelines (the epilogue is latency-bound).
+constexpr int kEpiWarps = 16;
+constexpr int kEpiPerQuadrant = kEpiWarps / 4;
 constexpr int kEpiThreads = 32 * kEpiWarps;
-constexpr int kThreads = 64 + kEpiThreads;         // warp 0 TMA, warp 1 MMA/TMEM, 2..9 epilogue
+constexpr int kThreads = 64 + kEpiThreads;         // warp 0 TMA, warp 1 MMA/TMEM, 2..17 epilogue
 constexpr int kRowBytes = 128;                     // one K block = one 128-byte swizzle row
-constexpr int kTransposeStride = 33;
-constexpr int kWarpScratch = 32 * kTransposeStride;  // floats per epilogue warp
+// Per epilogue warp: a 32 x 32 FP32 output tile staged with 128-byte swizzle
+// (row r at r*128 bytes, 16-byte chunk j at position j ^ (r & 7)), the source
+// layout of the TMA store and conflict-free for row- and column-wise access;
+// plus 96 floats of per-column parameters of the chunk being finished.
+constexpr int kWarpScratch = 32 * 32;              // floats per epilogue warp (4 KiB)
+constexpr int kWarpParams = 96;                    // floats per epilogue warp
+constexpr int kEpiSmem = kEpiWarps * (kWarpScratch + kWarpParams) * 4;
 
 constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block on sm_100
 // As many pipeline stages as fit beside the epilogue scratch (at most 10).
 __host__ __device__ constexpr int stages_for(int bn) {
-  return (kSmemLimit - 1024 - 256 - kEpiWarps * kWarpScratch * 4) / ((128 + bn) * kRowBytes) < 10
-             ? (kSmemLimit - 1024 - 256 - kEpiWarps * kWarpScratch * 4) / ((128 + bn) * kRowBytes)
+  return (kSmemLimit - 1024 - 256 - kEpiSmem) / ((128 + bn) * kRowBytes) < 10
+             ? (kSmemLimit - 1024 - 256 - kEpiSmem) / ((128 + bn) * kRowBytes)
              : 10;
 }
 __host__ __device__ constexpr int tmem_cols_for(int bn) {
@@ -298,7 +378,7 @@ __host__ __device__ constexpr int tmem_cols_for(int bn) {
 }
 __host__ __device__ constexpr size_t smem_bytes_for(int bn) {
   return 1024 /* alignment slack */ + static_cast<size_t>(stages_for(bn)) * (128 + bn) * kRowBytes +
-         static_cast<size_t>(kEpiWarps) * kWarpScratch * 4u + 256 /* barriers, tmem slot, flags */;
+         static_cast<size_t>(kEpiSmem) + 256 /* barriers, tmem slot, flags */;
 }
 static_assert(smem_bytes_for(256) <= kSmemLimit && smem_bytes_for(128) <= kSmemLimit &&
                   smem_bytes_for(64) <= kSmemLimit && smem_bytes_for(32) <= kSmemLimit &&
@@ -308,7 +388,8 @@ static_assert(smem_bytes_for(256) <= kSmemLimit && smem_bytes_for(128) <= kSmemL
 struct SmemLayout {
   uint8_t *a;          // STAGES x 128 rows x 128 B
   uint8_t *b;          // STAGES x BN rows x 128 B
-  float *scratch;      // per epilogue warp: column parameters, then the 32x33 transpose
+  float *scratch;      // per epilogue warp: the 32 x 32 staging tile (1024-byte aligned)
+  float *params;       // per epilogue warp: 96 floats of column parameters
   uint64_t *full, *empty, *tfull, *tempty, *mma_done;
   uint32_t *tmem_slot;
   uint32_t *flag;            // split-K "this CTA finishes the tile"
@@ -325,6 +406,8 @@ __device__ __forceinline__ SmemLayout carve(uint8_t *raw) {
   p += STAGES * BN * kRowBytes;
   L.scratch = reinterpret_cast<float *>(p);
   p += kEpiWarps * kWarpScratch * 4;
+  L.params = reinterpret_cast<float *>(p);
+  p += kEpiWarps * kWarpParams * 4;
   uint64_t *bars = reinterpret_cast<uint64_t *>(p);
   L.full = bars;
   L.empty = bars + STAGES;
@@ -358,36 +441,62 @@ struct KernelParams {
 struct EpiCtx {
   const GemmArgs *g;
   const KernelParams *P;
+  const CUtensorMap *tmOut;
   SmemLayout L;
-  float *scr;        // this warp's scratch
+  float *scr;        // this warp's staging tile
+  float *prm;        // this warp's column-parameter slots
   uint32_t t_row;    // TMEM address of lane quadrant q, accumulator buffer
+  uint32_t full_bar, full_parity;  // accumulator-full barrier of this unit
   Unit w;
-  int q, half, lane, epi_t;
-  bool ok;           // the accumulator-full wait succeeded
+  int row0;                        // first output row held by this CTA's TMEM lanes
+  int q, part, lane, epi_t;        // part: which of the quadrant's four warps
 };
 
 // Normal orientation: TMEM lane = activation row m, column = weight column n.
-// Each warp takes every other 32-column chunk of its lane quadrant.
+// The four warps of a lane quadrant take every fourth 32-column chunk.  The row
+// scale and the per-column parameters are loaded before the accumulator wait,
+// so their latency hides behind the MMAs.  Returns whether the wait succeeded.
 template <Kind KIND, int BN, int MODE, bool BIAS>
-__device__ __forceinline__ void epilogue_normal(const EpiCtx &c) {
+__device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
+  constexpr int kChunks = BN / 32;
+  constexpr int kMine = (kChunks + kEpiPerQuadrant - 1) / kEpiPerQuadrant;
   const GemmArgs &g = *c.g;
-  const int m = c.w.ta * 128 + c.q * 32 + c.lane;
+  const int m = c.row0 + c.q * 32 + c.lane;
   const bool m_ok = m < g.M;
   const float rs = (KIND == Kind::I8 && m_ok) ? __ldg(g.row_scale + m) : 0.0f;
+  float psw[kMine], pb[kMine];
+  int pcr[kMine];
+#pragma unroll
+  for (int i = 0; i < kMine; ++i) {
+    const int nl = c.w.tb * BN + (c.part + kEpiPerQuadrant * i) * 32 + c.lane;
+    const bool ok = c.part + kEpiPerQuadrant * i < kChunks && nl < g.N;
+    psw[i] = (KIND == Kind::I8 && ok) ? __ldg(g.col_scale + nl) : 0.0f;
+    pcr[i] = (KIND == Kind::I8 && ok) ? __ldg(g.col_corr + nl) : 0;
+    pb[i] = (BIAS && ok) ? __ldg(g.bias + nl) : 0.0f;
+  }
+  const bool ok = mbar_wait(c.full_bar, c.full_parity, g.watchdog, kWatchEpilogue, c.L.abort);
+  tc_fence_after();
+  if (!ok) return false;
   float *scr = c.scr;
-#pragma unroll 1
-  for (int ch = c.half; ch < BN / 32; ch += 2) {
+  float *prm = c.prm;
+  const bool tma = MODE != 3 && g.tma_store;
+  const int mbase = c.row0 + c.q * 32;
+#pragma unroll
+  for (int i = 0; i < kMine; ++i) {
+    const int ch = c.part + kEpiPerQuadrant * i;
+    if (ch >= kChunks) break;
     uint32_t r[32];
     tmem_ld32(c.t_row + ch * 32, r);
     const int n0 = c.w.tb * BN + ch * 32;
     const int nl = n0 + c.lane;
     const bool nl_ok = nl < g.N;
-    // per-column parameters of this chunk -> scratch[0..95], read back as broadcasts
+    // per-column parameters of this chunk -> prm[0..95], read back as broadcasts
+    __syncwarp();
     if (KIND == Kind::I8) {
-      scr[c.lane] = nl_ok ? __ldg(g.col_scale + nl) : 0.0f;
-      scr[32 + c.lane] = __int_as_float(nl_ok ? __ldg(g.col_corr + nl) : 0);
+      prm[c.lane] = psw[i];
+      prm[32 + c.lane] = __int_as_float(pcr[i]);
     }
-    if (BIAS) scr[64 + c.lane] = nl_ok ? __ldg(g.bias + nl) : 0.0f;
+    if (BIAS) prm[64 + c.lane] = pb[i];
     tmem_ld_wait();
     __syncwarp();
     float v[32];
@@ -395,10 +504,10 @@ __device__ __forceinline__ void epilogue_normal(const EpiCtx &c) {
     for (int j = 0; j < 32; j += 4) {
       float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f), c4 = s4, b4 = s4;
       if (KIND == Kind::I8) {
-        s4 = *reinterpret_cast<const float4 *>(scr + j);
-        c4 = *reinterpret_cast<const float4 *>(scr + 32 + j);
+        s4 = *reinterpret_cast<const float4 *>(prm + j);
+        c4 = *reinterpret_cast<const float4 *>(prm + 32 + j);
       }
-      if (BIAS) b4 = *reinterpret_cast<const float4 *>(scr + 64 + j);
+      if (BIAS) b4 = *reinterpret_cast<const float4 *>(prm + 64 + j);
       v[j + 0] = finish<KIND, MODE, BIAS>(r[j + 0], __float_as_int(c4.x), s4.x, rs, b4.x);
       v[j + 1] = finish<KIND, MODE, BIAS>(r[j + 1], __float_as_int(c4.y), s4.y, rs, b4.y);
       v[j + 2] = finish<KIND, MODE, BIAS>(r[j + 2], __float_as_int(c4.z), s4.z, rs, b4.z);
@@ -413,37 +522,59 @@ __device__ __forceinline__ void epilogue_normal(const EpiCtx &c) {
         if (m_ok && n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = v[j];
       }
     } else {
-      // row-major: transpose through shared memory so each store is one
-      // 128-byte row segment
-#pragma unroll
-      for (int j = 0; j < 32; ++j) scr[c.lane * kTransposeStride + j] = v[j];
-      __syncwarp();
-      const int mbase = c.w.ta * 128 + c.q * 32;
-#pragma unroll 8
-      for (int rr = 0; rr < 32; ++rr) {
-        const int mr = mbase + rr;
-        if (mr < g.M && nl_ok)
-          g.out[static_cast<long long>(mr) * g.ldo + nl] = scr[rr * kTransposeStride + c.lane];
+      // row-major: stage the 32 x 32 tile (128-byte swizzle), then one TMA
+      // store, or (unaligned output) coalesced 128-byte row stores.  The
+      // previous chunk's TMA store must be done reading the staging tile.
+      if (tma) {
+        if (c.lane == 0) bulk_wait_read_all();
+        __syncwarp();
       }
-      __syncwarp();
+      char *row = reinterpret_cast<char *>(scr) + c.lane * 128;
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4)
+        *reinterpret_cast<float4 *>(row + ((j4 ^ (c.lane & 7)) << 4)) =
+            make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+      if (tma) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (c.lane == 0) {
+          tma_store_2d(c.tmOut, smem_u32(scr), n0, mbase);
+          bulk_commit();
+        }
+      } else {
+        __syncwarp();
+        const char *base = reinterpret_cast<const char *>(scr);
+        const int cpos = c.lane >> 2, cofs = (c.lane & 3) * 4;
+#pragma unroll 8
+        for (int rr = 0; rr < 32; ++rr) {
+          const int mr = mbase + rr;
+          const float val =
+              *reinterpret_cast<const float *>(base + rr * 128 + ((cpos ^ (rr & 7)) << 4) + cofs);
+          if (mr < g.M && nl_ok) g.out[static_cast<long long>(mr) * g.ldo + nl] = val;
+        }
+        __syncwarp();
+      }
     }
   }
+  return true;
 }
 
 // Swapped orientation (small M): TMEM lane = weight column n, column = activation
-// row m (BN <= 32).  The first four warps hold the data; all eight take part in
-// the split-K barriers.
+// row m (BN <= 32).  One warp per lane quadrant holds the data; all epilogue
+// warps take part in the split-K barriers.  Returns whether the wait succeeded.
 template <Kind KIND, int BN, int MODE, bool BIAS>
-__device__ __forceinline__ void epilogue_swap(const EpiCtx &c) {
+__device__ __forceinline__ bool epilogue_swap(const EpiCtx &c) {
   const GemmArgs &g = *c.g;
   const KernelParams &P = *c.P;
-  const bool owner = c.half == 0;
+  const bool owner = c.part == 0;
   const int n = c.w.ta * 128 + c.q * 32 + c.lane;
   const bool n_ok = n < g.N;
+  const bool c_ok = mbar_wait(c.full_bar, c.full_parity, g.watchdog, kWatchEpilogue, c.L.abort);
+  tc_fence_after();
   uint32_t r[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) r[j] = 0u;
-  if (c.ok && owner) {
+  if (c_ok && owner) {
     if (BN == 16) {
       uint32_t r16[16];
       tmem_ld16(c.t_row, r16);
@@ -455,13 +586,13 @@ __device__ __forceinline__ void epilogue_swap(const EpiCtx &c) {
       tmem_ld_wait();
     }
   }
-  bool fin = c.ok;
+  bool fin = c_ok;
   if (P.splits > 1) {
     // exact INT32 split-K: partials meet in HBM; the last CTA of the tile
     // finishes it and leaves the accumulators and counter zeroed
     const int tile = c.w.ta * P.tiles_b + c.w.tb;
     int32_t *ws = g.ws + (static_cast<size_t>(tile) * 128 + c.q * 32 + c.lane) * BN;
-    if (c.ok && owner) {
+    if (c_ok && owner) {
 #pragma unroll
       for (int j = 0; j < BN; ++j) atomicAdd(ws + j, static_cast<int32_t>(r[j]));
       __threadfence();
@@ -476,7 +607,7 @@ __device__ __forceinline__ void epilogue_swap(const EpiCtx &c) {
       *c.L.flag = last;
     }
     named_bar_sync(1, kEpiThreads);
-    fin = c.ok && *c.L.flag != 0u;
+    fin = c_ok && *c.L.flag != 0u;
     if (fin && owner) {
       __threadfence();
 #pragma unroll
@@ -488,12 +619,12 @@ __device__ __forceinline__ void epilogue_swap(const EpiCtx &c) {
     }
     named_bar_sync(1, kEpiThreads);
   }
-  if (!fin || !owner) return;
+  if (!fin || !owner) return c_ok;
   float *scr = c.scr;
   const int mrow = c.w.tb * BN + c.lane;
   scr[c.lane] = (KIND == Kind::I8 && mrow < g.M) ? __ldg(g.row_scale + mrow) : 0.0f;
   __syncwarp();
-  if (!n_ok) return;
+  if (!n_ok) return c_ok;
   float sw = 0.0f, bn_ = 0.0f;
   int32_t cr = 0;
   if (KIND == Kind::I8) {
@@ -512,36 +643,36 @@ __device__ __forceinline__ void epilogue_swap(const EpiCtx &c) {
       g.out[static_cast<long long>(m) * g.ldo + n] = v;
     }
   }
+  return c_ok;
 }
 
 template <Kind KIND, int BN, bool SWAP, int MODE, bool BIAS>
-__device__ __forceinline__ void epilogue_unit(const EpiCtx &c) {
-  if constexpr (SWAP) {
-    epilogue_swap<KIND, BN, MODE, BIAS>(c);
-  } else {
-    if (c.ok) epilogue_normal<KIND, BN, MODE, BIAS>(c);
-  }
+__device__ __forceinline__ bool epilogue_unit(const EpiCtx &c) {
+  if constexpr (SWAP)
+    return epilogue_swap<KIND, BN, MODE, BIAS>(c);
+  else
+    return epilogue_normal<KIND, BN, MODE, BIAS>(c);
 }
 
 template <Kind KIND, int BN, bool SWAP>
-__device__ __forceinline__ void epilogue_dispatch(const EpiCtx &c, int mode, bool bias) {
+__device__ __forceinline__ bool epilogue_dispatch(const EpiCtx &c, int mode, bool bias) {
   switch (mode * 2 + (bias ? 1 : 0)) {
-    case 0: epilogue_unit<KIND, BN, SWAP, 0, false>(c); break;
-    case 1: epilogue_unit<KIND, BN, SWAP, 0, true>(c); break;
-    case 2: epilogue_unit<KIND, BN, SWAP, 1, false>(c); break;
-    case 3: epilogue_unit<KIND, BN, SWAP, 1, true>(c); break;
-    case 4: epilogue_unit<KIND, BN, SWAP, 2, false>(c); break;
-    case 5: epilogue_unit<KIND, BN, SWAP, 2, true>(c); break;
-    case 6: epilogue_unit<KIND, BN, SWAP, 3, false>(c); break;
-    case 7: epilogue_unit<KIND, BN, SWAP, 3, true>(c); break;
-    default: epilogue_unit<KIND, BN, SWAP, 4, false>(c); break;
+    case 0: return epilogue_unit<KIND, BN, SWAP, 0, false>(c);
+    case 1: return epilogue_unit<KIND, BN, SWAP, 0, true>(c);
+    case 2: return epilogue_unit<KIND, BN, SWAP, 1, false>(c);
+    case 3: return epilogue_unit<KIND, BN, SWAP, 1, true>(c);
+    case 4: return epilogue_unit<KIND, BN, SWAP, 2, false>(c);
+    case 5: return epilogue_unit<KIND, BN, SWAP, 2, true>(c);
+    case 6: return epilogue_unit<KIND, BN, SWAP, 3, false>(c);
+    case 7: return epilogue_unit<KIND, BN, SWAP, 3, true>(c);
+    default: return epilogue_unit<KIND, BN, SWAP, 4, false>(c);
   }
 }
 
 template <Kind KIND, int BN, bool SWAP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const KernelParams P) {
+                const __grid_constant__ CUtensorMap tmOut, const KernelParams P) {
   constexpr int STAGES = stages_for(BN);
   constexpr int TCOLS = tmem_cols_for(BN);
   constexpr uint32_t kStageBytes = (128 + BN) * kRowBytes;
@@ -667,12 +798,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     EpiCtx c;
     c.g = &g;
     c.P = &P;
+    c.tmOut = &tmOut;
     c.L = L;
     c.q = warp & 3;                            // TMEM lane quadrant of this warp
-    c.half = (warp - 2) / 4;                   // which of the two warps of the quadrant
+    c.part = (warp - 2) / 4;                   // which of the quadrant's four warps
     c.lane = lane;
     c.epi_t = threadIdx.x - 64;
     c.scr = L.scratch + (warp - 2) * kWarpScratch;
+    c.prm = L.params + (warp - 2) * kWarpParams;
     const bool has_bias = g.bias != nullptr;
     uint32_t iter = 0;
     // No early exit: all epilogue warps run the same iterations so their
@@ -682,15 +815,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       c.w = decode_unit(u, P.tiles_b, P.splits);
       const uint32_t buf = iter & 1u;
       const uint32_t acc_ph = (iter >> 1) & 1u;
-      c.ok = mbar_wait(smem_u32(&L.tfull[buf]), acc_ph, wd, kWatchEpilogue, L.abort);
-      tc_fence_after();
+      c.full_bar = smem_u32(&L.tfull[buf]);
+      c.full_parity = acc_ph;
+      c.row0 = c.w.ta * 128;
       c.t_row = tmem_base + (static_cast<uint32_t>(c.q * 32) << 16) + buf * BN;
-      epilogue_dispatch<KIND, BN, SWAP>(c, g.mode, has_bias);
+      const bool ok = epilogue_dispatch<KIND, BN, SWAP>(c, g.mode, has_bias);
       // this warp's TMEM reads of the buffer are complete (tcgen05.wait::ld)
       tc_fence_before();
       __syncwarp();
-      if (lane == 0 && c.ok) mbar_arrive(smem_u32(&L.tempty[buf]));
+      if (lane == 0 && ok) mbar_arrive(smem_u32(&L.tempty[buf]));
     }
+    if (lane == 0) bulk_wait_all();  // output stores of this warp have landed
   }
 
   tc_fence_before();
@@ -701,21 +836,239 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ================================================================ 2-SM GEMM
+// A CTA pair (cluster of two) computes one 256 x BN tile with
+// tcgen05.mma.cta_group::2.  CTA r loads A rows [ta*256 + r*128, +128) and B
+// rows [tb*BN + r*BN/2, +BN/2) into its own shared memory (no multicast); the
+// leader (rank 0) issues the MMAs, which read both CTAs' halves; CTA r's TMEM
+// receives output rows ta*256 + r*128 .. +127 (all BN columns) and its own
+// epilogue warps finish them.  Per SM this moves 16 KB instead of 24 KB of
+// operands through shared memory per 128 x 256 x 32 MMA step, which is what
+// lets the tensor pipe run past the shared-memory bandwidth ceiling of the
+// single-CTA tile.
+__host__ __device__ constexpr int stages2_for(int bn) {
+  return (kSmemLimit - 1024 - 256 - kEpiSmem) / ((128 + bn / 2) * kRowBytes) < 10
+             ? (kSmemLimit - 1024 - 256 - kEpiSmem) / ((128 + bn / 2) * kRowBytes)
+             : 10;
+}
+__host__ __device__ constexpr size_t smem2_bytes_for(int bn) {
+  return 1024 + static_cast<size_t>(stages2_for(bn)) * (128 + bn / 2) * kRowBytes +
+         static_cast<size_t>(kEpiSmem) + 256;
+}
+static_assert(smem2_bytes_for(256) <= kSmemLimit && smem2_bytes_for(128) <= kSmemLimit,
+              "shared memory budget (pair)");
+
+template <Kind KIND, int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmOut, const KernelParams P) {
+  constexpr int BH = BN / 2;  // B rows held by each CTA
+  constexpr int STAGES = stages2_for(BN);
+  constexpr int TCOLS = tmem_cols_for(BN);
+  constexpr uint32_t kStageBytes = (128 + BH) * kRowBytes;  // per CTA
+  constexpr int kElemsPerRow = KIND == Kind::I8 ? 128 : 64;
+  constexpr uint32_t kIdesc = KIND == Kind::I8 ? idesc_i8(256, BN) : idesc_f16(256, BN);
+  static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+
+  extern __shared__ uint8_t smem_raw[];
+  const SmemLayout L = carve<BH, STAGES>(smem_raw);
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const GemmArgs &g = P.a;
+  uint32_t *wd = g.watchdog;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const uint32_t peer_abort = mapa_shared(smem_u32(const_cast<uint32_t *>(L.abort)), rank ^ 1u);
+  // a failed wait also tells the peer CTA, whose waits then return at once
+  auto wait = [&](uint32_t bar, uint32_t parity, uint32_t bit) {
+    const bool ok = mbar_wait(bar, parity, wd, bit, L.abort);
+    if (!ok) st_shared_cluster(peer_abort, 1u);
+    return ok;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&L.full[s]), 1);
+      mbar_init(smem_u32(&L.empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&L.tfull[b]), 1);
+      mbar_init(smem_u32(&L.tempty[b]), 2 * kEpiWarps);  // epilogue warps of both CTAs
+    }
+    mbar_init(smem_u32(L.mma_done), 1);
+    *L.abort = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(L.tmem_slot), TCOLS);
+    tmem_relinquish_pair();
+  }
+  // both CTAs' barriers exist before either CTA signals the other
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *L.tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int s = 0;
+      uint32_t ph = 0;
+      int last_phase[STAGES];
+#pragma unroll
+      for (int i = 0; i < STAGES; ++i) last_phase[i] = -1;
+      bool ok = true;
+      for (int u = pair; ok && u < P.units; u += npairs) {
+        const Unit w = decode_unit(u, P.tiles_b, 1);
+        for (int kb = 0; kb < P.kb_total; ++kb) {
+          if (!wait(smem_u32(&L.empty[s]), ph ^ 1u, kWatchProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb_local = smem_u32(&L.full[s]);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);
+          const uint32_t fb = mapa_shared(fb_local, 0);
+          tma_load_2d_pair(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, kb * kElemsPerRow,
+                           w.ta * 256 + static_cast<int>(rank) * 128);
+          tma_load_2d_pair(smem_u32(L.b + s * BH * kRowBytes), &tmB, fb, kb * kElemsPerRow,
+                           w.tb * BN + static_cast<int>(rank) * BH);
+          last_phase[s] = static_cast<int>(ph);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // the leader's full barriers count both CTAs' bytes: once they have
+      // completed, no copy is still landing in either CTA
+      if (leader)
+        for (int i = 0; i < STAGES; ++i)
+          if (last_phase[i] >= 0)
+            wait(smem_u32(&L.full[i]), static_cast<uint32_t>(last_phase[i]), kWatchProducer);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (lane == 0 && leader) {
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t iter = 0;
+      bool ok = true;
+      for (int u = pair; ok && u < P.units; u += npairs, ++iter) {
+        const uint32_t buf = iter & 1u;
+        const uint32_t acc_ph = (iter >> 1) & 1u;
+        if (!wait(smem_u32(&L.tempty[buf]), acc_ph ^ 1u, kWatchMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < P.kb_total; ++kb) {
+          if (!wait(smem_u32(&L.full[s]), ph, kWatchMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(L.a + s * 128 * kRowBytes);
+          const uint32_t b_addr = smem_u32(L.b + s * BH * kRowBytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t da = umma_desc_sw128(a_addr + kk * 32);
+            const uint64_t db = umma_desc_sw128(b_addr + kk * 32);
+            const uint32_t accumulate = (kb > 0 || kk > 0) ? 1u : 0u;
+            if (KIND == Kind::I8)
+              umma_i8_pair(d_tmem, da, db, kIdesc, accumulate);
+            else
+              umma_f16_pair(d_tmem, da, db, kIdesc, accumulate);
+          }
+          tc_commit_pair_mc(smem_u32(&L.empty[s]), 0x3);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (ok) tc_commit_pair_mc(smem_u32(&L.tfull[buf]), 0x3);
+      }
+      tc_commit_pair(smem_u32(L.mma_done));
+      wait(smem_u32(L.mma_done), 0, kWatchMma);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    EpiCtx c;
+    c.g = &g;
+    c.P = &P;
+    c.tmOut = &tmOut;
+    c.L = L;
+    c.q = warp & 3;
+    c.part = (warp - 2) / 4;
+    c.lane = lane;
+    c.epi_t = threadIdx.x - 64;
+    c.scr = L.scratch + (warp - 2) * kWarpScratch;
+    c.prm = L.params + (warp - 2) * kWarpParams;
+    const bool has_bias = g.bias != nullptr;
+    uint32_t iter = 0;
+    for (int u = pair; u < P.units; u += npairs, ++iter) {
+      c.w = decode_unit(u, P.tiles_b, 1);
+      const uint32_t buf = iter & 1u;
+      c.full_bar = smem_u32(&L.tfull[buf]);
+      c.full_parity = (iter >> 1) & 1u;
+      c.row0 = c.w.ta * 256 + static_cast<int>(rank) * 128;
+      c.t_row = tmem_base + (static_cast<uint32_t>(c.q * 32) << 16) + buf * BN;
+      const bool ok = epilogue_dispatch<KIND, BN, false>(c, g.mode, has_bias);
+      if (!ok) st_shared_cluster(peer_abort, 1u);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive_cluster(mapa_shared(smem_u32(&L.tempty[buf]), 0));
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+
+  // the leader's MMAs (which read both CTAs' shared memory) are complete and
+  // every TMEM read is done before either CTA releases TMEM or exits
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TCOLS);
+  }
+}
+
 // --------------------------------------------------------------- planning
 // Tile plan keyed on M:
 //  * I8 and M <= 32: swapped orientation (weights fill the 128-row MMA
 //    dimension, the activation rows are the MMA N = 16 or 32); the K range is
 //    split over CTAs until the grid covers the SMs, with an exact INT32
 //    reduction.  These shapes stream the weight once and are HBM-bound.
+//  * large M: CTA-pair tiles of 256 rows x BN in {256, 128}, whichever needs
+//    fewer tile-rounds x BN over the SM pairs (wave quantisation), as long as
+//    the tiles fill at least half of the pairs.
 //  * otherwise: activation rows in 128-row tiles and the widest weight tile
-//    N in {256, 128, 64, 32} that still gives one CTA per SM; K stays whole
-//    inside a CTA (no split), so the FP16 accumulation order never depends on
-//    the plan.
+//    N in {256, 128, 64, 32} that still gives one CTA per SM.
+//  In the normal orientation K stays whole inside a CTA (no split), so the
+//  FP16 accumulation order never depends on the plan.
 GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms) {
   GemmPlan p;
   p.kind = kind;
   const int elems = kind == Kind::I8 ? 128 : 64;
   p.kb_total = (K + elems - 1) / elems;
+  const int pairs = num_sms / 2;
+  if (M > 128) {
+    const long long u256 = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+    const long long u128 = static_cast<long long>((M + 255) / 256) * ((N + 127) / 128);
+    if (u128 * 2 >= pairs) {
+      const long long cost256 = (u256 + pairs - 1) / pairs * 256;
+      const long long cost128 = (u128 + pairs - 1) / pairs * 128;
+      p.pair = true;
+      p.bn = cost256 <= cost128 ? 256 : 128;
+      p.tiles_a = (M + 255) / 256;
+      p.tiles_b = (N + p.bn - 1) / p.bn;
+      p.splits = 1;
+      p.kb_per_split = p.kb_total;
+      p.units = p.tiles_a * p.tiles_b;
+      p.grid = 2 * (p.units < pairs ? p.units : pairs);
+      p.smem = smem2_bytes_for(p.bn);
+      return p;
+    }
+  }
   if (kind == Kind::I8 && M <= 32) {
     p.swap = true;
     p.bn = M <= 16 ? 16 : 32;
@@ -758,15 +1111,18 @@ size_t splitk_count_bytes(const GemmPlan &p) {
 
 template <Kind KIND, int BN, bool SWAP>
 static cudaError_t launch_one(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
-                              const GemmArgs &a, cudaStream_t st) {
+                              const CUtensorMap &tmOut, const GemmArgs &a, cudaStream_t st) {
   auto fn = gemm_kernel<KIND, BN, SWAP>;
-  static bool configured = false;  // per instantiation; first call happens before any capture
+  static bool configured[64] = {};  // per instantiation and device
+  int dev = 0;
+  cudaGetDevice(&dev);
   const size_t smem = smem_bytes_for(BN);
-  if (!configured) {
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured[dev] = true;
   }
   KernelParams P;
   P.a = a;
@@ -776,31 +1132,69 @@ static cudaError_t launch_one(const GemmPlan &p, const CUtensorMap &tmA, const C
   P.kb_total = p.kb_total;
   P.kb_per_split = p.kb_per_split;
   P.units = p.units;
-  fn<<<p.grid, kThreads, smem, st>>>(tmA, tmB, P);
+  fn<<<p.grid, kThreads, smem, st>>>(tmA, tmB, tmOut, P);
+  return counted(cudaGetLastError());
+}
+
+template <Kind KIND, int BN>
+static cudaError_t launch_pair(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
+                               const CUtensorMap &tmOut, const GemmArgs &a, cudaStream_t st) {
+  auto fn = gemm2_kernel<KIND, BN>;
+  static bool configured[64] = {};  // per instantiation and device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = smem2_bytes_for(BN);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  KernelParams P;
+  P.a = a;
+  P.tiles_a = p.tiles_a;
+  P.tiles_b = p.tiles_b;
+  P.splits = 1;
+  P.kb_total = p.kb_total;
+  P.kb_per_split = p.kb_total;
+  P.units = p.units;
+  fn<<<p.grid, kThreads, smem, st>>>(tmA, tmB, tmOut, P);  // grid is a multiple of the pair
   return counted(cudaGetLastError());
 }
 
 cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
-                        const GemmArgs &a, cudaStream_t st) {
+                        const CUtensorMap &tmOut, const GemmArgs &a, cudaStream_t st) {
+  if (p.pair) {
+    if (p.grid % 2) return cudaErrorInvalidConfiguration;
+    if (p.kind == Kind::I8) {
+      if (p.bn == 256) return launch_pair<Kind::I8, 256>(p, tmA, tmB, tmOut, a, st);
+      if (p.bn == 128) return launch_pair<Kind::I8, 128>(p, tmA, tmB, tmOut, a, st);
+    } else {
+      if (p.bn == 256) return launch_pair<Kind::F16, 256>(p, tmA, tmB, tmOut, a, st);
+      if (p.bn == 128) return launch_pair<Kind::F16, 128>(p, tmA, tmB, tmOut, a, st);
+    }
+    return cudaErrorInvalidConfiguration;
+  }
   if (p.kind == Kind::I8) {
     if (p.swap) {
-      if (p.bn == 16) return launch_one<Kind::I8, 16, true>(p, tmA, tmB, a, st);
-      if (p.bn == 32) return launch_one<Kind::I8, 32, true>(p, tmA, tmB, a, st);
+      if (p.bn == 16) return launch_one<Kind::I8, 16, true>(p, tmA, tmB, tmOut, a, st);
+      if (p.bn == 32) return launch_one<Kind::I8, 32, true>(p, tmA, tmB, tmOut, a, st);
     } else {
       switch (p.bn) {
-        case 256: return launch_one<Kind::I8, 256, false>(p, tmA, tmB, a, st);
-        case 128: return launch_one<Kind::I8, 128, false>(p, tmA, tmB, a, st);
-        case 64: return launch_one<Kind::I8, 64, false>(p, tmA, tmB, a, st);
-        case 32: return launch_one<Kind::I8, 32, false>(p, tmA, tmB, a, st);
+        case 256: return launch_one<Kind::I8, 256, false>(p, tmA, tmB, tmOut, a, st);
+        case 128: return launch_one<Kind::I8, 128, false>(p, tmA, tmB, tmOut, a, st);
+        case 64: return launch_one<Kind::I8, 64, false>(p, tmA, tmB, tmOut, a, st);
+        case 32: return launch_one<Kind::I8, 32, false>(p, tmA, tmB, tmOut, a, st);
         default: break;
       }
     }
   } else if (!p.swap) {
     switch (p.bn) {
-      case 256: return launch_one<Kind::F16, 256, false>(p, tmA, tmB, a, st);
-      case 128: return launch_one<Kind::F16, 128, false>(p, tmA, tmB, a, st);
-      case 64: return launch_one<Kind::F16, 64, false>(p, tmA, tmB, a, st);
-      case 32: return launch_one<Kind::F16, 32, false>(p, tmA, tmB, a, st);
+      case 256: return launch_one<Kind::F16, 256, false>(p, tmA, tmB, tmOut, a, st);
+      case 128: return launch_one<Kind::F16, 128, false>(p, tmA, tmB, tmOut, a, st);
+      case 64: return launch_one<Kind::F16, 64, false>(p, tmA, tmB, tmOut, a, st);
+      case 32: return launch_one<Kind::F16, 32, false>(p, tmA, tmB, tmOut, a, st);
       default: break;
     }
   }

@@ -17,6 +17,7 @@ enum class Kind : int { I8 = 0, F16 = 1 };
 struct GemmPlan {
   Kind kind = Kind::I8;
   bool swap = false;
+  bool pair = false;     // CTA-pair tiles of 256 rows (tcgen05.mma.cta_group::2)
   int bn = 256;          // MMA N (rows of B per tile)
   int splits = 1;        // K splits (I8 swapped only; exact INT32 reduction)
   int tiles_a = 0, tiles_b = 0;
@@ -38,7 +39,15 @@ struct GemmArgs {
   int32_t *ws = nullptr;             // split-K accumulators
   uint32_t *ws_count = nullptr;      // split-K arrival counters (self-resetting)
   uint32_t *watchdog = nullptr;
+  int tma_store = 0;                 // row-major output written by TMA through tmOut
 };
+
+// Tensor map for TMA stores of a row-major FP32 output: `rows` x `cols`, row
+// pitch ldo floats, 32 x 32 boxes with 128-byte swizzle.  Usable when `out` is
+// 16-byte aligned and ldo is a multiple of 4.
+inline bool tma_store_ok(const float *out, long long ldo) {
+  return (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && ldo % 4 == 0;
+}
 
 // Plan for an M x N x K problem (see plan_gemm in kernels.cu for the rules).
 GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms);
@@ -46,11 +55,12 @@ GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms);
 size_t splitk_ws_bytes(const GemmPlan &p);
 size_t splitk_count_bytes(const GemmPlan &p);
 // Box rows of the A and B tensor maps for this plan.
+// (swapped plans use the weight as A and the activation as B)
 inline int box_rows_a(const GemmPlan &) { return 128; }
-inline int box_rows_b(const GemmPlan &p) { return p.bn; }
+inline int box_rows_b(const GemmPlan &p) { return p.pair ? p.bn / 2 : p.bn; }
 
 cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
-                        const GemmArgs &a, cudaStream_t st);
+                        const CUtensorMap &tmOut, const GemmArgs &a, cudaStream_t st);
 
 cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
                                  const float *inverse, int m, int k, cudaStream_t st);

@@ -13,7 +13,7 @@ import subprocess
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
-LIB_PATH = os.path.join(HERE, "libhtp_ops_b200.so")
+LIB_PATH = os.environ.get("HTPG_LIB") or os.path.join(HERE, "libhtp_ops_b200.so")
 INCLUDE = os.path.join(REPO, "include")
 
 # error codes (include/htp_ops_b200.h)

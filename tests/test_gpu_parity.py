@@ -33,7 +33,8 @@ def _quant_case(m, k, seed, kind="normal"):
 
 
 @pytest.mark.parametrize("m,k", [(1, 32), (3, 64), (77, 768), (256, 1152), (1000, 1536),
-                                 (2048, 1536), (16, 14336), (5, 4096), (9, 6144)])
+                                 (2048, 1536), (16, 14336), (5, 4096), (9, 6144), (4096, 768),
+                                 (1200, 2048), (1500, 160), (1300, 3072)])
 @pytest.mark.parametrize("inverse", [False, True])
 def test_quantize_rows_bitexact(gpu, lib, m, k, inverse):
     import torch
@@ -56,6 +57,8 @@ W8A8_SHAPES = [  # (m, k, n): swapped (m<=32) incl. split-K, and normal tiles wi
     (1, 128, 64), (4, 256, 128), (16, 512, 192), (32, 1152, 256), (33, 256, 192),
     (77, 768, 640), (128, 128, 128), (200, 1152, 640), (256, 1152, 4608), (300, 2048, 1024),
     (4, 14336, 4096), (16, 4096, 1024),
+    # CTA-pair (256-row) tiles: ragged M, BN = 128 and 256
+    (1000, 512, 1280), (2048, 768, 2304), (4100, 256, 4608),
 ]
 
 
@@ -102,7 +105,8 @@ def test_w8a8_output_bitexact_mode0(gpu, lib, m, k, n):
     np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("m,k,n", [(4, 256, 192), (77, 768, 640), (300, 512, 256), (16, 4096, 1024)])
+@pytest.mark.parametrize("m,k,n", [(4, 256, 192), (77, 768, 640), (300, 512, 256), (16, 4096, 1024),
+                                   (1100, 512, 1280)])
 @pytest.mark.parametrize("mode", [0, 1, 2, 3])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_w8a8_epilogue_modes(gpu, lib, m, k, n, mode, with_bias):
@@ -143,7 +147,7 @@ def _run_f16(lib, gpu, x, wperm, m, k, n, bias=None, channels=None, mode=0, raw=
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 32, 32), (77, 768, 3072), (128, 256, 96), (300, 1024, 512),
-                                   (512, 512, 1024)])
+                                   (512, 512, 1024), (1024, 512, 1536), (2000, 256, 2048)])
 def test_f16_accumulator_close_to_fp64(gpu, lib, m, k, n):
     x, w, wperm = _f16_case(m, k, n, 5 + m)
     got = _run_f16(lib, gpu, x, wperm, m, k, n, raw=True)
@@ -154,7 +158,7 @@ def test_f16_accumulator_close_to_fp64(gpu, lib, m, k, n):
     assert O.max_abs_rel(got, ref) <= 1e-5
 
 
-@pytest.mark.parametrize("m,k,n", [(77, 768, 3072), (5, 64, 96), (256, 512, 256)])
+@pytest.mark.parametrize("m,k,n", [(77, 768, 3072), (5, 64, 96), (256, 512, 256), (1030, 256, 1536)])
 @pytest.mark.parametrize("mode", [0, 1, 2, 3])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_f16_epilogue_modes(gpu, lib, m, k, n, mode, with_bias):
