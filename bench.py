@@ -294,13 +294,12 @@ def main():
     m, k, n = args.m, K_C4, N_C4
     workload = "C4" if m == M_C4 else f"C4-M{m}"
     assert n % (64 * world) == 0
-    n_loc = n // world
-    n0 = rank * n_loc
+    n0, n_loc = htpg.column_range(n, world, rank)
     x, blob_dev, bias, blob_host = make_c4_inputs(torch, dev, m, k, n)
     w = htpg.w8a8_weights(blob_dev, k, n, n0=n0, n_cols=n_loc)
     bias_loc = bias[n0:n0 + n_loc].contiguous()
     out_loc = torch.empty(m, n_loc, dtype=torch.float32, device=dev)
-    gathered = torch.empty(world, m, n_loc, dtype=torch.float32, device=dev) if world > 1 else None
+    gathered = torch.empty(world * m, n_loc, dtype=torch.float32, device=dev) if world > 1 else None
     full = torch.empty(m, n, dtype=torch.float32, device=dev) if world > 1 else None
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream()
@@ -311,7 +310,7 @@ def main():
                                    1, sp), "htpg_w8a8_run")
         if world > 1:
             dist.all_gather_into_tensor(gathered, out_loc)
-            full.view(m, world, n_loc).copy_(gathered.permute(1, 0, 2))
+            htpg.assemble_columns(full, gathered.view(world, m, n_loc))
 
     for _ in range(args.warmup):
         flush.zero_()

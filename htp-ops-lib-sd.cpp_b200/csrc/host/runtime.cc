@@ -22,6 +22,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <set>
 #include <thread>
 #include <tuple>
 #include <vector>
@@ -518,10 +519,15 @@ struct Backend {
 };
 
 std::mutex g_be_mu;
+std::mutex g_live_mu;
+std::set<Backend *> g_live;  // handles returned by htp_ops_open and not yet closed
 
+// Resolve a handle; stale or foreign handles give nullptr instead of a
+// dangling object.
 Backend *backend_of(remote_handle64 h) {
   Backend *b = reinterpret_cast<Backend *>(static_cast<uintptr_t>(h));
-  return (b && b->opened) ? b : nullptr;
+  std::lock_guard<std::mutex> lk(g_live_mu);
+  return (b && g_live.count(b) && b->opened) ? b : nullptr;
 }
 
 // The 8 state bytes sit at offset 0 of the channel buffer (8-byte aligned).
@@ -648,6 +654,10 @@ extern "C" AEEResult htp_ops_open(const char *uri, remote_handle64 *handle) {
     dev = 0;
   }
   b->device = dev;
+  {
+    std::lock_guard<std::mutex> lk(g_live_mu);
+    g_live.insert(b);
+  }
   *handle = static_cast<remote_handle64>(reinterpret_cast<uintptr_t>(b));
   return AEE_SUCCESS;
 }
@@ -656,6 +666,10 @@ extern "C" AEEResult htp_ops_close(remote_handle64 handle) {
   Backend *b = backend_of(handle);
   if (!b) return AEE_EBADSTATE;
   destroy_channel_internal(b);
+  {
+    std::lock_guard<std::mutex> lk(g_live_mu);
+    g_live.erase(b);
+  }
   b->opened = false;
   b->initialized = false;
   delete b;

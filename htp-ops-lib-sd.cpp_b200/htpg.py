@@ -269,3 +269,21 @@ def pack_f16_permuted(w_kn_bits):
     assert k % 32 == 0 and n % 32 == 0
     # k = t*32 + p*2 + b, n = s*32 + j  ->  [s][t][p][j][b]
     return w.reshape(k // 32, 16, 2, n // 32, 32).transpose(3, 0, 1, 4, 2).reshape(-1).copy()
+
+
+# ------------------------------------------------------------------ sharding
+# Column (N) tensor parallelism for the large linears: rank r owns output
+# columns [r*N/w, (r+1)*N/w) -- whole 64-column groups of the constants blob --
+# and the full row-major output is reassembled from the gathered shards.
+def column_range(n: int, world: int, rank: int, granule: int = 64) -> tuple[int, int]:
+    """(first column, columns) owned by `rank`; N must split into whole granules."""
+    if n % (granule * world):
+        raise ValueError(f"N={n} does not split into {world} shards of whole {granule}-column groups")
+    n_loc = n // world
+    return rank * n_loc, n_loc
+
+
+def assemble_columns(full, gathered) -> None:
+    """gathered: [world][M][N/world] shards (all-gather order) -> full: [M][N] row-major."""
+    world, m, n_loc = gathered.shape
+    full.view(m, world, n_loc).copy_(gathered.permute(1, 0, 2))

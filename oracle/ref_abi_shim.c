@@ -1,8 +1,9 @@
 /*
  * Shim compiled against the READ-ONLY reference headers (include/message.h,
- * include/op_reg.h, include/dsp/f16_gemm_plan.h) into oracle/_ref/.  It exposes
- * the reference's own struct sizes/offsets, message validator and FP16 planner
- * so tests can check this repository's wire ABI against the reference
+ * include/op_reg.h, include/dsp/f16_gemm_plan.h) into oracle/_ref/, and, with
+ * -DSHIM_NO_PLANNER, against this repository's include/ headers.  It exposes
+ * struct sizes/offsets and the message validator (and the reference's FP16
+ * planner) so tests can diff this repository's wire ABI against the reference
  * compiled here.  TEST INFRASTRUCTURE ONLY.
  */
 #include <stddef.h>
@@ -10,7 +11,9 @@
 
 #include "message.h"
 #include "op_reg.h"
+#ifndef SHIM_NO_PLANNER
 #include "dsp/f16_gemm_plan.h"
+#endif
 
 #define FIELD(s, f) offsetof(struct s, f)
 
@@ -88,6 +91,7 @@ int ref_validate_layout(const void *msg, size_t capacity, size_t *total) {
   return message_header_validate_layout((const struct MessageHeader *)msg, capacity, total);
 }
 
+#ifndef SHIM_NO_PLANNER
 int ref_f16_plan(int m, int k, int n, size_t vtcm, size_t reserved, size_t out[5]) {
   f16_gemm_plan_t p;
   if (!f16_gemm_make_plan(m, k, n, vtcm, reserved, &p)) return 0;
@@ -98,3 +102,4 @@ int ref_f16_plan(int m, int k, int n, size_t vtcm, size_t reserved, size_t out[5
   out[4] = p.output_bytes;
   return 1;
 }
+#endif

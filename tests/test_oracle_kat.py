@@ -1,0 +1,271 @@
+"""Known-answer tests that pin the CPU oracle to the reference.
+
+The reference has no golden FP32 outputs for this path; what it does pin are
+integer facts checked by its HMX probe against scalar integer arithmetic
+(tests/hmx-probe/integer_tests.c:79-134, study_data.h:1-21, study_dsp.c:70-86)
+and the tensor layouts its kernels and host demo address
+(linear_w8a8.c:117,281,453-487; src/host/test.c:548-556).  Each test below
+restates one of those checks for the oracle.  The FP32 steps are pinned by
+hand-computed cases of the reference formulas (linear_w8a8.c:34-59,
+mat_mul.c:788-826).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+
+
+# ------------------------------------------------------------------ layouts
+def test_deep_layout_matches_probe_recipe():
+    # study_dsp.c:79-84: tile (t*banks + h)*1024, inside (k/4)*128 + n*4 + k%4,
+    # banks = 2 for the N64 groups; groups of 64 columns are n0*K apart
+    # (linear_w8a8.c:453).
+    K = 96
+    for n in range(0, 192, 7):
+        for k in range(K):
+            g, h, j = n // 64, (n % 64) // 32, n % 32
+            t = k // 32
+            want = g * 64 * K + (t * 2 + h) * 1024 + ((k % 32) // 4) * 128 + j * 4 + k % 4
+            assert O.lib().orc_deep_offset(K, n, k) == want
+
+
+def test_permuted_f16_layout_matches_host_demo():
+    # src/host/test.c:548-556
+    K = 64
+    for k in range(K):
+        for n in range(0, 96, 5):
+            i0, i1, j0, j1 = k // 32, k % 32, n // 32, n % 32
+            tile = j0 * (K // 32) + i0
+            want = tile * 1024 + (i1 & ~1) * 32 + j1 * 2 + (i1 & 1)
+            assert O.lib().orc_f16_perm_offset(K, k, n) == want
+
+
+def test_cm_activation_layout():
+    # linear_w8a8.c:281 (tile base (row/64)*64*K), :117 (packed + (c/32)*2048 + r*32)
+    K = 128
+    for m in range(0, 200, 3):
+        for k in range(0, K, 5):
+            want = (m // 64) * 64 * K + (k // 32) * 2048 + (m % 64) * 32 + k % 32
+            assert O.lib().orc_cm_offset(K, m, k) == want
+
+
+def test_blob_round_trip_and_header():
+    n, k = 192, 96
+    w = O.int8_uniform(n * k, 11).reshape(n, k)
+    sw = O.uniform(n, 1e-3, 1e-2, 12)
+    inv = O.uniform(k, 0.5, 2.0, 13)
+    blob = O.w8a8_pack(w, sw, inv, signature=0xABCDEF)
+    hdr = blob[:40].view(np.uint32)
+    kn = k * n
+    assert list(hdr[:9]) == [0x38574D48, 1, k, n, 128, 128 + kn, 128 + kn + 4 * n,
+                             128 + kn + 8 * n, 128 + kn + 8 * n + 4 * k]
+    assert blob[40:48].view(np.uint64)[0] == 0xABCDEF
+    np.testing.assert_array_equal(O.w8a8_unpack(blob, k, n), w)
+    sums = blob[128 + kn + 4 * n:128 + kn + 8 * n].view(np.int32)
+    np.testing.assert_array_equal(sums, w.astype(np.int32).sum(1))
+
+
+# ------------------------------------------------------------------ integer KATs
+def _accumulate(a_u8, w_s8):
+    """acc[m][n] = sum_k a[m][k] * w[n][k] via the oracle."""
+    return O.w8a8_accumulate(np.ascontiguousarray(a_u8, np.uint8), np.ascontiguousarray(w_s8, np.int8))
+
+
+@pytest.mark.parametrize("target", [0, 1, -1, 32767, 32768, 32769, -32767, -32768, -32769, 65535,
+                                    65536, 65537, -65535, -65536, -65537, 131071, 131072, 1036320,
+                                    -1036320])
+def test_int32_boundary_targets(target):
+    # integer_tests.c:96-108: reach each target with 255*127 blocks, then a
+    # remainder; the UINT8 x INT8 dot product must reproduce it exactly.
+    K = 64
+    a = np.zeros((1, K), np.uint8)
+    w = np.zeros((1, K), np.int8)
+    rem, sign, k = abs(target), (-1 if target < 0 else 1), 0
+    while rem >= 32385:
+        a[0, k], w[0, k] = 255, sign * 127
+        rem -= 32385
+        k += 1
+    if rem >= 127:
+        a[0, k], w[0, k] = rem // 127, sign * 127
+        rem %= 127
+        k += 1
+    if rem:
+        a[0, k], w[0, k] = rem, sign
+    assert _accumulate(a, w)[0, 0] == target
+
+
+@pytest.mark.parametrize("kt", [1, 2, 3, 4])
+def test_zero_point_correction_with_padding(kt):
+    # integer_tests.c:111-134: signed activation through zero point 128;
+    # got - 128*colsum == sum (a-128)*w, with padded rows/columns and distinct
+    # K tiles (depth = kt*32 - 1, the last k is padding).
+    m, ncols, depth = 5, 17, kt * 32 - 1
+    K, N = kt * 32, 64
+    a = np.full((m, K), 128, np.uint8)            # padding codes are the zero point
+    w = np.zeros((N, K), np.int8)
+    for r in range(m):
+        for k in range(depth):
+            a[r, k] = (r * 13 + k * 17) % 256
+    for k in range(depth):
+        for n in range(ncols):
+            w[n, k] = (k * 11 + n * 5) % 16 - 8
+    acc = _accumulate(a, w)
+    colsum = w.astype(np.int64).sum(1)
+    expect = (a.astype(np.int64) - 128) @ w.astype(np.int64).T
+    np.testing.assert_array_equal(acc.astype(np.int64) - 128 * colsum[None, :], expect)
+
+
+def test_signed_accumulators_use_blob_column_sums():
+    # the operator subtracts (sum_k w) << 7 taken from the constants blob
+    # (linear_w8a8.c:159,168): with consistent sums this is sum (code-128)*w
+    c = O.make_w8a8(6, "t", 9, 96, 128, 0.01, False, 0)
+    _, codes, scales, sacc = O.w8a8_linear(c.x, c.blob, 96, 128, want_intermediates=True)
+    np.testing.assert_array_equal(sacc, (codes.astype(np.int64) - 128) @ c.w.astype(np.int64).T)
+    # a blob whose stored sums are off by d shifts every accumulator by -128*d
+    blob = c.blob.copy()
+    kn = 96 * 128
+    sums = blob[128 + kn + 4 * 128:128 + kn + 8 * 128].view(np.int32)
+    sums[5] += 3
+    _, _, _, sacc2 = O.w8a8_linear(c.x, blob, 96, 128, want_intermediates=True)
+    np.testing.assert_array_equal(sacc2[:, 5], sacc[:, 5] - 384)
+    np.testing.assert_array_equal(np.delete(sacc2, 5, 1), np.delete(sacc, 5, 1))
+
+
+def _study_hash(x):
+    x &= 0xFFFFFFFF
+    x ^= x >> 16
+    x = (x * 0x7FEB352D) & 0xFFFFFFFF
+    x ^= x >> 15
+    x = (x * 0x846CA68B) & 0xFFFFFFFF
+    return x ^ (x >> 16)
+
+
+def _study_a(r, k, seed):
+    if seed == 0:
+        return 129
+    if seed in (30, 31):
+        return 255
+    return _study_hash(r * 7919 + k * 13 + seed * 104729) & 255
+
+
+def _study_w(k, n, seed):  # INT8 kind (study_data.h:13-20, kind == 1)
+    if seed == 0:
+        return 1
+    if seed == 30:
+        return 127
+    if seed == 31:
+        return -128
+    if 12 <= seed < 24:
+        return (_study_hash(k * 3571 + n * 23 + seed * 65537) & 255) - 128
+    return (_study_hash(k * 3571 + n * 23 + seed * 65537) & 15) - 8
+
+
+@pytest.mark.parametrize("seed", [0, 3, 12, 17, 23, 30, 31])
+@pytest.mark.parametrize("kt", [1, 48])
+def test_study_generators_raw_and_signed_sums(seed, kt):
+    # study_host.c:160-187: raw = sum a*w, signed = sum (a-128)*w on the study
+    # generators (M64, N64 "weight:deep", K up to 6144).  Weight -128 (seed 31)
+    # is outside the [-127,127] codes of the operator but valid for the
+    # accumulator.
+    K, N, M = kt * 32, 64, 64
+    a = np.array([[_study_a(r, k, seed) for k in range(K)] for r in range(M)], np.uint8)
+    w = np.array([[_study_w(k, n, seed) for k in range(K)] for n in range(N)], np.int64)
+    raw = _accumulate(a, w.astype(np.int8))
+    np.testing.assert_array_equal(raw, a.astype(np.int64) @ w.T)
+    colsum = w.sum(1)
+    np.testing.assert_array_equal(raw.astype(np.int64) - 128 * colsum[None, :],
+                                  (a.astype(np.int64) - 128) @ w.T)
+
+
+# ------------------------------------------------------------------ FP32 steps
+def test_quantisation_round_half_even_and_clamp():
+    # scale = absmax/127 = 1 exactly: u = x + 128, RNE on ties (linear_w8a8.c:50-58)
+    x = np.array([[127.0, 0.5, 1.5, -0.5, -1.5, 2.5, -127.0, 0.49999997, 126.5, -126.5]], np.float32)
+    codes, scales = O.quantize_rows(x)
+    assert scales[0] == np.float32(1.0)
+    assert list(codes[0]) == [255, 128, 130, 128, 126, 130, 1, 128, 254, 2]
+
+
+def test_quantisation_zero_and_tiny_rows():
+    x = np.zeros((2, 64), np.float32)
+    x[1, 3] = 1e-20
+    codes, scales = O.quantize_rows(x)
+    assert scales[0] == np.float32(1e-12) and scales[1] == np.float32(1e-12)
+    assert (codes == 128).all()          # 1e-20 * 1e12 + 128 rounds to 128
+
+
+def test_quantisation_uses_ieee_steps():
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((7, 96)) * 3).astype(np.float32)
+    inv = rng.uniform(0.5, 2, 96).astype(np.float32)
+    codes, scales = O.quantize_rows(x, inv)
+    xs = (x * inv).astype(np.float32)
+    sc = np.maximum((np.abs(xs).max(1) / np.float32(127)).astype(np.float32), np.float32(1e-12))
+    np.testing.assert_array_equal(scales, sc)
+    s = (np.float32(1) / sc).astype(np.float32)
+    u = ((xs * s[:, None]).astype(np.float32) + np.float32(128)).astype(np.float32)
+    u = np.clip(u, 1, 255)
+    np.testing.assert_array_equal(codes, np.rint(u).astype(np.uint8))
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_activation_formulas(mode):
+    xs = np.linspace(-12, 12, 97)
+    for x in xs:
+        got = O.epilogue(float(np.float32(x)), mode)
+        if mode == 1:
+            ref = 0.5 * x * (1 + np.tanh(np.sqrt(2 / np.pi) * (x + 0.044715 * x ** 3)))
+        else:
+            ref = x / (1 + np.exp(-1.702 * x))
+        assert abs(got - ref) <= 1e-5 * max(1.0, abs(ref))
+    assert O.epilogue(3.0, 0) == 3.0 and O.epilogue(3.0, 3) == 3.0
+
+
+def test_w8a8_dequant_order_and_modes():
+    # out = fl(fl(float(y) * sw) * rs) then bias, then activation; mode 3 is the
+    # cropped channel-major store (mat_mul.c:847-858)
+    c = O.make_w8a8(9, "t", 6, 64, 128, 0.0, True, 0)
+    out, codes, scales, acc = O.w8a8_linear(c.x, c.blob, 64, 128, want_intermediates=True)
+    ref = ((acc.astype(np.float32) * c.sw[None, :]).astype(np.float32) * scales[:, None]).astype(np.float32)
+    np.testing.assert_array_equal(out, ref)
+    withb = O.w8a8_linear(c.x, c.blob, 64, 128, bias=c.bias, mode=0)
+    np.testing.assert_array_equal(withb, (ref + c.bias[None, :]).astype(np.float32))
+    chw = O.w8a8_linear(c.x, c.blob, 64, 128, bias=c.bias, channels=100, mode=3)
+    assert chw.shape == (100, 6)
+    np.testing.assert_array_equal(chw, withb[:, :100].T)
+
+
+def test_f16_epilogue_matches_fp64_reference():
+    m, k, n = 9, 64, 96
+    x = O.normal(m * k, 1.0, 0, 1, 21).reshape(m, k)
+    w = O.f16_normal(k * n, 0.02, 22).reshape(k, n)
+    wperm = O.f16_pack_permuted(w)
+    got = O.f16_linear(x, wperm, k, n)
+    ref = x.astype(np.float16).astype(np.float64) @ w.view(np.float16).astype(np.float64)
+    assert O.max_abs_rel(got, ref) < 1e-6
+    got16 = O.f16_linear(x, wperm, k, n, round_acc_f16=True)
+    np.testing.assert_array_equal(got16, got.astype(np.float16).astype(np.float32))
+
+
+def test_row_subset_equals_full():
+    c = O.make_w8a8(4, "t", 40, 128, 192, 0.01, True, 1)
+    full = O.w8a8_linear(c.x, c.blob, 128, 192, bias=c.bias, mode=1)
+    rows = [0, 7, 39, 13]
+    sub = O.w8a8_linear(c.x, c.blob, 128, 192, bias=c.bias, mode=1, rows=rows)
+    np.testing.assert_array_equal(sub, full[rows])
+
+
+def test_openmp_build_matches_single_thread():
+    c = O.config_c1()
+    a = O.w8a8_linear(c.x, c.blob, c.k, c.n)
+    b = O.w8a8_linear(c.x, c.blob, c.k, c.n, kind="omp")
+    np.testing.assert_array_equal(a, b)
+
+
+def test_seeded_generators_are_deterministic():
+    a = O.normal(1000, 1.0, 0.01, 20.0, 123)
+    b = O.normal(1000, 1.0, 0.01, 20.0, 123)
+    np.testing.assert_array_equal(a, b)
+    assert abs(float(np.std(O.normal(100000, 1.0, 0, 1, 7))) - 1.0) < 0.02
+    w = O.int8_uniform(100000, 3)
+    assert w.min() == -127 and w.max() == 127

@@ -1,0 +1,68 @@
+"""Legality sweep of the M-keyed tile planner (htpg_plan_info).
+
+Mirrors the structure of the reference's planner test
+(tests/test-f16-gemm-plan.c:5-44): every plan over a grid of shapes must be
+legal for the device — tiles cover the problem, shared memory fits, the grid
+fits the SMs (an even number of CTAs for CTA-pair tiles), K splits only where
+the reduction is exact (INT8) and never leave an empty split, and the FP16 path
+keeps K whole inside a CTA so its accumulation order does not depend on the plan.
+"""
+import itertools
+
+import pytest
+
+import htpg
+
+SMEM_LIMIT = 232448
+MS = [1, 2, 4, 16, 17, 31, 32, 33, 77, 128, 129, 255, 256, 257, 1000, 4096, 4100, 16384, 65536]
+NS = [32, 64, 128, 192, 640, 1536, 3072, 4096, 4608, 6144, 14336, 16384]
+KS = [32, 64, 160, 768, 1152, 1536, 4096, 6144, 14336, 16384]
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("sms", [148, 132, 16])
+def test_plans_are_legal(kind, sms):
+    checked = 0
+    for m, n, k in itertools.product(MS, NS, KS):
+        if kind == 0 and n % 64:
+            continue
+        p = htpg.plan_info(kind, m, n, k, sms)
+        elems = 128 if kind == 0 else 64
+        kb_total = -(-k // elems)
+        assert p["kb_total"] == kb_total
+        assert p["smem"] <= SMEM_LIMIT
+        assert p["units"] == p["tiles_a"] * p["tiles_b"] * p["splits"]
+        assert 1 <= p["grid"] <= sms and p["grid"] <= (2 * p["units"] if p["bn"] else p["units"])
+        # K ranges: every split non-empty, together exactly [0, kb_total)
+        assert p["splits"] * p["kb_per_split"] >= kb_total
+        assert (p["splits"] - 1) * p["kb_per_split"] < kb_total
+        if p["swap"]:
+            assert kind == 0 and m <= 32 and p["bn"] in (16, 32)
+            assert p["tiles_a"] * 128 >= n and p["tiles_b"] * p["bn"] >= m
+        else:
+            assert p["splits"] == 1                       # K whole in the normal orientation
+            pair = p["tiles_a"] * 256 >= m and p["tiles_a"] == -(-m // 256) and m > 128 \
+                and p["grid"] % 2 == 0 and p["bn"] in (128, 256)
+            rows = 256 if pair else 128
+            assert p["tiles_a"] * rows >= m and p["tiles_b"] * p["bn"] >= n
+            assert p["bn"] in (32, 64, 128, 256)
+        if kind == 1:
+            assert p["splits"] == 1 and not p["swap"]
+        checked += 1
+    assert checked > 1500
+
+
+def test_headline_shapes():
+    # C4 and the C3 linears take CTA-pair 256-row tiles; C5 decode shapes the
+    # swapped, K-split plan; C1/C2 single-CTA tiles that still fill the SMs.
+    c4 = htpg.plan_info(0, 16384, 6144, 1536)
+    assert c4["bn"] == 256 and c4["tiles_a"] == 64 and c4["grid"] == 148
+    for m in (1, 4, 16):
+        up = htpg.plan_info(0, m, 14336, 4096)
+        down = htpg.plan_info(0, m, 4096, 14336)
+        assert up["swap"] and down["swap"] and down["splits"] > 1
+        assert down["units"] <= 148 and up["units"] <= 148
+    c1 = htpg.plan_info(0, 256, 4608, 1152)
+    assert not c1["swap"] and c1["units"] >= 0.85 * 148
+    c2 = htpg.plan_info(1, 77, 3072, 768)
+    assert not c2["swap"] and c2["splits"] == 1
