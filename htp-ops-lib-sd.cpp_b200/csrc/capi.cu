@@ -18,6 +18,7 @@
 #include "../../include/htp_ops_b200.h"
 #include "../../include/op_reg.h"
 #include "kernels.h"
+#include "scratch_run.h"
 
 using namespace htpg;
 
@@ -204,6 +205,7 @@ extern "C" const char *htpg_strerror(int code) {
     case HTPG_ENOPLAN: return "no tile plan for this shape";
     case HTPG_EWATCHDOG: return "device wait expired";
     case HTPG_ENOMEM: return "device allocation failed";
+    case HTPG_ESCRATCH: return "request does not fit the static scratch array";
     case HTPG_EARCH: return "device is not sm_100";
     default: return "unknown error";
   }
@@ -558,6 +560,88 @@ extern "C" int htpg_f16_run(const htpg_weights *w, float *out, int ldo, const fl
   if (!w || w->kind != Kind::F16) return HTPG_EARGS;
   return run_common(const_cast<htpg_weights *>(w), out, ldo, x, bias, m, channels, mode, stream);
 }
+
+// W8A8 run whose scratch is the caller's fixed array [scratch, scratch+bytes)
+// instead of the per-stream workspace: the allocation-free entry point
+// (noalloc.cu) calls this.  Same checks and kernels as htpg_w8a8_run; no
+// profiling or phase events.
+int htpg::w8a8_run_in_scratch(const htpg_weights *w, float *out, int ldo, const float *x,
+                              const float *bias, int m, int channels, int mode, void *stream,
+                              void *scratch, size_t scratch_bytes) {
+  if (!w || w->kind != Kind::I8 || !out || !x || !scratch) return HTPG_EARGS;
+  const int n = w->ncols, k = w->k;
+  if (m < 1 || m > HTPG_W8A8_MAX_M) return HTPG_EARGS;
+  if (mode < 0 || mode > HTPG_MODE_RAW) return HTPG_ECAPACITY;
+  if (channels == 0) channels = n;
+  if (channels < 1 || channels > n || (mode != 3 && channels != n)) return HTPG_ECAPACITY;
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return HTPG_ECONTROL;
+  if (reinterpret_cast<uintptr_t>(out) & 3u) return HTPG_ECONTROL;
+  if (ldo == 0) ldo = mode == 3 ? m : n;
+  if ((mode == 3 && ldo < m) || (mode != 3 && ldo < n)) return HTPG_EARGS;
+  static_assert(kSplitKRegion == kStaticSplitKBytes, "split-K area size is part of the documented layout");
+  const size_t act_bytes = align_up(static_cast<size_t>(m) * k, 1024);
+  const size_t scale_bytes = align_up(4u * static_cast<size_t>(m), 1024);
+  if (kSplitKRegion + act_bytes + scale_bytes > scratch_bytes) {
+    t_last_cuda_error = "static scratch: m*k = " + std::to_string(static_cast<size_t>(m) * k) +
+                        " needs " + std::to_string(kSplitKRegion + act_bytes + scale_bytes) +
+                        " bytes, the array holds " + std::to_string(scratch_bytes);
+    return HTPG_ESCRATCH;
+  }
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t st = pick_stream(d, stream);
+  std::lock_guard<std::mutex> lk(g_mu);
+
+  const GemmPlan plan = plan_gemm(Kind::I8, m, n, k, d->sms);
+  const size_t splitk_bytes = splitk_ws_bytes(plan) + splitk_count_bytes(plan);
+  if (splitk_bytes > kSplitKRegion) return HTPG_ENOPLAN;
+  uint8_t *base = static_cast<uint8_t *>(scratch);
+  int32_t *wsk = reinterpret_cast<int32_t *>(base);
+  uint32_t *cnt = reinterpret_cast<uint32_t *>(base + splitk_ws_bytes(plan));
+  int8_t *act = reinterpret_cast<int8_t *>(base + kSplitKRegion);
+  float *scales = reinterpret_cast<float *>(base + kSplitKRegion + act_bytes);
+  // The array keeps whatever the previous call (or an aborted launch) left:
+  // the split-K partial sums and tile counters must start at zero.
+  cudaError_t e = cudaSuccess;
+  if (plan.splits > 1) e = cudaMemsetAsync(base, 0, splitk_bytes, st);
+  if (e != cudaSuccess) return record_cuda(e);
+  e = launch_quantize_rows(act, scales, x, w->inverse, m, k, st);
+  if (e != cudaSuccess) return record_cuda(e);
+
+  CUtensorMap act_map;
+  const CUtensorMap *wmap = nullptr;
+  rc = make_map(&act_map, act, Kind::I8, k, m, static_cast<size_t>(k), plan.swap ? plan.bn : 128);
+  if (rc) return rc;
+  rc = weight_map(const_cast<htpg_weights *>(w), plan.swap ? 128 : box_rows_b(plan), &wmap);
+  if (rc) return rc;
+  GemmArgs a;
+  a.M = m;
+  a.N = n;
+  a.K = k;
+  a.out = out;
+  a.ldo = ldo;
+  a.mode = mode;
+  a.channels = channels;
+  a.row_scale = scales;
+  a.col_scale = w->sw;
+  a.col_corr = w->corr;
+  a.bias = bias;
+  a.ws = wsk;
+  a.ws_count = cnt;
+  a.watchdog = d->watchdog;
+  CUtensorMap out_map = act_map;  // placeholder when unused
+  if (!plan.swap && mode != 3 && tma_store_ok(out, ldo)) {
+    rc = make_out_map(&out_map, out, m, n, ldo);
+    if (rc) return rc;
+    a.tma_store = 1;
+  }
+  e = plan.swap ? launch_gemm(plan, *wmap, act_map, out_map, a, st)
+                : launch_gemm(plan, act_map, *wmap, out_map, a, st);
+  return record_cuda(e);
+}
+
+void htpg::set_error_text(const char *text) { t_last_cuda_error = text ? text : ""; }
 
 // ================================================================ one-call
 namespace {

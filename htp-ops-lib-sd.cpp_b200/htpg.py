@@ -19,7 +19,7 @@ INCLUDE = os.path.join(REPO, "include")
 # error codes (include/htp_ops_b200.h)
 OK, EPAYLOAD, EUNMAPPED, EHEADER = 0, -1, -2, -3
 EARGS, ECAPACITY, ECONTROL, ELAUNCH, ENOPLAN = -10, -11, -12, -13, -14
-EWATCHDOG, ENOMEM, EARCH = -16, -17, -75
+EWATCHDOG, ENOMEM, ESCRATCH, EARCH = -16, -17, -18, -75
 BUF_DEVICE, BUF_HOST = 0, 1
 
 _lib = None
@@ -72,6 +72,7 @@ def lib() -> ctypes.CDLL:
         "htpg_weights_cols": (I, [P]),
         "htpg_w8a8_run": (I, [P, P, I, P, P, I, I, I, P]),
         "htpg_f16_run": (I, [P, P, I, P, P, I, I, I, P]),
+        "htpg_w8a8_run_static": (I, [P, P, I, P, P, I, I, I, P]),
         "htpg_w8a8_linear": (I, [P, P, P, P, I, I, I, I, I, P]),
         "htpg_f16_linear": (I, [P, P, P, P, I, I, I, I, I, P]),
         "htpg_weight_cache_drop": (None, [P]),

@@ -109,6 +109,32 @@ int htpg_w8a8_run(const htpg_weights *w, float *out, int ldo, const float *x, co
 int htpg_f16_run(const htpg_weights *w, float *out, int ldo, const float *x, const float *bias,
                  int m, int channels, int mode, void *stream);
 
+/* ---- W8A8 run that allocates nothing (no counterpart in the reference) -- */
+/* For callers that must not allocate device memory per call: code running
+ * under a fixed memory budget or a caching allocator that owns all device
+ * memory, real-time loops where cudaMalloc's implicit device synchronisation
+ * is not acceptable, and hosts that prepare every buffer up front.  Same
+ * arguments, checks and results as htpg_w8a8_run, but the activation codes,
+ * row scales and split-K partial sums live in one fixed static device array
+ * of HTPG_STATIC_SCRATCH_BYTES per device instead of the per-stream
+ * workspace, and no call allocates: no cudaMalloc, cudaFree or allocating
+ * library routine.  Layout of the array: the split-K area (2,101,248 bytes,
+ * cleared by every call that uses it), then m*k bytes of codes, then 4*m
+ * bytes of row scales, each rounded up to 1 KiB; a call that needs more than
+ * HTPG_STATIC_SCRATCH_BYTES returns HTPG_ESCRATCH and launches nothing
+ * (m*k up to 31,453,184 - 4*m: e.g. M = 16384 at K = 1536).  The prepared
+ * weight `w` is made beforehand with htpg_w8a8_weights_create, which does
+ * allocate.  The first call on each device does that device's one-time set-up
+ * (device properties, the array's device address, kernel attributes), so make
+ * it before any stream capture.  Every call on a device shares the one array,
+ * which keeps the previous call's contents: calls whose executions overlap on
+ * the GPU (different streams, or host threads racing on one device) race on
+ * it; order them on one stream. */
+#define HTPG_STATIC_SCRATCH_BYTES (32u << 20)
+#define HTPG_ESCRATCH (-18) /* request does not fit HTPG_STATIC_SCRATCH_BYTES */
+int htpg_w8a8_run_static(const htpg_weights *w, float *out, int ldo, const float *x,
+                         const float *bias, int m, int channels, int mode, void *stream);
+
 /* ---- one-call linear operators (weights cached by pointer) ------------- */
 /* W8A8 linear, opcode 15 (reference: linear_w8a8.c:327-530) plus the
  * optional opcode-16 epilogue (extension).  constants: device copy of the
