@@ -10,7 +10,9 @@ INT8 GEMM with the fused dequant/bias/GELU epilogue, (gather).  Metric: whole-
 job INT8 TOPS (2*M*N*K per step / device time, max over ranks).
 
 * value        device-resident inputs; per-step CUDA-event time (L2 flushed
-               between steps by a 256 MiB write outside the timed events).
+               between steps by a 256 MiB write + read-back outside the timed
+               events; a bounded sleep kernel lets the host queue the timed
+               steps ahead, so launch gaps are not counted).
 * e2e          the same operator through the reference-facing API: an opcode-15
                request (56-byte epilogue payload) posted on the shared-memory
                message channel with host (pinned) buffers; the receiver copies
@@ -43,6 +45,9 @@ sys.path.insert(0, PKG)
 
 M_C4, K_C4, N_C4 = 16384, 1536, 6144
 FLUSH_BYTES = 256 << 20
+L2_NOTE = ("256 MiB buffer written then read back between steps (outside the timed events): "
+           "the next step starts from a cold L2 holding only clean lines")
+SLEEP_CYCLES = 20_000_000   # ~10 ms of torch's bounded sleep kernel ahead of a timed loop
 
 
 def peaks():
@@ -114,7 +119,7 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ inputs
-def make_c4_inputs(torch, dev, m, k, n, seed=0x5EED0003):
+def make_c4_inputs(torch, dev, m, k, n, seed=0x5EED0003, outlier_p=0.005):
     """Seeded synthetic C4 tensors with BASELINE's distributions (config index 2
     values): X ~ N(0,1) with 0.5% of entries x20, W int8 uniform [-127,127],
     column scales U[1e-3,1e-2], bias N(0,0.01)."""
@@ -123,7 +128,7 @@ def make_c4_inputs(torch, dev, m, k, n, seed=0x5EED0003):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     x = torch.randn(m, k, device=dev, generator=g)
-    x = torch.where(torch.rand(m, k, device=dev, generator=g) < 0.005, x * 20.0, x).contiguous()
+    x = torch.where(torch.rand(m, k, device=dev, generator=g) < outlier_p, x * 20.0, x).contiguous()
     gc = torch.Generator()
     gc.manual_seed(seed + 1)
     w = torch.randint(-127, 128, (n, k), generator=gc, dtype=torch.int16).to(torch.int8).numpy()
@@ -131,6 +136,115 @@ def make_c4_inputs(torch, dev, m, k, n, seed=0x5EED0003):
     bias = (torch.randn(n, generator=gc) * 0.01).to(dev)
     blob = htpg.pack_w8a8_constants(w, sw, None, signature=seed)
     return x, torch.from_numpy(blob).to(dev), bias, blob
+
+
+class L2Flush:
+    """Evicts the L2 between timed steps: a write of a buffer twice the L2's
+    size, then a read of it, so no dirty line of the flush is left for the
+    next step's kernels to write back."""
+
+    def __init__(self, torch, dev):
+        self.buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+        self.sink = torch.empty((), dtype=torch.float32, device=dev)
+        self.torch = torch
+
+    def __call__(self):
+        self.buf.zero_()
+        self.torch.sum(self.buf, dim=0, out=self.sink)
+
+
+# ------------------------------------------------------------------ suite
+def _w8a8_operands(torch, htpg, dev, m, k, n, seed, outlier_p, bias):
+    """Seeded W8A8 operands (BASELINE value distributions) and prepared weights."""
+    x, blob_dev, b, _ = make_c4_inputs(torch, dev, m, k, n, seed=seed, outlier_p=outlier_p)
+    return x, htpg.w8a8_weights(blob_dev, k, n), (b if bias else None), blob_dev
+
+
+def suite(torch, L, htpg, dev, flush, reps=20):
+    """Per-config device times of the other BASELINE configs (one GPU): C1,
+    C2, the four C3 DiT linears and the six C5 decode linears.  Each run is the
+    whole operator (activation pass + GEMM), timed with CUDA events on the
+    launching stream, the L2 flushed (256 MiB written and read back) before
+    every run, the stream held by a bounded sleep kernel while the host queues
+    the runs; the median of `reps` runs.  `host_latency_us` is one call on an
+    idle GPU, host work included.  Algorithmic bytes: W8A8 4MK + KN + 4N + 4MN
+    (+4N bias); F16 4MK + 2KN + 4N + 4MN."""
+    import numpy as np
+    hbm, bf16, _, _ = peaks()
+    int8_peak = 2.0 * bf16
+    stream = torch.cuda.current_stream()
+    res = {}
+
+    def timed(fn):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for _ in range(3):
+            fn()
+        # host-inclusive latency: one call at a time on an idle GPU
+        lat = []
+        for _ in range(5):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            lat.append((time.perf_counter() - t0) * 1e6)
+        L.htpg_phase_timing(1)
+        htpg.phase_timing_read()
+        # device time: a bounded sleep kernel holds the stream while the host
+        # queues every run, so no run waits for its own launch
+        torch.cuda._sleep(SLEEP_CYCLES)
+        for a, b in ev:
+            flush()
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize()
+        L.htpg_phase_timing(0)
+        act_ms, gemm_ms, runs = htpg.phase_timing_read()
+        us = statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
+        return us, act_ms * 1e3 / max(runs, 1), gemm_ms * 1e3 / max(runs, 1), statistics.median(lat)
+
+    def record(name, m, k, n, timing, nbytes, peak_ops):
+        us, act_us, gemm_us, lat_us = timing
+        ops = 2.0 * m * n * k
+        t_tc, t_hbm = ops / (peak_ops * 1e12), nbytes / (hbm * 1e9)
+        res[name] = {"M": m, "K": k, "N": n, "us": us, "act_us": act_us, "gemm_us": gemm_us,
+                     "host_latency_us": lat_us,
+                     "TOPS": ops / us / 1e6, "GBps": nbytes / us / 1e3,
+                     "tensor_frac": ops / us / 1e6 / peak_ops, "hbm_frac": nbytes / us / 1e3 / hbm,
+                     "bound": "tensor" if t_tc >= t_hbm else "hbm",
+                     "roofline_frac": max(t_tc, t_hbm) / (us * 1e-6)}
+
+    def w8a8_case(name, m, k, n, seed, outlier_p, mode, bias):
+        x, w, b, keep = _w8a8_operands(torch, htpg, dev, m, k, n, seed, outlier_p, bias)
+        out = torch.empty(m, n, dtype=torch.float32, device=dev)
+        tm = timed(lambda: htpg.check(htpg.w8a8_run(w, out, x, b, mode=mode), name))
+        record(name, m, k, n, tm, 4 * m * k + k * n + 4 * n + 4 * m * n + (4 * n if bias else 0), int8_peak)
+        del keep
+
+    w8a8_case("C1", 256, 1152, 4608, 0x5EED0000, 0.01, 0, False)
+    # C2: CLIP fc1 through the FP16 path, bias + QuickGELU
+    m, k, n = 77, 768, 3072
+    g = torch.Generator(device=dev)
+    g.manual_seed(0x5EED0001)
+    x = torch.randn(m, k, device=dev, generator=g)
+    wf = (torch.randn(k, n, device=dev, generator=g) * 0.02).half()
+    bias = torch.randn(n, device=dev, generator=g) * 0.01
+    wperm = torch.from_numpy(htpg.pack_f16_permuted(wf.cpu().numpy().view(np.uint16)).view(np.int16)).to(dev)
+    wh = htpg.f16_weights(wperm, k, n)
+    out = torch.empty(m, n, dtype=torch.float32, device=dev)
+    tm = timed(lambda: htpg.check(htpg.f16_run(wh, out, x, bias, mode=2), "C2"))
+    record("C2", m, k, n, tm, 4 * m * k + 2 * k * n + 4 * n + 4 * m * n, bf16)
+    del wh, wperm
+    # C3: DiT block linears at M=4096
+    for name, k, n, mode, b in (("C3_qkv", 1536, 4608, 0, False), ("C3_out", 1536, 1536, 0, False),
+                                ("C3_fc1", 1536, 6144, 1, True), ("C3_fc2", 6144, 1536, 0, True)):
+        w8a8_case(name, 4096, k, n, 0x5EED0002 + k + n, 0.005, mode, b)
+    res["C3_stack_us"] = sum(res[c]["us"] for c in ("C3_qkv", "C3_out", "C3_fc1", "C3_fc2"))
+    # C5: decode shapes, no epilogue
+    for m in (1, 4, 16):
+        for name, k, n in (("up", 4096, 14336), ("down", 14336, 4096)):
+            w8a8_case(f"C5_{name}_M{m}", m, k, n, 0x5EED0004 + m + k, 0.0, 0, False)
+    return res
 
 
 # ------------------------------------------------------------------ CPU leg
@@ -264,6 +378,8 @@ def main():
                     help="rows of the C4 problem the CPU baseline computes per sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-suite", action="store_true",
+                    help="skip the per-config C1/C2/C3/C5 device times (one GPU only)")
     ap.add_argument("--m", type=int, default=M_C4,
                     help="token rows; smaller values only for profiling captures (workload C4-M<m>)")
     ap.add_argument("--settle", type=float, default=1.5,
@@ -301,7 +417,7 @@ def main():
     out_loc = torch.empty(m, n_loc, dtype=torch.float32, device=dev)
     gathered = torch.empty(world * m, n_loc, dtype=torch.float32, device=dev) if world > 1 else None
     full = torch.empty(m, n, dtype=torch.float32, device=dev) if world > 1 else None
-    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush = L2Flush(torch, dev)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
 
@@ -313,7 +429,7 @@ def main():
             htpg.assemble_columns(full, gathered.view(world, m, n_loc))
 
     for _ in range(args.warmup):
-        flush.zero_()
+        flush()
         step()
     torch.cuda.synchronize()
     htpg.check(htpg.check_device(), "watchdog")
@@ -329,7 +445,7 @@ def main():
     # 200 ms clock samples describe the timed steps; every rank runs the same count
     t0 = time.perf_counter()
     for _ in range(5):
-        flush.zero_()
+        flush()
         step()
     torch.cuda.synchronize()
     per = max((time.perf_counter() - t0) / 5, 1e-5)
@@ -339,15 +455,16 @@ def main():
     settle = int(cnt.item())
     with ClockSampler(local) as clocks:
         for i in range(settle):
-            flush.zero_()
+            flush()
             step()
             if i % 64 == 63:
                 htpg.phase_timing_read()   # keeps the pending event list short
         torch.cuda.synchronize()
         htpg.phase_timing_read()
         launches0 = L.htpg_launch_count()
+        torch.cuda._sleep(SLEEP_CYCLES)       # the host queues the timed steps meanwhile
         for i in range(args.steps):
-            flush.zero_()                      # L2 flush outside the timed events
+            flush()                            # L2 flush outside the timed events
             starts[i].record(stream)
             step()
             ends[i].record(stream)
@@ -406,7 +523,7 @@ def main():
         "config": {"workload": workload, "M": m, "K": k, "N": n, "N_per_gpu": n_loc,
                    "epilogue": "bias+gelu_tanh", "parallelism": f"tp{world} (columns)" if world > 1 else "single",
                    "exchange": "nccl all_gather + reassembly" if world > 1 else None,
-                   "l2": "256 MiB flush write between steps (outside the timed events)"},
+                   "l2": L2_NOTE},
         "roofline": roof,
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
@@ -417,8 +534,38 @@ def main():
         line["e2e"] = {"value": ops / dt / 1e12, "unit": "TOPS", "h2d_bytes_per_step": h2d,
                        "d2h_bytes_per_step": d2h, "path": "message channel, opcode 15 (56-byte payload), "
                        "pinned host buffers"}
-    elif world > 1:
-        line["e2e"] = None
+    elif world > 1 and not args.no_e2e:
+        # C-ABI run of this rank's column shard with host buffers: the pinned
+        # activation goes in every step on every rank, rank 0 reads the whole
+        # gathered output back; device time per step, max over ranks.
+        x_host = x.cpu().pin_memory()
+        out_host = torch.empty(m, n, dtype=torch.float32).pin_memory() if rank == 0 else None
+        e2e_steps = max(3, args.steps // 4)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(e2e_steps)]
+
+        def e2e_step():
+            x.copy_(x_host, non_blocking=True)
+            step()
+            if rank == 0:
+                out_host.copy_(full, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        for a, b in ev:
+            a.record(stream)
+            e2e_step()
+            b.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([sum(a.elapsed_time(b) for a, b in ev) / e2e_steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        line["e2e"] = {"value": ops / (float(t.item()) * 1e-3) / 1e12, "unit": "TOPS",
+                       "h2d_bytes_per_step": m * k * 4, "d2h_bytes_per_step": m * n * 4,
+                       "path": "C ABI htpg_w8a8_run per rank + NCCL all-gather; pinned host activation in "
+                               "(every rank), full output out (rank 0)"}
+    if world == 1 and not args.no_suite:
+        line["suite"] = suite(torch, L, htpg, dev, flush)
     if rank == 0 and world == 1 and not args.no_cpu:
         tops, threads, secs = cpu_sample(k, n, args.cpu_rows)
         line["cpu_baseline"] = {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port",

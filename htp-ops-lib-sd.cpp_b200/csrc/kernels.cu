@@ -309,26 +309,31 @@ cudaError_t launch_repack_f16(uint16_t *dst, const uint16_t *perm, int k, int n0
 // ====================================================================== GEMM
 // Optional epilogue activation (mat_mul.c:788-826): GELU(tanh) as
 // x*sigmoid(z), z = 1.5957691216057308*(x + 0.044715 x^3), QuickGELU as
-// x*sigmoid(1.702 x).  The sigmoid is evaluated as 1/(1 + 2^(-z log2 e)) with
-// the hardware 2^x and reciprocal (each within 2 ulp).  Neither step cancels,
-// so this matches the reference's sign-split form e = 2^-|z|, e*inv or inv
-// to a few ulp for every z: large -z overflows 2^x to +inf and 1/inf = 0,
-// large +z gives 1/(1+0) = 1.  MODE is a template parameter so the
-// per-element code is branch-free and the 32 elements of a chunk interleave.
+// x*sigmoid(1.702 x).  x*sigmoid(z) is evaluated as 0.5x*(1 + tanh(z/2)) with
+// the hardware tanh (one MUFU operation instead of a 2^x and a reciprocal; the
+// epilogue, not the tensor pipe, bounds short-K layers).  The tanh's relative
+// error of about 2^-11 becomes an absolute error below 2.5e-4*|x| in the
+// output, largest where 1 + tanh cancels (z near -6); against the tensor's
+// absolute maximum that stays far inside the 2e-3 / 1e-2 output tolerances.
+// Saturation is exact: tanh = -1 gives 0, tanh = 1 gives x.  MODE is a
+// template parameter so the per-element code is branch-free and the 32
+// elements of a chunk interleave.
 template <int MODE>
 __device__ __forceinline__ float epilogue_act(float x) {
   if constexpr (MODE != 1 && MODE != 2) {
     return x;
   } else {
-    float z;
+    // x * sigmoid(z) = 0.5x * (1 + tanh(z / 2)): one MUFU operation per element
+    float h;
     if constexpr (MODE == 1) {
-      constexpr float c1 = 1.5957691216057308f, c3 = 1.5957691216057308f * 0.044715f;
-      z = x * fmaf(x * x, c3, c1);
+      constexpr float c1 = 0.5f * 1.5957691216057308f, c3 = 0.5f * 1.5957691216057308f * 0.044715f;
+      h = x * fmaf(x * x, c3, c1);
     } else {
-      z = x * 1.702f;
+      h = x * (0.5f * 1.702f);
     }
-    const float e = ex2_approx(z * -1.4426950408889634f);
-    return x * rcp_approx(1.0f + e);
+    const float t = tanh_approx(h);
+    const float hx = 0.5f * x;
+    return fmaf(hx, t, hx);
   }
 }
 
@@ -361,9 +366,9 @@ constexpr int kRowBytes = 128;                     // one K block = one 128-byte
 // Per epilogue warp: a 32 x 32 FP32 output tile staged with 128-byte swizzle
 // (row r at r*128 bytes, 16-byte chunk j at position j ^ (r & 7)), the source
 // layout of the TMA store and conflict-free for row- and column-wise access;
-// plus 96 floats of per-column parameters of the chunk being finished.
+// plus 96 floats of per-column parameters for each of its (up to two) chunks.
 constexpr int kWarpScratch = 32 * 32;              // floats per epilogue warp (4 KiB)
-constexpr int kWarpParams = 96;                    // floats per epilogue warp
+constexpr int kWarpParams = 192;                   // floats per epilogue warp (two chunks)
 constexpr int kEpiSmem = kEpiWarps * (kWarpScratch + kWarpParams) * 4;
 
 constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block on sm_100
@@ -447,6 +452,8 @@ struct EpiCtx {
   float *prm;        // this warp's column-parameter slots
   uint32_t t_row;    // TMEM address of lane quadrant q, accumulator buffer
   uint32_t full_bar, full_parity;  // accumulator-full barrier of this unit
+  uint32_t empty_bar;              // accumulator-free barrier (the leader's, for pairs)
+  bool empty_remote;               // empty_bar is in the leader CTA of the pair
   Unit w;
   int row0;                        // first output row held by this CTA's TMEM lanes
   int q, part, lane, epi_t;        // part: which of the quadrant's four warps
@@ -455,12 +462,31 @@ struct EpiCtx {
 // Normal orientation: TMEM lane = activation row m, column = weight column n.
 // The four warps of a lane quadrant take every fourth 32-column chunk.  The row
 // scale and the per-column parameters are loaded before the accumulator wait,
-// so their latency hides behind the MMAs.  Returns whether the wait succeeded.
+// so their latency hides behind the MMAs.  A warp reads all of its chunks from
+// TMEM at once and hands the accumulator buffer back to the MMA warp before it
+// does any arithmetic or stores, so the next-but-one tile's MMAs never wait for
+// this tile's epilogue.  Returns whether the wait succeeded (the buffer has
+// then been released).
 template <Kind KIND, int BN, int MODE, bool BIAS>
 __device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
   constexpr int kChunks = BN / 32;
+  // BN < 128: one chunk for the first kChunks warps of a quadrant; BN >= 128:
+  // exactly kMine chunks for every warp
   constexpr int kMine = (kChunks + kEpiPerQuadrant - 1) / kEpiPerQuadrant;
+  static_assert(kMine * 96 <= kWarpParams, "parameter slots per warp");
   const GemmArgs &g = *c.g;
+  const bool active = c.part < kChunks;
+  if (!active) {
+    const bool ok = mbar_wait(c.full_bar, c.full_parity, g.watchdog, kWatchEpilogue, c.L.abort);
+    tc_fence_after();
+    if (ok && c.lane == 0) {
+      if (c.empty_remote)
+        mbar_arrive_cluster(c.empty_bar);
+      else
+        mbar_arrive(c.empty_bar);
+    }
+    return ok;
+  }
   const int m = c.row0 + c.q * 32 + c.lane;
   const bool m_ok = m < g.M;
   const float rs = (KIND == Kind::I8 && m_ok) ? __ldg(g.row_scale + m) : 0.0f;
@@ -469,7 +495,7 @@ __device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
 #pragma unroll
   for (int i = 0; i < kMine; ++i) {
     const int nl = c.w.tb * BN + (c.part + kEpiPerQuadrant * i) * 32 + c.lane;
-    const bool ok = c.part + kEpiPerQuadrant * i < kChunks && nl < g.N;
+    const bool ok = nl < g.N;
     psw[i] = (KIND == Kind::I8 && ok) ? __ldg(g.col_scale + nl) : 0.0f;
     pcr[i] = (KIND == Kind::I8 && ok) ? __ldg(g.col_corr + nl) : 0;
     pb[i] = (BIAS && ok) ? __ldg(g.bias + nl) : 0.0f;
@@ -477,63 +503,70 @@ __device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
   const bool ok = mbar_wait(c.full_bar, c.full_parity, g.watchdog, kWatchEpilogue, c.L.abort);
   tc_fence_after();
   if (!ok) return false;
-  float *scr = c.scr;
+  // per-column parameters -> prm[96 i + 0..95] (scale, correction, bias), read
+  // back as broadcasts; the previous unit's reads are complete (syncwarp)
   float *prm = c.prm;
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < kMine; ++i) {
+    if (KIND == Kind::I8) {
+      prm[96 * i + c.lane] = psw[i];
+      prm[96 * i + 32 + c.lane] = __int_as_float(pcr[i]);
+    }
+    if (BIAS) prm[96 * i + 64 + c.lane] = pb[i];
+  }
+  uint32_t r[kMine][32];
+#pragma unroll
+  for (int i = 0; i < kMine; ++i) tmem_ld32(c.t_row + (c.part + kEpiPerQuadrant * i) * 32, r[i]);
+  tmem_ld_wait();
+  tc_fence_before();
+  __syncwarp();
+  if (c.lane == 0) {
+    if (c.empty_remote)
+      mbar_arrive_cluster(c.empty_bar);
+    else
+      mbar_arrive(c.empty_bar);
+  }
+  float *scr = c.scr;
   const bool tma = MODE != 3 && g.tma_store;
   const int mbase = c.row0 + c.q * 32;
 #pragma unroll
   for (int i = 0; i < kMine; ++i) {
-    const int ch = c.part + kEpiPerQuadrant * i;
-    if (ch >= kChunks) break;
-    uint32_t r[32];
-    tmem_ld32(c.t_row + ch * 32, r);
-    const int n0 = c.w.tb * BN + ch * 32;
+    const int n0 = c.w.tb * BN + (c.part + kEpiPerQuadrant * i) * 32;
     const int nl = n0 + c.lane;
     const bool nl_ok = nl < g.N;
-    // per-column parameters of this chunk -> prm[0..95], read back as broadcasts
-    __syncwarp();
-    if (KIND == Kind::I8) {
-      prm[c.lane] = psw[i];
-      prm[32 + c.lane] = __int_as_float(pcr[i]);
-    }
-    if (BIAS) prm[64 + c.lane] = pb[i];
-    tmem_ld_wait();
-    __syncwarp();
-    float v[32];
+    const float *pi = prm + 96 * i;
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f), c4 = s4, b4 = s4;
       if (KIND == Kind::I8) {
-        s4 = *reinterpret_cast<const float4 *>(prm + j);
-        c4 = *reinterpret_cast<const float4 *>(prm + 32 + j);
+        s4 = *reinterpret_cast<const float4 *>(pi + j);
+        c4 = *reinterpret_cast<const float4 *>(pi + 32 + j);
       }
-      if (BIAS) b4 = *reinterpret_cast<const float4 *>(prm + 64 + j);
-      v[j + 0] = finish<KIND, MODE, BIAS>(r[j + 0], __float_as_int(c4.x), s4.x, rs, b4.x);
-      v[j + 1] = finish<KIND, MODE, BIAS>(r[j + 1], __float_as_int(c4.y), s4.y, rs, b4.y);
-      v[j + 2] = finish<KIND, MODE, BIAS>(r[j + 2], __float_as_int(c4.z), s4.z, rs, b4.z);
-      v[j + 3] = finish<KIND, MODE, BIAS>(r[j + 3], __float_as_int(c4.w), s4.w, rs, b4.w);
+      if (BIAS) b4 = *reinterpret_cast<const float4 *>(pi + 64 + j);
+      r[i][j + 0] = __float_as_uint(finish<KIND, MODE, BIAS>(r[i][j + 0], __float_as_int(c4.x), s4.x, rs, b4.x));
+      r[i][j + 1] = __float_as_uint(finish<KIND, MODE, BIAS>(r[i][j + 1], __float_as_int(c4.y), s4.y, rs, b4.y));
+      r[i][j + 2] = __float_as_uint(finish<KIND, MODE, BIAS>(r[i][j + 2], __float_as_int(c4.z), s4.z, rs, b4.z));
+      r[i][j + 3] = __float_as_uint(finish<KIND, MODE, BIAS>(r[i][j + 3], __float_as_int(c4.w), s4.w, rs, b4.w));
     }
-    __syncwarp();
     if (MODE == 3) {
       // channel-major out[n*ldo + m]: lanes hold consecutive m -> coalesced
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const int n = n0 + j;
-        if (m_ok && n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = v[j];
+        if (m_ok && n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = __uint_as_float(r[i][j]);
       }
     } else {
       // row-major: stage the 32 x 32 tile (128-byte swizzle), then one TMA
       // store, or (unaligned output) coalesced 128-byte row stores.  The
       // previous chunk's TMA store must be done reading the staging tile.
-      if (tma) {
-        if (c.lane == 0) bulk_wait_read_all();
-        __syncwarp();
-      }
+      if (tma && c.lane == 0) bulk_wait_read_all();
+      __syncwarp();
       char *row = reinterpret_cast<char *>(scr) + c.lane * 128;
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4)
-        *reinterpret_cast<float4 *>(row + ((j4 ^ (c.lane & 7)) << 4)) =
-            make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+        *reinterpret_cast<uint4 *>(row + ((j4 ^ (c.lane & 7)) << 4)) =
+            make_uint4(r[i][4 * j4], r[i][4 * j4 + 1], r[i][4 * j4 + 2], r[i][4 * j4 + 3]);
       if (tma) {
         fence_proxy_async_smem();
         __syncwarp();
@@ -620,7 +653,7 @@ __device__ __forceinline__ bool epilogue_swap(const EpiCtx &c) {
     named_bar_sync(1, kEpiThreads);
   }
   if (!fin || !owner) return c_ok;
-  float *scr = c.scr;
+  float *scr = c.prm;  // the row scales of this tile's (at most 32) activation rows
   const int mrow = c.w.tb * BN + c.lane;
   scr[c.lane] = (KIND == Kind::I8 && mrow < g.M) ? __ldg(g.row_scale + mrow) : 0.0f;
   __syncwarp();
@@ -819,11 +852,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       c.full_parity = acc_ph;
       c.row0 = c.w.ta * 128;
       c.t_row = tmem_base + (static_cast<uint32_t>(c.q * 32) << 16) + buf * BN;
+      c.empty_bar = smem_u32(&L.tempty[buf]);
+      c.empty_remote = false;
       const bool ok = epilogue_dispatch<KIND, BN, SWAP>(c, g.mode, has_bias);
-      // this warp's TMEM reads of the buffer are complete (tcgen05.wait::ld)
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0 && ok) mbar_arrive(smem_u32(&L.tempty[buf]));
+      if constexpr (SWAP) {
+        // this warp's TMEM reads of the buffer are complete (tcgen05.wait::ld);
+        // the normal orientation releases the buffer inside its epilogue
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0 && ok) mbar_arrive(c.empty_bar);
+      }
     }
     if (lane == 0) bulk_wait_all();  // output stores of this warp have landed
   }
@@ -1013,11 +1051,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       c.full_parity = (iter >> 1) & 1u;
       c.row0 = c.w.ta * 256 + static_cast<int>(rank) * 128;
       c.t_row = tmem_base + (static_cast<uint32_t>(c.q * 32) << 16) + buf * BN;
+      c.empty_bar = mapa_shared(smem_u32(&L.tempty[buf]), 0);
+      c.empty_remote = true;
+      // the epilogue hands the buffer back to the leader once its TMEM reads are done
       const bool ok = epilogue_dispatch<KIND, BN, false>(c, g.mode, has_bias);
       if (!ok) st_shared_cluster(peer_abort, 1u);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0 && ok) mbar_arrive_cluster(mapa_shared(smem_u32(&L.tempty[buf]), 0));
     }
     if (lane == 0) bulk_wait_all();
   }
