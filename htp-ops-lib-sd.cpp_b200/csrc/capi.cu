@@ -161,7 +161,7 @@ struct htpg_weights {
   Kind kind = Kind::I8;
   int k = 0, ncols = 0, n0 = 0, n_total = 0;
   int device = 0;
-  void *wk = nullptr;          // [ncols][k] int8 / fp16
+  void *wk = nullptr;          // k-block-major [KB][ncols][128 B] int8 / fp16
   float *sw = nullptr;         // I8: [ncols] column scales
   int32_t *corr = nullptr;     // I8: [ncols] zero-point correction differences
   float *inverse = nullptr;    // I8: [k], nullptr when every entry is 1.0
@@ -174,8 +174,11 @@ int weight_map(htpg_weights *w, int box_rows, const CUtensorMap **out) {
   auto it = w->maps.find(box_rows);
   if (it == w->maps.end()) {
     CUtensorMap m;
-    const size_t pitch = static_cast<size_t>(w->k) * (w->kind == Kind::I8 ? 1 : 2);
-    const int rc = make_map(&m, w->wk, w->kind, w->k, w->ncols, pitch, box_rows);
+    // rows kb * ncols + n of 128 bytes; a box is box_rows consecutive columns
+    // of one k-block.  Boxes of a partial last column tile run into the next
+    // k-block's rows: those columns are outside [0, ncols) and never stored.
+    const int rows = kblocks(w->kind, w->k) * w->ncols;
+    const int rc = make_map(&m, w->wk, w->kind, w->kind == Kind::I8 ? 128 : 64, rows, 128u, box_rows);
     if (rc != HTPG_OK) return rc;
     it = w->maps.emplace(box_rows, m).first;
   }
@@ -369,7 +372,8 @@ extern "C" int htpg_w8a8_weights_create(const void *constants, int k, int n, int
   w->n_total = n;
   w->device = d->ordinal;
   uint32_t *flag = nullptr;
-  bool ok = cudaMalloc(&w->wk, static_cast<size_t>(n_cols) * k) == cudaSuccess &&
+  const size_t wk_bytes = kblock_bytes(Kind::I8, k, n_cols);
+  bool ok = cudaMalloc(&w->wk, wk_bytes) == cudaSuccess &&
             cudaMalloc(&w->sw, 4u * n_cols) == cudaSuccess &&
             cudaMalloc(&w->corr, 4u * n_cols) == cudaSuccess &&
             cudaMalloc(&w->inverse, 4u * k) == cudaSuccess && cudaMalloc(&flag, 4) == cudaSuccess;
@@ -379,7 +383,10 @@ extern "C" int htpg_w8a8_weights_create(const void *constants, int k, int n, int
     htpg_weights_destroy(w);
     return HTPG_ENOMEM;
   }
-  cudaError_t e = launch_repack_w8(static_cast<int8_t *>(w->wk), blob + h.weight_offset, k, n0, n_cols, st);
+  // the zero padding of a partial last k-block adds nothing to the products
+  cudaError_t e = k % 128 ? cudaMemsetAsync(w->wk, 0, wk_bytes, st) : cudaSuccess;
+  if (e == cudaSuccess)
+    e = launch_repack_w8(static_cast<int8_t *>(w->wk), blob + h.weight_offset, k, n0, n_cols, st);
   if (e == cudaSuccess)
     e = launch_colsum_corr(w->corr, static_cast<const int8_t *>(w->wk),
                            reinterpret_cast<const int32_t *>(blob + h.sum_offset), k, n0, n_cols, st);
@@ -425,12 +432,15 @@ extern "C" int htpg_f16_weights_create(const uint16_t *permuted_weight, int k, i
   w->n0 = n0;
   w->n_total = n;
   w->device = d->ordinal;
-  if (cudaMalloc(&w->wk, static_cast<size_t>(n_cols) * k * 2) != cudaSuccess) {
+  const size_t wk_bytes = kblock_bytes(Kind::F16, k, n_cols);
+  if (cudaMalloc(&w->wk, wk_bytes) != cudaSuccess) {
     cudaGetLastError();
     delete w;
     return HTPG_ENOMEM;
   }
-  cudaError_t e = launch_repack_f16(static_cast<uint16_t *>(w->wk), permuted_weight, k, n0, n_cols, st);
+  cudaError_t e = k % 64 ? cudaMemsetAsync(w->wk, 0, wk_bytes, st) : cudaSuccess;
+  if (e == cudaSuccess)
+    e = launch_repack_f16(static_cast<uint16_t *>(w->wk), permuted_weight, k, n0, n_cols, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) {
     htpg_weights_destroy(w);

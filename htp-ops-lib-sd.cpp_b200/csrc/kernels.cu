@@ -64,6 +64,9 @@ __global__ void __launch_bounds__(TPR *ROWS) quantize_rows_kernel(int8_t *__rest
                                                                  int m, int k) {
   constexpr int kWarps = TPR / 32;
   __shared__ float red[ROWS][kWarps > 0 ? kWarps : 1];
+  grid_dependents_launch();  // the GEMM may start its prologue and weight prefetch
+  grid_dependency_wait();    // x may be the previous operator's output; the codes
+                             // overwrite what the previous GEMM may still be reading
   const int local_row = threadIdx.x / TPR;
   const int t = threadIdx.x % TPR;
   const int row = blockIdx.x * ROWS + local_row;
@@ -114,6 +117,9 @@ __global__ void __launch_bounds__(256) quantize_rows_reg_kernel(int8_t *__restri
                                                                 const float *__restrict__ x,
                                                                 const float *__restrict__ inverse,
                                                                 int m, int k) {
+  grid_dependents_launch();  // the GEMM may start its prologue and weight prefetch
+  grid_dependency_wait();    // x may be the previous operator's output; the codes
+                             // overwrite what the previous GEMM may still be reading
   const int row = blockIdx.x * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= m) return;
@@ -160,10 +166,28 @@ __global__ void __launch_bounds__(256) quantize_rows_reg_kernel(int8_t *__restri
   }
 }
 
+// Activation kernels are launched as programmatic dependents too: they may be
+// scheduled while the previous operator's GEMM drains and wait (griddepcontrol)
+// before reading its output.
+template <typename Fn, typename... Args>
+static cudaError_t launch_pdl(Fn fn, unsigned grid, unsigned block, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(block, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, args...);
+}
+
 template <int STEPS>
-static void launch_reg(int8_t *codes, float *scales, const float *x, const float *inverse, int m,
-                       int k, cudaStream_t st) {
-  quantize_rows_reg_kernel<STEPS><<<(m + 7) / 8, 256, 0, st>>>(codes, scales, x, inverse, m, k);
+static cudaError_t launch_reg(int8_t *codes, float *scales, const float *x, const float *inverse, int m,
+                              int k, cudaStream_t st) {
+  return launch_pdl(quantize_rows_reg_kernel<STEPS>, (m + 7) / 8, 256, st, codes, scales, x, inverse, m, k);
 }
 
 cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
@@ -171,27 +195,31 @@ cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
   // Many rows of at most 2048 elements: a register-resident warp per row.
   // Long rows or few rows: a 256-thread block per row (two passes, the
   // second from L1/L2).
+  cudaError_t e;
   if (k <= 2048 && m >= 1184) {
     switch ((k + 255) / 256) {
-      case 1: launch_reg<1>(codes, scales, x, inverse, m, k, st); break;
-      case 2: launch_reg<2>(codes, scales, x, inverse, m, k, st); break;
-      case 3: launch_reg<3>(codes, scales, x, inverse, m, k, st); break;
-      case 4: launch_reg<4>(codes, scales, x, inverse, m, k, st); break;
-      case 5: launch_reg<5>(codes, scales, x, inverse, m, k, st); break;
-      case 6: launch_reg<6>(codes, scales, x, inverse, m, k, st); break;
-      case 7: launch_reg<7>(codes, scales, x, inverse, m, k, st); break;
-      default: launch_reg<8>(codes, scales, x, inverse, m, k, st); break;
+      case 1: e = launch_reg<1>(codes, scales, x, inverse, m, k, st); break;
+      case 2: e = launch_reg<2>(codes, scales, x, inverse, m, k, st); break;
+      case 3: e = launch_reg<3>(codes, scales, x, inverse, m, k, st); break;
+      case 4: e = launch_reg<4>(codes, scales, x, inverse, m, k, st); break;
+      case 5: e = launch_reg<5>(codes, scales, x, inverse, m, k, st); break;
+      case 6: e = launch_reg<6>(codes, scales, x, inverse, m, k, st); break;
+      case 7: e = launch_reg<7>(codes, scales, x, inverse, m, k, st); break;
+      default: e = launch_reg<8>(codes, scales, x, inverse, m, k, st); break;
     }
   } else if (k >= 4096 || m < 1184) {
-    quantize_rows_kernel<256, 1><<<m, 256, 0, st>>>(codes, scales, x, inverse, m, k);
+    e = launch_pdl(quantize_rows_kernel<256, 1>, static_cast<unsigned>(m), 256, st, codes, scales, x, inverse, m, k);
   } else {
-    quantize_rows_kernel<32, 8><<<(m + 7) / 8, 256, 0, st>>>(codes, scales, x, inverse, m, k);
+    e = launch_pdl(quantize_rows_kernel<32, 8>, static_cast<unsigned>((m + 7) / 8), 256, st, codes, scales, x,
+                   inverse, m, k);
   }
-  return counted(cudaGetLastError());
+  return counted(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 __global__ void to_f16_kernel(uint16_t *__restrict__ dst, const float *__restrict__ x,
                               long long count) {
+  grid_dependents_launch();
+  grid_dependency_wait();
   const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   if (i >= count) return;
   const float4 a = __ldg(reinterpret_cast<const float4 *>(x + i));
@@ -209,8 +237,8 @@ __global__ void to_f16_kernel(uint16_t *__restrict__ dst, const float *__restric
 
 cudaError_t launch_to_f16(uint16_t *dst, const float *x, long long count, cudaStream_t st) {
   const long long threads = (count + 7) / 8;
-  to_f16_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(dst, x, count);
-  return counted(cudaGetLastError());
+  const cudaError_t e = launch_pdl(to_f16_kernel, static_cast<unsigned>((threads + 255) / 256), 256, st, dst, x, count);
+  return counted(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 // ==================================================================== repack
@@ -230,7 +258,8 @@ __global__ void repack_w8_kernel(int8_t *__restrict__ dst, const uint8_t *__rest
   const int c = static_cast<int>(i / (k / 4));
   const int kk = static_cast<int>(i % (k / 4)) * 4;
   const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(deep + deep_offset(k, n0 + c, kk)));
-  *reinterpret_cast<uint32_t *>(dst + static_cast<size_t>(c) * k + kk) = v;
+  const size_t row = static_cast<size_t>(kk / 128) * ncols + c;
+  *reinterpret_cast<uint32_t *>(dst + row * 128u + kk % 128) = v;
 }
 
 cudaError_t launch_repack_w8(int8_t *dst, const uint8_t *deep, int k, int n0, int ncols,
@@ -250,10 +279,11 @@ __global__ void colsum_corr_kernel(int32_t *__restrict__ corr, const int8_t *__r
   const int c = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (c >= ncols) return;
-  const int8_t *row = wk + static_cast<size_t>(c) * k;
   int s = 0;
   for (int i = lane * 4; i < k; i += 128) {
-    const uint32_t w = *reinterpret_cast<const uint32_t *>(row + i);
+    // k-block-major: bytes [i, i+4) of column c sit in row (i/128)*ncols + c
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(
+        wk + (static_cast<size_t>(i / 128) * ncols + c) * 128u + i % 128);
     s += static_cast<int8_t>(w & 0xff) + static_cast<int8_t>((w >> 8) & 0xff) +
          static_cast<int8_t>((w >> 16) & 0xff) + static_cast<int8_t>(w >> 24);
   }
@@ -295,7 +325,8 @@ __global__ void repack_f16_kernel(uint16_t *__restrict__ dst, const uint16_t *__
   const size_t tile = static_cast<size_t>(n / 32) * static_cast<size_t>(k / 32) + kk / 32;
   const size_t off = tile * 1024u + static_cast<size_t>(kk % 32) * 32u + static_cast<size_t>(n % 32) * 2u;
   const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(perm + off));
-  *reinterpret_cast<uint32_t *>(dst + static_cast<size_t>(c) * k + kk) = v;
+  const size_t row = static_cast<size_t>(kk / 64) * ncols + c;
+  *reinterpret_cast<uint32_t *>(dst + row * 64u + kk % 64) = v;
 }
 
 cudaError_t launch_repack_f16(uint16_t *dst, const uint16_t *perm, int k, int n0, int ncols,
@@ -363,6 +394,7 @@ constexpr int kEpiPerQuadrant = kEpiWarps / 4;
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 64 + kEpiThreads;         // warp 0 TMA, warp 1 MMA/TMEM, 2..17 epilogue
 constexpr int kRowBytes = 128;                     // one K block = one 128-byte swizzle row
+constexpr int kPrefetchBytes = 512 * 1024;         // L2 warm-up per CTA while the activation pass runs
 // Per epilogue warp: a 32 x 32 FP32 output tile staged with 128-byte swizzle
 // (row r at r*128 bytes, 16-byte chunk j at position j ^ (r & 7)), the source
 // layout of the TMA store and conflict-free for row- and column-wise access;
@@ -372,22 +404,29 @@ constexpr int kWarpParams = 192;                   // floats per epilogue warp (
 constexpr int kEpiSmem = kEpiWarps * (kWarpScratch + kWarpParams) * 4;
 
 constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block on sm_100
-// As many pipeline stages as fit beside the epilogue scratch (at most 10).
-__host__ __device__ constexpr int stages_for(int bn) {
-  return (kSmemLimit - 1024 - 256 - kEpiSmem) / ((128 + bn) * kRowBytes) < 10
-             ? (kSmemLimit - 1024 - 256 - kEpiSmem) / ((128 + bn) * kRowBytes)
-             : 10;
+constexpr int kMaxStages = 12;      // the 256-byte barrier block holds 2 x 12 + 5 barriers
+// Epilogue shared memory: swapped (small-M) tiles need only the parameter
+// slots, the normal orientation also the staging tiles of the TMA stores.
+__host__ __device__ constexpr int epi_smem_for(bool swap) {
+  return swap ? kEpiWarps * kWarpParams * 4 : kEpiSmem;
+}
+// As many pipeline stages as fit beside the epilogue's shared memory.
+__host__ __device__ constexpr int stages_for(int bn, bool swap = false) {
+  return (kSmemLimit - 1024 - 256 - epi_smem_for(swap)) / ((128 + bn) * kRowBytes) < kMaxStages
+             ? (kSmemLimit - 1024 - 256 - epi_smem_for(swap)) / ((128 + bn) * kRowBytes)
+             : kMaxStages;
 }
 __host__ __device__ constexpr int tmem_cols_for(int bn) {
   return 2 * bn <= 32 ? 32 : 2 * bn <= 64 ? 64 : 2 * bn <= 128 ? 128 : 2 * bn <= 256 ? 256 : 512;
 }
-__host__ __device__ constexpr size_t smem_bytes_for(int bn) {
-  return 1024 /* alignment slack */ + static_cast<size_t>(stages_for(bn)) * (128 + bn) * kRowBytes +
-         static_cast<size_t>(kEpiSmem) + 256 /* barriers, tmem slot, flags */;
+__host__ __device__ constexpr size_t smem_bytes_for(int bn, bool swap = false) {
+  return 1024 /* alignment slack */ + static_cast<size_t>(stages_for(bn, swap)) * (128 + bn) * kRowBytes +
+         static_cast<size_t>(epi_smem_for(swap)) + 256 /* barriers, tmem slot, flags */;
 }
+static_assert((2 * kMaxStages + 5) * 8 + 12 <= 256, "barrier block");
 static_assert(smem_bytes_for(256) <= kSmemLimit && smem_bytes_for(128) <= kSmemLimit &&
                   smem_bytes_for(64) <= kSmemLimit && smem_bytes_for(32) <= kSmemLimit &&
-                  smem_bytes_for(16) <= kSmemLimit,
+                  smem_bytes_for(16, true) <= kSmemLimit && smem_bytes_for(32, true) <= kSmemLimit,
               "shared memory budget");
 
 struct SmemLayout {
@@ -401,7 +440,7 @@ struct SmemLayout {
   volatile uint32_t *abort;  // sticky: some wait of this CTA gave up
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool SWAP = false>
 __device__ __forceinline__ SmemLayout carve(uint8_t *raw) {
   SmemLayout L;
   uint8_t *p = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -409,8 +448,8 @@ __device__ __forceinline__ SmemLayout carve(uint8_t *raw) {
   p += STAGES * 128 * kRowBytes;
   L.b = p;
   p += STAGES * BN * kRowBytes;
-  L.scratch = reinterpret_cast<float *>(p);
-  p += kEpiWarps * kWarpScratch * 4;
+  L.scratch = reinterpret_cast<float *>(p);  // swapped tiles stage nothing
+  if (!SWAP) p += kEpiWarps * kWarpScratch * 4;
   L.params = reinterpret_cast<float *>(p);
   p += kEpiWarps * kWarpParams * 4;
   uint64_t *bars = reinterpret_cast<uint64_t *>(p);
@@ -706,7 +745,7 @@ template <Kind KIND, int BN, bool SWAP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmOut, const KernelParams P) {
-  constexpr int STAGES = stages_for(BN);
+  constexpr int STAGES = stages_for(BN, SWAP);
   constexpr int TCOLS = tmem_cols_for(BN);
   constexpr uint32_t kStageBytes = (128 + BN) * kRowBytes;
   constexpr int kElemsPerRow = KIND == Kind::I8 ? 128 : 64;
@@ -715,11 +754,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(!SWAP || BN <= 32, "swapped tiles hold at most 32 activation rows");
 
   extern __shared__ uint8_t smem_raw[];
-  const SmemLayout L = carve<BN, STAGES>(smem_raw);
+  const SmemLayout L = carve<BN, STAGES, SWAP>(smem_raw);
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   const GemmArgs &g = P.a;
   uint32_t *wd = g.watchdog;
+  // the next operator's kernels may be scheduled now (they wait for this one
+  // before they read anything it writes)
+  grid_dependents_launch();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -748,13 +790,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
+      // The weights do not depend on the activation pass that may still be
+      // running: put this CTA's first weight tiles into the ring (and warm the
+      // L2 with the next ones) before waiting for it.
+      int pre = 0;  // leading stages of the first unit whose weight tile is in flight
+      if (blockIdx.x < P.units) {
+        const Unit w = decode_unit(blockIdx.x, P.tiles_b, P.splits);
+        const int kb0 = w.ks * P.kb_per_split;
+        const int kb1 = min(kb0 + P.kb_per_split, P.kb_total);
+        pre = min(STAGES, kb1 - kb0);
+        for (int i = 0; i < pre; ++i) {
+          const uint32_t fb = smem_u32(&L.full[i]);
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          if (SWAP)
+            tma_load_2d(smem_u32(L.a + i * 128 * kRowBytes), &tmA, fb, 0, (kb0 + i) * g.N + w.ta * 128);
+          else
+            tma_load_2d(smem_u32(L.b + i * BN * kRowBytes), &tmB, fb, 0, (kb0 + i) * g.N + w.tb * BN);
+        }
+        const int kb2 = min(kb1, kb0 + kPrefetchBytes / ((SWAP ? 128 : BN) * kRowBytes));
+        for (int kb = kb0 + pre; kb < kb2; ++kb) {
+          if (SWAP)
+            tma_prefetch_l2_2d(&tmA, 0, kb * g.N + w.ta * 128);
+          else
+            tma_prefetch_l2_2d(&tmB, 0, kb * g.N + w.tb * BN);
+        }
+      }
+      grid_dependency_wait();
       int s = 0;
       uint32_t ph = 0;
       int last_phase[STAGES];
 #pragma unroll
-      for (int i = 0; i < STAGES; ++i) last_phase[i] = -1;
+      for (int i = 0; i < STAGES; ++i) last_phase[i] = i < pre ? 0 : -1;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < P.units; u += gridDim.x) {
+      bool first = true;
+      for (int u = blockIdx.x; ok && u < P.units; u += gridDim.x, first = false) {
         const Unit w = decode_unit(u, P.tiles_b, P.splits);
         const int kb0 = w.ks * P.kb_per_split;
         const int kb1 = min(kb0 + P.kb_per_split, P.kb_total);
@@ -764,9 +833,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t fb = smem_u32(&L.full[s]);
-          mbar_arrive_expect_tx(fb, kStageBytes);
-          tma_load_2d(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, kb * kElemsPerRow, w.ta * 128);
-          tma_load_2d(smem_u32(L.b + s * BN * kRowBytes), &tmB, fb, kb * kElemsPerRow, w.tb * BN);
+          // the weight operand (A when swapped, else B) is k-block-major:
+          // its box starts at row kb * N + first column
+          const bool weight_done = first && kb - kb0 < pre;
+          if (!weight_done) mbar_arrive_expect_tx(fb, kStageBytes);
+          if (SWAP) {
+            if (!weight_done) tma_load_2d(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, 0, kb * g.N + w.ta * 128);
+            tma_load_2d(smem_u32(L.b + s * BN * kRowBytes), &tmB, fb, kb * kElemsPerRow, w.tb * BN);
+          } else {
+            tma_load_2d(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, kb * kElemsPerRow, w.ta * 128);
+            if (!weight_done) tma_load_2d(smem_u32(L.b + s * BN * kRowBytes), &tmB, fb, 0, kb * g.N + w.tb * BN);
+          }
           last_phase[s] = static_cast<int>(ph);
           if (++s == STAGES) {
             s = 0;
@@ -783,6 +860,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      grid_dependency_wait();  // bounded waits start once the operands can exist
       int s = 0;
       uint32_t ph = 0;
       uint32_t iter = 0;
@@ -840,6 +918,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     c.scr = L.scratch + (warp - 2) * kWarpScratch;
     c.prm = L.params + (warp - 2) * kWarpParams;
     const bool has_bias = g.bias != nullptr;
+    grid_dependency_wait();  // row scales come from the activation pass
     uint32_t iter = 0;
     // No early exit: all epilogue warps run the same iterations so their
     // named barriers always match; after a failed wait the unit's work is
@@ -918,6 +997,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const uint32_t peer_abort = mapa_shared(smem_u32(const_cast<uint32_t *>(L.abort)), rank ^ 1u);
+  grid_dependents_launch();  // the next operator's kernels may be scheduled now
   // a failed wait also tells the peer CTA, whose waits then return at once
   auto wait = [&](uint32_t bar, uint32_t parity, uint32_t bit) {
     const bool ok = mbar_wait(bar, parity, wd, bit, L.abort);
@@ -953,13 +1033,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
+      // this CTA's half of its first weight tile goes into the ring (the next
+      // k-blocks into the L2) before waiting for the activation pass
+      int pre = 0;
+      if (pair < P.units) {
+        const Unit w = decode_unit(pair, P.tiles_b, 1);
+        pre = min(STAGES, P.kb_total);
+        for (int i = 0; i < pre; ++i) {
+          const uint32_t fb_local = smem_u32(&L.full[i]);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);
+          tma_load_2d_pair(smem_u32(L.b + i * BH * kRowBytes), &tmB, mapa_shared(fb_local, 0), 0,
+                           i * g.N + w.tb * BN + static_cast<int>(rank) * BH);
+        }
+        const int kb2 = min(P.kb_total, kPrefetchBytes / (BH * kRowBytes));
+        for (int kb = pre; kb < kb2; ++kb)
+          tma_prefetch_l2_2d(&tmB, 0, kb * g.N + w.tb * BN + static_cast<int>(rank) * BH);
+      }
+      grid_dependency_wait();
       int s = 0;
       uint32_t ph = 0;
       int last_phase[STAGES];
 #pragma unroll
-      for (int i = 0; i < STAGES; ++i) last_phase[i] = -1;
+      for (int i = 0; i < STAGES; ++i) last_phase[i] = i < pre ? 0 : -1;
       bool ok = true;
-      for (int u = pair; ok && u < P.units; u += npairs) {
+      bool first = true;
+      for (int u = pair; ok && u < P.units; u += npairs, first = false) {
         const Unit w = decode_unit(u, P.tiles_b, 1);
         for (int kb = 0; kb < P.kb_total; ++kb) {
           if (!wait(smem_u32(&L.empty[s]), ph ^ 1u, kWatchProducer)) {
@@ -967,12 +1065,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t fb_local = smem_u32(&L.full[s]);
-          if (leader) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);
+          const bool weight_done = first && kb < pre;
+          if (leader && !weight_done) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);
           const uint32_t fb = mapa_shared(fb_local, 0);
           tma_load_2d_pair(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, kb * kElemsPerRow,
                            w.ta * 256 + static_cast<int>(rank) * 128);
-          tma_load_2d_pair(smem_u32(L.b + s * BH * kRowBytes), &tmB, fb, kb * kElemsPerRow,
-                           w.tb * BN + static_cast<int>(rank) * BH);
+          if (!weight_done)
+            tma_load_2d_pair(smem_u32(L.b + s * BH * kRowBytes), &tmB, fb, 0,
+                             kb * g.N + w.tb * BN + static_cast<int>(rank) * BH);
           last_phase[s] = static_cast<int>(ph);
           if (++s == STAGES) {
             s = 0;
@@ -990,6 +1090,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
     if (lane == 0 && leader) {
+      grid_dependency_wait();  // bounded waits start once the operands can exist
       int s = 0;
       uint32_t ph = 0;
       uint32_t iter = 0;
@@ -1043,6 +1144,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     c.scr = L.scratch + (warp - 2) * kWarpScratch;
     c.prm = L.params + (warp - 2) * kWarpParams;
     const bool has_bias = g.bias != nullptr;
+    grid_dependency_wait();  // row scales come from the activation pass
     uint32_t iter = 0;
     for (int u = pair; u < P.units; u += npairs, ++iter) {
       c.w = decode_unit(u, P.tiles_b, 1);
@@ -1136,7 +1238,7 @@ GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms) {
   }
   p.units = p.tiles_a * p.tiles_b * p.splits;
   p.grid = p.units < num_sms ? p.units : num_sms;
-  p.smem = smem_bytes_for(p.bn);
+  p.smem = smem_bytes_for(p.bn, p.swap);
   return p;
 }
 
@@ -1147,6 +1249,25 @@ size_t splitk_count_bytes(const GemmPlan &p) {
   return p.splits > 1 ? static_cast<size_t>(p.tiles_a) * p.tiles_b * 4 : 0;
 }
 
+// GEMM launch with programmatic stream serialisation: its prologue (barriers,
+// TMEM, descriptor and L2 weight prefetch) overlaps the activation pass.
+template <typename Fn>
+static cudaError_t launch_dependent(Fn fn, int grid, size_t smem, cudaStream_t st, const CUtensorMap &tmA,
+                                    const CUtensorMap &tmB, const CUtensorMap &tmOut, const KernelParams &P) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, tmA, tmB, tmOut, P);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 template <Kind KIND, int BN, bool SWAP>
 static cudaError_t launch_one(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
                               const CUtensorMap &tmOut, const GemmArgs &a, cudaStream_t st) {
@@ -1154,7 +1275,7 @@ static cudaError_t launch_one(const GemmPlan &p, const CUtensorMap &tmA, const C
   static bool configured[64] = {};  // per instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
-  const size_t smem = smem_bytes_for(BN);
+  const size_t smem = smem_bytes_for(BN, SWAP);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1170,8 +1291,7 @@ static cudaError_t launch_one(const GemmPlan &p, const CUtensorMap &tmA, const C
   P.kb_total = p.kb_total;
   P.kb_per_split = p.kb_per_split;
   P.units = p.units;
-  fn<<<p.grid, kThreads, smem, st>>>(tmA, tmB, tmOut, P);
-  return counted(cudaGetLastError());
+  return counted(launch_dependent(fn, p.grid, smem, st, tmA, tmB, tmOut, P));
 }
 
 template <Kind KIND, int BN>
@@ -1197,8 +1317,8 @@ static cudaError_t launch_pair(const GemmPlan &p, const CUtensorMap &tmA, const 
   P.kb_total = p.kb_total;
   P.kb_per_split = p.kb_total;
   P.units = p.units;
-  fn<<<p.grid, kThreads, smem, st>>>(tmA, tmB, tmOut, P);  // grid is a multiple of the pair
-  return counted(cudaGetLastError());
+  // grid is a multiple of the pair (cluster dimensions are compiled in)
+  return counted(launch_dependent(fn, p.grid, smem, st, tmA, tmB, tmOut, P));
 }
 
 cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,

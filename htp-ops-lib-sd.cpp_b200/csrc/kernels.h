@@ -65,6 +65,14 @@ cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtenso
 cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
                                  const float *inverse, int m, int k, cudaStream_t st);
 cudaError_t launch_to_f16(uint16_t *dst, const float *x, long long count, cudaStream_t st);
+// Prepared weights are stored k-block-major: block kb (128 bytes of K: 128
+// INT8 or 64 FP16 elements) of column n is row kb*ncols + n of a [KB*ncols][128 B]
+// array, so the weight tile of one pipeline stage (consecutive columns, one
+// k-block) is one contiguous run in HBM.  The last block is zero-padded.
+inline int kblocks(Kind kind, int k) { return (k + (kind == Kind::I8 ? 127 : 63)) / (kind == Kind::I8 ? 128 : 64); }
+inline size_t kblock_bytes(Kind kind, int k, int ncols) {
+  return static_cast<size_t>(kblocks(kind, k)) * static_cast<size_t>(ncols) * 128u;
+}
 cudaError_t launch_repack_w8(int8_t *dst, const uint8_t *deep, int k, int n0, int ncols,
                              cudaStream_t st);
 cudaError_t launch_colsum_corr(int32_t *corr, const int8_t *wk, const int32_t *sums, int k,

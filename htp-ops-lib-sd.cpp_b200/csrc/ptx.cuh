@@ -82,6 +82,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
+// Warm the L2 with one box of a 2-D tensor map (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+               :
+               : "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y)
+               : "memory");
+}
 
 // 2-D tiled store of one box from shared memory (bulk-group completion).
 // Rows / columns outside the tensor map's extent are not written.
@@ -117,6 +124,14 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start while the kernel before it in the stream still runs;
+// griddepcontrol.wait returns once that kernel has completed and its writes
+// are visible (at once when there is no such kernel).  launch_dependents lets
+// the next kernel start early.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Hardware tanh approximation (PTX tanh.approx.f32, relative error about 2^-11).
 __device__ __forceinline__ float tanh_approx(float x) {
   float y;
