@@ -160,14 +160,17 @@ def _w8a8_operands(torch, htpg, dev, m, k, n, seed, outlier_p, bias):
     return x, htpg.w8a8_weights(blob_dev, k, n), (b if bias else None), blob_dev
 
 
-def suite(torch, L, htpg, dev, flush, reps=20):
+def suite(torch, L, htpg, dev, flush, reps=20, only=None):
     """Per-config device times of the other BASELINE configs (one GPU): C1,
     C2, the four C3 DiT linears and the six C5 decode linears.  Each run is the
     whole operator (activation pass + GEMM), timed with CUDA events on the
     launching stream, the L2 flushed (256 MiB written and read back) before
     every run, the stream held by a bounded sleep kernel while the host queues
     the runs; the median of `reps` runs.  `host_latency_us` is one call on an
-    idle GPU, host work included.  Algorithmic bytes: W8A8 4MK + KN + 4N + 4MN
+    idle GPU, host work included.  For the decode shapes `stream_us` is the
+    per-linear time of back-to-back runs over six operand sets (352 MB of
+    weights, more than the L2), the throughput a sequence of decode linears
+    sees.  Algorithmic bytes: W8A8 4MK + KN + 4N + 4MN
     (+4N bias); F16 4MK + 2KN + 4N + 4MN."""
     import numpy as np
     hbm, bf16, _, _ = peaks()
@@ -187,21 +190,42 @@ def suite(torch, L, htpg, dev, flush, reps=20):
             fn()
             torch.cuda.synchronize()
             lat.append((time.perf_counter() - t0) * 1e6)
-        L.htpg_phase_timing(1)
-        htpg.phase_timing_read()
         # device time: a bounded sleep kernel holds the stream while the host
         # queues every run, so no run waits for its own launch
-        torch.cuda._sleep(SLEEP_CYCLES)
-        for a, b in ev:
-            flush()
-            a.record(stream)
-            fn()
-            b.record(stream)
-        torch.cuda.synchronize()
+        def pass_us():
+            torch.cuda._sleep(SLEEP_CYCLES)
+            for a, b in ev:
+                flush()
+                a.record(stream)
+                fn()
+                b.record(stream)
+            torch.cuda.synchronize()
+            return statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
+        us = pass_us()
+        # the split between the activation pass and the GEMM comes from a second
+        # pass with the library's phase events (which serialise the two kernels)
+        L.htpg_phase_timing(1)
+        htpg.phase_timing_read()
+        pass_us()
         L.htpg_phase_timing(0)
         act_ms, gemm_ms, runs = htpg.phase_timing_read()
-        us = statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
         return us, act_ms * 1e3 / max(runs, 1), gemm_ms * 1e3 / max(runs, 1), statistics.median(lat)
+
+    def stream_us(fns):
+        """Back-to-back runs over rotating operand sets larger than the L2 (no
+        flush, no events between runs): the per-operator time of a sequence of
+        linears, each reading its weight from HBM."""
+        for f in fns:
+            f()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        runs = 8 * len(fns)
+        torch.cuda._sleep(SLEEP_CYCLES)
+        a.record(stream)
+        for i in range(runs):
+            fns[i % len(fns)]()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) * 1e3 / runs
 
     def record(name, m, k, n, timing, nbytes, peak_ops):
         us, act_us, gemm_us, lat_us = timing
@@ -214,36 +238,52 @@ def suite(torch, L, htpg, dev, flush, reps=20):
                      "bound": "tensor" if t_tc >= t_hbm else "hbm",
                      "roofline_frac": max(t_tc, t_hbm) / (us * 1e-6)}
 
-    def w8a8_case(name, m, k, n, seed, outlier_p, mode, bias):
+    def w8a8_case(name, m, k, n, seed, outlier_p, mode, bias, sets=1):
+        if only and name != only:
+            return
         x, w, b, keep = _w8a8_operands(torch, htpg, dev, m, k, n, seed, outlier_p, bias)
         out = torch.empty(m, n, dtype=torch.float32, device=dev)
         tm = timed(lambda: htpg.check(htpg.w8a8_run(w, out, x, b, mode=mode), name))
-        record(name, m, k, n, tm, 4 * m * k + k * n + 4 * n + 4 * m * n + (4 * n if bias else 0), int8_peak)
+        nbytes = 4 * m * k + k * n + 4 * n + 4 * m * n + (4 * n if bias else 0)
+        record(name, m, k, n, tm, nbytes, int8_peak)
+        if sets > 1:
+            ops = [(x, w, b)] + [_w8a8_operands(torch, htpg, dev, m, k, n, seed + 0x100 * i, outlier_p, bias)[:3]
+                                 for i in range(1, sets)]
+            t = stream_us([lambda o=o: htpg.check(htpg.w8a8_run(o[1], out, o[0], o[2], mode=mode), name)
+                           for o in ops])
+            res[name]["stream_us"] = t
+            res[name]["stream_GBps"] = nbytes / t / 1e3
+            res[name]["stream_hbm_frac"] = nbytes / t / 1e3 / hbm
+            del ops
         del keep
 
     w8a8_case("C1", 256, 1152, 4608, 0x5EED0000, 0.01, 0, False)
     # C2: CLIP fc1 through the FP16 path, bias + QuickGELU
     m, k, n = 77, 768, 3072
-    g = torch.Generator(device=dev)
-    g.manual_seed(0x5EED0001)
-    x = torch.randn(m, k, device=dev, generator=g)
-    wf = (torch.randn(k, n, device=dev, generator=g) * 0.02).half()
-    bias = torch.randn(n, device=dev, generator=g) * 0.01
-    wperm = torch.from_numpy(htpg.pack_f16_permuted(wf.cpu().numpy().view(np.uint16)).view(np.int16)).to(dev)
-    wh = htpg.f16_weights(wperm, k, n)
-    out = torch.empty(m, n, dtype=torch.float32, device=dev)
-    tm = timed(lambda: htpg.check(htpg.f16_run(wh, out, x, bias, mode=2), "C2"))
-    record("C2", m, k, n, tm, 4 * m * k + 2 * k * n + 4 * n + 4 * m * n, bf16)
-    del wh, wperm
+    if only and only != "C2":
+        m = 0
+    if m:
+        g = torch.Generator(device=dev)
+        g.manual_seed(0x5EED0001)
+        x = torch.randn(m, k, device=dev, generator=g)
+        wf = (torch.randn(k, n, device=dev, generator=g) * 0.02).half()
+        bias = torch.randn(n, device=dev, generator=g) * 0.01
+        wperm = torch.from_numpy(htpg.pack_f16_permuted(wf.cpu().numpy().view(np.uint16)).view(np.int16)).to(dev)
+        wh = htpg.f16_weights(wperm, k, n)
+        out = torch.empty(m, n, dtype=torch.float32, device=dev)
+        tm = timed(lambda: htpg.check(htpg.f16_run(wh, out, x, bias, mode=2), "C2"))
+        record("C2", m, k, n, tm, 4 * m * k + 2 * k * n + 4 * n + 4 * m * n, bf16)
+        del wh, wperm
     # C3: DiT block linears at M=4096
     for name, k, n, mode, b in (("C3_qkv", 1536, 4608, 0, False), ("C3_out", 1536, 1536, 0, False),
                                 ("C3_fc1", 1536, 6144, 1, True), ("C3_fc2", 6144, 1536, 0, True)):
         w8a8_case(name, 4096, k, n, 0x5EED0002 + k + n, 0.005, mode, b)
-    res["C3_stack_us"] = sum(res[c]["us"] for c in ("C3_qkv", "C3_out", "C3_fc1", "C3_fc2"))
+    if not only:
+        res["C3_stack_us"] = sum(res[c]["us"] for c in ("C3_qkv", "C3_out", "C3_fc1", "C3_fc2"))
     # C5: decode shapes, no epilogue
     for m in (1, 4, 16):
         for name, k, n in (("up", 4096, 14336), ("down", 14336, 4096)):
-            w8a8_case(f"C5_{name}_M{m}", m, k, n, 0x5EED0004 + m + k, 0.0, 0, False)
+            w8a8_case(f"C5_{name}_M{m}", m, k, n, 0x5EED0004 + m + k, 0.0, 0, False, sets=6)
     return res
 
 
@@ -262,6 +302,8 @@ def cpu_sample(k, n, rows, reps=1):
         O.lib("native")
     except Exception:
         kind = "omp"
+    # every host thread, whatever OMP_NUM_THREADS the launcher exported
+    O.lib(kind).orc_set_threads(len(os.sched_getaffinity(0)))
     key = (rows, k, n)
     if key not in _CPU_CASES:
         _CPU_CASES[key] = O.make_w8a8(3, "C4-sample", rows, k, n, 0.005, True, 1)
@@ -380,6 +422,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-suite", action="store_true",
                     help="skip the per-config C1/C2/C3/C5 device times (one GPU only)")
+    ap.add_argument("--suite-only", default=None,
+                    help="run only this suite config (e.g. C5_up_M16) and print its timings; for profiling")
     ap.add_argument("--m", type=int, default=M_C4,
                     help="token rows; smaller values only for profiling captures (workload C4-M<m>)")
     ap.add_argument("--settle", type=float, default=1.5,
@@ -401,6 +445,11 @@ def main():
     dev = torch.device("cuda", local)
     L = htpg.lib()
     htpg.check(L.htpg_init(local), "htpg_init")
+    if args.suite_only:
+        res = suite(torch, L, htpg, dev, L2Flush(torch, dev), only=args.suite_only)
+        htpg.check(htpg.check_device(), "watchdog")
+        print(json.dumps({"suite": res}), flush=True)
+        return
     dist = None
     if world > 1:
         import datetime

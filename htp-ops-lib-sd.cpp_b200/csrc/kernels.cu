@@ -166,6 +166,63 @@ __global__ void __launch_bounds__(256) quantize_rows_reg_kernel(int8_t *__restri
   }
 }
 
+// Few long rows (decode): a 512-thread block per row that keeps the whole row
+// in registers (J float4 per thread, J * 2048 >= k), so the row is read from
+// HBM once, with all loads in flight together, and reduced across the block.
+constexpr int kWideThreads = 512;
+template <int J>
+__global__ void __launch_bounds__(kWideThreads) quantize_rows_wide_kernel(int8_t *__restrict__ codes,
+                                                                       float *__restrict__ scales,
+                                                                       const float *__restrict__ x,
+                                                                       const float *__restrict__ inverse,
+                                                                       int m, int k) {
+  __shared__ float red[kWideThreads / 32];
+  grid_dependents_launch();  // the GEMM may start its prologue and weight prefetch
+  grid_dependency_wait();    // x may be the previous operator's output; the codes
+                             // overwrite what the previous GEMM may still be reading
+  const int row = blockIdx.x;
+  const int t = threadIdx.x;
+  const float *xr = x + static_cast<size_t>(row) * k;
+  float v[J][4];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = (j * kWideThreads + t) * 4;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < k) a = __ldg(reinterpret_cast<const float4 *>(xr + c));
+    v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = (j * kWideThreads + t) * 4;
+    if (c < k) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[j][i] = scaled_input(v[j][i], inverse, c + i);
+        amax = fmaxf(amax, fabsf(v[j][i]));
+      }
+    }
+  }
+  amax = warp_max(amax);
+  if ((t & 31) == 0) red[t >> 5] = amax;
+  __syncthreads();
+  amax = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kWideThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+  const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+  const float inv_scale = __fdiv_rn(1.0f, scale);
+  if (t == 0) scales[row] = scale;
+  int8_t *cr = codes + static_cast<size_t>(row) * k;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = (j * kWideThreads + t) * 4;
+    if (c < k)
+      *reinterpret_cast<uint32_t *>(cr + c) =
+          pack4(quant_code(v[j][0], inv_scale), quant_code(v[j][1], inv_scale), quant_code(v[j][2], inv_scale),
+                quant_code(v[j][3], inv_scale));
+  }
+}
+
 // Activation kernels are launched as programmatic dependents too: they may be
 // scheduled while the previous operator's GEMM drains and wait (griddepcontrol)
 // before reading its output.
@@ -196,7 +253,20 @@ cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
   // Long rows or few rows: a 256-thread block per row (two passes, the
   // second from L1/L2).
   cudaError_t e;
-  if (k <= 2048 && m >= 1184) {
+  if (m <= 64) {
+    // decode shapes: one block per row, the row in registers
+    const unsigned g = static_cast<unsigned>(m);
+    switch ((k + 2047) / 2048) {
+      case 1: e = launch_pdl(quantize_rows_wide_kernel<1>, g, kWideThreads, st, codes, scales, x, inverse, m, k); break;
+      case 2: e = launch_pdl(quantize_rows_wide_kernel<2>, g, kWideThreads, st, codes, scales, x, inverse, m, k); break;
+      case 3: e = launch_pdl(quantize_rows_wide_kernel<3>, g, kWideThreads, st, codes, scales, x, inverse, m, k); break;
+      case 4: e = launch_pdl(quantize_rows_wide_kernel<4>, g, kWideThreads, st, codes, scales, x, inverse, m, k); break;
+      case 5: e = launch_pdl(quantize_rows_wide_kernel<5>, g, kWideThreads, st, codes, scales, x, inverse, m, k); break;
+      case 6: e = launch_pdl(quantize_rows_wide_kernel<6>, g, kWideThreads, st, codes, scales, x, inverse, m, k); break;
+      case 7: e = launch_pdl(quantize_rows_wide_kernel<7>, g, kWideThreads, st, codes, scales, x, inverse, m, k); break;
+      default: e = launch_pdl(quantize_rows_wide_kernel<8>, g, kWideThreads, st, codes, scales, x, inverse, m, k); break;
+    }
+  } else if (k <= 2048 && m >= 1184) {
     switch ((k + 255) / 256) {
       case 1: e = launch_reg<1>(codes, scales, x, inverse, m, k, st); break;
       case 2: e = launch_reg<2>(codes, scales, x, inverse, m, k, st); break;

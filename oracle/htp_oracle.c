@@ -22,6 +22,14 @@ int orc_threads(void) {
 #endif
 }
 
+void orc_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 /* ------------------------------------------------------------------------ */
 /* Seeded generators                                                        */
 /* ------------------------------------------------------------------------ */

@@ -91,6 +91,9 @@ void orc_f16_linear_rows(float *out, const float *x, const uint16_t *wperm, cons
 
 /* Number of OpenMP threads this build uses (1 without OpenMP). */
 int orc_threads(void);
+/* Use n OpenMP threads from now on (ignored without OpenMP); launchers such as
+   torchrun export OMP_NUM_THREADS=1, the CPU baseline wants every host thread. */
+void orc_set_threads(int n);
 
 #ifdef __cplusplus
 }

@@ -66,6 +66,7 @@ def lib(kind: str = "st") -> ctypes.CDLL:
     L.orc_epilogue_activation.restype = ctypes.c_float
     L.orc_f16_linear_rows.argtypes = [P, P, P, P, I, I, I, I, I, I, P, I]
     L.orc_threads.restype = I
+    L.orc_set_threads.argtypes = [I]
     _libs[kind] = L
     return L
 
