@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200 linear-operator path (the driver's contract).
 
-Workload (default, every N): BASELINE config C4 — W8A8 MLP fc1 with bias +
+Workload (default, every N): configuration C4 — W8A8 MLP fc1 with bias +
 GELU(tanh) epilogue, M=16384 tokens, K=1536, N=6144, column-sharded over the
 N GPUs (N/world columns per GPU); for N > 1 each step ends with an NCCL
 all-gather of the output slices over NVLink and the reassembly of the
@@ -120,9 +120,9 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ inputs
 def make_c4_inputs(torch, dev, m, k, n, seed=0x5EED0003, outlier_p=0.005):
-    """Seeded synthetic C4 tensors with BASELINE's distributions (config index 2
-    values): X ~ N(0,1) with 0.5% of entries x20, W int8 uniform [-127,127],
-    column scales U[1e-3,1e-2], bias N(0,0.01)."""
+    """Seeded synthetic C4 tensors with the benchmark's value distributions:
+    X ~ N(0,1) with 0.5% of entries x20, W int8 uniform [-127,127], column
+    scales U[1e-3,1e-2], bias N(0,0.01)."""
     import numpy as np
     import htpg
     g = torch.Generator(device=dev)
@@ -155,13 +155,13 @@ class L2Flush:
 
 # ------------------------------------------------------------------ suite
 def _w8a8_operands(torch, htpg, dev, m, k, n, seed, outlier_p, bias):
-    """Seeded W8A8 operands (BASELINE value distributions) and prepared weights."""
+    """Seeded W8A8 operands (the benchmark's value distributions) and prepared weights."""
     x, blob_dev, b, _ = make_c4_inputs(torch, dev, m, k, n, seed=seed, outlier_p=outlier_p)
     return x, htpg.w8a8_weights(blob_dev, k, n), (b if bias else None), blob_dev
 
 
 def suite(torch, L, htpg, dev, flush, reps=20, only=None):
-    """Per-config device times of the other BASELINE configs (one GPU): C1,
+    """Per-config device times of the other benchmark configurations (one GPU): C1,
     C2, the four C3 DiT linears and the six C5 decode linears.  Each run is the
     whole operator (activation pass + GEMM), timed with CUDA events on the
     launching stream, the L2 flushed (256 MiB written and read back) before
@@ -332,7 +332,7 @@ def run_reference_arm(args, rank):
         "metric": "W8A8 linear INT8 TOPS (C4 fc1 M=16384 K=1536 N=6144 bias+GELU)",
         "value": v, "unit": "TOPS", "higher_is_better": True, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "dtype": "u8xs8->s32, f32 io",
-        "data": "synthetic (seeded; BASELINE C4 distributions)",
+        "data": "synthetic (seeded; C4 value distributions)",
         "config": {"workload": "C4", "M": M_C4, "K": K_C4, "N": N_C4, "epilogue": "bias+gelu_tanh"},
         "cpu_baseline": {"value": v, "unit": "TOPS", "cores": threads, "kind": "port",
                          "sample": f"{rows} of {M_C4} rows per step, all {N_C4} columns"},
@@ -422,6 +422,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-suite", action="store_true",
                     help="skip the per-config C1/C2/C3/C5 device times (one GPU only)")
+    ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
+                    help="N>1: how the column blocks reach every rank")
     ap.add_argument("--suite-only", default=None,
                     help="run only this suite config (e.g. C5_up_M16) and print its timings; for profiling")
     ap.add_argument("--m", type=int, default=M_C4,
@@ -464,13 +466,29 @@ def main():
     w = htpg.w8a8_weights(blob_dev, k, n, n0=n0, n_cols=n_loc)
     bias_loc = bias[n0:n0 + n_loc].contiguous()
     out_loc = torch.empty(m, n_loc, dtype=torch.float32, device=dev)
-    gathered = torch.empty(world * m, n_loc, dtype=torch.float32, device=dev) if world > 1 else None
+    fused = world > 1 and args.exchange == "fused"
+    gathered = torch.empty(world * m, n_loc, dtype=torch.float32, device=dev) if world > 1 and not fused else None
     full = torch.empty(m, n, dtype=torch.float32, device=dev) if world > 1 else None
     flush = L2Flush(torch, dev)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
+    peers = []
+    if fused:
+        # every rank's [M][N] output, mapped into this process; this rank's
+        # GEMM stores its column block into all of them
+        handles = [None] * world
+        dist.all_gather_object(handles, htpg.ipc_export(full))
+        peers = [htpg.ipc_import(handles[p]) for p in range(world) if p != rank]
+        outs = (ctypes.c_void_p * world)(full.data_ptr() + 4 * n0, *[q + 4 * n0 for q in peers])
+        token = torch.zeros(1, dtype=torch.float32, device=dev)
 
     def step():
+        if fused:
+            htpg.check(L.htpg_w8a8_run_gather(w.handle, outs, world, n, htpg.ptr(x), htpg.ptr(bias_loc), m, n_loc,
+                                              1, sp), "htpg_w8a8_run_gather")
+            # stream-ordered: completes once every rank's stores have landed
+            dist.all_reduce(token)
+            return
         htpg.check(L.htpg_w8a8_run(w.handle, htpg.ptr(out_loc), 0, htpg.ptr(x), htpg.ptr(bias_loc), m, n_loc,
                                    1, sp), "htpg_w8a8_run")
         if world > 1:
@@ -568,10 +586,13 @@ def main():
         "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "u8xs8->s32 (int8 tensor cores), f32 io",
-        "data": "synthetic (seeded; BASELINE C4 distributions)",
+        "data": "synthetic (seeded; C4 value distributions)",
         "config": {"workload": workload, "M": m, "K": k, "N": n, "N_per_gpu": n_loc,
                    "epilogue": "bias+gelu_tanh", "parallelism": f"tp{world} (columns)" if world > 1 else "single",
-                   "exchange": "nccl all_gather + reassembly" if world > 1 else None,
+                   "exchange": (None if world == 1 else
+                                "fused: the GEMM epilogue TMA-stores each tile into every rank's [M][N] output "
+                                "over NVLink (CUDA IPC); NCCL all-reduce of a token orders the step" if fused else
+                                "nccl all_gather + reassembly"),
                    "l2": L2_NOTE},
         "roofline": roof,
         "gpu_launches": int(launches),
@@ -619,6 +640,21 @@ def main():
         tops, threads, secs = cpu_sample(k, n, args.cpu_rows)
         line["cpu_baseline"] = {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port",
                                 "sample": f"{args.cpu_rows} of {m} rows, all {n} columns ({secs:.2f} s)"}
+    if world > 1:
+        # the assembled output against one GPU computing all N columns
+        torch.cuda.synchronize()
+        if rank == 0:
+            w_all = htpg.w8a8_weights(blob_dev, k, n)
+            ref = torch.empty(m, n, dtype=torch.float32, device=dev)
+            htpg.check(L.htpg_w8a8_run(w_all.handle, htpg.ptr(ref), 0, htpg.ptr(x), htpg.ptr(bias), m, n, 1, sp),
+                       "reference run")
+            torch.cuda.synchronize()
+            line["config"]["check"] = {"vs_single_gpu_max_abs_diff": float((ref - full).abs().max().item()),
+                                       "bit_exact": bool(torch.equal(ref.view(torch.int32), full.view(torch.int32)))}
+            del w_all, ref
+        dist.barrier()
+        for q in peers:
+            htpg.check(L.htpg_ipc_close(q), "htpg_ipc_close")
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:

@@ -453,9 +453,14 @@ extern "C" int htpg_f16_weights_create(const uint16_t *permuted_weight, int k, i
 // ================================================================ run
 namespace {
 
-int run_common(htpg_weights *w, float *out, int ldo, const float *x, const float *bias, int m,
-               int channels, int mode, void *stream) {
-  if (!w || !out || !x) return HTPG_EARGS;
+// outs[0..n_outs): destinations of the output (n_outs > 1: the same output
+// block in several buffers, each written by TMA stores from the epilogue).
+int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const float *x,
+               const float *bias, int m, int channels, int mode, void *stream) {
+  if (!w || !outs || n_outs < 1 || n_outs > kMaxOutputs || !x) return HTPG_EARGS;
+  for (int i = 0; i < n_outs; ++i)
+    if (!outs[i]) return HTPG_EARGS;
+  float *out = outs[0];
   const int n = w->ncols, k = w->k;
   if (m < 1 || m > HTPG_W8A8_MAX_M) return HTPG_EARGS;
   if (mode < 0 || mode > HTPG_MODE_RAW) return HTPG_ECAPACITY;
@@ -472,6 +477,8 @@ int run_common(htpg_weights *w, float *out, int ldo, const float *x, const float
   std::lock_guard<std::mutex> lk(g_mu);
 
   const GemmPlan plan = plan_gemm(w->kind, m, n, k, d->sms);
+  // several destinations need the TMA-store epilogue (normal orientation, row-major, aligned)
+  if (n_outs > 1 && (plan.swap || mode == 3 || !tma_store_ok(out, ldo))) return HTPG_ECAPACITY;
   // Workspace: [split-K accumulators + counters | activation codes / FP16 | row scales].
   // The split-K region sits at a fixed offset and is kept all-zero (zeroed at
   // allocation, left zeroed by every launch), so no per-call clear is needed.
@@ -534,14 +541,18 @@ int run_common(htpg_weights *w, float *out, int ldo, const float *x, const float
   a.ws_count = cnt;
   a.watchdog = d->watchdog;
   // row-major outputs of the normal orientation leave the SM through TMA stores
-  CUtensorMap out_map = act_map;  // placeholder when unused
+  OutMaps out_maps;
   if (!plan.swap && mode != 3 && tma_store_ok(out, ldo)) {
-    rc = make_out_map(&out_map, out, m, n, ldo);
-    if (rc) return rc;
+    for (int i = 0; i < n_outs; ++i) {
+      if (!tma_store_ok(outs[i], ldo)) return HTPG_ECONTROL;
+      rc = make_out_map(&out_maps.map[i], outs[i], m, n, ldo);
+      if (rc) return rc;
+    }
+    out_maps.count = n_outs;
     a.tma_store = 1;
   }
-  e = plan.swap ? launch_gemm(plan, *wmap, act_map, out_map, a, st)
-                : launch_gemm(plan, act_map, *wmap, out_map, a, st);
+  e = plan.swap ? launch_gemm(plan, *wmap, act_map, out_maps, a, st)
+                : launch_gemm(plan, act_map, *wmap, out_maps, a, st);
   if (e != cudaSuccess) return record_cuda(e);
   if (phase) {
     cudaEventRecord(pe.e[2], st);
@@ -562,13 +573,84 @@ int run_common(htpg_weights *w, float *out, int ldo, const float *x, const float
 extern "C" int htpg_w8a8_run(const htpg_weights *w, float *out, int ldo, const float *x,
                              const float *bias, int m, int channels, int mode, void *stream) {
   if (!w || w->kind != Kind::I8) return HTPG_EARGS;
-  return run_common(const_cast<htpg_weights *>(w), out, ldo, x, bias, m, channels, mode, stream);
+  return run_common(const_cast<htpg_weights *>(w), &out, 1, ldo, x, bias, m, channels, mode, stream);
 }
 
 extern "C" int htpg_f16_run(const htpg_weights *w, float *out, int ldo, const float *x,
                             const float *bias, int m, int channels, int mode, void *stream) {
   if (!w || w->kind != Kind::F16) return HTPG_EARGS;
-  return run_common(const_cast<htpg_weights *>(w), out, ldo, x, bias, m, channels, mode, stream);
+  return run_common(const_cast<htpg_weights *>(w), &out, 1, ldo, x, bias, m, channels, mode, stream);
+}
+
+extern "C" int htpg_w8a8_run_gather(const htpg_weights *w, float *const *outs, int n_outs, int ldo,
+                                    const float *x, const float *bias, int m, int channels, int mode,
+                                    void *stream) {
+  if (!w || w->kind != Kind::I8) return HTPG_EARGS;
+  return run_common(const_cast<htpg_weights *>(w), outs, n_outs, ldo, x, bias, m, channels, mode, stream);
+}
+
+// ---------------------------------------------------------------- IPC
+namespace {
+typedef CUresult (*AddressRangeFn)(CUdeviceptr *, size_t *, CUdeviceptr);
+std::map<void *, void *> g_ipc_bases;  // imported address -> base returned by the open
+}  // namespace
+
+extern "C" int htpg_ipc_export(const void *dev_ptr, void *handle) {
+  if (!dev_ptr || !handle) return HTPG_EARGS;
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  static AddressRangeFn range = nullptr;
+  if (!range) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return record_cuda(cudaErrorNotSupported);
+    range = reinterpret_cast<AddressRangeFn>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS) return HTPG_EARGS;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+  if (e != cudaSuccess) return record_cuda(e);
+  const int64_t offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  std::memcpy(handle, &h, sizeof(h));
+  std::memcpy(static_cast<uint8_t *>(handle) + sizeof(h), &offset, sizeof(offset));
+  return HTPG_OK;
+}
+
+extern "C" int htpg_ipc_import(const void *handle, void **dev_ptr) {
+  if (!handle || !dev_ptr) return HTPG_EARGS;
+  *dev_ptr = nullptr;
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  int64_t offset = 0;
+  std::memcpy(&h, handle, sizeof(h));
+  std::memcpy(&offset, static_cast<const uint8_t *>(handle) + sizeof(h), sizeof(offset));
+  void *base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return record_cuda(e);
+  void *p = static_cast<uint8_t *>(base) + offset;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_ipc_bases[p] = base;
+  *dev_ptr = p;
+  return HTPG_OK;
+}
+
+extern "C" int htpg_ipc_close(void *dev_ptr) {
+  void *base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_ipc_bases.find(dev_ptr);
+    if (it == g_ipc_bases.end()) return HTPG_EARGS;
+    base = it->second;
+    g_ipc_bases.erase(it);
+  }
+  return record_cuda(cudaIpcCloseMemHandle(base));
 }
 
 // W8A8 run whose scratch is the caller's fixed array [scratch, scratch+bytes)
@@ -640,14 +722,15 @@ int htpg::w8a8_run_in_scratch(const htpg_weights *w, float *out, int ldo, const 
   a.ws = wsk;
   a.ws_count = cnt;
   a.watchdog = d->watchdog;
-  CUtensorMap out_map = act_map;  // placeholder when unused
+  OutMaps out_maps;
   if (!plan.swap && mode != 3 && tma_store_ok(out, ldo)) {
-    rc = make_out_map(&out_map, out, m, n, ldo);
+    rc = make_out_map(&out_maps.map[0], out, m, n, ldo);
     if (rc) return rc;
+    out_maps.count = 1;
     a.tma_store = 1;
   }
-  e = plan.swap ? launch_gemm(plan, *wmap, act_map, out_map, a, st)
-                : launch_gemm(plan, act_map, *wmap, out_map, a, st);
+  e = plan.swap ? launch_gemm(plan, *wmap, act_map, out_maps, a, st)
+                : launch_gemm(plan, act_map, *wmap, out_maps, a, st);
   return record_cuda(e);
 }
 
@@ -708,7 +791,7 @@ extern "C" int htpg_w8a8_linear(float *out, const float *x, const void *constant
   htpg_weights *w = nullptr;
   int rc = cached_weights(Kind::I8, constants, k, n, stream, &w);
   if (rc) return rc;
-  return run_common(w, out, 0, x, bias, m, channels, mode, stream);
+  return run_common(w, &out, 1, 0, x, bias, m, channels, mode, stream);
 }
 
 extern "C" int htpg_f16_linear(float *out, const float *x, const uint16_t *permuted_weight,
@@ -724,7 +807,7 @@ extern "C" int htpg_f16_linear(float *out, const float *x, const uint16_t *permu
   htpg_weights *w = nullptr;
   int rc = cached_weights(Kind::F16, permuted_weight, k, n, stream, &w);
   if (rc) return rc;
-  return run_common(w, out, 0, x, bias, m, channels, mode, stream);
+  return run_common(w, &out, 1, 0, x, bias, m, channels, mode, stream);
 }
 
 // ================================================================ reference kernel names
@@ -758,7 +841,7 @@ extern "C" int hmx_mat_mul_native_w8a8_profiled(float *dst, const float *activat
   const auto t1 = std::chrono::steady_clock::now();
   const int prev = g_profiling;
   if (profile) g_profiling = 1;
-  rc = finish_sync(run_common(w, dst, 0, activation, nullptr, m, 0, 0, nullptr));
+  rc = finish_sync(run_common(w, &dst, 1, 0, activation, nullptr, m, 0, 0, nullptr));
   g_profiling = prev;
   if (profile && rc == HTPG_OK) {
     const double tick_per_ms = 19200.0;  // the reference reports 19.2 MHz qtimer ticks

@@ -555,7 +555,7 @@ struct KernelParams {
 struct EpiCtx {
   const GemmArgs *g;
   const KernelParams *P;
-  const CUtensorMap *tmOut;
+  const OutMaps *tmOut;
   SmemLayout L;
   float *scr;        // this warp's staging tile
   float *prm;        // this warp's column-parameter slots
@@ -680,7 +680,7 @@ __device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
         fence_proxy_async_smem();
         __syncwarp();
         if (c.lane == 0) {
-          tma_store_2d(c.tmOut, smem_u32(scr), n0, mbase);
+          for (int d = 0; d < c.tmOut->count; ++d) tma_store_2d(&c.tmOut->map[d], smem_u32(scr), n0, mbase);
           bulk_commit();
         }
       } else {
@@ -814,7 +814,7 @@ __device__ __forceinline__ bool epilogue_dispatch(const EpiCtx &c, int mode, boo
 template <Kind KIND, int BN, bool SWAP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmOut, const KernelParams P) {
+                const __grid_constant__ OutMaps tmOut, const KernelParams P) {
   constexpr int STAGES = stages_for(BN, SWAP);
   constexpr int TCOLS = tmem_cols_for(BN);
   constexpr uint32_t kStageBytes = (128 + BN) * kRowBytes;
@@ -1048,7 +1048,7 @@ static_assert(smem2_bytes_for(256) <= kSmemLimit && smem2_bytes_for(128) <= kSme
 template <Kind KIND, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 const __grid_constant__ CUtensorMap tmOut, const KernelParams P) {
+                 const __grid_constant__ OutMaps tmOut, const KernelParams P) {
   constexpr int BH = BN / 2;  // B rows held by each CTA
   constexpr int STAGES = stages2_for(BN);
   constexpr int TCOLS = tmem_cols_for(BN);
@@ -1323,7 +1323,7 @@ size_t splitk_count_bytes(const GemmPlan &p) {
 // TMEM, descriptor and L2 weight prefetch) overlaps the activation pass.
 template <typename Fn>
 static cudaError_t launch_dependent(Fn fn, int grid, size_t smem, cudaStream_t st, const CUtensorMap &tmA,
-                                    const CUtensorMap &tmB, const CUtensorMap &tmOut, const KernelParams &P) {
+                                    const CUtensorMap &tmB, const OutMaps &tmOut, const KernelParams &P) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -1340,7 +1340,7 @@ static cudaError_t launch_dependent(Fn fn, int grid, size_t smem, cudaStream_t s
 
 template <Kind KIND, int BN, bool SWAP>
 static cudaError_t launch_one(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
-                              const CUtensorMap &tmOut, const GemmArgs &a, cudaStream_t st) {
+                              const OutMaps &tmOut, const GemmArgs &a, cudaStream_t st) {
   auto fn = gemm_kernel<KIND, BN, SWAP>;
   static bool configured[64] = {};  // per instantiation and device
   int dev = 0;
@@ -1366,7 +1366,7 @@ static cudaError_t launch_one(const GemmPlan &p, const CUtensorMap &tmA, const C
 
 template <Kind KIND, int BN>
 static cudaError_t launch_pair(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
-                               const CUtensorMap &tmOut, const GemmArgs &a, cudaStream_t st) {
+                               const OutMaps &tmOut, const GemmArgs &a, cudaStream_t st) {
   auto fn = gemm2_kernel<KIND, BN>;
   static bool configured[64] = {};  // per instantiation and device
   int dev = 0;
@@ -1392,7 +1392,7 @@ static cudaError_t launch_pair(const GemmPlan &p, const CUtensorMap &tmA, const 
 }
 
 cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
-                        const CUtensorMap &tmOut, const GemmArgs &a, cudaStream_t st) {
+                        const OutMaps &tmOut, const GemmArgs &a, cudaStream_t st) {
   if (p.pair) {
     if (p.grid % 2) return cudaErrorInvalidConfiguration;
     if (p.kind == Kind::I8) {

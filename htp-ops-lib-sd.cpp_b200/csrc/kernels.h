@@ -59,8 +59,18 @@ size_t splitk_count_bytes(const GemmPlan &p);
 inline int box_rows_a(const GemmPlan &) { return 128; }
 inline int box_rows_b(const GemmPlan &p) { return p.pair ? p.bn / 2 : p.bn; }
 
+// Destinations of the row-major output: the epilogue stores every finished
+// tile to each of them with TMA (the local output, and for the column-sharded
+// multi-GPU run the same block of every peer's output).  count 0: no TMA
+// stores (GemmArgs::tma_store is 0).
+constexpr int kMaxOutputs = 8;
+struct OutMaps {
+  CUtensorMap map[kMaxOutputs];
+  int count = 0;
+};
+
 cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
-                        const CUtensorMap &tmOut, const GemmArgs &a, cudaStream_t st);
+                        const OutMaps &tmOut, const GemmArgs &a, cudaStream_t st);
 
 cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
                                  const float *inverse, int m, int k, cudaStream_t st);

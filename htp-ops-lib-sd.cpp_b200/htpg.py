@@ -73,6 +73,10 @@ def lib() -> ctypes.CDLL:
         "htpg_w8a8_run": (I, [P, P, I, P, P, I, I, I, P]),
         "htpg_f16_run": (I, [P, P, I, P, P, I, I, I, P]),
         "htpg_w8a8_run_static": (I, [P, P, I, P, P, I, I, I, P]),
+        "htpg_w8a8_run_gather": (I, [P, ctypes.POINTER(P), I, I, P, P, I, I, I, P]),
+        "htpg_ipc_export": (I, [P, P]),
+        "htpg_ipc_import": (I, [P, ctypes.POINTER(P)]),
+        "htpg_ipc_close": (I, [P]),
         "htpg_w8a8_linear": (I, [P, P, P, P, I, I, I, I, I, P]),
         "htpg_f16_linear": (I, [P, P, P, P, I, I, I, I, I, P]),
         "htpg_weight_cache_drop": (None, [P]),
@@ -288,3 +292,21 @@ def assemble_columns(full, gathered) -> None:
     """gathered: [world][M][N/world] shards (all-gather order) -> full: [M][N] row-major."""
     world, m, n_loc = gathered.shape
     full.view(m, world, n_loc).copy_(gathered.permute(1, 0, 2))
+
+
+IPC_HANDLE_BYTES = 72
+
+
+def ipc_export(t) -> bytes:
+    """72-byte CUDA IPC handle (+ offset) of a device tensor's storage."""
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    check(lib().htpg_ipc_export(ptr(t), buf), "htpg_ipc_export")
+    return buf.raw
+
+
+def ipc_import(handle: bytes) -> int:
+    """Device address, in this process, of a peer's exported buffer."""
+    p = ctypes.c_void_p()
+    check(lib().htpg_ipc_import(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(p)),
+          "htpg_ipc_import")
+    return p.value

@@ -109,6 +109,28 @@ int htpg_w8a8_run(const htpg_weights *w, float *out, int ldo, const float *x, co
 int htpg_f16_run(const htpg_weights *w, float *out, int ldo, const float *x, const float *bias,
                  int m, int channels, int mode, void *stream);
 
+/* ---- column-sharded run with a fused output exchange -------------------- */
+/* Multi-GPU form of htpg_w8a8_run for a weight split by output columns (N)
+ * across ranks, each rank holding a column block: the epilogue stores every finished output tile to each of outs[0..n_outs)
+ * (n_outs <= 8) with TMA, so one launch both computes this rank's column block
+ * and writes it into every rank's row-major [M][N] output over NVLink.  outs[i]
+ * points at the block's first column in buffer i (its row pitch is ldo floats,
+ * ldo = the full N); peers' buffers come from htpg_ipc_import.  Needs the
+ * TMA-store epilogue: mode 0-2, 16-byte aligned blocks, M > 32 (else
+ * HTPG_ECAPACITY).  The stores to peers are complete when the launch is; the
+ * caller orders the ranks after it (e.g. a stream-ordered all-reduce of a token)
+ * before anyone reads the assembled output.  No counterpart in the reference
+ * (it has no multi-device path). */
+int htpg_w8a8_run_gather(const htpg_weights *w, float *const *outs, int n_outs, int ldo, const float *x,
+                         const float *bias, int m, int channels, int mode, void *stream);
+/* CUDA IPC for peer buffers: export a device address as a 72-byte handle
+ * (cudaIpcMemHandle_t of its allocation + the byte offset into it), import a
+ * peer's handle as a local address (peer access enabled lazily), close it. */
+#define HTPG_IPC_HANDLE_BYTES 72
+int htpg_ipc_export(const void *dev_ptr, void *handle);
+int htpg_ipc_import(const void *handle, void **dev_ptr);
+int htpg_ipc_close(void *dev_ptr);
+
 /* ---- W8A8 run that allocates nothing (no counterpart in the reference) -- */
 /* For callers that must not allocate device memory per call: code running
  * under a fixed memory budget or a caching allocator that owns all device

@@ -19,7 +19,7 @@
  *    CMakeLists.txt:97-98).  The reference executes these steps in HVX QFloat,
  *    whose ulp-level rounding is undocumented and cannot run here, so the FP32
  *    steps are pinned only by this restatement ("parity unpinned" at the ulp
- *    level of QFloat; within the BASELINE tolerances otherwise).
+ *    level of QFloat; within the output tolerances otherwise).
  */
 #ifndef HTP_ORACLE_H
 #define HTP_ORACLE_H

@@ -5,7 +5,7 @@ bench.py's CPU-baseline leg, never by the library.  See htp_oracle.h for what
 the oracle restates (reference linear_w8a8.c / mat_mul.c arithmetic) and how
 it is pinned.
 
-Synthetic inputs follow the measurement plan of the five BASELINE configs:
+Synthetic inputs follow the measurement plan of the five benchmark configurations:
 splitmix64 with seed 0x5EED0000 + config_index (0-based), one derived stream
 per tensor, Box-Muller normals on FP64 rounded to FP32.
 """
@@ -194,7 +194,7 @@ def epilogue(v: float, mode: int) -> float:
 
 
 def max_abs_rel(got: np.ndarray, ref: np.ndarray) -> float:
-    """max_i |g_i - o_i| / max(max_j |o_j|, 1e-30) — the BASELINE tolerance metric."""
+    """max_i |g_i - o_i| / max(max_j |o_j|, 1e-30) — the tolerance metric of the parity bars."""
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     denom = max(float(np.max(np.abs(ref))) if ref.size else 0.0, 1e-30)

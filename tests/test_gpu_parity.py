@@ -1,6 +1,6 @@
 """GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
 
-Bars (BASELINE north_star): INT8 activation codes, row scales and INT32
+Bars: INT8 activation codes, row scales and INT32
 accumulators bit-exact; W8A8 FP32 outputs within max-abs-rel 2e-3 (achieved
 bit-exact without an activation); FP16-weight GEMM outputs within
 max-abs-rel 1e-2 of the oracle with FP32 accumulation.
