@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -164,6 +165,7 @@ struct htpg_weights {
   void *wk = nullptr;          // k-block-major [KB][ncols][128 B] int8 / fp16
   float *sw = nullptr;         // I8: [ncols] column scales
   int32_t *corr = nullptr;     // I8: [ncols] zero-point correction differences
+  int32_t *sum7 = nullptr;     // I8: [ncols] (sum_k w) << 7, for the plane export
   float *inverse = nullptr;    // I8: [k], nullptr when every entry is 1.0
   std::map<int, CUtensorMap> maps;  // by box rows
 };
@@ -334,6 +336,7 @@ extern "C" void htpg_weights_destroy(htpg_weights *w) {
   cudaFree(w->wk);
   cudaFree(w->sw);
   cudaFree(w->corr);
+  cudaFree(w->sum7);
   cudaFree(w->inverse);
   delete w;
 }
@@ -375,7 +378,7 @@ extern "C" int htpg_w8a8_weights_create(const void *constants, int k, int n, int
   const size_t wk_bytes = kblock_bytes(Kind::I8, k, n_cols);
   bool ok = cudaMalloc(&w->wk, wk_bytes) == cudaSuccess &&
             cudaMalloc(&w->sw, 4u * n_cols) == cudaSuccess &&
-            cudaMalloc(&w->corr, 4u * n_cols) == cudaSuccess &&
+            cudaMalloc(&w->corr, 4u * n_cols) == cudaSuccess && cudaMalloc(&w->sum7, 4u * n_cols) == cudaSuccess &&
             cudaMalloc(&w->inverse, 4u * k) == cudaSuccess && cudaMalloc(&flag, 4) == cudaSuccess;
   if (!ok) {
     cudaGetLastError();
@@ -388,7 +391,7 @@ extern "C" int htpg_w8a8_weights_create(const void *constants, int k, int n, int
   if (e == cudaSuccess)
     e = launch_repack_w8(static_cast<int8_t *>(w->wk), blob + h.weight_offset, k, n0, n_cols, st);
   if (e == cudaSuccess)
-    e = launch_colsum_corr(w->corr, static_cast<const int8_t *>(w->wk),
+    e = launch_colsum_corr(w->corr, w->sum7, static_cast<const int8_t *>(w->wk),
                            reinterpret_cast<const int32_t *>(blob + h.sum_offset), k, n0, n_cols, st);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(w->sw, blob + h.scale_offset + 4u * n0, 4u * n_cols, cudaMemcpyDeviceToDevice, st);
@@ -456,20 +459,23 @@ namespace {
 // outs[0..n_outs): destinations of the output (n_outs > 1: the same output
 // block in several buffers, each written by TMA stores from the epilogue).
 int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const float *x,
-               const float *bias, int m, int channels, int mode, void *stream) {
+               const float *bias, int m, int channels, int mode, void *stream,
+               const float **row_scales_out = nullptr) {
   if (!w || !outs || n_outs < 1 || n_outs > kMaxOutputs || !x) return HTPG_EARGS;
   for (int i = 0; i < n_outs; ++i)
     if (!outs[i]) return HTPG_EARGS;
   float *out = outs[0];
   const int n = w->ncols, k = w->k;
   if (m < 1 || m > HTPG_W8A8_MAX_M) return HTPG_EARGS;
-  if (mode < 0 || mode > HTPG_MODE_RAW) return HTPG_ECAPACITY;
+  if (mode < 0 || mode > HTPG_MODE_PLANES || (mode == HTPG_MODE_PLANES && w->kind != Kind::I8))
+    return HTPG_ECAPACITY;
   if (channels == 0) channels = n;
   if (channels < 1 || channels > n || (mode != 3 && channels != n)) return HTPG_ECAPACITY;
   if (reinterpret_cast<uintptr_t>(x) & 15u) return HTPG_ECONTROL;
   if (reinterpret_cast<uintptr_t>(out) & 3u) return HTPG_ECONTROL;
   if (ldo == 0) ldo = mode == 3 ? m : n;
-  if ((mode == 3 && ldo < m) || (mode != 3 && ldo < n)) return HTPG_EARGS;
+  if ((mode == 3 && ldo < m) || (mode != 3 && ldo < n) || (mode == HTPG_MODE_PLANES && ldo != n))
+    return HTPG_EARGS;
   Device *d;
   int rc = current_device(&d);
   if (rc) return rc;
@@ -494,6 +500,7 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
   uint32_t *cnt = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(base) + splitk_ws_bytes(plan));
   uint8_t *act = static_cast<uint8_t *>(base) + wsk_bytes;
   float *scales = reinterpret_cast<float *>(act + act_bytes);
+  if (row_scales_out) *row_scales_out = scales;
 
   const bool prof = g_profiling != 0;
   PhaseEvents pe;
@@ -536,13 +543,16 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
   a.row_scale = scales;
   a.col_scale = w->sw;
   a.col_corr = w->corr;
+  a.col_sum7 = w->sum7;
   a.bias = bias;
   a.ws = wsk;
   a.ws_count = cnt;
   a.watchdog = d->watchdog;
   // row-major outputs of the normal orientation leave the SM through TMA stores
   OutMaps out_maps;
-  if (!plan.swap && mode != 3 && tma_store_ok(out, ldo)) {
+  if (mode == HTPG_MODE_PLANES) {
+    a.tma_store = tma_store_ok(out, ldo) ? 1 : 0;  // 16-byte aligned rows: vector plane stores
+  } else if (!plan.swap && mode != 3 && tma_store_ok(out, ldo)) {
     for (int i = 0; i < n_outs; ++i) {
       if (!tma_store_ok(outs[i], ldo)) return HTPG_ECONTROL;
       rc = make_out_map(&out_maps.map[i], outs[i], m, n, ldo);
@@ -580,6 +590,45 @@ extern "C" int htpg_f16_run(const htpg_weights *w, float *out, int ldo, const fl
                             const float *bias, int m, int channels, int mode, void *stream) {
   if (!w || w->kind != Kind::F16) return HTPG_EARGS;
   return run_common(const_cast<htpg_weights *>(w), &out, 1, ldo, x, bias, m, channels, mode, stream);
+}
+
+namespace {
+// Control block of the CPU-epilogue form, filled after the planes are written
+// (linear_w8a8.c:421-427, 512-526).  This build computes all M rows in one
+// batch and streams the weight once; it has no VTCM (vtcm_bytes 0).
+int fill_control(W8A8CpuControl *control, const float *scales_dev, int m, int k, int n, cudaStream_t st) {
+  cudaError_t e = cudaMemcpyAsync(control->scales, scales_dev, 4u * static_cast<size_t>(m),
+                                  cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return record_cuda(e);
+  control->vtcm_bytes = 0;
+  control->activation_rows = static_cast<uint32_t>(m);
+  control->weight_columns = static_cast<uint32_t>(n / 64);
+  control->weight_loads = 1;
+  control->weight_loaded_bytes = static_cast<uint64_t>(k) * static_cast<uint64_t>(n);
+  control->batches[0].m0 = 0;
+  control->batches[0].rows = m;
+  control->batches[0].n0 = 0;
+  control->batches[0].columns = n / 64;
+  std::atomic_thread_fence(std::memory_order_release);
+  reinterpret_cast<volatile uint32_t *>(&control->produced)[0] = 1u;  // published last
+  return HTPG_OK;
+}
+}  // namespace
+
+extern "C" int htpg_w8a8_run_planes(const htpg_weights *w, float *dst, const float *x, int m,
+                                    struct W8A8CpuControl *control, void *stream) {
+  if (!control) return HTPG_ECONTROL;
+  if (!w || w->kind != Kind::I8 || !dst || !x) return HTPG_EARGS;
+  if (m < 1 || m > 4096) return HTPG_EARGS;  // the control block holds 4096 row scales
+  const float *scales = nullptr;
+  float *outs[1] = {dst};
+  int rc = run_common(const_cast<htpg_weights *>(w), outs, 1, 0, x, nullptr, m, 0, HTPG_MODE_PLANES, stream,
+                      &scales);
+  if (rc) return rc;
+  rc = htpg_check_device(stream, nullptr);
+  if (rc) return rc;
+  return fill_control(control, scales, m, w->k, w->ncols, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int htpg_w8a8_run_gather(const htpg_weights *w, float *const *outs, int n_outs, int ldo,
@@ -718,6 +767,7 @@ int htpg::w8a8_run_in_scratch(const htpg_weights *w, float *out, int ldo, const 
   a.row_scale = scales;
   a.col_scale = w->sw;
   a.col_corr = w->corr;
+  a.col_sum7 = w->sum7;
   a.bias = bias;
   a.ws = wsk;
   a.ws_count = cnt;
@@ -879,14 +929,15 @@ extern "C" int hmx_mat_mul_native_w8a8(float *dst, const float *activation, cons
 extern "C" int hmx_mat_mul_native_w8a8_cpu(float *dst, const float *activation,
                                            const uint8_t *constants, int m, int k, int n,
                                            struct W8A8CpuControl *control) {
-  (void)dst;
-  (void)activation;
-  (void)constants;
-  (void)m;
-  (void)k;
-  (void)n;
   if (!control) return HTPG_ECONTROL;
-  return HTPG_EARCH;
+  // argument checks as the reference kernel (linear_w8a8.c:337-338)
+  if (!dst || !activation || !constants || m < 1 || m > 4096 || k < 32 || k > HTPG_W8A8_MAX_K || k % 32 ||
+      n < 64 || n > HTPG_W8A8_MAX_N || n % 64)
+    return HTPG_EARGS;
+  htpg_weights *w = nullptr;
+  int rc = cached_weights(Kind::I8, constants, k, n, nullptr, &w);
+  if (rc) return rc;
+  return htpg_w8a8_run_planes(w, dst, activation, m, control, nullptr);
 }
 
 extern "C" int hmx_mat_mul_f16_epilogue(float *dst, const float *activation, const uint16_t *weight,

@@ -359,12 +359,35 @@ int exec_w8a8(uint8_t *payload, size_t payload_size) {
     if (prof.mode != 1 && prof.mode != 2 && prof.mode != 3) return -1;
   }
   if (cpu) {
-    // raw byte-plane export is a Hexagon HMX readout feature (see capi.cu)
+    // CPU-epilogue form (linear_w8a8.c:512-526): raw byte planes into the
+    // output tensor, row scales and the batch descriptor into the control block
+    if (m > 4096) return -10;
+    htpg_weights *w = nullptr;
+    int rc = exec_weights(cst, true, k, n, &w);
+    if (rc) return rc;
+    if ((rc = stage_in({&act}, {&out}))) return rc;
+    W8A8CpuControl *control = static_cast<W8A8CpuControl *>(ctl.host);
+    std::vector<uint8_t> ctl_copy;
+    if (ctl.buf.kind == HTPG_BUF_DEVICE) {  // the control block lives in HBM: work on a host copy
+      ctl_copy.resize(sizeof(W8A8CpuControl));
+      if (cudaMemcpy(ctl_copy.data(), ctl.device, ctl_copy.size(), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return HTPG_ELAUNCH;
+      }
+      control = reinterpret_cast<W8A8CpuControl *>(ctl_copy.data());
+    }
     const auto t0 = Clock::now();
-    const int rc = hmx_mat_mul_native_w8a8_cpu(nullptr, nullptr, nullptr, m, k, n,
-                                                static_cast<W8A8CpuControl *>(ctl.host));
+    rc = htpg_w8a8_run_planes(w, static_cast<float *>(out.device), static_cast<const float *>(act.device), m,
+                              control, nullptr);
     p->elapsed_us = elapsed_us(t0);
-    return rc;
+    if (rc) return rc;
+    if ((rc = stage_out({&out}))) return rc;
+    if (!ctl_copy.empty() &&
+        cudaMemcpy(ctl.device, ctl_copy.data(), ctl_copy.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaGetLastError();
+      return HTPG_ELAUNCH;
+    }
+    return 0;
   }
   htpg_weights *w = nullptr;
   const auto t_setup = Clock::now();

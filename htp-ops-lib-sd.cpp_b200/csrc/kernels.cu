@@ -344,8 +344,9 @@ cudaError_t launch_repack_w8(int8_t *dst, const uint8_t *deep, int k, int n0, in
 // difference between the reference's zero-point correction, which uses the
 // blob's stored column sums (linear_w8a8.c:159, 168), and the signed
 // accumulation done here.  Zero for every blob whose sums are consistent.
-__global__ void colsum_corr_kernel(int32_t *__restrict__ corr, const int8_t *__restrict__ wk,
-                                   const int32_t *__restrict__ sums, int k, int n0, int ncols) {
+__global__ void colsum_corr_kernel(int32_t *__restrict__ corr, int32_t *__restrict__ sum7,
+                                   const int8_t *__restrict__ wk, const int32_t *__restrict__ sums, int k,
+                                   int n0, int ncols) {
   const int c = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (c >= ncols) return;
@@ -362,12 +363,13 @@ __global__ void colsum_corr_kernel(int32_t *__restrict__ corr, const int8_t *__r
   if (lane == 0) {
     const uint32_t diff = static_cast<uint32_t>(s) - static_cast<uint32_t>(sums[n0 + c]);
     corr[c] = static_cast<int32_t>(diff << 7);
+    sum7[c] = static_cast<int32_t>(static_cast<uint32_t>(s) << 7);
   }
 }
 
-cudaError_t launch_colsum_corr(int32_t *corr, const int8_t *wk, const int32_t *sums, int k, int n0,
-                               int ncols, cudaStream_t st) {
-  colsum_corr_kernel<<<(ncols + 7) / 8, 256, 0, st>>>(corr, wk, sums, k, n0, ncols);
+cudaError_t launch_colsum_corr(int32_t *corr, int32_t *sum7, const int8_t *wk, const int32_t *sums, int k,
+                               int n0, int ncols, cudaStream_t st) {
+  colsum_corr_kernel<<<(ncols + 7) / 8, 256, 0, st>>>(corr, sum7, wk, sums, k, n0, ncols);
   return counted(cudaGetLastError());
 }
 
@@ -447,11 +449,11 @@ __device__ __forceinline__ float finish(uint32_t acc, int32_t corr, float sw, fl
   float v;
   if constexpr (KIND == Kind::I8) {
     const int32_t y = static_cast<int32_t>(acc + static_cast<uint32_t>(corr));
-    if constexpr (MODE == 4) return __int_as_float(y);
+    if constexpr (MODE == 4 || MODE == 5) return __int_as_float(y);  // 5: corr holds (sum w) << 7
     v = __fmul_rn(__fmul_rn(__int2float_rn(y), sw), rs);
   } else {
     v = __uint_as_float(acc);
-    if constexpr (MODE == 4) return v;
+    if constexpr (MODE == 4 || MODE == 5) return v;
   }
   if constexpr (BIAS) v = __fadd_rn(v, bias);
   return epilogue_act<MODE>(v);
@@ -568,6 +570,20 @@ struct EpiCtx {
   int q, part, lane, epi_t;        // part: which of the quadrant's four warps
 };
 
+// Plane export (the opcode-15 CPU-epilogue form, linear_w8a8.c:205-227): the
+// unsigned-code INT32 accumulator of (m, n) is split into its four bytes.  In
+// the 64-row tile of m (rows = the tile's valid rows) and the 32-column half of
+// n, byte p sits at position p*rows*32 + (m%64)*32 + n%32 of the half's byte
+// stream, and that stream fills the half's 128 output bytes of the tile's rows
+// in order.  Returns where byte p of (m, n) goes.
+__device__ __forceinline__ uint8_t *plane_dst(float *out, long long ldo, int M, int m, int n, int p) {
+  const int t = m >> 6;
+  const int rows = min(64, M - (t << 6));
+  const int o = p * rows * 32 + (m & 63) * 32 + (n & 31);
+  return reinterpret_cast<uint8_t *>(out + (static_cast<long long>(t) * 64 + o / 128) * ldo + (n & ~31)) +
+         (o & 127);
+}
+
 // Normal orientation: TMEM lane = activation row m, column = weight column n.
 // The four warps of a lane quadrant take every fourth 32-column chunk.  The row
 // scale and the per-column parameters are loaded before the accumulator wait,
@@ -606,7 +622,7 @@ __device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
     const int nl = c.w.tb * BN + (c.part + kEpiPerQuadrant * i) * 32 + c.lane;
     const bool ok = nl < g.N;
     psw[i] = (KIND == Kind::I8 && ok) ? __ldg(g.col_scale + nl) : 0.0f;
-    pcr[i] = (KIND == Kind::I8 && ok) ? __ldg(g.col_corr + nl) : 0;
+    pcr[i] = (KIND == Kind::I8 && ok) ? __ldg((MODE == 5 ? g.col_sum7 : g.col_corr) + nl) : 0;
     pb[i] = (BIAS && ok) ? __ldg(g.bias + nl) : 0.0f;
   }
   const bool ok = mbar_wait(c.full_bar, c.full_parity, g.watchdog, kWatchEpilogue, c.L.abort);
@@ -664,6 +680,26 @@ __device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
       for (int j = 0; j < 32; ++j) {
         const int n = n0 + j;
         if (m_ok && n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = __uint_as_float(r[i][j]);
+      }
+    } else if (MODE == 5) {
+      // byte planes: 32 contiguous bytes per plane for this row's 32 columns
+      if (m_ok && n0 < g.N) {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          uint32_t wv[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            wv[q] = ((r[i][4 * q] >> (8 * p)) & 0xffu) | (((r[i][4 * q + 1] >> (8 * p)) & 0xffu) << 8) |
+                    (((r[i][4 * q + 2] >> (8 * p)) & 0xffu) << 16) | (((r[i][4 * q + 3] >> (8 * p)) & 0xffu) << 24);
+          uint8_t *d = plane_dst(g.out, g.ldo, g.M, m, n0, p);
+          if (g.tma_store) {  // 16-byte aligned rows
+            reinterpret_cast<uint4 *>(d)[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            reinterpret_cast<uint4 *>(d)[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) d[q] = static_cast<uint8_t>(wv[q >> 2] >> (8 * (q & 3)));
+          }
+        }
       }
     } else {
       // row-major: stage the 32 x 32 tile (128-byte swizzle), then one TMA
@@ -771,7 +807,7 @@ __device__ __forceinline__ bool epilogue_swap(const EpiCtx &c) {
   int32_t cr = 0;
   if (KIND == Kind::I8) {
     sw = __ldg(g.col_scale + n);
-    cr = __ldg(g.col_corr + n);
+    cr = __ldg((MODE == 5 ? g.col_sum7 : g.col_corr) + n);
   }
   if (BIAS) bn_ = __ldg(g.bias + n);
 #pragma unroll
@@ -779,7 +815,11 @@ __device__ __forceinline__ bool epilogue_swap(const EpiCtx &c) {
     const int m = c.w.tb * BN + j;
     if (m >= g.M) break;
     const float v = finish<KIND, MODE, BIAS>(r[j], cr, sw, scr[j], bn_);
-    if (MODE == 3) {
+    if (MODE == 5) {
+      const uint32_t u = __float_as_uint(v);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) *plane_dst(g.out, g.ldo, g.M, m, n, p) = static_cast<uint8_t>(u >> (8 * p));
+    } else if (MODE == 3) {
       if (n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = v;
     } else {
       g.out[static_cast<long long>(m) * g.ldo + n] = v;
@@ -807,6 +847,7 @@ __device__ __forceinline__ bool epilogue_dispatch(const EpiCtx &c, int mode, boo
     case 5: return epilogue_unit<KIND, BN, SWAP, 2, true>(c);
     case 6: return epilogue_unit<KIND, BN, SWAP, 3, false>(c);
     case 7: return epilogue_unit<KIND, BN, SWAP, 3, true>(c);
+    case 10: return epilogue_unit<KIND, BN, SWAP, 5, false>(c);
     default: return epilogue_unit<KIND, BN, SWAP, 4, false>(c);
   }
 }

@@ -35,6 +35,7 @@ struct GemmArgs {
   const float *row_scale = nullptr;  // I8: [M]
   const float *col_scale = nullptr;  // I8: [N]
   const int32_t *col_corr = nullptr; // I8: [N]
+  const int32_t *col_sum7 = nullptr; // I8, plane export: [N] (sum_k w[n][k]) << 7
   const float *bias = nullptr;       // [N] or null
   int32_t *ws = nullptr;             // split-K accumulators
   uint32_t *ws_count = nullptr;      // split-K arrival counters (self-resetting)
@@ -85,7 +86,7 @@ inline size_t kblock_bytes(Kind kind, int k, int ncols) {
 }
 cudaError_t launch_repack_w8(int8_t *dst, const uint8_t *deep, int k, int n0, int ncols,
                              cudaStream_t st);
-cudaError_t launch_colsum_corr(int32_t *corr, const int8_t *wk, const int32_t *sums, int k,
+cudaError_t launch_colsum_corr(int32_t *corr, int32_t *sum7, const int8_t *wk, const int32_t *sums, int k,
                                int n0, int ncols, cudaStream_t st);
 cudaError_t launch_check_ones(uint32_t *flag, const float *v, int count, cudaStream_t st);
 cudaError_t launch_repack_f16(uint16_t *dst, const uint16_t *perm, int k, int n0, int ncols,

@@ -74,6 +74,7 @@ def lib() -> ctypes.CDLL:
         "htpg_f16_run": (I, [P, P, I, P, P, I, I, I, P]),
         "htpg_w8a8_run_static": (I, [P, P, I, P, P, I, I, I, P]),
         "htpg_w8a8_run_gather": (I, [P, ctypes.POINTER(P), I, I, P, P, I, I, I, P]),
+        "htpg_w8a8_run_planes": (I, [P, P, P, I, P, P]),
         "htpg_ipc_export": (I, [P, P]),
         "htpg_ipc_import": (I, [P, ctypes.POINTER(P)]),
         "htpg_ipc_close": (I, [P]),

@@ -59,6 +59,13 @@ extern "C" {
  * sum_k (code-128)*w[n][k] (equal to the reference's acc - (colsum << 7)),
  * stored as int32; FP16: the FP32 accumulator. */
 #define HTPG_MODE_RAW 4
+/* W8A8 only: the reference's raw byte-plane export (the opcode-15 CPU-epilogue
+ * layout).  For each 64-row tile (rows = its valid rows) and 32-column half,
+ * byte p (LSB first) of the unsigned-code accumulator sum_k code_u8*w of
+ * (m, n) is byte p*rows*32 + (m%64)*32 + n%32 of the half's stream, which
+ * fills the half's 32 FP32 output columns of the tile's rows, 128 bytes a row.
+ * The output must be dense (ldo = n). */
+#define HTPG_MODE_PLANES 5
 
 /* ---- library / device ------------------------------------------------- */
 /* Select `device` for this thread and check it is sm_100.
@@ -84,6 +91,7 @@ int htpg_quantize_rows(int8_t *codes, float *row_scales, const float *x, const f
 
 /* ---- prepared weights ------------------------------------------------- */
 typedef struct htpg_weights htpg_weights;
+struct W8A8CpuControl; /* include/op_reg.h */
 
 /* Repack a W8A8 constants blob (device memory, reference layout:
  * include/op_reg.h W8A8Header) into the tensor-core layout; columns
@@ -109,10 +117,18 @@ int htpg_w8a8_run(const htpg_weights *w, float *out, int ldo, const float *x, co
 int htpg_f16_run(const htpg_weights *w, float *out, int ldo, const float *x, const float *bias,
                  int m, int channels, int mode, void *stream);
 
+/* Plane export on prepared weights: HTPG_MODE_PLANES into dst ([m][n] FP32
+ * bytes), then fills `control` (host memory) as hmx_mat_mul_native_w8a8_cpu
+ * does.  Synchronous.  No counterpart of this exact signature in the reference
+ * (its kernel takes the constants blob). */
+int htpg_w8a8_run_planes(const htpg_weights *w, float *dst, const float *x, int m,
+                         struct W8A8CpuControl *control, void *stream);
+
 /* ---- column-sharded run with a fused output exchange -------------------- */
 /* Multi-GPU form of htpg_w8a8_run for a weight split by output columns (N)
- * across ranks, each rank holding a column block: the epilogue stores every finished output tile to each of outs[0..n_outs)
- * (n_outs <= 8) with TMA, so one launch both computes this rank's column block
+ * across ranks, each rank holding a column block: the epilogue stores every
+ * finished output tile to each of outs[0..n_outs) (n_outs <= 8) with TMA, so
+ * one launch both computes this rank's column block
  * and writes it into every rank's row-major [M][N] output over NVLink.  outs[i]
  * points at the block's first column in buffer i (its row pitch is ldo floats,
  * ldo = the full N); peers' buffers come from htpg_ipc_import.  Needs the
@@ -198,13 +214,16 @@ int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]);
  * synchronous (they return once the output is written).  The FP16 weight
  * type __fp16 of the reference is passed as its 16-bit pattern. */
 struct NativeW8A8Profile;
-struct W8A8CpuControl;
 int hmx_mat_mul_native_w8a8(float *dst, const float *activation, const uint8_t *constants, int m,
                             int k, int n);
 int hmx_mat_mul_native_w8a8_profiled(float *dst, const float *activation, const uint8_t *constants,
                                      int m, int k, int n, struct NativeW8A8Profile *profile);
-/* Raw byte-plane export of the HMX readout: not available on this device (-75;
- * -12 when control is NULL), as on a DSP without the feature. */
+/* CPU-epilogue form of opcode 15 (reference: linear_w8a8.c:205-227, 512-526):
+ * dst receives the raw byte planes of the unsigned-code INT32 accumulators
+ * (see HTPG_MODE_PLANES) instead of FP32 values, and the control block (host
+ * memory, include/op_reg.h W8A8CpuControl) the row scales, one batch
+ * {0, m, 0, n/64} and produced = 1 (published last).  m <= 4096 (the control
+ * block holds 4096 row scales); -12 when control is NULL. */
 int hmx_mat_mul_native_w8a8_cpu(float *dst, const float *activation, const uint8_t *constants,
                                 int m, int k, int n, struct W8A8CpuControl *control);
 int hmx_mat_mul_f16_epilogue(float *dst, const float *activation, const uint16_t *weight,

@@ -72,6 +72,13 @@ void orc_quantize_rows(uint8_t *codes, float *scales, const float *x, const floa
 /* acc[m][n] = sum_k code[m][k] * w[n][k]  (UINT8 x INT8 -> INT32, a4). */
 void orc_w8a8_accumulate(int32_t *acc, const uint8_t *codes, const int8_t *w_nk,
                          int m, int k, int n);
+/* CPU-epilogue export (reference: linear_w8a8.c:205-227, read_int32 :130-138):
+ * the unsigned-code accumulators acc[m][n] as byte planes in the output
+ * tensor's bytes.  out: m*n*4 bytes (the FP32 output tensor).  For every 64-row
+ * tile (rows = its valid rows), 64-column group g and half h: the half's four
+ * 64x32-byte planes (byte p of each accumulator, row-major) are concatenated
+ * and written 128 bytes per output row into columns g*64+h*32 .. +31. */
+void orc_w8a8_planes(uint8_t *out, const int32_t *acc, int m, int n);
 /* Full operator on a subset of rows.  rows: `nrows` row indices of x (NULL =
  * rows 0..m-1 with nrows = m).  out: [nrows][n] for mode 0-2; for mode 3
  * [channels][nrows].  bias may be NULL.  Also returns codes/scales/signed

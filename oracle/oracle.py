@@ -62,6 +62,7 @@ def lib(kind: str = "st") -> ctypes.CDLL:
     L.orc_quantize_rows.argtypes = [P, P, P, P, I, I]
     L.orc_w8a8_accumulate.argtypes = [P, P, P, I, I, I]
     L.orc_w8a8_linear_rows.argtypes = [P, P, P, P, I, I, I, I, I, P, I, P, P, P]
+    L.orc_w8a8_planes.argtypes = [P, P, I, I]
     L.orc_epilogue_activation.argtypes = [ctypes.c_float, I]
     L.orc_epilogue_activation.restype = ctypes.c_float
     L.orc_f16_linear_rows.argtypes = [P, P, P, P, I, I, I, I, I, I, P, I]
@@ -122,6 +123,12 @@ def w8a8_unpack(blob: np.ndarray, k: int, n: int) -> np.ndarray:
     return w
 
 
+def blob_inverse(blob: np.ndarray, k: int, n: int) -> np.ndarray:
+    """inverse[k] of a constants blob (W8A8Header.inverse_offset = 128 + k*n + 8n)."""
+    off = 128 + k * n + 8 * n
+    return blob[off:off + 4 * k].view(np.float32).copy()
+
+
 def f16_pack_permuted(w_kn_bits: np.ndarray) -> np.ndarray:
     k, n = w_kn_bits.shape
     out = np.empty(k * n, np.uint16)
@@ -148,6 +155,19 @@ def w8a8_accumulate(codes: np.ndarray, w_nk: np.ndarray, kind="st"):
     lib(kind).orc_w8a8_accumulate(_p(acc), _p(np.ascontiguousarray(codes)),
                                   _p(np.ascontiguousarray(w_nk, np.int8)), m, k, n)
     return acc
+
+
+def w8a8_planes(x, blob, k, n, kind="st"):
+    """Oracle opcode-15 CPU-epilogue output: (plane bytes [m][n*4] uint8, row
+    scales, unsigned-code INT32 accumulators)."""
+    m = x.shape[0]
+    inverse = blob_inverse(blob, k, n)
+    codes, scales = quantize_rows(x, None if np.all(inverse == 1.0) else inverse, kind)
+    w_nk = w8a8_unpack(blob, k, n)
+    acc = w8a8_accumulate(codes, w_nk, kind)
+    out = np.zeros((m, n * 4), np.uint8)
+    lib(kind).orc_w8a8_planes(_p(out), _p(acc), m, n)
+    return out, scales, acc
 
 
 def w8a8_linear(x, blob, k, n, bias=None, channels=None, mode=0, rows=None, kind="st",

@@ -269,3 +269,29 @@ def test_seeded_generators_are_deterministic():
     assert abs(float(np.std(O.normal(100000, 1.0, 0, 1, 7))) - 1.0) < 0.02
     w = O.int8_uniform(100000, 3)
     assert w.min() == -127 and w.max() == 127
+
+
+@pytest.mark.parametrize("m,k,n", [(70, 64, 128), (64, 32, 64), (130, 96, 192), (5, 32, 64)])
+def test_plane_export_layout(m, k, n):
+    """The CPU-epilogue export (linear_w8a8.c:205-227): walking each half's
+    byte stream as export_plane_tile lays it out and joining plane p as byte p
+    (the readout order of output_tile_impl, :153-163) gives back the
+    unsigned-code accumulators sum_k code_u8 * w."""
+    c = O.make_w8a8(9, "planes", m, k, n, 0.01, False, 0, inverse_range=(0.5, 2.0))
+    planes, scales, acc = O.w8a8_planes(c.x, c.blob, k, n)
+    pb = planes.reshape(m, n * 4)
+    dec = np.zeros((m, n), np.uint32)
+    for t in range((m + 63) // 64):
+        rows = min(64, m - t * 64)
+        for g in range(n // 64):
+            for h in range(2):
+                col = (g * 64 + h * 32) * 4
+                stream = np.concatenate([pb[t * 64 + r, col:col + 128] for r in range(rows)])
+                for p in range(4):
+                    plane = stream[p * rows * 32:(p + 1) * rows * 32].reshape(rows, 32).astype(np.uint32)
+                    dec[t * 64:t * 64 + rows, g * 64 + h * 32:g * 64 + h * 32 + 32] |= plane << (8 * p)
+    assert np.array_equal(dec.view(np.int32), acc)
+    codes, sc = O.quantize_rows(c.x, O.blob_inverse(c.blob, k, n))
+    w = O.w8a8_unpack(c.blob, k, n).astype(np.int64)
+    assert np.array_equal((codes.astype(np.int64) @ w.T).astype(np.int32), acc)
+    assert np.array_equal(sc, scales)
