@@ -280,6 +280,33 @@ def suite(torch, L, htpg, dev, flush, reps=20, only=None):
         w8a8_case(name, 4096, k, n, 0x5EED0002 + k + n, 0.005, mode, b)
     if not only:
         res["C3_stack_us"] = sum(res[c]["us"] for c in ("C3_qkv", "C3_out", "C3_fc1", "C3_fc2"))
+    # opcode 17: SD-VAE-decoder-shaped convolutions (512 -> 512 channels, 3x3,
+    # pad 1) at 64x64, and after a nearest 2x upsample (128x128 output)
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    for name, hw, up in (("C6_conv_64", 64, 1), ("C6_upconv_128", 64, 2)):
+        if only and name != only:
+            continue
+        ic = oc = 512
+        ow = oh = hw * up
+        kp, np_ = 9 * ic, oc
+        g = torch.Generator(device=dev)
+        g.manual_seed(0x5EED0006 + up)
+        x = torch.randn(1, ic, hw, hw, device=dev, generator=g)
+        wkn = (torch.randn(kp, np_, device=dev, generator=g) * 0.02).half()
+        bias = torch.randn(oc, device=dev, generator=g) * 0.01
+        wperm = torch.from_numpy(htpg.pack_f16_permuted(wkn.cpu().numpy().view(np.uint16)).view(np.int16)).to(dev)
+        wc = htpg.f16_weights(wperm, kp, np_)
+        prm = dict(iw=hw, ih=hw, ic=ic, oc=oc, batch=1, ow=ow, oh=oh, kw=3, kh=3, sx=1, sy=1, px=1, py=1, dx=1,
+                   dy=1, kp=kp, np=np_, upscale=up)
+        pbuf = (ctypes.c_uint8 * 124).from_buffer_copy(htpg.conv_params_bytes(prm))
+        out = torch.empty(1, oc, oh, ow, device=dev)
+        tm = timed(lambda: htpg.check(L.htpg_conv2d_run(wc.handle, htpg.ptr(out), htpg.ptr(x), htpg.ptr(bias), pbuf,
+                                                         htpg.stream_ptr()), name))
+        spatial = ow * oh
+        # algorithmic bytes: input read, FP16 weight, bias, FP32 output
+        record(name, spatial, kp, oc, tm, 4 * ic * hw * hw + 2 * kp * np_ + 4 * oc + 4 * oc * spatial, bf16)
+        res[name]["note"] = "conv as im2col GEMM: M = output pixels, K = 9*ic, N = oc; FP16 in, FP32 accumulate"
+        del wc, wperm
     # C5: decode shapes, no epilogue
     for m in (1, 4, 16):
         for name, k, n in (("up", 4096, 14336), ("down", 14336, 4096)):

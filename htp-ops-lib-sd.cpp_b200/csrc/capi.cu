@@ -5,7 +5,9 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
+#include <climits>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -458,10 +460,13 @@ namespace {
 
 // outs[0..n_outs): destinations of the output (n_outs > 1: the same output
 // block in several buffers, each written by TMA stores from the epilogue).
+// act_f16: FP16 activations [m][k] already in HBM (FP16 weights only; x is
+// then unused and no conversion runs).
 int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const float *x,
                const float *bias, int m, int channels, int mode, void *stream,
-               const float **row_scales_out = nullptr) {
-  if (!w || !outs || n_outs < 1 || n_outs > kMaxOutputs || !x) return HTPG_EARGS;
+               const float **row_scales_out = nullptr, const uint16_t *act_f16 = nullptr) {
+  if (act_f16 && w && w->kind != Kind::F16) return HTPG_EARGS;
+  if (!w || !outs || n_outs < 1 || n_outs > kMaxOutputs || (!x && !act_f16)) return HTPG_EARGS;
   for (int i = 0; i < n_outs; ++i)
     if (!outs[i]) return HTPG_EARGS;
   float *out = outs[0];
@@ -471,7 +476,7 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
     return HTPG_ECAPACITY;
   if (channels == 0) channels = n;
   if (channels < 1 || channels > n || (mode != 3 && channels != n)) return HTPG_ECAPACITY;
-  if (reinterpret_cast<uintptr_t>(x) & 15u) return HTPG_ECONTROL;
+  if ((reinterpret_cast<uintptr_t>(act_f16 ? static_cast<const void *>(act_f16) : x)) & 15u) return HTPG_ECONTROL;
   if (reinterpret_cast<uintptr_t>(out) & 3u) return HTPG_ECONTROL;
   if (ldo == 0) ldo = mode == 3 ? m : n;
   if ((mode == 3 && ldo < m) || (mode != 3 && ldo < n) || (mode == HTPG_MODE_PLANES && ldo != n))
@@ -491,15 +496,16 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
   const size_t wsk_bytes = kSplitKRegion;
   if (splitk_ws_bytes(plan) + splitk_count_bytes(plan) > wsk_bytes) return HTPG_ENOPLAN;
   const size_t act_elem = w->kind == Kind::I8 ? 1 : 2;
-  const size_t act_bytes = align_up(static_cast<size_t>(m) * k * act_elem, 1024);
+  const size_t act_bytes = act_f16 ? 0 : align_up(static_cast<size_t>(m) * k * act_elem, 1024);
   const size_t scale_bytes = align_up(4u * static_cast<size_t>(m), 1024);
   void *base = nullptr;
   rc = workspace(d, st, wsk_bytes + act_bytes + scale_bytes, &base);
   if (rc) return rc;
   int32_t *wsk = static_cast<int32_t *>(base);
   uint32_t *cnt = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(base) + splitk_ws_bytes(plan));
-  uint8_t *act = static_cast<uint8_t *>(base) + wsk_bytes;
-  float *scales = reinterpret_cast<float *>(act + act_bytes);
+  uint8_t *act = act_f16 ? reinterpret_cast<uint8_t *>(const_cast<uint16_t *>(act_f16))
+                         : static_cast<uint8_t *>(base) + wsk_bytes;
+  float *scales = reinterpret_cast<float *>(static_cast<uint8_t *>(base) + wsk_bytes + act_bytes);
   if (row_scales_out) *row_scales_out = scales;
 
   const bool prof = g_profiling != 0;
@@ -515,10 +521,10 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
     cudaEventRecord(pe.e[0], st);
   }
   if (prof) cudaEventRecord(d->ev[0], st);
-  cudaError_t e;
+  cudaError_t e = cudaSuccess;
   if (w->kind == Kind::I8)
     e = launch_quantize_rows(reinterpret_cast<int8_t *>(act), scales, x, w->inverse, m, k, st);
-  else
+  else if (!act_f16)
     e = launch_to_f16(reinterpret_cast<uint16_t *>(act), x, static_cast<long long>(m) * k, st);
   if (e != cudaSuccess) return record_cuda(e);
   if (prof) cudaEventRecord(d->ev[1], st);
@@ -636,6 +642,137 @@ extern "C" int htpg_w8a8_run_gather(const htpg_weights *w, float *const *outs, i
                                     void *stream) {
   if (!w || w->kind != Kind::I8) return HTPG_EARGS;
   return run_common(const_cast<htpg_weights *>(w), outs, n_outs, ldo, x, bias, m, channels, mode, stream);
+}
+
+// ---------------------------------------------------------------- opcode 17
+namespace {
+int cached_weights(Kind kind, const void *ptr, int k, int n, void *stream, htpg_weights **out);
+// im2col staging, per device, grown as needed (one chunk of output rows)
+struct ConvBuf {
+  void *base = nullptr;
+  size_t bytes = 0;
+};
+ConvBuf g_conv_buf[16];
+size_t g_conv_chunk_bytes = 256u << 20;  // FP16 im2col bytes per GEMM launch (staging budget)
+
+int conv_geometry_ok(const NativeConvParams *p) {
+  // the executor's acceptance rules (op_executor.cc:405-418)
+  if (p->iw <= 0 || p->ih <= 0 || p->ic <= 0 || p->oc <= 0 || p->batch <= 0 || p->ow <= 0 || p->oh <= 0 ||
+      p->kw <= 0 || p->kh <= 0 || p->sx <= 0 || p->sy <= 0 || p->dx <= 0 || p->dy <= 0 || p->kp % 32 ||
+      p->np % 32 || p->np < p->oc || p->kp < static_cast<int64_t>(p->kw) * p->kh * p->ic ||
+      (p->upscale != 1 && p->upscale != 2) ||
+      p->ow != (p->upscale * p->iw + 2 * p->px - p->dx * (p->kw - 1) - 1) / p->sx + 1 ||
+      p->oh != (p->upscale * p->ih + 2 * p->py - p->dy * (p->kh - 1) - 1) / p->sy + 1)
+    return 0;
+  const size_t in_size = static_cast<size_t>(p->iw) * p->ih * p->ic * p->batch * 4;
+  const size_t out_size = static_cast<size_t>(p->ow) * p->oh * p->oc * p->batch * 4;
+  return in_size <= INT32_MAX && out_size <= INT32_MAX && static_cast<size_t>(p->kp) * p->np * 2 <= INT32_MAX;
+}
+
+// Per image: im2col of a chunk of output rows into FP16, then the FP16 GEMM
+// (K = kp, N = np) with the bias + channel-major epilogue over oc channels
+// (mat_mul.c:2291-2343).  times (optional, synchronises): gather and GEMM ms.
+int conv_core(htpg_weights *w, float *dst, const float *x, const float *bias, const NativeConvParams *p,
+              cudaStream_t st, double *gather_ms, double *gemm_ms) {
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  const int spatial = p->ow * p->oh;
+  const size_t row_bytes = static_cast<size_t>(p->kp) * 2;
+  int chunk = static_cast<int>(std::min<size_t>(spatial, std::max<size_t>(128, g_conv_chunk_bytes / row_bytes)));
+  ConvBuf &cb = g_conv_buf[d->ordinal];
+  const size_t need = static_cast<size_t>(chunk) * row_bytes;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (cb.bytes < need) {
+      if (cb.base) {
+        cudaStreamSynchronize(st);
+        cudaFree(cb.base);
+        cb.base = nullptr;
+        cb.bytes = 0;
+      }
+      if (cudaMalloc(&cb.base, need) != cudaSuccess) {
+        cudaGetLastError();
+        return HTPG_ENOMEM;
+      }
+      cb.bytes = need;
+    }
+  }
+  const ConvGeom g = {p->iw, p->ih, p->ic, p->ow, p->oh, p->kw, p->kh, p->sx, p->sy,
+                      p->px, p->py, p->dx, p->dy, p->kp, p->upscale};
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+  const bool timed = gather_ms || gemm_ms;
+  if (timed) {
+    for (auto &e : ev) cudaEventCreate(&e);
+    *gather_ms = *gemm_ms = 0.0;
+  }
+  uint16_t *a = static_cast<uint16_t *>(cb.base);
+  for (int b = 0; b < p->batch && rc == HTPG_OK; ++b) {
+    const float *xb = x + static_cast<size_t>(b) * p->ic * p->ih * p->iw;
+    for (int m0 = 0; m0 < spatial; m0 += chunk) {
+      const int rows = std::min(chunk, spatial - m0);
+      if (timed) cudaEventRecord(ev[0], st);
+      cudaError_t e = launch_im2col_f16(a, xb, g, m0, rows, st);
+      if (e != cudaSuccess) {
+        rc = record_cuda(e);
+        break;
+      }
+      if (timed) cudaEventRecord(ev[1], st);
+      float *out = dst + static_cast<size_t>(b) * p->oc * spatial + m0;
+      rc = run_common(w, &out, 1, spatial, nullptr, bias, rows, p->oc, 3, st, nullptr, a);
+      if (rc) break;
+      if (timed) {
+        cudaEventRecord(ev[2], st);
+        cudaEventSynchronize(ev[2]);
+        float t01 = 0, t12 = 0;
+        cudaEventElapsedTime(&t01, ev[0], ev[1]);
+        cudaEventElapsedTime(&t12, ev[1], ev[2]);
+        *gather_ms += t01;
+        *gemm_ms += t12;
+      }
+    }
+  }
+  if (timed)
+    for (auto &e : ev) cudaEventDestroy(e);
+  return rc;
+}
+}  // namespace
+
+extern "C" int htpg_conv_set_chunk_bytes(size_t bytes) {
+  if (bytes == 0) return HTPG_EARGS;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_conv_chunk_bytes = bytes;
+  return HTPG_OK;
+}
+
+extern "C" int htpg_conv2d_run(const htpg_weights *w, float *dst, const float *x, const float *bias,
+                               const struct NativeConvParams *p, void *stream) {
+  if (!w || w->kind != Kind::F16 || !dst || !x || !p) return HTPG_EARGS;
+  if (!conv_geometry_ok(p)) return HTPG_EPAYLOAD;
+  if (w->k != p->kp || w->ncols != p->np) return HTPG_EARGS;
+  return conv_core(const_cast<htpg_weights *>(w), dst, x, bias, p, static_cast<cudaStream_t>(stream), nullptr,
+                   nullptr);
+}
+
+extern "C" int hmx_conv2d_nchw_f16(float *dst, const float *input, const uint16_t *weight, const float *bias,
+                                   struct NativeConvParams *p) {
+  if (!dst || !input || !weight || !p) return HTPG_EARGS;
+  if (!conv_geometry_ok(p)) return HTPG_EPAYLOAD;
+  const auto t0 = std::chrono::steady_clock::now();
+  htpg_weights *w = nullptr;
+  int rc = cached_weights(Kind::F16, weight, p->kp, p->np, nullptr, &w);
+  if (rc) return rc;
+  const double weight_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  double gather_ms = 0, gemm_ms = 0;
+  rc = conv_core(w, dst, input, bias, p, nullptr, &gather_ms, &gemm_ms);
+  if (rc == HTPG_OK) rc = htpg_check_device(nullptr, nullptr);
+  // the reference reports its phases in microseconds (mat_mul.c:2340); the
+  // epilogue is fused into the GEMM here, so the store phase is 0
+  p->gather_us = static_cast<int32_t>(gather_ms * 1e3);
+  p->weight_us = static_cast<int32_t>(weight_ms * 1e3);
+  p->hmx_us = static_cast<int32_t>(gemm_ms * 1e3);
+  p->store_us = 0;
+  return rc;
 }
 
 // ---------------------------------------------------------------- IPC

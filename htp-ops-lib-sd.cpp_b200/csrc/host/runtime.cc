@@ -22,6 +22,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <climits>
 #include <set>
 #include <thread>
 #include <tuple>
@@ -453,6 +454,46 @@ int exec_f16_epilogue(uint8_t *payload, size_t payload_size) {
   return stage_out({&out});
 }
 
+// ---- opcode 17: packed-FP16 NCHW convolution (op_executor.cc:405-425) ----------
+int exec_conv(uint8_t *payload, size_t payload_size) {
+  if (payload_size != sizeof(NativeConvParams)) return -1;
+  NativeConvParams *p = reinterpret_cast<NativeConvParams *>(payload);
+  if (p->iw <= 0 || p->ih <= 0 || p->ic <= 0 || p->oc <= 0 || p->batch <= 0 || p->ow <= 0 || p->oh <= 0 ||
+      p->kw <= 0 || p->kh <= 0 || p->sx <= 0 || p->sy <= 0 || p->dx <= 0 || p->dy <= 0 || p->kp % 32 ||
+      p->np % 32 || p->np < p->oc || p->kp < static_cast<int64_t>(p->kw) * p->kh * p->ic ||
+      (p->upscale != 1 && p->upscale != 2) ||
+      p->ow != (p->upscale * p->iw + 2 * p->px - p->dx * (p->kw - 1) - 1) / p->sx + 1 ||
+      p->oh != (p->upscale * p->ih + 2 * p->py - p->dy * (p->kh - 1) - 1) / p->sy + 1)
+    return -1;
+  const size_t in_size = static_cast<size_t>(p->iw) * p->ih * p->ic * p->batch * 4;
+  const size_t out_size = static_cast<size_t>(p->ow) * p->oh * p->oc * p->batch * 4;
+  const size_t w_size = static_cast<size_t>(p->kp) * p->np * 2;
+  if (in_size > INT32_MAX || out_size > INT32_MAX || w_size > INT32_MAX) return -1;
+  Operand out, act, wt, bias;
+  if (resolve(out, p->output.fd, p->output.offset, out_size) ||
+      resolve(act, p->activation.fd, p->activation.offset, in_size) ||
+      resolve(wt, p->weight.fd, p->weight.offset, w_size))
+    return -1;
+  if (p->bias.fd >= 0 && resolve(bias, p->bias.fd, p->bias.offset, static_cast<size_t>(p->oc) * 4)) return -1;
+  const auto t0 = Clock::now();
+  htpg_weights *w = nullptr;
+  int rc = exec_weights(wt, false, p->kp, p->np, &w);
+  if (rc) return rc;
+  const int32_t weight_us = elapsed_us(t0);
+  if ((rc = stage_in({&act, &bias}, {&out}))) return rc;
+  rc = htpg_conv2d_run(w, static_cast<float *>(out.device), static_cast<const float *>(act.device),
+                       bias.present ? static_cast<const float *>(bias.device) : nullptr, p, nullptr);
+  rc = sync_status(rc);
+  p->elapsed_us = elapsed_us(t0);
+  // im2col and GEMM run back to back on the device; the epilogue is fused
+  p->weight_us = weight_us;
+  p->gather_us = 0;
+  p->hmx_us = p->elapsed_us - weight_us;
+  p->store_us = 0;
+  if (rc) return rc;
+  return stage_out({&out});
+}
+
 // ---- opcode 1: packed FP16 GEMM, no epilogue (op_executor.cc:473-540) ----------
 bool op_trace_enabled() { return std::getenv("HTPG_OP_TRACE") != nullptr; }
 
@@ -510,6 +551,7 @@ extern "C" int execute_op_simple(struct OpComputeRequest *req, size_t req_size) 
     case HTP_OPS_MAT_MUL_NATIVE_W8A8: return exec_w8a8(req->payload, payload_size);
     case HTP_OPS_MAT_MUL_F16_EPILOGUE: return exec_f16_epilogue(req->payload, payload_size);
     case HTP_OPS_MAT_MUL_PERMUTED_W16A32: return exec_w16a32(req->payload, payload_size);
+    case HTP_OPS_CONV2D_NCHW_F16: return exec_conv(req->payload, payload_size);
     default:
       // Registered opcodes outside this library's path are refused so the
       // caller keeps them on its own backend; unknown opcodes are ignored with

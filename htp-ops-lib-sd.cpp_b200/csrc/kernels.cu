@@ -409,6 +409,63 @@ cudaError_t launch_repack_f16(uint16_t *dst, const uint16_t *perm, int k, int n0
   return counted(cudaGetLastError());
 }
 
+// ====================================================================== conv
+// im2col of opcode 17 (the reference gathers the same values, mat_mul.c:2230-2290):
+// row t (output position oy*ow + ox), column col = ci*kh*kw + ky*kw + kx reads
+// the nearest-upsampled input at (ox*sx - px + kx*dx, oy*sy - py + ky*dy).
+// A block transposes a tile of 128 rows x 32 columns through shared memory:
+// consecutive threads gather consecutive rows of one column (consecutive x,
+// coalesced), then the FP16 tile leaves as 64-byte row segments.
+constexpr int kI2cRows = 128, kI2cCols = 32, kI2cPitch = kI2cCols + 2;  // halves per staged row
+__global__ void __launch_bounds__(256) im2col_f16_kernel(uint16_t *__restrict__ a, const float *__restrict__ x,
+                                                        ConvGeom g, int m0, int rows) {
+  __shared__ uint16_t tile[kI2cRows * kI2cPitch];
+  __shared__ int col_ci[kI2cCols], col_ky[kI2cCols], col_kx[kI2cCols];
+  grid_dependents_launch();  // the GEMM may start its prologue and weight prefetch
+  const int r0 = blockIdx.x * kI2cRows, c0 = blockIdx.y * kI2cCols;
+  if (threadIdx.x < kI2cCols) {
+    const int col = c0 + threadIdx.x, khw = g.kw * g.kh;
+    const int ci = col / khw, rem = col - ci * khw, ky = rem / g.kw;
+    col_ci[threadIdx.x] = ci;
+    col_ky[threadIdx.x] = ky * g.dy;
+    col_kx[threadIdx.x] = (rem - ky * g.kw) * g.dx;
+  }
+  __syncthreads();
+  const int tr = threadIdx.x % kI2cRows, tc = threadIdx.x / kI2cRows;  // row, column phase (0..1)
+  const int r = r0 + tr;
+  const bool row_ok = r < rows;
+  const int t = m0 + (row_ok ? r : 0);
+  const int oy = t / g.ow, ox = t - oy * g.ow;
+  const int xbase = ox * g.sx - g.px, ybase = oy * g.sy - g.py;
+  const int wu = g.iw * g.up, hu = g.ih * g.up;
+  const int ush = g.up == 2 ? 1 : 0;  // nearest upsample: source index = index >> 1
+#pragma unroll 4
+  for (int cc = tc; cc < kI2cCols; cc += 2) {
+    const int ci = col_ci[cc], xx = xbase + col_kx[cc], yy = ybase + col_ky[cc];
+    const float v = (row_ok && ci < g.ic && xx >= 0 && xx < wu && yy >= 0 && yy < hu)
+                        ? __ldg(x + (static_cast<size_t>(ci) * g.ih + (yy >> ush)) * g.iw + (xx >> ush))
+                        : 0.0f;
+    tile[tr * kI2cPitch + cc] = __half_as_ushort(__float2half_rn(v));
+  }
+  __syncthreads();
+  // 128 rows x 64 bytes = 512 segments of 16 bytes, two per thread
+#pragma unroll
+  for (int q = threadIdx.x; q < kI2cRows * 4; q += 256) {
+    const int rr = q >> 2, part = q & 3;
+    if (r0 + rr >= rows) continue;
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(tile + rr * kI2cPitch + part * 8);
+    *reinterpret_cast<uint4 *>(a + static_cast<size_t>(r0 + rr) * g.kp + c0 + part * 8) =
+        make_uint4(src[0], src[1], src[2], src[3]);
+  }
+}
+
+cudaError_t launch_im2col_f16(uint16_t *a, const float *x, const ConvGeom &g, int m0, int rows,
+                              cudaStream_t st) {
+  const dim3 grid(static_cast<unsigned>((rows + kI2cRows - 1) / kI2cRows), static_cast<unsigned>(g.kp / kI2cCols));
+  im2col_f16_kernel<<<grid, 256, 0, st>>>(a, x, g, m0, rows);
+  return counted(cudaGetLastError());
+}
+
 // ====================================================================== GEMM
 // Optional epilogue activation (mat_mul.c:788-826): GELU(tanh) as
 // x*sigmoid(z), z = 1.5957691216057308*(x + 0.044715 x^3), QuickGELU as

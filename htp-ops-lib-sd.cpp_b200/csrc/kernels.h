@@ -92,6 +92,16 @@ cudaError_t launch_check_ones(uint32_t *flag, const float *v, int count, cudaStr
 cudaError_t launch_repack_f16(uint16_t *dst, const uint16_t *perm, int k, int n0, int ncols,
                               cudaStream_t st);
 
+// Opcode-17 geometry (NativeConvParams without the buffers).
+struct ConvGeom {
+  int iw, ih, ic, ow, oh, kw, kh, sx, sy, px, py, dx, dy, kp, up;
+};
+// im2col rows [m0, m0 + rows) of one image (x: [ic][ih][iw] FP32) into
+// a: [rows][kp] FP16 (round to nearest even), zero outside the (upsampled)
+// image and for K columns past ic*kh*kw.
+cudaError_t launch_im2col_f16(uint16_t *a, const float *x, const ConvGeom &g, int m0, int rows,
+                              cudaStream_t st);
+
 // Kernel launches issued since load (all launchers above count themselves).
 uint64_t launches();
 

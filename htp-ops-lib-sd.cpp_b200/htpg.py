@@ -75,6 +75,9 @@ def lib() -> ctypes.CDLL:
         "htpg_w8a8_run_static": (I, [P, P, I, P, P, I, I, I, P]),
         "htpg_w8a8_run_gather": (I, [P, ctypes.POINTER(P), I, I, P, P, I, I, I, P]),
         "htpg_w8a8_run_planes": (I, [P, P, P, I, P, P]),
+        "htpg_conv2d_run": (I, [P, P, P, P, P, P]),
+        "htpg_conv_set_chunk_bytes": (I, [S]),
+        "hmx_conv2d_nchw_f16": (I, [P, P, P, P, P]),
         "htpg_ipc_export": (I, [P, P]),
         "htpg_ipc_import": (I, [P, ctypes.POINTER(P)]),
         "htpg_ipc_close": (I, [P]),
@@ -311,3 +314,15 @@ def ipc_import(handle: bytes) -> int:
     check(lib().htpg_ipc_import(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(p)),
           "htpg_ipc_import")
     return p.value
+
+
+# ------------------------------------------------------------------ opcode 17
+CONV_FIELDS = ("iw", "ih", "ic", "oc", "batch", "ow", "oh", "kw", "kh", "sx", "sy", "px", "py", "dx", "dy",
+               "kp", "np", "upscale")
+
+
+def conv_params_bytes(prm: dict, output=(-1, 0), activation=(-1, 0), weight=(-1, 0), bias=(-1, 0)) -> bytes:
+    """124-byte NativeConvParams (include/op_reg.h) with the timing fields zero."""
+    import struct
+    bufs = struct.pack("<8i", *output, *activation, *weight, *bias)
+    return bufs + struct.pack("<18i", *[prm[f] for f in CONV_FIELDS]) + b"\0" * 20

@@ -124,6 +124,25 @@ int htpg_f16_run(const htpg_weights *w, float *out, int ldo, const float *x, con
 int htpg_w8a8_run_planes(const htpg_weights *w, float *dst, const float *x, int m,
                          struct W8A8CpuControl *control, void *stream);
 
+/* ---- opcode 17: packed-FP16 2-D convolution, NCHW (reference:
+ * mat_mul.c:2189-2343) ------------------------------------------------- */
+/* On prepared FP16 weights (htpg_f16_weights_create(weight, kp, np, ...)):
+ * per image, im2col (nearest 2x upsample when upscale = 2; FP16 round to
+ * nearest) into an internal grow-only buffer, then the FP16 GEMM with the
+ * bias + channel-major epilogue: dst [batch][oc][oh][ow].  Geometry checks as
+ * the reference executor (HTPG_EPAYLOAD). */
+struct NativeConvParams; /* include/op_reg.h */
+int htpg_conv2d_run(const htpg_weights *w, float *dst, const float *x, const float *bias,
+                    const struct NativeConvParams *p, void *stream);
+/* Budget of the im2col staging buffer (default 256 MiB): each GEMM launch
+ * covers max(128, bytes / (2*kp)) output rows of one image. */
+int htpg_conv_set_chunk_bytes(size_t bytes);
+/* The reference's kernel name: device pointers, the weight in the permuted FP16
+ * layout [kp][np] (cached per pointer like the other one-call entry points);
+ * synchronous; fills gather_us, weight_us, hmx_us, store_us. */
+int hmx_conv2d_nchw_f16(float *dst, const float *input, const uint16_t *weight, const float *bias,
+                        struct NativeConvParams *p);
+
 /* ---- column-sharded run with a fused output exchange -------------------- */
 /* Multi-GPU form of htpg_w8a8_run for a weight split by output columns (N)
  * across ranks, each rank holding a column block: the epilogue stores every
@@ -176,8 +195,11 @@ int htpg_w8a8_run_static(const htpg_weights *w, float *out, int ldo, const float
 /* ---- one-call linear operators (weights cached by pointer) ------------- */
 /* W8A8 linear, opcode 15 (reference: linear_w8a8.c:327-530) plus the
  * optional opcode-16 epilogue (extension).  constants: device copy of the
- * blob.  The repacked weight is cached keyed by (constants, k, n); a caller
- * that rewrites a blob in place calls htpg_weight_cache_drop(constants). */
+ * blob.  The repacked weight is cached keyed by (address, k, n): a caller that
+ * rewrites a blob in place, or frees it and may get the same address for a
+ * different weight (caching allocators do), calls
+ * htpg_weight_cache_drop(address) first.  The same holds for every one-call
+ * entry point below (hmx_* names, htpg_f16_linear, hmx_conv2d_nchw_f16). */
 int htpg_w8a8_linear(float *out, const float *x, const void *constants, const float *bias,
                      int m, int k, int n, int channels, int mode, void *stream);
 /* Packed FP16 GEMM with fused epilogue, opcodes 1 and 16

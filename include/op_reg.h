@@ -8,6 +8,7 @@
  *   opcode 15  HTP_OPS_MAT_MUL_NATIVE_W8A8      NativeW8A8Params (40 B), +profile (104 B),
  *                                               +CPU control (48 B), +epilogue (56 B, new)
  *   opcode 16  HTP_OPS_MAT_MUL_F16_EPILOGUE     F16EpilogueParams (56 B)
+ *   opcode 17  HTP_OPS_CONV2D_NCHW_F16          NativeConvParams (124 B)
  * The opcode numbering is the reference's, including the ops that are not
  * executed here (they are answered with AEE_EUNSUPPORTED by the dispatcher).
  */
@@ -160,6 +161,18 @@ struct F16EpilogueParams {
   int32_t m, k, n, channels, mode, elapsed_us;
 } __attribute__((packed));
 
+/* Opcode 17: packed-FP16 2-D convolution, NCHW in and out (reference:
+ * op_reg.h:491-495).  Input [batch][ic][ih][iw] FP32, optionally upsampled 2x
+ * by nearest neighbour (upscale 2) before the convolution; weight: permuted
+ * FP16 [kp][np] (the opcode-16 tile layout) with K index ci*kh*kw + ky*kw + kx
+ * (kp >= ic*kh*kw, np >= oc, both multiples of 32); output [batch][oc][oh][ow]
+ * FP32 = conv + bias.  The *_us fields are written back. */
+struct NativeConvParams {
+  struct RpcmemBufAddr output, activation, weight, bias;
+  int32_t iw, ih, ic, oc, batch, ow, oh, kw, kh, sx, sy, px, py, dx, dy, kp, np, upscale;
+  int32_t elapsed_us, gather_us, weight_us, hmx_us, store_us;
+} __attribute__((packed));
+
 #ifdef __cplusplus
 #define HTPB_STATIC_ASSERT(c, msg) static_assert(c, msg)
 #else
@@ -178,6 +191,7 @@ HTPB_STATIC_ASSERT(sizeof(struct NativeW8A8ProfileParams) == 104, "opcode 15 pro
 HTPB_STATIC_ASSERT(sizeof(struct MatMulParams) == 92, "opcode 1 payload ABI");
 HTPB_STATIC_ASSERT(sizeof(struct MatMulProfileParams) == 96, "opcode 1 profile payload ABI");
 HTPB_STATIC_ASSERT(sizeof(struct F16EpilogueParams) == 56, "opcode 16 payload ABI");
+HTPB_STATIC_ASSERT(sizeof(struct NativeConvParams) == 124, "opcode 17 payload ABI");
 HTPB_STATIC_ASSERT(HTP_OPS_MAT_MUL_PERMUTED_W16A32 == 1, "opcode 1");
 HTPB_STATIC_ASSERT(HTP_OPS_MAT_MUL_NATIVE_W8A8 == 15, "opcode 15");
 HTPB_STATIC_ASSERT(HTP_OPS_MAT_MUL_F16_EPILOGUE == 16, "opcode 16");

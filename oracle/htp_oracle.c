@@ -380,3 +380,41 @@ void orc_w8a8_planes(uint8_t *out, const int32_t *acc, int m, int n) {
     }
   }
 }
+
+/* Follows conv_gather_worker (mat_mul.c:2230-2290), general branch :2281-2286:
+ * for output position t and K column col (kx = (col%kw)*dx, ky =
+ * ((col/kw)%kh)*dy, ci = col/(kw*kh)), x = (t%ow)*sx - px + kx and
+ * y = (t/ow)*sy - py + ky in the upsampled image; the value is
+ * input[ci][y/up][x/up] inside it and 0 outside or for ci >= ic. */
+void orc_conv_im2col(float *a, const float *x, const int32_t *prm, int b) {
+  const int iw = prm[0], ih = prm[1], ic = prm[2], ow = prm[5], oh = prm[6], kw = prm[7], kh = prm[8];
+  const int sx = prm[9], sy = prm[10], px = prm[11], py = prm[12], dx = prm[13], dy = prm[14], kp = prm[15];
+  const int up = prm[17];
+  const float *in = x + (size_t)b * iw * ih * ic;
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < ow * oh; ++t) {
+    for (int col = 0; col < kp; ++col) {
+      const int kx = (col % kw) * dx, ky = ((col / kw) % kh) * dy, ci = col / (kw * kh);
+      const int xx = (t % ow) * sx - px + kx, yy = (t / ow) * sy - py + ky;
+      float v = 0.0f;
+      if (ci < ic && xx >= 0 && xx < iw * up && yy >= 0 && yy < ih * up)
+        v = in[((size_t)ci * ih + yy / up) * iw + xx / up];
+      a[(size_t)t * kp + col] = v;
+    }
+  }
+}
+
+/* hmx_conv2d_nchw_f16 (mat_mul.c:2291-2343): per batch, im2col then the FP16
+ * GEMM with the mode-3 (bias + channel-major) epilogue over oc channels. */
+void orc_conv2d_nchw_f16(float *out, const float *x, const uint16_t *wperm, const float *bias,
+                         const int32_t *prm, int round_acc_f16) {
+  const int oc = prm[3], batch = prm[4], ow = prm[5], oh = prm[6], kp = prm[15], np = prm[16];
+  const int spatial = ow * oh;
+  float *a = (float *)malloc((size_t)spatial * kp * sizeof(float));
+  for (int b = 0; b < batch; ++b) {
+    orc_conv_im2col(a, x, prm, b);
+    orc_f16_linear_rows(out + (size_t)b * oc * spatial, a, wperm, bias, spatial, kp, np, oc, 3, round_acc_f16,
+                        NULL, spatial);
+  }
+  free(a);
+}

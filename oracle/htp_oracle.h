@@ -96,6 +96,16 @@ void orc_f16_linear_rows(float *out, const float *x, const uint16_t *wperm, cons
                          int m, int k, int n, int channels, int mode, int round_acc_f16,
                          const int32_t *rows, int nrows);
 
+/* ---- opcode 17 packed-FP16 convolution (reference: mat_mul.c:2189-2343) --
+ * prm: iw, ih, ic, oc, batch, ow, oh, kw, kh, sx, sy, px, py, dx, dy, kp, np,
+ * upscale (NativeConvParams order).  x: [batch][ic][ih][iw]; wperm: permuted
+ * FP16 [kp][np]; out: [batch][oc][oh][ow].  im2col row pos = oy*ow + ox,
+ * column col = ci*kh*kw + ky*kw + kx, then the opcode-16 GEMM in mode 3. */
+void orc_conv2d_nchw_f16(float *out, const float *x, const uint16_t *wperm, const float *bias,
+                         const int32_t *prm, int round_acc_f16);
+/* One im2col matrix (FP32, [oh*ow][kp]) of batch b, as the reference gathers it. */
+void orc_conv_im2col(float *a, const float *x, const int32_t *prm, int b);
+
 /* Number of OpenMP threads this build uses (1 without OpenMP). */
 int orc_threads(void);
 /* Use n OpenMP threads from now on (ignored without OpenMP); launchers such as

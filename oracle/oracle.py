@@ -63,6 +63,8 @@ def lib(kind: str = "st") -> ctypes.CDLL:
     L.orc_w8a8_accumulate.argtypes = [P, P, P, I, I, I]
     L.orc_w8a8_linear_rows.argtypes = [P, P, P, P, I, I, I, I, I, P, I, P, P, P]
     L.orc_w8a8_planes.argtypes = [P, P, I, I]
+    L.orc_conv2d_nchw_f16.argtypes = [P, P, P, P, P, I]
+    L.orc_conv_im2col.argtypes = [P, P, P, I]
     L.orc_epilogue_activation.argtypes = [ctypes.c_float, I]
     L.orc_epilogue_activation.restype = ctypes.c_float
     L.orc_f16_linear_rows.argtypes = [P, P, P, P, I, I, I, I, I, I, P, I]
@@ -336,3 +338,44 @@ def config_c5() -> list[W8A8Case]:
             c = make_w8a8(4, f"{name}_m{m}", m, k, n, 0.0, False, 0, layer=i)
             cases.append(c)
     return cases
+
+
+# ---------------------------------------------------------------- opcode 17
+CONV_FIELDS = ("iw", "ih", "ic", "oc", "batch", "ow", "oh", "kw", "kh", "sx", "sy", "px", "py", "dx", "dy",
+               "kp", "np", "upscale")
+
+
+def conv_params(iw, ih, ic, oc, batch=1, kw=3, kh=3, sx=1, sy=1, px=1, py=1, dx=1, dy=1, upscale=1,
+                kp=None, np_=None) -> dict:
+    """NativeConvParams geometry with the output size the reference's executor
+    requires (op_executor.cc:410-414) and the smallest legal kp/np."""
+    ow = (upscale * iw + 2 * px - dx * (kw - 1) - 1) // sx + 1
+    oh = (upscale * ih + 2 * py - dy * (kh - 1) - 1) // sy + 1
+    kp = kp or -(-(kw * kh * ic) // 32) * 32
+    np_ = np_ or -(-oc // 32) * 32
+    return dict(iw=iw, ih=ih, ic=ic, oc=oc, batch=batch, ow=ow, oh=oh, kw=kw, kh=kh, sx=sx, sy=sy, px=px,
+                py=py, dx=dx, dy=dy, kp=kp, np=np_, upscale=upscale)
+
+
+def conv2d(x, wperm, bias, prm: dict, round_acc_f16=False, kind="st"):
+    """Oracle opcode-17 output [batch][oc][oh][ow]."""
+    p = np.array([prm[f] for f in CONV_FIELDS], np.int32)
+    out = np.empty((prm["batch"], prm["oc"], prm["oh"], prm["ow"]), np.float32)
+    lib(kind).orc_conv2d_nchw_f16(_p(out), _p(np.ascontiguousarray(x, np.float32)), _p(wperm),
+                                  _p(None if bias is None else np.ascontiguousarray(bias, np.float32)),
+                                  _p(p), 1 if round_acc_f16 else 0)
+    return out
+
+
+def conv_case(seed, prm: dict, bias=True):
+    """Seeded opcode-17 operands: x ~ N(0,1) NCHW, weight FP16 ~ N(0, 0.05)
+    logical [oc][ic][kh][kw] placed in the [kp][np] K x N matrix (zero
+    padding), bias ~ N(0, 0.01).  Returns x, w_logical (float, FP16 values),
+    wperm, bias."""
+    b, ic, ih, iw, oc, kh, kw = prm["batch"], prm["ic"], prm["ih"], prm["iw"], prm["oc"], prm["kh"], prm["kw"]
+    x = normal(b * ic * ih * iw, 1.0, 0, 1, seed).reshape(b, ic, ih, iw)
+    bits = f16_normal(oc * ic * kh * kw, 0.05, seed + 1).reshape(oc, ic, kh, kw)
+    wkn = np.zeros((prm["kp"], prm["np"]), np.uint16)
+    wkn[:ic * kh * kw, :oc] = bits.reshape(oc, ic * kh * kw).T
+    bb = normal(oc, 0.01, 0, 1, seed + 2) if bias else None
+    return x, bits.view(np.float16).astype(np.float32), f16_pack_permuted(wkn), bb

@@ -72,6 +72,16 @@ static const struct ref_fact facts[] = {
     {"offsetof.F16EpilogueParams.channels", FIELD(F16EpilogueParams, channels)},
     {"offsetof.F16EpilogueParams.mode", FIELD(F16EpilogueParams, mode)},
     {"offsetof.F16EpilogueParams.elapsed_us", FIELD(F16EpilogueParams, elapsed_us)},
+    {"sizeof.NativeConvParams", sizeof(struct NativeConvParams)},
+    {"offsetof.NativeConvParams.bias", FIELD(NativeConvParams, bias)},
+    {"offsetof.NativeConvParams.iw", FIELD(NativeConvParams, iw)},
+    {"offsetof.NativeConvParams.batch", FIELD(NativeConvParams, batch)},
+    {"offsetof.NativeConvParams.kw", FIELD(NativeConvParams, kw)},
+    {"offsetof.NativeConvParams.dy", FIELD(NativeConvParams, dy)},
+    {"offsetof.NativeConvParams.kp", FIELD(NativeConvParams, kp)},
+    {"offsetof.NativeConvParams.upscale", FIELD(NativeConvParams, upscale)},
+    {"offsetof.NativeConvParams.elapsed_us", FIELD(NativeConvParams, elapsed_us)},
+    {"offsetof.NativeConvParams.store_us", FIELD(NativeConvParams, store_us)},
     {"enum.HTP_OPS_RMS_NORM_F32", HTP_OPS_RMS_NORM_F32},
     {"enum.HTP_OPS_MAT_MUL_PERMUTED_W16A32", HTP_OPS_MAT_MUL_PERMUTED_W16A32},
     {"enum.HTP_OPS_MAT_MUL_NATIVE_W8A8", HTP_OPS_MAT_MUL_NATIVE_W8A8},

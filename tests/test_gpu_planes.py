@@ -32,6 +32,7 @@ def test_planes_and_control_match_oracle(gpu, lib, m, k, n):
     control = (ctypes.c_uint8 * CONTROL_BYTES)()
     struct.pack_into("<II", control, 0, 0, 0)
     rc = lib.hmx_mat_mul_native_w8a8_cpu(htpg.ptr(out), htpg.ptr(x), htpg.ptr(blob), m, k, n, control)
+    lib.htpg_weight_cache_drop(htpg.ptr(blob))   # cached by address (see the header)
     assert rc == 0, (rc, lib.htpg_last_cuda_error())
     got = out.cpu().numpy().view(np.uint8).reshape(m, n * 4)
     assert np.array_equal(got, planes)

@@ -326,3 +326,34 @@ def test_sessions_and_active_handle(L, monkeypatch):
     assert L.htp_ops_session_handle(None) == 2 ** 64 - 1
     L.close_dsp_session()
     assert not L.htp_ops_default_session()
+
+
+def _conv_prm(**kw):
+    return O.conv_params(**kw)
+
+
+@pytest.mark.parametrize("change", [dict(kp=32), dict(np_=32), dict(upscale=3), dict(ow_off=1), dict(size=-4)])
+def test_conv_payload_validation(L, change):
+    """Opcode 17 acceptance rules (op_executor.cc:405-418): -1 for a bad size,
+    kp < ic*kh*kw, np < oc, upscale not 1/2, or an output size that does not
+    follow from the geometry."""
+    prm = _conv_prm(iw=8, ih=8, ic=8, oc=40)
+    if "kp" in change:
+        prm["kp"] = change["kp"]          # 8*3*3 = 72 > 32
+    if "np_" in change:
+        prm["np"] = change["np_"]         # oc 40 > 32
+    if "upscale" in change:
+        prm["upscale"] = change["upscale"]
+    if "ow_off" in change:
+        prm["ow"] += 1
+    payload = htpg.conv_params_bytes(prm)
+    if "size" in change:
+        payload = payload[:change["size"]]
+    rc, _ = run(L, 17, payload)
+    assert rc == -1
+
+
+def test_conv_unmapped_buffers(L):
+    prm = _conv_prm(iw=8, ih=8, ic=8, oc=40)
+    rc, _ = run(L, 17, htpg.conv_params_bytes(prm, output=(4242, 0), activation=(4243, 0), weight=(4244, 0)))
+    assert rc == -1

@@ -295,3 +295,42 @@ def test_plane_export_layout(m, k, n):
     w = O.w8a8_unpack(c.blob, k, n).astype(np.int64)
     assert np.array_equal((codes.astype(np.int64) @ w.T).astype(np.int32), acc)
     assert np.array_equal(sc, scales)
+
+
+def _direct_conv(x, w, bias, prm):
+    """fp64 NCHW convolution on FP16-rounded operands, nearest 2x upsample."""
+    up = prm["upscale"]
+    xu = np.repeat(np.repeat(x.astype(np.float16).astype(np.float64), up, axis=2), up, axis=3)
+    b, ic, H, W = xu.shape
+    oc, _, kh, kw = w.shape
+    out = np.zeros((b, oc, prm["oh"], prm["ow"]))
+    for oy in range(prm["oh"]):
+        for ox in range(prm["ow"]):
+            for ky in range(kh):
+                for kx in range(kw):
+                    yy = oy * prm["sy"] - prm["py"] + ky * prm["dy"]
+                    xx = ox * prm["sx"] - prm["px"] + kx * prm["dx"]
+                    if 0 <= yy < H and 0 <= xx < W:
+                        out[:, :, oy, ox] += xu[:, :, yy, xx] @ w[:, :, ky, kx].astype(np.float64).T
+    if bias is not None:
+        out += bias[None, :, None, None]
+    return out
+
+
+@pytest.mark.parametrize("geom", [
+    dict(iw=9, ih=7, ic=3, oc=5),                                   # 3x3, pad 1
+    dict(iw=6, ih=5, ic=4, oc=40, upscale=2),                       # nearest 2x upsample
+    dict(iw=11, ih=9, ic=2, oc=8, sx=2, sy=2, px=0, py=0),          # stride 2, no padding
+    dict(iw=10, ih=8, ic=3, oc=7, dx=2, dy=2, px=2, py=2),          # dilation 2
+    dict(iw=5, ih=4, ic=33, oc=9, kw=1, kh=1, px=0, py=0, batch=2),  # 1x1, K padding, batch 2
+])
+def test_conv_oracle_matches_direct_convolution(geom):
+    """Opcode 17 (mat_mul.c:2189-2343): the oracle's im2col (the reference's
+    gather rule) + FP16 GEMM + channel-major epilogue equals a direct fp64
+    convolution of the FP16-rounded operands."""
+    prm = O.conv_params(**geom)
+    x, wl, wperm, bias = O.conv_case(77, prm)
+    got = O.conv2d(x, wperm, bias, prm)
+    ref = _direct_conv(x, wl, bias, prm)
+    assert got.shape == ref.shape
+    assert np.max(np.abs(got - ref)) <= 1e-5 * max(1.0, np.max(np.abs(ref)))
