@@ -307,6 +307,32 @@ def suite(torch, L, htpg, dev, flush, reps=20, only=None):
         record(name, spatial, kp, oc, tm, 4 * ic * hw * hw + 2 * kp * np_ + 4 * oc + 4 * oc * spatial, bf16)
         res[name]["note"] = "conv as im2col GEMM: M = output pixels, K = 9*ic, N = oc; FP16 in, FP32 accumulate"
         del wc, wperm
+    # opcode 19: DiT auxiliaries around the linears (HBM-bound)
+    for name, mode, rows, width, chans in (("C7_adaln_modulate", 9, 8192, 1536, 1), ("C7_swiglu", 12, 4096, 6144, 12288)):
+        if only and name != only:
+            continue
+        g = torch.Generator(device=dev)
+        g.manual_seed(0x5EED0007 + mode)
+        if mode == 9:
+            x = torch.randn(rows, width, device=dev, generator=g)
+            w = torch.randn(2, width, device=dev, generator=g)
+            b = torch.randn(2, width, device=dev, generator=g)
+            prm = dict(mode=9, count=rows * width, width=width, channels=1, spatial=rows // 2, groups=1, batch=2,
+                       other_count=2 * width, activation=0)
+            nbytes = 8 * rows * width + 16 * width
+        else:
+            x = torch.randn(rows, chans, device=dev, generator=g)
+            w = b = None
+            prm = dict(mode=12, count=rows * width, width=width, channels=chans, spatial=rows, groups=1, batch=1,
+                       other_count=0, activation=0)
+            nbytes = 4 * rows * chans + 4 * rows * width
+        out = torch.empty(prm["count"], device=dev)
+        pbuf = (ctypes.c_uint8 * 76).from_buffer_copy(htpg.aux_params_bytes(prm))
+        tm = timed(lambda: htpg.check(L.htpg_model_aux(htpg.ptr(out), htpg.ptr(x), htpg.ptr(w), htpg.ptr(b), pbuf,
+                                                        htpg.stream_ptr()), name))
+        us = tm[0]
+        res[name] = {"rows": rows, "width": width, "us": us, "GBps": nbytes / us / 1e3, "hbm_frac": nbytes / us / 1e3 / hbm,
+                     "bound": "hbm", "host_latency_us": tm[3]}
     # C5: decode shapes, no epilogue
     for m in (1, 4, 16):
         for name, k, n in (("up", 4096, 14336), ("down", 14336, 4096)):

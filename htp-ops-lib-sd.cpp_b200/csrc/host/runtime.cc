@@ -494,6 +494,34 @@ int exec_conv(uint8_t *payload, size_t payload_size) {
   return stage_out({&out});
 }
 
+// ---- opcode 19: FP32 model auxiliaries (op_executor.cc:371-401) -------------
+int exec_aux(uint8_t *payload, size_t payload_size) {
+  if (payload_size != sizeof(NativeAuxParams)) return -1;
+  NativeAuxParams *p = reinterpret_cast<NativeAuxParams *>(payload);
+  if (htpg_model_aux_check(p, p->weight.fd >= 0, p->bias.fd >= 0) != HTPG_OK) return -1;
+  const int n = p->mode == 2 ? p->channels : p->mode == 9 ? p->other_count : p->mode == 10 ? p->count : p->width;
+  size_t input_bytes = static_cast<size_t>(p->count) * 4;
+  if (p->mode == 12 || p->mode == 13)
+    input_bytes = (static_cast<size_t>(p->spatial) * p->batch - 1) * p->channels * 4 + static_cast<size_t>(2) * p->width * 4;
+  Operand out, in, w, b;
+  if (resolve(out, p->output.fd, p->output.offset, static_cast<size_t>(p->count) * 4) ||
+      resolve(in, p->input.fd, p->input.offset, input_bytes))
+    return -1;
+  if (p->weight.fd >= 0 && resolve(w, p->weight.fd, p->weight.offset, static_cast<size_t>(p->other_count) * 4))
+    return -1;
+  if (p->bias.fd >= 0 && resolve(b, p->bias.fd, p->bias.offset, static_cast<size_t>(n) * 4)) return -1;
+  int rc = stage_in({&in, &w, &b}, {&out});
+  if (rc) return rc;
+  const auto t0 = Clock::now();
+  rc = htpg_model_aux(static_cast<float *>(out.device), static_cast<const float *>(in.device),
+                      w.present ? static_cast<const float *>(w.device) : nullptr,
+                      b.present ? static_cast<const float *>(b.device) : nullptr, p, nullptr);
+  rc = sync_status(rc);
+  p->elapsed_us = elapsed_us(t0);
+  if (rc) return rc;
+  return stage_out({&out});
+}
+
 // ---- opcode 1: packed FP16 GEMM, no epilogue (op_executor.cc:473-540) ----------
 bool op_trace_enabled() { return std::getenv("HTPG_OP_TRACE") != nullptr; }
 
@@ -552,6 +580,7 @@ extern "C" int execute_op_simple(struct OpComputeRequest *req, size_t req_size) 
     case HTP_OPS_MAT_MUL_F16_EPILOGUE: return exec_f16_epilogue(req->payload, payload_size);
     case HTP_OPS_MAT_MUL_PERMUTED_W16A32: return exec_w16a32(req->payload, payload_size);
     case HTP_OPS_CONV2D_NCHW_F16: return exec_conv(req->payload, payload_size);
+    case HTP_OPS_MODEL_AUX_F32: return exec_aux(req->payload, payload_size);
     default:
       // Registered opcodes outside this library's path are refused so the
       // caller keeps them on its own backend; unknown opcodes are ignored with

@@ -78,6 +78,9 @@ def lib() -> ctypes.CDLL:
         "htpg_conv2d_run": (I, [P, P, P, P, P, P]),
         "htpg_conv_set_chunk_bytes": (I, [S]),
         "hmx_conv2d_nchw_f16": (I, [P, P, P, P, P]),
+        "htpg_model_aux_check": (I, [P, I, I]),
+        "htpg_model_aux": (I, [P, P, P, P, P, P]),
+        "hvx_model_aux_f32": (I, [P, P, P, P, P]),
         "htpg_ipc_export": (I, [P, P]),
         "htpg_ipc_import": (I, [P, ctypes.POINTER(P)]),
         "htpg_ipc_close": (I, [P]),
@@ -326,3 +329,15 @@ def conv_params_bytes(prm: dict, output=(-1, 0), activation=(-1, 0), weight=(-1,
     import struct
     bufs = struct.pack("<8i", *output, *activation, *weight, *bias)
     return bufs + struct.pack("<18i", *[prm[f] for f in CONV_FIELDS]) + b"\0" * 20
+
+
+# ------------------------------------------------------------------ opcode 19
+AUX_FIELDS = ("mode", "count", "width", "channels", "spatial", "groups", "batch", "other_count", "activation")
+
+
+def aux_params_bytes(prm: dict, eps: float = 1e-6, output=(-1, 0), input_=(-1, 0), weight=(-1, 0),
+                     bias=(-1, 0)) -> bytes:
+    """76-byte NativeAuxParams (include/op_reg.h), elapsed_us zero."""
+    import struct
+    return (struct.pack("<8i", *output, *input_, *weight, *bias) +
+            struct.pack("<9i", *[prm[f] for f in AUX_FIELDS]) + struct.pack("<fi", eps, 0))

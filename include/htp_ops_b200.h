@@ -143,6 +143,19 @@ int htpg_conv_set_chunk_bytes(size_t bytes);
 int hmx_conv2d_nchw_f16(float *dst, const float *input, const uint16_t *weight, const float *bias,
                         struct NativeConvParams *p);
 
+/* ---- opcode 19: FP32 model auxiliaries (reference: mat_mul.c:2344-2480) -- */
+/* All 14 modes of NativeAuxParams (include/op_reg.h) on device pointers; w and
+ * b stand for the payload's weight/bias buffers (NULL = absent).  Checks as
+ * the reference executor (HTPG_EPAYLOAD), plus GroupNorm's element count must
+ * equal spatial*channels*batch. */
+struct NativeAuxParams; /* include/op_reg.h */
+int htpg_model_aux_check(const struct NativeAuxParams *p, int has_w, int has_b);
+int htpg_model_aux(float *dst, const float *x, const float *w, const float *b,
+                   const struct NativeAuxParams *p, void *stream);
+/* The reference's kernel name; synchronous. */
+int hvx_model_aux_f32(float *dst, const float *x, const float *w, const float *b,
+                      const struct NativeAuxParams *p);
+
 /* ---- column-sharded run with a fused output exchange -------------------- */
 /* Multi-GPU form of htpg_w8a8_run for a weight split by output columns (N)
  * across ranks, each rank holding a column block: the epilogue stores every

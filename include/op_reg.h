@@ -9,6 +9,7 @@
  *                                               +CPU control (48 B), +epilogue (56 B, new)
  *   opcode 16  HTP_OPS_MAT_MUL_F16_EPILOGUE     F16EpilogueParams (56 B)
  *   opcode 17  HTP_OPS_CONV2D_NCHW_F16          NativeConvParams (124 B)
+ *   opcode 19  HTP_OPS_MODEL_AUX_F32            NativeAuxParams (76 B)
  * The opcode numbering is the reference's, including the ops that are not
  * executed here (they are answered with AEE_EUNSUPPORTED by the dispatcher).
  */
@@ -173,6 +174,22 @@ struct NativeConvParams {
   int32_t elapsed_us, gather_us, weight_us, hmx_us, store_us;
 } __attribute__((packed));
 
+/* Opcode 19: FP32 model auxiliaries around the linears (reference:
+ * op_reg.h:503-508, mat_mul.c:2344-2480).  mode: 0 LayerNorm, 1 RMSNorm,
+ * 2 GroupNorm, 3 broadcast add, 4 broadcast multiply, 5 SiLU, 6 GELU(tanh),
+ * 7 QuickGELU, 8 [batch][width][spatial] -> [batch][spatial][width] transpose,
+ * 9 LayerNorm + modulation (v + v*scale + shift), 10 gated residual
+ * (x*gate + residual), 11 RoPE with 2x2 position matrices (into the attention
+ * layout), 12 SwiGLU, 13 SwiGLU concatenated after an attention output.
+ * activation: SiLU after the norms (modes 0-2, 9), or the gate/up order of
+ * modes 12/13.  elapsed_us is written back. */
+struct NativeAuxParams {
+  struct RpcmemBufAddr output, input, weight, bias;
+  int32_t mode, count, width, channels, spatial, groups, batch, other_count, activation;
+  float eps;
+  int32_t elapsed_us;
+} __attribute__((packed));
+
 #ifdef __cplusplus
 #define HTPB_STATIC_ASSERT(c, msg) static_assert(c, msg)
 #else
@@ -192,6 +209,7 @@ HTPB_STATIC_ASSERT(sizeof(struct MatMulParams) == 92, "opcode 1 payload ABI");
 HTPB_STATIC_ASSERT(sizeof(struct MatMulProfileParams) == 96, "opcode 1 profile payload ABI");
 HTPB_STATIC_ASSERT(sizeof(struct F16EpilogueParams) == 56, "opcode 16 payload ABI");
 HTPB_STATIC_ASSERT(sizeof(struct NativeConvParams) == 124, "opcode 17 payload ABI");
+HTPB_STATIC_ASSERT(sizeof(struct NativeAuxParams) == 76, "opcode 19 payload ABI");
 HTPB_STATIC_ASSERT(HTP_OPS_MAT_MUL_PERMUTED_W16A32 == 1, "opcode 1");
 HTPB_STATIC_ASSERT(HTP_OPS_MAT_MUL_NATIVE_W8A8 == 15, "opcode 15");
 HTPB_STATIC_ASSERT(HTP_OPS_MAT_MUL_F16_EPILOGUE == 16, "opcode 16");

@@ -418,3 +418,115 @@ void orc_conv2d_nchw_f16(float *out, const float *x, const uint16_t *wperm, cons
   }
   free(a);
 }
+
+/* epilogue_activation (mat_mul.c:788-826): z = x (SiLU), 1.702x (QuickGELU) or
+ * 1.5957691216057308*(x + 0.044715x^3) (GELU); x*sigmoid(z) with the stable
+ * split e = 2^(-|z| log2 e), sigmoid = z < 0 ? e/(1+e) : 1/(1+e). */
+float orc_activation(float x, int mode) {
+  if (mode != 1 && mode != 2 && mode != 4 && mode != 5) return x;
+  float z = x;
+  if (mode == 1) z = x + (x * x * x) * 0.044715f;
+  z = z * (mode == 1 ? 1.5957691216057308f : (mode == 4 || mode == 5) ? 1.0f : 1.702f);
+  float neg = fabsf(z) * -1.4426950408889634f;
+  if (neg < -126.0f) neg = -126.0f;
+  const float e = exp2f(neg);
+  const float inv = 1.0f / (e + 1.0f);
+  const float sig = z < 0.0f ? e * inv : inv;
+  return x * sig;
+}
+
+/* Mean and 1/sqrt(var + eps) of n values as the reference forms them: sums
+ * in double, mean and the scale as FP32 (mat_mul.c:2397-2408). */
+static void aux_stats(const float *x, long n, int center, float eps, float *mean, float *inv) {
+  double s = 0.0;
+  if (center)
+    for (long i = 0; i < n; ++i) s += x[i];
+  const float m = center ? (float)(s / n) : 0.0f;
+  double q = 0.0;
+  for (long i = 0; i < n; ++i) {
+    const float d = x[i] - m;
+    q += (double)d * d;
+  }
+  *mean = m;
+  *inv = 1.0f / sqrtf((float)(q / n + eps));
+}
+
+/* Follows model_aux_worker (mat_mul.c:2356-2470) mode by mode. */
+void orc_model_aux(float *out, const float *x, const float *w, const float *b, const int32_t *prm, float eps) {
+  const int mode = prm[0], count = prm[1], width = prm[2], channels = prm[3], spatial = prm[4];
+  const int groups = prm[5], batch = prm[6], other = prm[7], act = prm[8];
+  if (mode <= 2 || mode == 9) {
+    const long n = mode == 2 ? (long)spatial * (channels / groups) : width;
+    const long tasks = mode == 2 ? (long)groups * batch : count / width;
+    for (long t = 0; t < tasks; ++t) {
+      const long off = t * n;
+      float mean, inv;
+      aux_stats(x + off, n, mode != 1, eps, &mean, &inv);
+      for (long i = 0; i < n; ++i) {
+        float v = (x[off + i] - mean) * inv;
+        if (mode == 2) {
+          const int ch = (int)(((off + i) / spatial) % channels);
+          if (w) v = v * w[ch];
+          if (b) v = v + b[ch];
+        } else if (mode == 9) {
+          const long pb = other == width ? 0 : t / spatial;
+          v = v + v * w[pb * width + i];
+          v = v + b[pb * width + i];
+        } else {
+          if (w) v = v * w[i];
+          if (b) v = v + b[i];
+        }
+        if (act) v = orc_activation(v, 4);
+        out[off + i] = v;
+      }
+    }
+  } else if (mode == 8) {
+    for (int bb = 0; bb < batch; ++bb)
+      for (int r = 0; r < width; ++r)
+        for (int c = 0; c < spatial; ++c)
+          out[((long)bb * spatial + c) * width + r] = x[((long)bb * width + r) * spatial + c];
+  } else if (mode == 11) {
+    const int dim = width, heads = channels;
+    for (int bb = 0; bb < batch; ++bb)
+      for (int tok = 0; tok < spatial; ++tok) {
+        const float *pe = w + ((long)(groups == 1 ? 0 : bb) * spatial + tok) * dim * 2;
+        for (int h = 0; h < heads; ++h) {
+          const float *xi = x + (((long)bb * spatial + tok) * heads + h) * dim;
+          float *o = out + (((long)bb * heads + h) * spatial + tok) * dim;
+          for (int e = 0; e < dim; e += 2) {
+            const float *m = pe + 2 * e;
+            o[e] = xi[e] * m[0] + xi[e + 1] * m[1];
+            o[e + 1] = xi[e + 1] * m[3] + xi[e] * m[2];
+          }
+        }
+      }
+  } else if (mode == 12) {
+    for (long i = 0; i < count; ++i) {
+      const long row = i / width, col = i % width;
+      const float *a = x + row * channels + col;
+      const float gate = act ? a[0] : a[width], up = act ? a[width] : a[0];
+      out[i] = orc_activation(gate, 5) * up;
+    }
+  } else if (mode == 13) {
+    const int att = groups, ow = width + att;
+    for (long t = 0; t < (long)spatial * batch; ++t) {
+      for (int i = 0; i < att; ++i) out[t * ow + i] = w[t * att + i];
+      const float *a = x + t * channels;
+      for (int i = 0; i < width; ++i) {
+        const float gate = act ? a[i] : a[i + width], up = act ? a[i + width] : a[i];
+        out[t * ow + att + i] = orc_activation(gate, 5) * up;
+      }
+    }
+  } else if (mode == 10) {
+    for (long i = 0; i < count; ++i) {
+      const int ch = (int)(i % width);
+      const long bb = i / ((long)width * spatial), pb = other == width ? 0 : bb;
+      out[i] = x[i] * w[pb * width + ch] + b[i];
+    }
+  } else if (mode == 3 || mode == 4) {
+    for (long i = 0; i < count; ++i) out[i] = mode == 3 ? x[i] + w[i % other] : x[i] * w[i % other];
+  } else {
+    const int am = mode == 5 ? 4 : mode == 6 ? 1 : 2;
+    for (long i = 0; i < count; ++i) out[i] = orc_activation(x[i], am);
+  }
+}

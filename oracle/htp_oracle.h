@@ -106,6 +106,15 @@ void orc_conv2d_nchw_f16(float *out, const float *x, const uint16_t *wperm, cons
 /* One im2col matrix (FP32, [oh*ow][kp]) of batch b, as the reference gathers it. */
 void orc_conv_im2col(float *a, const float *x, const int32_t *prm, int b);
 
+/* ---- opcode 19 model auxiliaries (reference: mat_mul.c:2344-2480) --------
+ * prm: mode, count, width, channels, spatial, groups, batch, other_count,
+ * activation (NativeAuxParams order); eps.  w, b may be NULL where the mode
+ * allows.  out holds `count` floats. */
+void orc_model_aux(float *out, const float *x, const float *w, const float *b, const int32_t *prm, float eps);
+/* x*sigmoid(z) activations of the epilogues: mode 1 GELU(tanh), 2 QuickGELU,
+ * 4/5 SiLU (mat_mul.c:788-826). */
+float orc_activation(float x, int mode);
+
 /* Number of OpenMP threads this build uses (1 without OpenMP). */
 int orc_threads(void);
 /* Use n OpenMP threads from now on (ignored without OpenMP); launchers such as

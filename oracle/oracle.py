@@ -65,6 +65,9 @@ def lib(kind: str = "st") -> ctypes.CDLL:
     L.orc_w8a8_planes.argtypes = [P, P, I, I]
     L.orc_conv2d_nchw_f16.argtypes = [P, P, P, P, P, I]
     L.orc_conv_im2col.argtypes = [P, P, P, I]
+    L.orc_model_aux.argtypes = [P, P, P, P, P, ctypes.c_float]
+    L.orc_activation.argtypes = [ctypes.c_float, I]
+    L.orc_activation.restype = ctypes.c_float
     L.orc_epilogue_activation.argtypes = [ctypes.c_float, I]
     L.orc_epilogue_activation.restype = ctypes.c_float
     L.orc_f16_linear_rows.argtypes = [P, P, P, P, I, I, I, I, I, I, P, I]
@@ -379,3 +382,16 @@ def conv_case(seed, prm: dict, bias=True):
     wkn[:ic * kh * kw, :oc] = bits.reshape(oc, ic * kh * kw).T
     bb = normal(oc, 0.01, 0, 1, seed + 2) if bias else None
     return x, bits.view(np.float16).astype(np.float32), f16_pack_permuted(wkn), bb
+
+
+# ---------------------------------------------------------------- opcode 19
+AUX_FIELDS = ("mode", "count", "width", "channels", "spatial", "groups", "batch", "other_count", "activation")
+
+
+def model_aux(x, w, b, prm: dict, eps=1e-6, kind="st"):
+    """Oracle opcode-19 output (count floats)."""
+    p = np.array([prm[f] for f in AUX_FIELDS], np.int32)
+    out = np.zeros(prm["count"], np.float32)
+    f = lambda a: None if a is None else np.ascontiguousarray(a, np.float32)
+    lib(kind).orc_model_aux(_p(out), _p(f(x)), _p(f(w)), _p(f(b)), _p(p), eps)
+    return out

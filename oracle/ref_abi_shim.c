@@ -82,6 +82,12 @@ static const struct ref_fact facts[] = {
     {"offsetof.NativeConvParams.upscale", FIELD(NativeConvParams, upscale)},
     {"offsetof.NativeConvParams.elapsed_us", FIELD(NativeConvParams, elapsed_us)},
     {"offsetof.NativeConvParams.store_us", FIELD(NativeConvParams, store_us)},
+    {"sizeof.NativeAuxParams", sizeof(struct NativeAuxParams)},
+    {"offsetof.NativeAuxParams.mode", FIELD(NativeAuxParams, mode)},
+    {"offsetof.NativeAuxParams.groups", FIELD(NativeAuxParams, groups)},
+    {"offsetof.NativeAuxParams.activation", FIELD(NativeAuxParams, activation)},
+    {"offsetof.NativeAuxParams.eps", FIELD(NativeAuxParams, eps)},
+    {"offsetof.NativeAuxParams.elapsed_us", FIELD(NativeAuxParams, elapsed_us)},
     {"enum.HTP_OPS_RMS_NORM_F32", HTP_OPS_RMS_NORM_F32},
     {"enum.HTP_OPS_MAT_MUL_PERMUTED_W16A32", HTP_OPS_MAT_MUL_PERMUTED_W16A32},
     {"enum.HTP_OPS_MAT_MUL_NATIVE_W8A8", HTP_OPS_MAT_MUL_NATIVE_W8A8},

@@ -357,3 +357,27 @@ def test_conv_unmapped_buffers(L):
     prm = _conv_prm(iw=8, ih=8, ic=8, oc=40)
     rc, _ = run(L, 17, htpg.conv_params_bytes(prm, output=(4242, 0), activation=(4243, 0), weight=(4244, 0)))
     assert rc == -1
+
+
+def _aux(**kw):
+    prm = dict(mode=0, count=64, width=16, channels=1, spatial=4, groups=1, batch=1, other_count=16, activation=0)
+    prm.update(kw)
+    return prm
+
+
+@pytest.mark.parametrize("prm,wfd,bfd", [
+    (_aux(mode=14), -1, -1), (_aux(count=0), -1, -1), (_aux(mode=8, count=63), -1, -1),
+    (_aux(mode=2, groups=3, channels=4), -1, -1), (_aux(mode=12, channels=20), -1, -1),
+    (_aux(mode=12, channels=40), 5, -1), (_aux(mode=9), -1, -1), (_aux(mode=10, other_count=17), 5, 6),
+    (_aux(mode=11, width=15), 5, -1), (_aux(mode=3, other_count=0), 5, -1), (_aux(mode=3, other_count=7), 5, -1),
+    (_aux(mode=0, other_count=15), 5, -1)])
+def test_model_aux_validation(L, prm, wfd, bfd):
+    """Opcode 19 acceptance rules (op_executor.cc:371-395): -1 before any buffer."""
+    rc, _ = run(L, 19, htpg.aux_params_bytes(prm, output=(4242, 0), input_=(4243, 0), weight=(wfd, 0),
+                                             bias=(bfd, 0)))
+    assert rc == -1
+
+
+def test_model_aux_payload_size(L):
+    rc, _ = run(L, 19, htpg.aux_params_bytes(_aux())[:-4])
+    assert rc == -1

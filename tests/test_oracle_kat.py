@@ -334,3 +334,99 @@ def test_conv_oracle_matches_direct_convolution(geom):
     ref = _direct_conv(x, wl, bias, prm)
     assert got.shape == ref.shape
     assert np.max(np.abs(got - ref)) <= 1e-5 * max(1.0, np.max(np.abs(ref)))
+
+
+# ---------------------------------------------------------------- opcode 19
+def _sig(z):
+    return 1.0 / (1.0 + np.exp(-z))
+
+
+def _act(x, mode):
+    x = x.astype(np.float64)
+    if mode in (4, 5):
+        return x * _sig(x)
+    if mode == 1:
+        return x * _sig(1.5957691216057308 * (x + 0.044715 * x ** 3))
+    return x * _sig(1.702 * x)
+
+
+def aux_cases():
+    rng = np.random.default_rng(5)
+    f = lambda *s: rng.standard_normal(s).astype(np.float32)
+    C = []
+    # (name, prm, x, w, b, reference)
+    x = f(6, 96); w = f(96); b = f(96)
+    for act in (0, 1):
+        mu = x.astype(np.float64).mean(1, keepdims=True); var = ((x - mu) ** 2).mean(1, keepdims=True)
+        y = (x - mu) / np.sqrt(var + 1e-6) * w + b
+        C.append(("layernorm", dict(mode=0, count=576, width=96, channels=1, spatial=6, groups=1, batch=1,
+                                     other_count=96, activation=act), x, w, b, _act(y, 4) if act else y))
+    x = f(5, 64); w = f(64)
+    y = x / np.sqrt((x.astype(np.float64) ** 2).mean(1, keepdims=True) + 1e-6) * w
+    C.append(("rmsnorm", dict(mode=1, count=320, width=64, channels=1, spatial=5, groups=1, batch=1,
+                              other_count=64, activation=0), x, w, None, y))
+    x = f(2, 8, 20); w = f(8); b = f(8)
+    g = x.reshape(2, 4, 2 * 20).astype(np.float64)
+    y = ((g - g.mean(2, keepdims=True)) / np.sqrt(g.var(2, keepdims=True) + 1e-6)).reshape(2, 8, 20)
+    y = y * w[None, :, None] + b[None, :, None]
+    C.append(("groupnorm", dict(mode=2, count=320, width=1, channels=8, spatial=20, groups=4, batch=2,
+                                other_count=8, activation=0), x, w, b, y))
+    x = f(200); w = f(50)
+    C.append(("add", dict(mode=3, count=200, width=1, channels=1, spatial=1, groups=1, batch=1, other_count=50,
+                          activation=0), x, w, None, x + np.tile(w, 4)))
+    C.append(("mul", dict(mode=4, count=200, width=1, channels=1, spatial=1, groups=1, batch=1, other_count=50,
+                          activation=0), x, w, None, x * np.tile(w, 4)))
+    for mode, am in ((5, 4), (6, 1), (7, 2)):
+        C.append((f"act{mode}", dict(mode=mode, count=200, width=1, channels=1, spatial=1, groups=1, batch=1,
+                                     other_count=0, activation=0), x, None, None, _act(x, am)))
+    x = f(2, 5, 7)
+    C.append(("transpose", dict(mode=8, count=70, width=5, channels=1, spatial=7, groups=1, batch=2,
+                                other_count=0, activation=0), x, None, None, x.transpose(0, 2, 1)))
+    x = f(2, 6, 32)
+    for shared in (False, True):
+        w = f(32) if shared else f(2, 32); b = f(32) if shared else f(2, 32)
+        mu = x.astype(np.float64).mean(2, keepdims=True); var = ((x - mu) ** 2).mean(2, keepdims=True)
+        v = (x - mu) / np.sqrt(var + 1e-6)
+        ww = w[None, None, :] if shared else w[:, None, :]; bb = b[None, None, :] if shared else b[:, None, :]
+        C.append((f"modulate{int(shared)}", dict(mode=9, count=384, width=32, channels=1, spatial=6, groups=1,
+                                                 batch=2, other_count=32 if shared else 64, activation=0),
+                  x, w, b, v + v * ww + bb))
+    x = f(2, 4, 32); w = f(2, 32); b = f(2, 4, 32)
+    C.append(("gate", dict(mode=10, count=256, width=32, channels=1, spatial=4, groups=1, batch=2, other_count=64,
+                           activation=0), x, w, b, x * w[:, None, :] + b))
+    for groups in (1, 2):
+        x = f(2, 4, 3, 8); pe = f(groups, 4, 8, 2)  # [groups][tokens][dim/2 pairs... as dim*2 floats]
+        pe = pe.reshape(groups, 4, 16)
+        y = np.zeros((2, 3, 4, 8))
+        for bb in range(2):
+            for t in range(4):
+                m = pe[0 if groups == 1 else bb, t].reshape(4, 4)
+                for h in range(3):
+                    v = x[bb, t, h].astype(np.float64)
+                    for e in range(0, 8, 2):
+                        mm = m[e // 2]
+                        y[bb, h, t, e] = v[e] * mm[0] + v[e + 1] * mm[1]
+                        y[bb, h, t, e + 1] = v[e + 1] * mm[3] + v[e] * mm[2]
+        C.append((f"rope{groups}", dict(mode=11, count=192, width=8, channels=3, spatial=4, groups=groups,
+                                         batch=2, other_count=2 * 8 * 4 * groups, activation=0), x, pe, None, y))
+    x = f(6, 40)
+    for act in (0, 1):
+        gate = x[:, :16] if act else x[:, 16:32]; up = x[:, 16:32] if act else x[:, :16]
+        C.append((f"swiglu{act}", dict(mode=12, count=96, width=16, channels=40, spatial=3, groups=1, batch=2,
+                                       other_count=0, activation=act), x, None, None, _act(gate, 5) * up))
+        att = f(6, 8)
+        C.append((f"swiglu_cat{act}", dict(mode=13, count=144, width=16, channels=40, spatial=3, groups=8, batch=2,
+                                           other_count=48, activation=act), x, att, None,
+                  np.concatenate([att, _act(gate, 5) * up], axis=1)))
+    return C
+
+
+@pytest.mark.parametrize("case", aux_cases(), ids=lambda c: c[0])
+def test_model_aux_oracle(case):
+    """Opcode 19 (mat_mul.c:2344-2480): each mode of the oracle against an
+    independent fp64 statement of the same operation."""
+    name, prm, x, w, b, ref = case
+    got = O.model_aux(x, w, b, prm)
+    ref = np.asarray(ref, np.float64).reshape(-1)
+    assert got.shape == ref.shape
+    assert np.max(np.abs(got - ref)) <= 2e-5 * max(1.0, np.max(np.abs(ref))), name
