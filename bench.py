@@ -333,6 +333,45 @@ def suite(torch, L, htpg, dev, flush, reps=20, only=None):
         us = tm[0]
         res[name] = {"rows": rows, "width": width, "us": us, "GBps": nbytes / us / 1e3, "hbm_frac": nbytes / us / 1e3 / hbm,
                      "bound": "hbm", "host_latency_us": tm[3]}
+    # opcodes 2-4: ggml-block weights (Q4_0 / Q8_0 / IQ4_NL) at the LLM decode
+    # shapes of C5 and one prefill shape.  Random codes and FP16 scales
+    # generated on the device (the kernels have no data-dependent paths).
+    # Algorithmic bytes 4MK + K*N/256*block + 4MN; FLOPs 2MNK.
+    def qk0_weight(wtype, k, n, seed):
+        bb = 272 if wtype == 8 else 144
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        src = torch.randint(0, 256, (k * n // 256, bb), dtype=torch.uint8, device=dev, generator=g)
+        sc = (torch.randn(k * n // 256, 8, device=dev, generator=g) * 0.002).half()
+        src[:, :16] = sc.view(torch.uint8)
+        return src.reshape(-1).contiguous()
+
+    for tname, wtype in (("q4_0", 2), ("q8_0", 8), ("iq4_nl", 20)):
+        bb = 272 if wtype == 8 else 144
+        for shape, m, k, n in (("up_M1", 1, 4096, 14336), ("down_M16", 16, 14336, 4096),
+                               ("prefill_M4096", 4096, 4096, 14336)):
+            name = f"C8_{tname}_{shape}"
+            if (only and name != only) or (shape == "prefill_M4096" and wtype != 2):
+                continue
+            g = torch.Generator(device=dev)
+            g.manual_seed(0x5EED0008 + wtype)
+            x = torch.randn(m, k, device=dev, generator=g)
+            src = qk0_weight(wtype, k, n, 0x5EED0108 + wtype)
+            out = torch.empty(m, n, device=dev)
+            tm = timed(lambda: htpg.check(htpg.qk0_linear(out, x, src, wtype, m, k, n), name))
+            nbytes = 4 * m * k + k * n // 256 * bb + 4 * m * n
+            record(name, m, k, n, tm, nbytes, bf16)
+            if m <= 32:
+                sets = [(x, src)] + [(x, qk0_weight(wtype, k, n, 0x5EED0208 + wtype + i)) for i in range(1, 6)]
+                t = stream_us([lambda o=o: htpg.check(htpg.qk0_linear(out, o[0], o[1], wtype, m, k, n), name)
+                               for o in sets])
+                res[name].update(stream_us=t, stream_GBps=nbytes / t / 1e3, stream_hbm_frac=nbytes / t / 1e3 / hbm)
+                for o in sets[1:]:
+                    L.htpg_weight_cache_drop(htpg.ptr(o[1]))
+                del sets
+            # the one-call entry point caches the prepared weight by address
+            L.htpg_weight_cache_drop(htpg.ptr(src))
+            del src
     # C5: decode shapes, no epilogue
     for m in (1, 4, 16):
         for name, k, n in (("up", 4096, 14336), ("down", 14336, 4096)):

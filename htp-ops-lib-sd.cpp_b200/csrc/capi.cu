@@ -58,6 +58,7 @@ struct Device {
   int sms = 148;
   uint32_t *watchdog = nullptr;
   std::map<cudaStream_t, Workspace> ws;
+  std::map<cudaStream_t, Workspace> qws;  // opcodes 2-4: counters | partials | FP16 operands
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
 };
 
@@ -169,6 +170,7 @@ struct htpg_weights {
   int32_t *corr = nullptr;     // I8: [ncols] zero-point correction differences
   int32_t *sum7 = nullptr;     // I8: [ncols] (sum_k w) << 7, for the plane export
   float *inverse = nullptr;    // I8: [k], nullptr when every entry is 1.0
+  int qtype = 0;               // QK0: ggml type; wk holds the stage records
   std::map<int, CUtensorMap> maps;  // by box rows
 };
 
@@ -193,6 +195,7 @@ int weight_map(htpg_weights *w, int box_rows, const CUtensorMap **out) {
 // pointer-keyed cache of prepared weights for the one-call entry points
 typedef std::tuple<const void *, int, int, int, int> CacheKey;  // ptr, kind, k, n, device
 std::map<CacheKey, htpg_weights *> g_cache;
+
 
 }  // namespace
 
@@ -464,8 +467,10 @@ namespace {
 // then unused and no conversion runs).
 int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const float *x,
                const float *bias, int m, int channels, int mode, void *stream,
-               const float **row_scales_out = nullptr, const uint16_t *act_f16 = nullptr) {
+               const float **row_scales_out = nullptr, const uint16_t *act_f16 = nullptr,
+               bool late_weights = false) {
   if (act_f16 && w && w->kind != Kind::F16) return HTPG_EARGS;
+  if (w && w->kind == Kind::QK0) return HTPG_EARGS;
   if (!w || !outs || n_outs < 1 || n_outs > kMaxOutputs || (!x && !act_f16)) return HTPG_EARGS;
   for (int i = 0; i < n_outs; ++i)
     if (!outs[i]) return HTPG_EARGS;
@@ -554,6 +559,7 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
   a.ws = wsk;
   a.ws_count = cnt;
   a.watchdog = d->watchdog;
+  a.late_weights = late_weights ? 1 : 0;
   // row-major outputs of the normal orientation leave the SM through TMA stores
   OutMaps out_maps;
   if (mode == HTPG_MODE_PLANES) {
@@ -646,7 +652,7 @@ extern "C" int htpg_w8a8_run_gather(const htpg_weights *w, float *const *outs, i
 
 // ---------------------------------------------------------------- opcode 17
 namespace {
-int cached_weights(Kind kind, const void *ptr, int k, int n, void *stream, htpg_weights **out);
+int cached_weights(Kind kind, const void *ptr, int k, int n, void *stream, htpg_weights **out, int qtype = 0);
 // im2col staging, per device, grown as needed (one chunk of output rows)
 struct ConvBuf {
   void *base = nullptr;
@@ -926,10 +932,10 @@ void htpg::set_error_text(const char *text) { t_last_cuda_error = text ? text : 
 // ================================================================ one-call
 namespace {
 
-int cached_weights(Kind kind, const void *ptr, int k, int n, void *stream, htpg_weights **out) {
+int cached_weights(Kind kind, const void *ptr, int k, int n, void *stream, htpg_weights **out, int qtype) {
   int dev = 0;
   cudaGetDevice(&dev);
-  const CacheKey key(ptr, static_cast<int>(kind), k, n, dev);
+  const CacheKey key(ptr, static_cast<int>(kind) + 100 * qtype, k, n, dev);
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_cache.find(key);
@@ -939,7 +945,8 @@ int cached_weights(Kind kind, const void *ptr, int k, int n, void *stream, htpg_
     }
   }
   htpg_weights *w = nullptr;
-  const int rc = kind == Kind::I8
+  const int rc = kind == Kind::QK0 ? htpg_qk0_weights_create(ptr, k, n, qtype, stream, &w)
+                 : kind == Kind::I8
                      ? htpg_w8a8_weights_create(ptr, k, n, 0, 0, stream, &w)
                      : htpg_f16_weights_create(static_cast<const uint16_t *>(ptr), k, n, 0, 0, stream, &w);
   if (rc) return rc;
@@ -995,6 +1002,170 @@ extern "C" int htpg_f16_linear(float *out, const float *x, const uint16_t *permu
   int rc = cached_weights(Kind::F16, permuted_weight, k, n, stream, &w);
   if (rc) return rc;
   return run_common(w, &out, 1, 0, x, bias, m, channels, mode, stream);
+}
+
+// ================================================================ opcodes 2-4
+namespace {
+
+constexpr size_t kQCounterBytes = 64u * 1024u;  // stream-K arrival counters, kept zero
+
+// Stream-private opcode 2-4 scratch: [counters | partial tiles | FP16 activations
+// or the dequantised weight].  Zeroed when (re)allocated; the counters are
+// left zero by every launch.
+int qworkspace(Device *d, cudaStream_t st, size_t bytes, uint8_t **out) {
+  Workspace &w = d->qws[st];
+  if (w.bytes < bytes) {
+    if (w.base) {
+      cudaStreamSynchronize(st);
+      cudaFree(w.base);
+      w.base = nullptr;
+      w.bytes = 0;
+    }
+    const size_t want = bytes + bytes / 4 + (1u << 20);
+    if (cudaMalloc(&w.base, want) != cudaSuccess) {
+      cudaGetLastError();
+      return HTPG_ENOMEM;
+    }
+    if (cudaMemsetAsync(w.base, 0, want, st) != cudaSuccess) return HTPG_ELAUNCH;
+    w.bytes = want;
+  }
+  *out = static_cast<uint8_t *>(w.base);
+  return HTPG_OK;
+}
+
+bool qk0_type_ok(int qt) { return qk0_block_bytes(qt) != 0; }
+
+}  // namespace
+
+extern "C" size_t htpg_qk0_weight_bytes(int weight_type, int k, int n) {
+  if (!qk0_type_ok(weight_type) || k < 32 || n < 32 || k % 32 || n % 32) return 0;
+  return static_cast<size_t>(k) * static_cast<size_t>(n) / 256u * static_cast<size_t>(qk0_block_bytes(weight_type));
+}
+
+extern "C" int htpg_qk0_dequantize(uint16_t *w_nk, const void *weight, int k, int n, int weight_type,
+                                   void *stream) {
+  if (!w_nk || !weight || !qk0_type_ok(weight_type)) return HTPG_EARGS;
+  if (k < 32 || n < 32 || k % 32 || n % 32) return HTPG_ECAPACITY;
+  if ((reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(w_nk)) & 15u) return HTPG_ECONTROL;
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  return record_cuda(launch_qk0_dequant(w_nk, static_cast<const uint8_t *>(weight), weight_type, k, n, 64, k,
+                                        false, pick_stream(d, stream)));
+}
+
+extern "C" int htpg_qk0_weights_create(const void *weight, int k, int n, int weight_type, void *stream,
+                                       htpg_weights **out) {
+  if (!out) return HTPG_EARGS;
+  *out = nullptr;
+  if (!weight || !qk0_type_ok(weight_type)) return HTPG_EARGS;
+  if (k < 32 || n < 32 || k % 32 || n % 32) return HTPG_ECAPACITY;
+  if (reinterpret_cast<uintptr_t>(weight) & 15u) return HTPG_ECONTROL;
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t st = pick_stream(d, stream);
+  htpg_weights *w = new htpg_weights;
+  w->kind = Kind::QK0;
+  w->qtype = weight_type;
+  w->k = k;
+  w->ncols = n;
+  w->n_total = n;
+  w->device = d->ordinal;
+  if (cudaMalloc(&w->wk, qk0_stage_records_bytes(weight_type, k, n)) != cudaSuccess) {
+    cudaGetLastError();
+    delete w;
+    return HTPG_ENOMEM;
+  }
+  cudaError_t e = launch_qk0_repack(static_cast<uint8_t *>(w->wk), static_cast<const uint8_t *>(weight), weight_type,
+                                    k, n, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    htpg_weights_destroy(w);
+    return record_cuda(e);
+  }
+  *out = w;
+  return HTPG_OK;
+}
+
+extern "C" int htpg_qk0_run(const htpg_weights *w, float *out, const float *x, int m, void *stream) {
+  if (!w || w->kind != Kind::QK0 || !out || !x) return HTPG_EARGS;
+  const int k = w->k, n = w->ncols, qt = w->qtype;
+  if (m < 1 || m > HTPG_W8A8_MAX_M) return HTPG_ECAPACITY;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(out) & 3u)) return HTPG_ECONTROL;
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t st = pick_stream(d, stream);
+  const uint8_t *records = static_cast<const uint8_t *>(w->wk);
+  if (m > kQGemmMaxM) {
+    // large M: the weight is dequantised once into K-major FP16 k-blocks and
+    // the FP16 GEMM runs on it (its weight tiles load only after that pass)
+    const size_t wbytes = kblock_bytes(Kind::F16, k, n);
+    uint8_t *base = nullptr;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      rc = qworkspace(d, st, kQCounterBytes + wbytes, &base);
+      if (rc) return rc;
+      const cudaError_t e = launch_qk0_dequant(reinterpret_cast<uint16_t *>(base + kQCounterBytes), records, qt, k, n,
+                                               64LL * n, 64, true, st);
+      if (e != cudaSuccess) return record_cuda(e);
+    }
+    htpg_weights f;
+    f.kind = Kind::F16;
+    f.k = k;
+    f.ncols = n;
+    f.n_total = n;
+    f.device = d->ordinal;
+    f.wk = base + kQCounterBytes;
+    return run_common(&f, &out, 1, 0, x, nullptr, m, n, 0, stream, nullptr, nullptr, true);
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  const QGemmPlan plan = plan_qgemm(qt, m, n, k, d->sms);
+  if (qgemm_counter_bytes(plan) > kQCounterBytes) return HTPG_ENOPLAN;
+  const size_t part = align_up(qgemm_partial_bytes(plan), 1024);
+  const size_t act = align_up(static_cast<size_t>(m) * k * 2u, 1024);
+  uint8_t *base = nullptr;
+  rc = qworkspace(d, st, kQCounterBytes + part + act, &base);
+  if (rc) return rc;
+  uint16_t *act16 = reinterpret_cast<uint16_t *>(base + kQCounterBytes + part);
+  cudaError_t e = launch_to_f16(act16, x, static_cast<long long>(m) * k, st);
+  if (e != cudaSuccess) return record_cuda(e);
+  CUtensorMap tmB;
+  rc = make_map(&tmB, act16, Kind::F16, k, m, static_cast<size_t>(k) * 2u, plan.bn);
+  if (rc) return rc;
+  QGemmArgs a;
+  a.M = m;
+  a.N = n;
+  a.K = k;
+  a.out = out;
+  a.ldo = n;
+  a.partials = reinterpret_cast<float *>(base + kQCounterBytes);
+  a.counters = reinterpret_cast<uint32_t *>(base);
+  a.watchdog = d->watchdog;
+  return record_cuda(launch_qgemm(qt, plan, records, tmB, a, st));
+}
+
+extern "C" int htpg_qk0_plan_info(int weight_type, int m, int n, int k, int sms, int64_t out[6]) {
+  if (!out || !qk0_type_ok(weight_type) || m < 1 || m > kQGemmMaxM) return HTPG_EARGS;
+  const QGemmPlan p = plan_qgemm(weight_type, m, n, k, sms);
+  out[0] = p.bn;
+  out[1] = p.tiles_a;
+  out[2] = p.tiles_b;
+  out[3] = p.kb_total;
+  out[4] = p.grid;
+  out[5] = static_cast<int64_t>(p.smem);
+  return HTPG_OK;
+}
+
+extern "C" int htpg_qk0_linear(float *out, const float *x, const void *weight, int m, int k, int n,
+                               int weight_type, void *stream) {
+  if (!out || !x || !weight || !qk0_type_ok(weight_type)) return HTPG_EARGS;
+  if (m < 1 || m > HTPG_W8A8_MAX_M || k < 32 || n < 32 || k % 32 || n % 32) return HTPG_ECAPACITY;
+  htpg_weights *w = nullptr;
+  int rc = cached_weights(Kind::QK0, weight, k, n, stream, &w, weight_type);
+  if (rc) return rc;
+  return htpg_qk0_run(w, out, x, m, stream);
 }
 
 // ================================================================ reference kernel names
@@ -1089,6 +1260,20 @@ extern "C" int hmx_mat_mul_f16_epilogue(float *dst, const float *activation, con
        reinterpret_cast<uintptr_t>(weight)) & 127u)
     return HTPG_ECONTROL;
   return finish_sync(htpg_f16_linear(dst, activation, weight, bias, m, k, n, channels, mode, nullptr));
+}
+
+// mat_mul.c:1601-1618: -1 for a missing operand, a zero size, K or N not a
+// multiple of 32, an operand not 128-byte aligned or an unknown weight type.
+extern "C" int hmx_mat_mul_permuted_qk_0_d16a32(float *dst, const float *activation,
+                                                const uint8_t *permuted_weight, int m, int k, int n,
+                                                int weight_type) {
+  if (!dst || !activation || !permuted_weight || !m || !n || !k) return -1;
+  if (k % 32 || n % 32) return -1;
+  if ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(activation) |
+       reinterpret_cast<uintptr_t>(permuted_weight)) & 127u)
+    return -1;
+  if (!qk0_type_ok(weight_type) || m < 0 || k < 0 || n < 0) return -1;
+  return finish_sync(htpg_qk0_linear(dst, activation, permuted_weight, m, k, n, weight_type, nullptr));
 }
 
 extern "C" int hmx_mat_mul_permuted_w16a32(float *dst, const float *activation,

@@ -232,8 +232,9 @@ int stage_out(std::vector<Operand *> outputs) {
 
 // Prepared weight for a {fd, offset} weight operand.  Host-memory blobs are
 // copied to the device once per (fd, offset, generation).
-int exec_weights(const Operand &o, bool int8, int k, int n, htpg_weights **out) {
-  const WeightKey key(o.fd, o.offset, o.buf.generation, int8 ? 0 : 1, k, n);
+// qtype (opcodes 2-4): the ggml type of a super-block stream (int8 unused).
+int exec_weights(const Operand &o, bool int8, int k, int n, htpg_weights **out, int qtype = 0) {
+  const WeightKey key(o.fd, o.offset, o.buf.generation, qtype ? 100 + qtype : int8 ? 0 : 1, k, n);
   {
     std::lock_guard<std::recursive_mutex> lk(g_reg_mu);
     auto it = g_exec_weights.find(key);
@@ -257,8 +258,9 @@ int exec_weights(const Operand &o, bool int8, int k, int n, htpg_weights **out) 
     src = tmp;
   }
   htpg_weights *w = nullptr;
-  const int rc = int8 ? htpg_w8a8_weights_create(src, k, n, 0, 0, nullptr, &w)
-                      : htpg_f16_weights_create(static_cast<const uint16_t *>(src), k, n, 0, 0, nullptr, &w);
+  const int rc = qtype ? htpg_qk0_weights_create(src, k, n, qtype, nullptr, &w)
+                 : int8 ? htpg_w8a8_weights_create(src, k, n, 0, 0, nullptr, &w)
+                        : htpg_f16_weights_create(static_cast<const uint16_t *>(src), k, n, 0, 0, nullptr, &w);
   if (tmp) cudaFree(tmp);
   if (rc) return rc;
   std::lock_guard<std::recursive_mutex> lk(g_reg_mu);
@@ -569,6 +571,43 @@ int exec_w16a32(uint8_t *payload, size_t payload_size) {
   return rc;
 }
 
+// ---- opcodes 2-4: ggml-block weight GEMMs (op_executor.cc:771-808) ----------
+// MatMulParams payload (at least 92 bytes; 96 with elapsed_us); the weight
+// operand is k*n/256 super-blocks of the opcode's type, prepared once per
+// {fd, offset, generation} like the other weights.  Kernel-level checks
+// (mat_mul.c:1604-1613) answer -1.
+int exec_qk0(int op, uint8_t *payload, size_t payload_size) {
+  if (payload_size < sizeof(MatMulParams)) return -1;
+  const int qt = op == HTP_OPS_MAT_MUL_PERMUTED_W4D16A32   ? HTPG_GGML_Q4_0
+                 : op == HTP_OPS_MAT_MUL_PERMUTED_W8D16A32 ? HTPG_GGML_Q8_0
+                                                           : HTPG_GGML_IQ4_NL;
+  MatMulParams *p = reinterpret_cast<MatMulParams *>(payload);
+  const int m = p->m, k = p->k, n = p->n;
+  if (m <= 0 || k <= 0 || n <= 0) return -1;
+  const size_t wbytes = static_cast<size_t>(k) * static_cast<size_t>(n) / 256u *
+                        (qt == HTPG_GGML_Q8_0 ? 272u : 144u);
+  Operand out, act, wt;
+  if (resolve(out, p->output.fd, p->output.offset, static_cast<size_t>(m) * n * 4) ||
+      resolve(act, p->activation.fd, p->activation.offset, static_cast<size_t>(m) * k * 4) ||
+      resolve(wt, p->weight.fd, p->weight.offset, wbytes))
+    return -2;
+  if (k % 32 || n % 32) return -1;
+  if ((reinterpret_cast<uintptr_t>(out.host) | reinterpret_cast<uintptr_t>(act.host) |
+       reinterpret_cast<uintptr_t>(wt.host)) & 127u)
+    return -1;
+  htpg_weights *w = nullptr;
+  int rc = exec_weights(wt, false, k, n, &w, qt);  // stage records, made once per {fd, offset, generation}
+  if (rc) return rc;
+  if ((rc = stage_in({&act}, {&out}))) return rc;
+  const auto t0 = Clock::now();
+  rc = htpg_qk0_run(w, static_cast<float *>(out.device), static_cast<const float *>(act.device), m, nullptr);
+  rc = sync_status(rc);
+  if (payload_size >= sizeof(MatMulProfileParams))
+    reinterpret_cast<MatMulProfileParams *>(payload)->elapsed_us = elapsed_us(t0);
+  if (rc) return rc;
+  return stage_out({&out});
+}
+
 }  // namespace
 
 extern "C" int execute_op_simple(struct OpComputeRequest *req, size_t req_size) {
@@ -581,6 +620,9 @@ extern "C" int execute_op_simple(struct OpComputeRequest *req, size_t req_size) 
     case HTP_OPS_MAT_MUL_PERMUTED_W16A32: return exec_w16a32(req->payload, payload_size);
     case HTP_OPS_CONV2D_NCHW_F16: return exec_conv(req->payload, payload_size);
     case HTP_OPS_MODEL_AUX_F32: return exec_aux(req->payload, payload_size);
+    case HTP_OPS_MAT_MUL_PERMUTED_W4D16A32:
+    case HTP_OPS_MAT_MUL_PERMUTED_W8D16A32:
+    case HTP_OPS_MAT_MUL_PERMUTED_W4D16A32_IQ4_NL: return exec_qk0(req->op, req->payload, payload_size);
     default:
       // Registered opcodes outside this library's path are refused so the
       // caller keeps them on its own backend; unknown opcodes are ignored with

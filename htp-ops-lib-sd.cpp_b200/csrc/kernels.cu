@@ -22,7 +22,7 @@ namespace htpg {
 
 static std::atomic<uint64_t> g_launches{0};
 uint64_t launches() { return g_launches.load(); }
-static inline cudaError_t counted(cudaError_t e) {
+cudaError_t counted(cudaError_t e) {
   if (e == cudaSuccess) g_launches.fetch_add(1);
   return e;
 }
@@ -966,7 +966,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Unit w = decode_unit(blockIdx.x, P.tiles_b, P.splits);
         const int kb0 = w.ks * P.kb_per_split;
         const int kb1 = min(kb0 + P.kb_per_split, P.kb_total);
-        pre = min(STAGES, kb1 - kb0);
+        pre = g.late_weights ? 0 : min(STAGES, kb1 - kb0);
         for (int i = 0; i < pre; ++i) {
           const uint32_t fb = smem_u32(&L.full[i]);
           mbar_arrive_expect_tx(fb, kStageBytes);
@@ -1206,7 +1206,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int pre = 0;
       if (pair < P.units) {
         const Unit w = decode_unit(pair, P.tiles_b, 1);
-        pre = min(STAGES, P.kb_total);
+        pre = g.late_weights ? 0 : min(STAGES, P.kb_total);
         for (int i = 0; i < pre; ++i) {
           const uint32_t fb_local = smem_u32(&L.full[i]);
           if (leader) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);

@@ -8,7 +8,7 @@
 
 namespace htpg {
 
-enum class Kind : int { I8 = 0, F16 = 1 };
+enum class Kind : int { I8 = 0, F16 = 1, QK0 = 2 };  // QK0: ggml-block stage records (never a GEMM kind)
 
 // One GEMM launch: D[rows_a x rows_b] = A[rows_a x K] * B[rows_b x K]^T, both
 // operands K-major in HBM and fetched by TMA.  Normal orientation: A = the
@@ -41,6 +41,9 @@ struct GemmArgs {
   uint32_t *ws_count = nullptr;      // split-K arrival counters (self-resetting)
   uint32_t *watchdog = nullptr;
   int tma_store = 0;                 // row-major output written by TMA through tmOut
+  int late_weights = 0;              // the weight is written by the kernels just before this
+                                     // launch: no weight tile is loaded before the
+                                     // programmatic-dependency wait (L2 prefetches only)
 };
 
 // Tensor map for TMA stores of a row-major FP32 output: `rows` x `cols`, row
@@ -102,7 +105,64 @@ struct ConvGeom {
 cudaError_t launch_im2col_f16(uint16_t *a, const float *x, const ConvGeom &g, int m0, int rows,
                               cudaStream_t st);
 
+// ---- opcodes 2-4: ggml-block weights dequantised to FP16 (qk0.cu) --------
+// The weight is the reference's stream of K*N/256 super-blocks (8 FP16 scales +
+// codes); super-block i dequantises to elements [256i, 256i+256) of the packed
+// FP16 weight (element (k, n) at tile (n/32)*(K/32) + k/32, offset
+// ((k%32)&~1)*32 + (n%32)*2 + (k&1)).  So one 32 x 32 tile is four
+// consecutive super-blocks, super-block j of a tile holds k%32 in [8j, 8j+8)
+// for all 32 columns, and its scale g covers the column half g%2 of the k pair
+// g/2.
+constexpr int kGgmlQ4_0 = 2, kGgmlQ8_0 = 8, kGgmlIQ4_NL = 20;
+inline int qk0_block_bytes(int qt) {
+  return qt == kGgmlQ8_0 ? 272 : (qt == kGgmlQ4_0 || qt == kGgmlIQ4_NL) ? 144 : 0;
+}
+// FP16 element (n, k) -> dst[(k/64)*stride_kb + n*stride_n + k%64].  src is
+// the reference's stream, or (records) the stage records of
+// launch_qk0_repack, whose zero padding also fills the k-block tail
+// k in [K, 64*ceil(K/64)) (the K-major GEMM operand); from the stream that
+// tail is left unwritten.
+cudaError_t launch_qk0_dequant(uint16_t *dst, const uint8_t *src, int qt, int k, int n, long long stride_kb,
+                               long long stride_n, bool records, cudaStream_t st);
+// Stage records of the fused kernel (see qk0_repack_kernel): bytes, and the
+// one-time reorder of the reference's stream into them.
+size_t qk0_stage_records_bytes(int qt, int k, int n);
+cudaError_t launch_qk0_repack(uint8_t *dst, const uint8_t *src, int qt, int k, int n, cudaStream_t st);
+// Fused small-M GEMM: out[M][N] = f16(x) * dequant(W), the dequantised weight
+// tile as the 128-row MMA operand, stream-K over (tile, k-block) iterations.
+struct QGemmPlan {
+  int bn = 16;                  // activation rows per tile (MMA N)
+  int tiles_a = 0, tiles_b = 0; // 128-column weight tiles x activation-row tiles
+  int kb_total = 0;             // 64-deep k-blocks
+  long long iters = 0;          // tiles_a * tiles_b * kb_total
+  int grid = 0;                 // CTAs (each owns a contiguous range of iterations)
+  size_t smem = 0;
+};
+constexpr int kQGemmMaxM = 32;
+QGemmPlan plan_qgemm(int qt, int M, int N, int K, int num_sms);
+// Partial-tile slots (two per CTA) and per-tile arrival counters.
+inline size_t qgemm_partial_bytes(const QGemmPlan &p) {
+  return static_cast<size_t>(2) * p.grid * p.bn * 128 * 4;
+}
+inline size_t qgemm_counter_bytes(const QGemmPlan &p) {
+  return static_cast<size_t>(p.tiles_a) * p.tiles_b * 4;
+}
+struct QGemmArgs {
+  int M = 0, N = 0, K = 0;
+  float *out = nullptr;
+  long long ldo = 0;
+  float *partials = nullptr;     // qgemm_partial_bytes
+  uint32_t *counters = nullptr;  // zero before the launch, left zero
+  uint32_t *watchdog = nullptr;
+};
+// w: the stage records (launch_qk0_repack); tmB: FP16 activations [M][K],
+// box 64 x bn, 128-byte swizzle.
+cudaError_t launch_qgemm(int qt, const QGemmPlan &p, const uint8_t *w, const CUtensorMap &tmB,
+                         const QGemmArgs &a, cudaStream_t st);
+
 // Kernel launches issued since load (all launchers above count themselves).
 uint64_t launches();
+// Counts one launch when e is cudaSuccess; returns e.
+cudaError_t counted(cudaError_t e);
 
 }  // namespace htpg

@@ -11,7 +11,8 @@ namespace htpg {
 // Every device-side wait gives up after this many nanoseconds of %globaltimer
 // and records which role gave up in the watchdog word (host: htpg_check_device).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s; a correct launch waits microseconds
-constexpr uint32_t kWatchProducer = 1u, kWatchMma = 2u, kWatchEpilogue = 4u, kWatchSplitK = 8u;
+constexpr uint32_t kWatchProducer = 1u, kWatchMma = 2u, kWatchEpilogue = 4u, kWatchSplitK = 8u,
+                   kWatchDequant = 16u;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -81,6 +82,32 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
       : "memory");
+}
+// Linear bulk copy global -> shared (no tensor map): both addresses 16-byte
+// aligned, bytes a multiple of 16; completes `bar`'s transaction count.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+// 3-D tiled load of one box (innermost coordinate first).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
+                                            int32_t x, int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap *map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];"
+               :
+               : "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z)
+               : "memory");
 }
 // Warm the L2 with one box of a 2-D tensor map (no shared memory, no barrier).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int x, int y) {
@@ -212,6 +239,25 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Four kind::f16 MMAs over the K = 64 of one 128-byte swizzled k-block (one
+// asm block, so nothing is scheduled between them): descriptors advance by 32
+// bytes (2 in the start-address field) per K = 16 step.  accumulate applies to
+// the first MMA; the other three always accumulate.
+__device__ __forceinline__ void umma_f16_kblock(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 q, %4, %4;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %6, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %8, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %9, %10, %3, q;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "l"(a_desc + 2), "l"(b_desc + 2), "l"(a_desc + 4),
+      "l"(b_desc + 4), "l"(a_desc + 6), "l"(b_desc + 6)
       : "memory");
 }
 

@@ -1,0 +1,673 @@
+// Opcodes 2-4 of the reference (HTP_OPS_MAT_MUL_PERMUTED_W4D16A32 /
+// W8D16A32 / W4D16A32_IQ4_NL): FP32 activations times a weight stored as
+// ggml blocks (Q4_0, Q8_0, IQ4_NL), dequantised to FP16 and accumulated in
+// FP32 (reference: mat_mul.c:246-430 dequantisation, :1601-1874 GEMM;
+// quants.h:11-31 block layouts).
+//
+//  * dq_chunk            one 16-byte row chunk (8 consecutive k of one column)
+//                        of the FP16 weight from a super-block, in registers
+//  * qk0_dequant_kernel  whole weight -> FP16 rows (the large-M path feeds the
+//                        FP16 GEMM with it; also the standalone dequantiser)
+//  * qk0_repack_kernel   one-time reorder of the super-blocks into per-stage
+//                        records (cached per weight like the other repacks)
+//  * qgemm_swap_kernel   small M: one bulk copy per stage streams the
+//                        super-block record, dequantiser warps write the
+//                        FP16 weight tile into shared memory in the 128-byte
+//                        swizzled K-major layout, one thread issues
+//                        tcgen05.mma with that tile as the 128-row operand and
+//                        the FP16 activations as the narrow one; iterations
+//                        (tile, k-block) are split evenly over the CTAs
+//                        (stream-K) and partial tiles are summed in a fixed
+//                        order by the last CTA to finish them.
+#include <cuda_fp16.h>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace htpg {
+
+// ================================================================ decode
+// IQ4_NL levels (the reference's iq4_nl_to_fp16_lut, mat_mul.c:34-37), stored
+// as level + 128 so that 0x64 | byte is the FP16 number 1024 + level + 128.
+constexpr int kIq4Levels[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+constexpr uint32_t iq4_word(int i) {
+  return static_cast<uint32_t>(kIq4Levels[i] + 128) | static_cast<uint32_t>(kIq4Levels[i + 1] + 128) << 8 |
+         static_cast<uint32_t>(kIq4Levels[i + 2] + 128) << 16 | static_cast<uint32_t>(kIq4Levels[i + 3] + 128) << 24;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_perm(a, b, sel); }
+// Packed FP16 arithmetic with explicit round-to-nearest (never contracted).
+__device__ __forceinline__ uint32_t hsub2_rn(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmul2_rn(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Bytes level+128 of the four nibbles in bits [0, 16) of x: two 8-entry byte
+// tables selected by the nibbles' low three bits, merged by their fourth bit.
+__device__ __forceinline__ uint32_t iq4_lookup4(uint32_t x) {
+  const uint32_t sel = x & 0x7777u;
+  const uint32_t lo = prmt(iq4_word(0), iq4_word(4), sel);
+  const uint32_t hi = prmt(iq4_word(8), iq4_word(12), sel);
+  const uint32_t msk = prmt(0u, 0xFFFFFFFFu, (x >> 1) & 0x4444u);  // 0xFF where the nibble is >= 8
+  return (hi & msk) | (lo & ~msk);
+}
+
+// FP16 elements k = 8j .. 8j+7 (of the tile's 32) of column m (of the tile's
+// 32) from super-block j of a 32 x 32 tile.  Element e of a super-block is the
+// packed-FP16 offset e (see kernels.h), so these eight elements are
+// e = {0,1, 64,65, 128,129, 192,193} + 2m: the pairs (k, k+1) belong to the
+// reference's output vectors v = 0..3 and use scale 2v + m/16.
+//  Q8_0:        code = byte e.
+//  Q4_0/IQ4_NL: code = low (v < 2) or high nibble of byte 2*(e%64) + (v&1),
+//               i.e. of the four bytes b0..b3 at 4m: k order b0.lo, b2.lo,
+//               b1.lo, b3.lo, b0.hi, b2.hi, b1.hi, b3.hi (mat_mul.c:389-424).
+// Codes become exact FP16 integers by the magic-number method (0x64XX is the
+// FP16 number 1024 + XX, minus 1024 + offset), then one packed multiply with
+// the scale rounds code * scale to nearest: the FP16 value the reference's
+// qf16 multiply and conversion produce (mat_mul.c:420-423, 521-524).
+// The raw words of one chunk: the super-block's scale vector and the codes
+// (Q4_0/IQ4_NL: the word at 4m; Q8_0: the four byte pairs at 2m + 64v).
+struct ChunkWords {
+  uint4 sc;
+  uint32_t q[4];
+};
+template <int QT>
+__device__ __forceinline__ ChunkWords chunk_words_global(const uint8_t *blk, int m) {
+  ChunkWords w;
+  w.sc = __ldg(reinterpret_cast<const uint4 *>(blk));
+  if constexpr (QT == kGgmlQ8_0) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) w.q[v] = __ldg(reinterpret_cast<const uint16_t *>(blk + 16 + 2 * m + 64 * v));
+  } else {
+    w.q[0] = __ldg(reinterpret_cast<const uint32_t *>(blk + 16 + 4 * m));
+  }
+  return w;
+}
+template <int QT>
+__device__ __forceinline__ ChunkWords chunk_words_shared(uint32_t blk, int m) {
+  ChunkWords w;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(w.sc.x), "=r"(w.sc.y), "=r"(w.sc.z), "=r"(w.sc.w)
+               : "r"(blk));
+  if constexpr (QT == kGgmlQ8_0) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      uint16_t h;
+      asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(blk + 16 + 2 * m + 64 * v));
+      w.q[v] = h;
+    }
+  } else {
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w.q[0]) : "r"(blk + 16 + 4 * m));
+  }
+  return w;
+}
+
+template <int QT>
+__device__ __forceinline__ uint4 dq_decode(const ChunkWords &cw, int m) {
+  const uint4 sc = cw.sc;
+  const uint32_t ssel = (m & 16) ? 0x3232u : 0x1010u;  // broadcast scale 2v + (m >= 16)
+  const uint32_t s0 = prmt(sc.x, sc.x, ssel), s1 = prmt(sc.y, sc.y, ssel);
+  const uint32_t s2 = prmt(sc.z, sc.z, ssel), s3 = prmt(sc.w, sc.w, ssel);
+  uint32_t h0, h1, h2, h3, bias;
+  if constexpr (QT == kGgmlQ8_0) {
+    // [code_k, 0x64, code_k+1, 0x64], sign bit flipped: 1024 + code + 128
+    h0 = prmt(cw.q[0], 0x64646464u, 0x5140u) ^ 0x00800080u;
+    h1 = prmt(cw.q[1], 0x64646464u, 0x5140u) ^ 0x00800080u;
+    h2 = prmt(cw.q[2], 0x64646464u, 0x5140u) ^ 0x00800080u;
+    h3 = prmt(cw.q[3], 0x64646464u, 0x5140u) ^ 0x00800080u;
+    bias = 0x64806480u;  // 1152
+  } else {
+    const uint32_t w = cw.q[0];
+    if constexpr (QT == kGgmlQ4_0) {
+      h0 = (w & 0x000F000Fu) | 0x64006400u;          // b0.lo, b2.lo
+      h1 = ((w >> 8) & 0x000F000Fu) | 0x64006400u;   // b1.lo, b3.lo
+      h2 = ((w >> 4) & 0x000F000Fu) | 0x64006400u;   // b0.hi, b2.hi
+      h3 = ((w >> 12) & 0x000F000Fu) | 0x64006400u;  // b1.hi, b3.hi
+      bias = 0x64086408u;                            // 1032: nibble - 8
+    } else {
+      const uint32_t ra = iq4_lookup4(w);        // b0.lo b0.hi b1.lo b1.hi
+      const uint32_t rb = iq4_lookup4(w >> 16);  // b2.lo b2.hi b3.lo b3.hi
+      h0 = (prmt(ra, rb, 0x0400u) & 0x00FF00FFu) | 0x64006400u;
+      h1 = (prmt(ra, rb, 0x0602u) & 0x00FF00FFu) | 0x64006400u;
+      h2 = (prmt(ra, rb, 0x0501u) & 0x00FF00FFu) | 0x64006400u;
+      h3 = (prmt(ra, rb, 0x0703u) & 0x00FF00FFu) | 0x64006400u;
+      bias = 0x64806480u;  // 1152
+    }
+  }
+  return make_uint4(hmul2_rn(hsub2_rn(h0, bias), s0), hmul2_rn(hsub2_rn(h1, bias), s1),
+                    hmul2_rn(hsub2_rn(h2, bias), s2), hmul2_rn(hsub2_rn(h3, bias), s3));
+}
+
+// ============================================================ dequantiser
+// A warp per (32-column tile, 64-deep k-block); lane = column.  Each lane
+// writes the 128 bytes of its column's k-block (eight chunks); the reads of a
+// chunk step are 32 consecutive words of one super-block.  REC: the source is
+// the stage records (zero-padded past K and N) instead of the stream.
+template <int QT, bool REC>
+__global__ void __launch_bounds__(256) qk0_dequant_kernel(uint16_t *__restrict__ dst, const uint8_t *__restrict__ src,
+                                                          int k, int n, long long stride_kb, long long stride_n) {
+  grid_dependents_launch();
+  grid_dependency_wait();  // the weight may come from the kernel before this one
+  constexpr int BLK = QT == kGgmlQ8_0 ? 272 : 144;
+  const int ntiles = n / 32, ktiles = k / 32;
+  const long long wid = static_cast<long long>(blockIdx.x) * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const int kb_total = (ktiles + 1) / 2;
+  if (wid >= static_cast<long long>(ntiles) * kb_total) return;
+  const int nt = static_cast<int>(wid % ntiles), kb = static_cast<int>(wid / ntiles);
+  uint16_t *row = dst + kb * stride_kb + static_cast<long long>(nt * 32 + lane) * stride_n;
+  // record (nt/4, kb) holds this tile's eight super-blocks at ((nt%4)*2 + c/4)*4 + c%4
+  const uint8_t *rec = src + ((static_cast<size_t>(nt / 4) * kb_total + kb) * 32 + (nt % 4) * 8) * BLK;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int kt = 2 * kb + c / 4;
+    if (REC || kt < ktiles) {
+      const uint8_t *blk = REC ? rec + c * BLK : src + ((static_cast<size_t>(nt) * ktiles + kt) * 4 + (c & 3)) * BLK;
+      *reinterpret_cast<uint4 *>(row + c * 8) = dq_decode<QT>(chunk_words_global<QT>(blk, lane), lane);
+    }
+  }
+}
+
+cudaError_t launch_qk0_dequant(uint16_t *dst, const uint8_t *src, int qt, int k, int n, long long stride_kb,
+                               long long stride_n, bool records, cudaStream_t st) {
+  const long long warps = static_cast<long long>(n / 32) * ((k / 32 + 1) / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((warps + 7) / 8), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
+#define HTPG_QK0_DQ(T)                                                                                  \
+  (records ? cudaLaunchKernelEx(&cfg, qk0_dequant_kernel<T, true>, dst, src, k, n, stride_kb, stride_n) \
+           : cudaLaunchKernelEx(&cfg, qk0_dequant_kernel<T, false>, dst, src, k, n, stride_kb, stride_n))
+  if (qt == kGgmlQ4_0)
+    e = HTPG_QK0_DQ(kGgmlQ4_0);
+  else if (qt == kGgmlQ8_0)
+    e = HTPG_QK0_DQ(kGgmlQ8_0);
+  else if (qt == kGgmlIQ4_NL)
+    e = HTPG_QK0_DQ(kGgmlIQ4_NL);
+  else
+    return cudaErrorInvalidValue;
+#undef HTPG_QK0_DQ
+  return counted(e != cudaSuccess ? e : cudaGetLastError());
+}
+
+// ================================================================ repack
+// Stage records for the fused kernel: record (ta, kb) holds, contiguously and
+// in this order, the super-blocks of column tiles 4ta..4ta+3, k-tiles 2kb and
+// 2kb+1 (tile r, k-tile e, super-block j at ((r*2 + e)*4 + j) blocks), with
+// zeros for tiles past N or K.  Records are ordered (ta, kb), so one
+// pipeline stage is one contiguous copy.  One thread per 16 bytes.
+__global__ void __launch_bounds__(256) qk0_repack_kernel(uint4 *__restrict__ dst, const uint4 *__restrict__ src,
+                                                         int blk16, int ktiles, int ntiles, int kb_total,
+                                                         long long units) {
+  const long long u = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (u >= units) return;
+  const int per_rec = 32 * blk16;  // 16-byte units per record
+  const long long rec = u / per_rec;
+  const int w = static_cast<int>(u % per_rec);
+  const int sb = w / blk16, part = w % blk16;  // super-block of the record, unit within it
+  const int r = sb >> 3, e = (sb >> 2) & 1, j = sb & 3;
+  const int ta = static_cast<int>(rec / kb_total), kb = static_cast<int>(rec % kb_total);
+  const int nt = 4 * ta + r, kt = 2 * kb + e;
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (nt < ntiles && kt < ktiles)
+    v = __ldg(src + ((static_cast<long long>(nt) * ktiles + kt) * 4 + j) * blk16 + part);
+  dst[u] = v;
+}
+
+size_t qk0_stage_records_bytes(int qt, int k, int n) {
+  const size_t recs = static_cast<size_t>((n + 127) / 128) * static_cast<size_t>((k / 32 + 1) / 2);
+  return recs * 32u * static_cast<size_t>(qk0_block_bytes(qt));
+}
+
+cudaError_t launch_qk0_repack(uint8_t *dst, const uint8_t *src, int qt, int k, int n, cudaStream_t st) {
+  const int blk16 = qk0_block_bytes(qt) / 16;
+  if (!blk16) return cudaErrorInvalidValue;
+  const int ktiles = k / 32, ntiles = n / 32, kb_total = (ktiles + 1) / 2;
+  const long long units = static_cast<long long>(qk0_stage_records_bytes(qt, k, n) / 16u);
+  qk0_repack_kernel<<<static_cast<unsigned>((units + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<uint4 *>(dst), reinterpret_cast<const uint4 *>(src), blk16, ktiles, ntiles, kb_total, units);
+  return counted(cudaGetLastError());
+}
+
+// ============================================================ fused GEMM
+// Dequantisers: kQGroups groups of four warps; group g converts the CTA's
+// iterations g, g + kQGroups, ...; warp r of a group (r = warp % 4, its TMEM
+// lane quadrant) converts the 32 rows of column tile r, eight independent
+// chunks per lane.
+//
+// The MMA issuer commits once per kCommit iterations: a tcgen05.commit costs
+// about as much as a dozen N=16 MMAs on this part, so the FP16 operand ring is
+// released kCommit slots at a time (one commit barrier per half of the ring).
+// The activation tile of an iteration lives with its operand slot and is
+// loaded by the converting group; the super-block ring is released by the
+// dequantisers alone.
+constexpr int kQGroups = 4;
+constexpr int kQDeqWarps = 4 * kQGroups;
+constexpr int kQEpiWarps = 4;   // one per TMEM lane quadrant
+constexpr int kQThreads = 32 * (2 + kQEpiWarps + kQDeqWarps);
+constexpr int kCommit = 4;              // iterations per MMA commit
+constexpr int kAStages = 2 * kCommit;  // FP16 operand ring (dequantisers -> MMA)
+constexpr int kQMaxStages = 24;         // super-block ring (bulk copies -> dequantisers)
+constexpr int kQSmemLimit = 232448;
+constexpr int kQBarBytes = 1024;
+static_assert(kQGroups == kCommit, "each commit group holds one iteration of every dequantiser group");
+
+__host__ __device__ constexpr int q_block_bytes(int qt) { return qt == kGgmlQ8_0 ? 272 : 144; }
+// one stage: 4 column tiles x 2 k-tiles x 4 super-blocks (128 columns x 64 k)
+__host__ __device__ constexpr int q_stage_bytes(int qt) { return 32 * q_block_bytes(qt); }
+__host__ __device__ constexpr int q_stages(int qt, int bn) {
+  return (kQSmemLimit - 1024 - kQBarBytes - kAStages * (16384 + bn * 128)) / q_stage_bytes(qt) < kQMaxStages
+             ? (kQSmemLimit - 1024 - kQBarBytes - kAStages * (16384 + bn * 128)) / q_stage_bytes(qt)
+             : kQMaxStages;
+}
+__host__ __device__ constexpr size_t qgemm_smem(int qt, int bn) {
+  return 1024 + static_cast<size_t>(kAStages) * (16384 + bn * 128) +
+         static_cast<size_t>(q_stages(qt, bn)) * q_stage_bytes(qt) + kQBarBytes;
+}
+static_assert((2 * kQMaxStages + 3 * kAStages + 7) * 8 + 16 <= kQBarBytes, "barrier block");
+static_assert(kQGroups <= q_stages(kGgmlQ8_0, 32), "super-block slots advance by kQGroups");
+static_assert(qgemm_smem(kGgmlQ8_0, 32) <= kQSmemLimit && qgemm_smem(kGgmlQ4_0, 32) <= kQSmemLimit,
+              "shared memory budget");
+
+struct QGemmParams {
+  QGemmArgs a;
+  const uint8_t *w;  // stage records (qk0_repack_kernel)
+  int tiles_b, kb_total;
+  long long iters;
+};
+
+// Stream-K bookkeeping: CTA c owns iterations [c*T/G, (c+1)*T/G).
+__device__ __forceinline__ int sk_owner(long long i, long long T, int G) {
+  return static_cast<int>(((i + 1) * G - 1) / T);
+}
+__device__ __forceinline__ long long sk_begin(int c, long long T, int G) { return static_cast<long long>(c) * T / G; }
+// Partial slot of CTA c's piece of tile t: slot 0 for its first tile, slot 1
+// for its last (only these two can be partial).
+__device__ __forceinline__ int sk_slot(int c, int t, long long T, int G, int KB) {
+  return 2 * c + (t == static_cast<int>(sk_begin(c, T, G) / KB) ? 0 : 1);
+}
+
+template <int BN>
+__device__ __forceinline__ void qgemm_store(const QGemmArgs &g, const float (&v)[BN], int n, int tb) {
+  if (n >= g.N) return;
+#pragma unroll
+  for (int j = 0; j < BN; ++j) {
+    const int m = tb * BN + j;
+    if (m < g.M) g.out[static_cast<long long>(m) * g.ldo + n] = v[j];
+  }
+}
+
+template <int QT, int BN>
+__global__ void __launch_bounds__(kQThreads, 1)
+    qgemm_swap_kernel(const __grid_constant__ CUtensorMap tmB, const QGemmParams P) {
+  constexpr int QS = q_stages(QT, BN);
+  constexpr uint32_t QSB = q_stage_bytes(QT);
+  constexpr uint32_t BB = BN * 128;
+  constexpr int BLK = q_block_bytes(QT);
+  constexpr uint32_t TCOLS = 2 * BN <= 32 ? 32 : 64;
+  constexpr uint32_t kIdesc = idesc_f16(128, BN);
+  static_assert(BN == 16 || BN == 32, "activation rows per tile");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sA = base;                    // kAStages x 128 rows x 128 B (FP16 weight, swizzled)
+  uint8_t *sB = sA + kAStages * 16384;   // kAStages x BN rows x 128 B (FP16 activations, swizzled by TMA)
+  uint8_t *sQ = sB + kAStages * BB;      // QS x one stage record
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sQ + QS * QSB);
+  uint64_t *qfull = bars, *qempty = qfull + QS;
+  uint64_t *afull = qempty + QS, *bfull = afull + kAStages;
+  uint64_t *mdone = bfull + kAStages;    // [2]: the MMAs of a commit group have completed
+  uint64_t *tfull = mdone + 2, *tempty = tfull + 2, *mma_done = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+  volatile uint32_t *flag = tmem_slot + 1;
+  volatile uint32_t *abort = tmem_slot + 2;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const QGemmArgs &g = P.a;
+  uint32_t *wd = g.watchdog;
+  grid_dependents_launch();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < QS; ++s) {
+      mbar_init(smem_u32(&qfull[s]), 1);
+      mbar_init(smem_u32(&qempty[s]), 4);  // the converting group's four warps
+    }
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(smem_u32(&afull[s]), 4);
+      mbar_init(smem_u32(&bfull[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&mdone[b]), 1);
+      mbar_init(smem_u32(&tfull[b]), 1);
+      mbar_init(smem_u32(&tempty[b]), kQEpiWarps);
+    }
+    mbar_init(smem_u32(mma_done), 1);
+    *abort = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), TCOLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const long long T = P.iters;
+  const int G = gridDim.x, cta = blockIdx.x, KB = P.kb_total;
+  const long long i0 = sk_begin(cta, T, G), i1 = sk_begin(cta + 1, T, G);
+
+  if (warp == 0) {
+    // ------------------------------------------------ super-block producer
+    if (lane == 0) {
+      // (tile, k-block) of the first iteration; later ones by incrementing
+      // (a 64-bit division per iteration would cost more than the iteration)
+      const int t0 = static_cast<int>(i0 / KB), kb0 = static_cast<int>(i0 % KB);
+      // stage record of iteration (ta, kb): one contiguous run of QSB bytes
+      auto record = [&](int ta, int kb) { return P.w + (static_cast<size_t>(ta) * KB + kb) * QSB; };
+      // warm the L2 with the first records; loads wait for the previous kernel
+      {
+        int ta = t0 / P.tiles_b, tb = t0 % P.tiles_b, kb = kb0;
+        for (long long i = i0; i < i1 && i < i0 + QS; ++i) {
+          bulk_prefetch_l2(record(ta, kb), QSB);
+          if (++kb == KB) {
+            kb = 0;
+            if (++tb == P.tiles_b) tb = 0, ++ta;
+          }
+        }
+      }
+      grid_dependency_wait();
+      int s = 0;
+      uint32_t ph = 0;
+      int last_phase[QS];
+#pragma unroll
+      for (int j = 0; j < QS; ++j) last_phase[j] = -1;
+      int ta = t0 / P.tiles_b, tb = t0 % P.tiles_b, kb = kb0;
+      for (long long i = i0; i < i1; ++i) {
+        if (!mbar_wait(smem_u32(&qempty[s]), ph ^ 1u, wd, kWatchProducer, abort)) break;
+        const uint32_t fb = smem_u32(&qfull[s]);
+        mbar_arrive_expect_tx(fb, QSB);
+        bulk_load(smem_u32(sQ + s * QSB), record(ta, kb), QSB, fb);
+        if (++kb == KB) {
+          kb = 0;
+          if (++tb == P.tiles_b) tb = 0, ++ta;
+        }
+        last_phase[s] = static_cast<int>(ph);
+        if (++s == QS) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      // no copy may still be landing when the CTA exits
+      for (int j = 0; j < QS; ++j)
+        if (last_phase[j] >= 0)
+          mbar_wait(smem_u32(&qfull[j]), static_cast<uint32_t>(last_phase[j]), wd, kWatchProducer, abort);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    // Iterations go in commit groups of kCommit, split where a new accumulator
+    // piece starts (its buffer may only be waited for once every earlier
+    // piece's completion has been committed): every wait of a run first, then
+    // its MMAs back to back; one commit per group frees its operand slots.
+    if (lane == 0) {
+      grid_dependency_wait();
+      bool ok = true;
+      uint32_t piece = 0;  // accumulator pieces (tiles or tile parts) finished
+      int kb_g = static_cast<int>(i0 % KB);
+      for (long long i = i0; ok && i < i1;) {
+        const long long j = i - i0;
+        const long long gend = i0 + (j / kCommit + 1) * kCommit < i1 ? i0 + (j / kCommit + 1) * kCommit : i1;
+        // the run [i, send): up to the group's end or the next piece start
+        long long send = i + 1;
+        for (int kb = kb_g + 1 == KB ? 0 : kb_g + 1; send < gend && kb != 0; kb = kb + 1 == KB ? 0 : kb + 1) ++send;
+        if (i == i0 || kb_g == 0)
+          ok = mbar_wait(smem_u32(&tempty[piece & 1u]), ((piece >> 1) & 1u) ^ 1u, wd, kWatchMma, abort);
+        for (long long t = i; ok && t < send; ++t) {
+          const int sa = static_cast<int>((t - i0) % kAStages);
+          const uint32_t aph = static_cast<uint32_t>(((t - i0) / kAStages) & 1);
+          ok = mbar_wait(smem_u32(&afull[sa]), aph, wd, kWatchMma, abort);
+          ok = ok && mbar_wait(smem_u32(&bfull[sa]), aph, wd, kWatchMma, abort);
+        }
+        if (!ok) break;
+        tc_fence_after();
+        for (long long t = i; t < send; ++t, kb_g = kb_g + 1 == KB ? 0 : kb_g + 1) {
+          const int sa = static_cast<int>((t - i0) % kAStages);
+          const uint32_t buf = piece & 1u;
+          umma_f16_kblock(tmem_base + buf * BN, umma_desc_sw128(smem_u32(sA + sa * 16384)),
+                          umma_desc_sw128(smem_u32(sB + sa * BB)), kIdesc, (t == i0 || kb_g == 0) ? 0u : 1u);
+          if (t == i1 - 1 || kb_g == KB - 1) {
+            tc_commit(smem_u32(&tfull[buf]));
+            ++piece;
+          }
+        }
+        if (send == gend && (gend - i0) % kCommit == 0) tc_commit(smem_u32(&mdone[(j / kCommit) & 1]));
+        i = send;
+      }
+      // every MMA of this thread completes before TMEM is released
+      tc_commit(smem_u32(mma_done));
+      mbar_wait(smem_u32(mma_done), 0, wd, kWatchMma, abort);
+    }
+  } else if (warp < 2 + kQEpiWarps) {
+    // ------------------------------------------------ epilogue (one warp per lane quadrant)
+    const int q = warp & 3;
+    const bool lead = threadIdx.x == 64;
+    grid_dependency_wait();  // nothing is stored before the previous kernel is done
+    uint32_t piece = 0;
+    for (long long i = i0; i < i1; ++piece) {
+      const int t = static_cast<int>(i / KB);
+      const long long tile_end = static_cast<long long>(t + 1) * KB;
+      const long long end = i1 < tile_end ? i1 : tile_end;
+      const bool whole = (i % KB) == 0 && end == tile_end;
+      const uint32_t buf = piece & 1u;
+      const bool ok = mbar_wait(smem_u32(&tfull[buf]), (piece >> 1) & 1u, wd, kWatchEpilogue, abort);
+      tc_fence_after();
+      float v[BN];
+#pragma unroll
+      for (int j = 0; j < BN; ++j) v[j] = 0.0f;
+      if (ok) {
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+        if constexpr (BN == 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+        } else {
+          uint32_t r[32];
+          tmem_ld32(taddr, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive(smem_u32(&tempty[buf]));
+      const int tb = t % P.tiles_b;
+      const int n = (t / P.tiles_b) * 128 + q * 32 + lane;
+      if (whole) {
+        if (ok) qgemm_store<BN>(g, v, n, tb);
+      } else {
+        // partial tile: park it, count it; the last contributor sums all
+        // contributions in CTA order (deterministic) and stores the tile
+        float *mine = g.partials + static_cast<size_t>(sk_slot(cta, t, T, G, KB)) * BN * 128 + q * 32 + lane;
+#pragma unroll
+        for (int j = 0; j < BN; ++j) mine[j * 128] = v[j];
+        __threadfence();
+        named_bar_sync(1, 32 * kQEpiWarps);
+        const int c_first = sk_owner(static_cast<long long>(t) * KB, T, G);
+        const int c_last = sk_owner(tile_end - 1, T, G);
+        if (lead) {
+          uint32_t fin = 0u;
+          if (!*abort) {
+            const uint32_t prev = atomicAdd(g.counters + t, 1u);
+            fin = prev == static_cast<uint32_t>(c_last - c_first) ? 1u : 0u;
+          }
+          *flag = fin;
+        }
+        named_bar_sync(1, 32 * kQEpiWarps);
+        if (*flag) {
+          __threadfence();
+          float acc[BN];
+#pragma unroll
+          for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
+          for (int cc = c_first; cc <= c_last; ++cc) {
+            const float *p = g.partials + static_cast<size_t>(sk_slot(cc, t, T, G, KB)) * BN * 128 + q * 32 + lane;
+#pragma unroll
+            for (int j = 0; j < BN; ++j) acc[j] += __ldcg(p + j * 128);
+          }
+          qgemm_store<BN>(g, acc, n, tb);
+          if (lead) g.counters[t] = 0u;
+        }
+        named_bar_sync(1, 32 * kQEpiWarps);  // the flag is reused by the next piece
+      }
+      i = end;
+    }
+  } else {
+    // ------------------------------------------------ dequantisers
+    const int dw = warp - 2 - kQEpiWarps;
+    const int grp = dw >> 2, nt = warp & 3;  // group; column tile = this warp's lane quadrant
+    const bool issuer = nt == 0 && lane == 0;  // loads the group's activation tiles
+    if (issuer) tma_prefetch_desc(&tmB);
+    grid_dependency_wait();  // the activations come from the kernel before this one
+    const uint32_t sQs = smem_u32(sQ), sAs = smem_u32(sA);
+    const int row = nt * 32 + lane;
+    const uint32_t row_off = static_cast<uint32_t>(row) * 128u;
+    // ring slots and phases of iteration j = grp, grp + kQGroups, ...
+    int sq = grp;
+    uint32_t qph = 0;
+    int tb = 0, kb = 0;
+    {
+      const long long ig = i0 + grp;
+      if (ig < i1) tb = static_cast<int>((ig / KB) % P.tiles_b), kb = static_cast<int>(ig % KB);
+    }
+    int last_b[kAStages];
+#pragma unroll
+    for (int s = 0; s < kAStages; ++s) last_b[s] = -1;
+    for (long long i = i0 + grp; i < i1; i += kQGroups) {
+      const long long j = i - i0;
+      const int sa = static_cast<int>(j % kAStages);
+      // the operand slot is free once the MMAs of iteration j - kAStages completed
+      const uint32_t md_par = static_cast<uint32_t>(((j / kAStages) & 1) ^ 1);
+      bool ok = mbar_wait(smem_u32(&mdone[(j / kCommit) & 1]), md_par, wd, kWatchDequant, abort);
+      if (issuer && ok) {
+        const uint32_t fb = smem_u32(&bfull[sa]);
+        mbar_arrive_expect_tx(fb, BB);
+        tma_load_2d(smem_u32(sB + sa * BB), &tmB, fb, kb * 64, tb * BN);
+        last_b[sa] = static_cast<int>((j / kAStages) & 1);
+      }
+      ok = ok && mbar_wait(smem_u32(&qfull[sq]), qph, wd, kWatchDequant, abort);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const uint32_t qs = sQs + sq * QSB + nt * 8 * BLK;  // this column tile's 2 k-tiles x 4 super-blocks
+      const uint32_t as = sAs + sa * 16384 + row_off;
+      ChunkWords cw[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) cw[c] = chunk_words_shared<QT>(qs + c * BLK, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&qempty[sq]));  // the record has been read
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 val = dq_decode<QT>(cw[c], lane);
+        // 128-byte swizzle: chunk c of row r at position c ^ (r % 8)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(as + ((c ^ (row & 7)) << 4)),
+                     "r"(val.x), "r"(val.y), "r"(val.z), "r"(val.w)
+                     : "memory");
+      }
+      fence_proxy_async_smem();  // the MMA (async proxy) reads what this thread wrote
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&afull[sa]));
+      if ((sq += kQGroups) >= QS) sq -= QS, qph ^= 1u;
+      for (kb += kQGroups; kb >= KB;) {
+        kb -= KB;
+        if (++tb == P.tiles_b) tb = 0;
+      }
+    }
+    // no activation copy may still be landing when the CTA exits
+    if (issuer)
+      for (int s = 0; s < kAStages; ++s)
+        if (last_b[s] >= 0) mbar_wait(smem_u32(&bfull[s]), static_cast<uint32_t>(last_b[s]), wd, kWatchDequant, abort);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TCOLS);
+  }
+}
+
+QGemmPlan plan_qgemm(int qt, int M, int N, int K, int num_sms) {
+  QGemmPlan p;
+  p.bn = M <= 16 ? 16 : 32;
+  p.tiles_a = (N + 127) / 128;
+  p.tiles_b = (M + p.bn - 1) / p.bn;
+  p.kb_total = (K + 63) / 64;
+  p.iters = static_cast<long long>(p.tiles_a) * p.tiles_b * p.kb_total;
+  // at least four k-blocks per CTA, at most one CTA per SM
+  long long g = p.iters / 4;
+  g = g < 1 ? 1 : g;
+  p.grid = static_cast<int>(g < num_sms ? g : num_sms);
+  p.smem = qgemm_smem(qt, p.bn);
+  return p;
+}
+
+template <int QT, int BN>
+static cudaError_t launch_qgemm_t(const QGemmPlan &p, const uint8_t *w, const CUtensorMap &tmB,
+                                  const QGemmArgs &a, cudaStream_t st) {
+  auto fn = qgemm_swap_kernel<QT, BN>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const size_t smem = qgemm_smem(QT, BN);
+  if (!configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  QGemmParams P;
+  P.a = a;
+  P.w = w;
+  P.tiles_b = p.tiles_b;
+  P.kb_total = p.kb_total;
+  P.iters = p.iters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+  cfg.blockDim = dim3(kQThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, tmB, P);
+  return counted(e != cudaSuccess ? e : cudaGetLastError());
+}
+
+cudaError_t launch_qgemm(int qt, const QGemmPlan &p, const uint8_t *w, const CUtensorMap &tmB,
+                         const QGemmArgs &a, cudaStream_t st) {
+  if (p.grid < 1 || p.iters < p.grid) return cudaErrorInvalidConfiguration;
+  if (qt == kGgmlQ4_0) return p.bn == 16 ? launch_qgemm_t<kGgmlQ4_0, 16>(p, w, tmB, a, st)
+                                         : launch_qgemm_t<kGgmlQ4_0, 32>(p, w, tmB, a, st);
+  if (qt == kGgmlQ8_0) return p.bn == 16 ? launch_qgemm_t<kGgmlQ8_0, 16>(p, w, tmB, a, st)
+                                         : launch_qgemm_t<kGgmlQ8_0, 32>(p, w, tmB, a, st);
+  if (qt == kGgmlIQ4_NL) return p.bn == 16 ? launch_qgemm_t<kGgmlIQ4_NL, 16>(p, w, tmB, a, st)
+                                           : launch_qgemm_t<kGgmlIQ4_NL, 32>(p, w, tmB, a, st);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace htpg

@@ -106,6 +106,13 @@ def lib() -> ctypes.CDLL:
         "hmx_mat_mul_native_w8a8_cpu": (I, [P, P, P, I, I, I, P]),
         "hmx_mat_mul_f16_epilogue": (I, [P, P, P, P, I, I, I, I, I]),
         "hmx_mat_mul_permuted_w16a32": (I, [P, P, P, I, I, I]),
+        "hmx_mat_mul_permuted_qk_0_d16a32": (I, [P, P, P, I, I, I, I]),
+        "htpg_qk0_weight_bytes": (S, [I, I, I]),
+        "htpg_qk0_linear": (I, [P, P, P, I, I, I, I, P]),
+        "htpg_qk0_weights_create": (I, [P, I, I, I, P, ctypes.POINTER(P)]),
+        "htpg_qk0_run": (I, [P, P, P, I, P]),
+        "htpg_qk0_dequantize": (I, [P, P, I, I, I, P]),
+        "htpg_qk0_plan_info": (I, [I, I, I, I, I, ctypes.POINTER(I64)]),
         "htp_ops_open": (I, [ctypes.c_char_p, ctypes.POINTER(U64)]),
         "htp_ops_close": (I, [U64]),
         "htp_ops_init_backend": (I, [U64]),
@@ -229,6 +236,30 @@ def plan_info(kind: int, m: int, n: int, k: int, sms: int = 148) -> dict:
     out = (ctypes.c_int64 * 10)()
     check(lib().htpg_plan_info(kind, m, n, k, sms, out), "htpg_plan_info")
     return dict(zip(PLAN_FIELDS, list(out)))
+
+
+def qk0_plan_info(weight_type: int, m: int, n: int, k: int, sms: int = 148) -> dict:
+    """Plan of the fused small-M opcode 2-4 kernel."""
+    out = (ctypes.c_int64 * 6)()
+    check(lib().htpg_qk0_plan_info(weight_type, m, n, k, sms, out), "htpg_qk0_plan_info")
+    return dict(zip(("bn", "tiles_a", "tiles_b", "kb_total", "grid", "smem"), list(out)))
+
+
+def qk0_weights(weight_dev, weight_type: int, k: int, n: int, stream=None) -> Weights:
+    """Prepared opcode 2-4 weight (stage records) from the reference's super-block stream."""
+    h = ctypes.c_void_p()
+    check(lib().htpg_qk0_weights_create(ptr(weight_dev), k, n, weight_type, stream_ptr(stream), ctypes.byref(h)),
+          "htpg_qk0_weights_create")
+    return Weights(h.value, n)
+
+
+def qk0_run(w: Weights, out, x, m: int, stream=None) -> int:
+    return lib().htpg_qk0_run(w.handle, ptr(out), ptr(x), m, stream_ptr(stream))
+
+
+def qk0_linear(out, x, weight, weight_type: int, m: int, k: int, n: int, stream=None) -> int:
+    """Opcodes 2-4 on device tensors: out[m][n] = fp16(x) * dequant(weight)."""
+    return lib().htpg_qk0_linear(ptr(out), ptr(x), ptr(weight), m, k, n, weight_type, stream_ptr(stream))
 
 
 def phase_timing_read() -> tuple[float, float, int]:

@@ -156,6 +156,36 @@ int htpg_model_aux(float *dst, const float *x, const float *w, const float *b,
 int hvx_model_aux_f32(float *dst, const float *x, const float *w, const float *b,
                       const struct NativeAuxParams *p);
 
+/* ---- opcodes 2-4: ggml-block weights (reference: mat_mul.c:246-430,
+ *      1601-1874; quants.h:11-31; op_executor.cc:771-808) ------------------
+ * The weight is the reference's permuted stream of K*N/256 super-blocks
+ * (my_block_q4_0: 8 FP16 scales + 128 bytes of nibbles, 144 bytes;
+ * my_block_q8_0: 8 FP16 scales + 256 INT8, 272 bytes), used in place (no
+ * prepared copy).  weight_type is the ggml type: */
+#define HTPG_GGML_Q4_0 2
+#define HTPG_GGML_Q8_0 8
+#define HTPG_GGML_IQ4_NL 20
+/* Bytes of the super-block stream (0 for an unsupported type or shape). */
+size_t htpg_qk0_weight_bytes(int weight_type, int k, int n);
+/* Prepared weight (destroy with htpg_weights_destroy): the super-blocks
+ * reordered once into per-stage records (128 columns x 64 k each, zero-padded
+ * past N and K), so that the fused kernel loads a stage with one copy.  The
+ * caller's buffer is not used afterwards. */
+int htpg_qk0_weights_create(const void *weight, int k, int n, int weight_type, void *stream, htpg_weights **out);
+/* out[m][n] = fp16(x[m][k]) * dequant(W) on a prepared weight (see below). */
+int htpg_qk0_run(const htpg_weights *w, float *out, const float *x, int m, void *stream);
+/* out[m][n] (FP32) = fp16(x[m][k]) * W16, FP32 accumulation.  M <= 32: one
+ * fused kernel that dequantises weight tiles on the fly; larger M: the weight
+ * is dequantised to FP16 in a stream-private scratch buffer and the FP16 GEMM
+ * runs on it.  Device pointers, x and weight 16-byte aligned.  The prepared
+ * weight is cached by address like the other one-call entry points. */
+int htpg_qk0_linear(float *out, const float *x, const void *weight, int m, int k, int n, int weight_type,
+                    void *stream);
+/* The dequantised weight as FP16 bits, row-major w_nk[n][k]. */
+int htpg_qk0_dequantize(uint16_t *w_nk, const void *weight, int k, int n, int weight_type, void *stream);
+/* Plan of the fused kernel: {bn, tiles_a, tiles_b, k-blocks, CTAs, shared bytes}. */
+int htpg_qk0_plan_info(int weight_type, int m, int n, int k, int sms, int64_t out[6]);
+
 /* ---- column-sharded run with a fused output exchange -------------------- */
 /* Multi-GPU form of htpg_w8a8_run for a weight split by output columns (N)
  * across ranks, each rank holding a column block: the epilogue stores every
@@ -265,6 +295,9 @@ int hmx_mat_mul_f16_epilogue(float *dst, const float *activation, const uint16_t
                              const float *bias, int m, int k, int n, int channels, int mode);
 int hmx_mat_mul_permuted_w16a32(float *dst, const float *activation,
                                 const uint16_t *permuted_weight, int m, int k, int n);
+/* opcodes 2-4 (include/dsp/ops.h:60 of the reference): returns 0 or -1. */
+int hmx_mat_mul_permuted_qk_0_d16a32(float *dst, const float *activation, const uint8_t *permuted_weight,
+                                     int m, int k, int n, int weight_type);
 
 /* ---- buffer registry (replaces the DSP fd->pointer map cache,
  *      src/dsp/mmap_mgr.cc:10-139) ----------------------------------------- */

@@ -5,6 +5,8 @@
  *
  * Only the payloads of the ops this library executes are declared here:
  *   opcode  1  HTP_OPS_MAT_MUL_PERMUTED_W16A32  MatMulParams (92 B, 96 B with elapsed_us)
+ *   opcodes 2-4 HTP_OPS_MAT_MUL_PERMUTED_W4D16A32, _W8D16A32, _W4D16A32_IQ4_NL
+ *                                               MatMulParams; weight = ggml super-blocks
  *   opcode 15  HTP_OPS_MAT_MUL_NATIVE_W8A8      NativeW8A8Params (40 B), +profile (104 B),
  *                                               +CPU control (48 B), +epilogue (56 B, new)
  *   opcode 16  HTP_OPS_MAT_MUL_F16_EPILOGUE     F16EpilogueParams (56 B)
@@ -26,9 +28,9 @@ extern "C" {
 enum HtpOpsIndex {
   HTP_OPS_RMS_NORM_F32,                        /* 0 */
   HTP_OPS_MAT_MUL_PERMUTED_W16A32,             /* 1  (executed) */
-  HTP_OPS_MAT_MUL_PERMUTED_W4D16A32,           /* 2 */
-  HTP_OPS_MAT_MUL_PERMUTED_W8D16A32,           /* 3 */
-  HTP_OPS_MAT_MUL_PERMUTED_W4D16A32_IQ4_NL,    /* 4 */
+  HTP_OPS_MAT_MUL_PERMUTED_W4D16A32,           /* 2  (executed) */
+  HTP_OPS_MAT_MUL_PERMUTED_W8D16A32,           /* 3  (executed) */
+  HTP_OPS_MAT_MUL_PERMUTED_W4D16A32_IQ4_NL,    /* 4  (executed) */
   HTP_OPS_FLASH_ATTN_QO_F32_KV_F16,            /* 5 */
   HTP_OPS_BLOCK_SPARSE_ATTN_QO_F32_KV_F16,     /* 6 */
   HTP_OPS_BLOCK_SPARSE_SCORE_QO_F32_KM_F16,    /* 7 */

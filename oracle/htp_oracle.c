@@ -419,6 +419,127 @@ void orc_conv2d_nchw_f16(float *out, const float *x, const uint16_t *wperm, cons
   free(a);
 }
 
+/* ------------------------------------------------------------------------ */
+/* Opcodes 2-4: ggml-block weights (mat_mul.c:246-430, 1601-1874)           */
+/* ------------------------------------------------------------------------ */
+
+/* IQ4_NL levels (iq4_nl_to_fp16_lut, mat_mul.c:34-37: the table holds its 16
+ * entries at the even half-word positions that vlut16 reads). */
+static const int8_t kIq4nlLevels[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
+                                        1,    13,   25,  38,  53,  69,  89,  113};
+
+size_t orc_qk0_block_bytes(int type) {
+  switch (type) {
+    case ORC_GGML_Q4_0:
+    case ORC_GGML_IQ4_NL: return 16 + 128; /* my_block_q4_0 (quants.h:16-19) */
+    case ORC_GGML_Q8_0: return 16 + 256;   /* my_block_q8_0 (quants.h:28-31) */
+    default: return 0;
+  }
+}
+
+/* Element e of a super-block, following the per-block body of
+ * dequantize_permuted_weight_q4_0_to_fp16_hvx_task (mat_mul.c:389-424) and
+ * ..._q8_0_... (:488-525).  Q4: vlut16 on the low nibbles (v = 0: even bytes,
+ * v = 1: odd bytes) and on the bytes shifted right by 4 (v = 2, 3); the scale
+ * vectors hold scales[2v] for lanes 0..31 and scales[2v+1] for 32..63 (the
+ * vlut16 of the {0,2 | 1,3} index pattern over the unpacked scales).  Q8:
+ * vunpack keeps byte order, so element e is byte e. */
+uint16_t orc_qk0_element(const uint8_t *block, int type, int e) {
+  uint16_t sbits;
+  memcpy(&sbits, block + 2 * (e / 32), 2);
+  const float scale = orc_f16_to_f32(sbits);
+  const uint8_t *q = block + 16;
+  float level;
+  if (type == ORC_GGML_Q8_0) {
+    level = (float)(int8_t)q[e];
+  } else {
+    const int v = e / 64, i = e % 64;
+    const uint8_t byte = q[2 * i + (v & 1)];
+    const int nib = v < 2 ? (byte & 15) : (byte >> 4);
+    level = type == ORC_GGML_IQ4_NL ? (float)kIq4nlLevels[nib] : (float)(nib - 8);
+  }
+  /* |level| <= 128 and an 11-bit significand: the product is exact in FP32,
+     so one rounding to FP16 remains */
+  return orc_f32_to_f16(level * scale);
+}
+
+/* The dequantised stream is the packed FP16 weight itself. */
+static void qk0_stream(uint16_t *perm, const uint8_t *src, int type, int k, int n) {
+  const size_t bb = orc_qk0_block_bytes(type);
+  const size_t blocks = (size_t)k * (size_t)n / 256u;
+#pragma omp parallel for schedule(static)
+  for (size_t b = 0; b < blocks; ++b)
+    for (int e = 0; e < 256; ++e) perm[b * 256u + (size_t)e] = orc_qk0_element(src + b * bb, type, e);
+}
+
+void orc_qk0_dequant(uint16_t *w_nk, const uint8_t *src, int type, int k, int n) {
+  uint16_t *perm = (uint16_t *)malloc((size_t)k * n * 2u);
+  qk0_stream(perm, src, type, k, n);
+  for (int c = 0; c < n; ++c)
+    for (int r = 0; r < k; ++r) w_nk[(size_t)c * k + r] = perm[orc_f16_perm_offset(k, r, c)];
+  free(perm);
+}
+
+/* (k, n) of packed FP16 position f: the inverse of orc_f16_perm_offset. */
+static void perm_position(size_t f, int k_total, int *k, int *n) {
+  const size_t tile = f / 1024u, o = f % 1024u;
+  const int kt = (int)(tile % (size_t)(k_total / 32)), nt = (int)(tile / (size_t)(k_total / 32));
+  *k = kt * 32 + (int)(o / 64u) * 2 + (int)(o & 1u);
+  *n = nt * 32 + (int)((o % 64u) / 2u);
+}
+
+void orc_qk0_quantize(uint8_t *dst, const float *w_kn, int type, int k, int n) {
+  const size_t bb = orc_qk0_block_bytes(type);
+  const size_t blocks = (size_t)k * (size_t)n / 256u;
+  for (size_t b = 0; b < blocks; ++b) {
+    uint8_t *blk = dst + b * bb;
+    memset(blk, 0, bb);
+    for (int g = 0; g < 8; ++g) {
+      float vals[32], mx = 0.0f;
+      for (int j = 0; j < 32; ++j) {
+        int r, c;
+        perm_position(b * 256u + (size_t)(g * 32 + j), k, &r, &c);
+        vals[j] = w_kn[(size_t)r * n + c];
+        if (fabsf(vals[j]) > fabsf(mx)) mx = vals[j];
+      }
+      /* the extreme value maps onto the most negative level exactly */
+      const float lo = type == ORC_GGML_Q4_0 ? -8.0f : -127.0f;
+      const uint16_t dbits = orc_f32_to_f16(type == ORC_GGML_Q8_0 ? fabsf(mx) / 127.0f : mx / lo);
+      memcpy(blk + 2 * g, &dbits, 2);
+      const float d = orc_f16_to_f32(dbits);
+      for (int j = 0; j < 32; ++j) {
+        const int e = g * 32 + j;
+        int code;
+        if (type == ORC_GGML_IQ4_NL) {
+          code = 0;
+          for (int t = 1; t < 16; ++t)
+            if (fabsf(vals[j] - d * kIq4nlLevels[t]) < fabsf(vals[j] - d * kIq4nlLevels[code])) code = t;
+        } else {
+          const float r = d != 0.0f ? nearbyintf(vals[j] / d) : 0.0f;
+          const float hi = type == ORC_GGML_Q4_0 ? 7.0f : 127.0f;
+          code = (int)fminf(fmaxf(r, type == ORC_GGML_Q4_0 ? -8.0f : -127.0f), hi);
+          if (type == ORC_GGML_Q4_0) code += 8;
+        }
+        if (type == ORC_GGML_Q8_0) {
+          blk[16 + e] = (uint8_t)(int8_t)code;
+        } else {
+          const int v = e / 64, i = e % 64;
+          uint8_t *byte = blk + 16 + 2 * i + (v & 1);
+          *byte |= (uint8_t)(v < 2 ? code : code << 4);
+        }
+      }
+    }
+  }
+}
+
+void orc_qk0_linear_rows(float *out, const float *x, const uint8_t *src, int type, int m, int k, int n,
+                         int round_acc_f16, const int32_t *rows, int nrows) {
+  uint16_t *perm = (uint16_t *)malloc((size_t)k * n * 2u);
+  qk0_stream(perm, src, type, k, n);
+  orc_f16_linear_rows(out, x, perm, NULL, m, k, n, n, 0, round_acc_f16, rows, nrows);
+  free(perm);
+}
+
 /* epilogue_activation (mat_mul.c:788-826): z = x (SiLU), 1.702x (QuickGELU) or
  * 1.5957691216057308*(x + 0.044715x^3) (GELU); x*sigmoid(z) with the stable
  * split e = 2^(-|z| log2 e), sigmoid = z < 0 ? e/(1+e) : 1/(1+e). */

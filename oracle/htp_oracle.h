@@ -1,6 +1,8 @@
 /*
  * htp_oracle — CPU restatement of the reference library's linear-operator
- * arithmetic (W8A8 opcode 15, packed FP16 GEMM + epilogue opcodes 1/16).
+ * arithmetic (W8A8 opcode 15, packed FP16 GEMM + epilogue opcodes 1/16, the
+ * ggml-block dequantising GEMMs of opcodes 2-4, convolution opcode 17 and the
+ * model auxiliaries of opcode 19).
  *
  * TEST INFRASTRUCTURE ONLY.  Nothing in libhtp_ops_b200.so links or calls this
  * code; only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg
@@ -114,6 +116,37 @@ void orc_model_aux(float *out, const float *x, const float *w, const float *b, c
 /* x*sigmoid(z) activations of the epilogues: mode 1 GELU(tanh), 2 QuickGELU,
  * 4/5 SiLU (mat_mul.c:788-826). */
 float orc_activation(float x, int mode);
+
+/* ---- opcodes 2-4: ggml-block weights dequantised to FP16 -----------------
+ * (reference: mat_mul.c:246-430 dequantisation, :1601-1874 GEMM; quants.h:11-31
+ * block layouts).  The weight is a stream of K*N/256 super-blocks; super-block i
+ * dequantises to FP16 elements [256i, 256i+256) of the packed FP16 weight
+ * (orc_f16_perm_offset layout).  A super-block is 8 FP16 scales followed by the
+ * codes (Q4_0 / IQ4_NL: 128 bytes of nibbles, Q8_0: 256 INT8); element e uses
+ * scale e/32.  Q8_0: code = byte e.  Q4_0 / IQ4_NL: with v = e/64, i = e%64,
+ * the nibble is the low (v < 2) or high (v >= 2) half of byte 2i + (v & 1);
+ * value = nibble - 8 (Q4_0) or the IQ4_NL table entry.  The element is the
+ * FP16 product code * scale rounded to nearest even (HVX qf16 multiply then
+ * conversion; its ulp-level rounding is undocumented). */
+#define ORC_GGML_Q4_0 2
+#define ORC_GGML_Q8_0 8
+#define ORC_GGML_IQ4_NL 20
+/* Bytes of one 256-element super-block (144, 272), 0 for other types. */
+size_t orc_qk0_block_bytes(int type);
+/* FP16 bits of element e (0..255) of one super-block. */
+uint16_t orc_qk0_element(const uint8_t *block, int type, int e);
+/* Dequantised weight as FP16 bits, row-major w_nk[n][k]. */
+void orc_qk0_dequant(uint16_t *w_nk, const uint8_t *src, int type, int k, int n);
+/* Quantise FP32 w_kn[k][n] into the super-block stream (test data: the
+ * inverse of orc_qk0_dequant up to the codec's rounding; scale per 32-element
+ * group = the group's largest magnitude / 8, 127 or 127 for Q4_0, Q8_0,
+ * IQ4_NL, codes by rounding to the nearest level). */
+void orc_qk0_quantize(uint8_t *dst, const float *w_kn, int type, int k, int n);
+/* out[i][c] = sum_k f16(x[row][k]) * W16(k, c) in FP32 (the reference reads
+ * the accumulator through FP16, mat_mul.c:751-778: round_acc_f16 applies that
+ * rounding); rows as in orc_f16_linear_rows. */
+void orc_qk0_linear_rows(float *out, const float *x, const uint8_t *src, int type, int m, int k, int n,
+                         int round_acc_f16, const int32_t *rows, int nrows);
 
 /* Number of OpenMP threads this build uses (1 without OpenMP). */
 int orc_threads(void);

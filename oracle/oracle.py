@@ -71,6 +71,13 @@ def lib(kind: str = "st") -> ctypes.CDLL:
     L.orc_epilogue_activation.argtypes = [ctypes.c_float, I]
     L.orc_epilogue_activation.restype = ctypes.c_float
     L.orc_f16_linear_rows.argtypes = [P, P, P, P, I, I, I, I, I, I, P, I]
+    L.orc_qk0_block_bytes.argtypes = [I]
+    L.orc_qk0_block_bytes.restype = S
+    L.orc_qk0_element.argtypes = [P, I, I]
+    L.orc_qk0_element.restype = ctypes.c_uint16
+    L.orc_qk0_dequant.argtypes = [P, P, I, I, I]
+    L.orc_qk0_quantize.argtypes = [P, P, I, I, I]
+    L.orc_qk0_linear_rows.argtypes = [P, P, P, I, I, I, I, I, P, I]
     L.orc_threads.restype = I
     L.orc_set_threads.argtypes = [I]
     _libs[kind] = L
@@ -211,6 +218,50 @@ def f16_linear(x, wperm, k, n, bias=None, channels=None, mode=0, round_acc_f16=F
     b = None if bias is None else np.ascontiguousarray(bias, np.float32)
     lib(kind).orc_f16_linear_rows(_p(out), _p(x), _p(np.ascontiguousarray(wperm, np.uint16)), _p(b),
                                   m, k, n, channels, mode, int(round_acc_f16), _p(rows_arr), nrows)
+    return out
+
+
+# ggml types of opcodes 2-4 (quants.h:36-74; op_executor.cc:75-88)
+GGML_Q4_0, GGML_Q8_0, GGML_IQ4_NL = 2, 8, 20
+QK0_TYPES = {2: GGML_Q4_0, 3: GGML_Q8_0, 4: GGML_IQ4_NL}  # opcode -> weight type
+
+
+def qk0_block_bytes(wtype: int) -> int:
+    return int(lib().orc_qk0_block_bytes(wtype))
+
+
+def qk0_weight_bytes(wtype: int, k: int, n: int) -> int:
+    return k * n // 256 * qk0_block_bytes(wtype)
+
+
+def qk0_quantize(w_kn: np.ndarray, wtype: int) -> np.ndarray:
+    """FP32 [k][n] -> super-block stream (uint8) of the given ggml type."""
+    k, n = w_kn.shape
+    out = np.zeros(qk0_weight_bytes(wtype, k, n), np.uint8)
+    lib().orc_qk0_quantize(_p(out), _p(np.ascontiguousarray(w_kn, np.float32)), wtype, k, n)
+    return out
+
+
+def qk0_random(wtype: int, k: int, n: int, seed: int, sigma: float = 0.02) -> np.ndarray:
+    """Seeded super-block stream: an N(0, sigma) weight quantised to the type."""
+    return qk0_quantize(normal(k * n, sigma, seed=seed).reshape(k, n), wtype)
+
+
+def qk0_dequant(src: np.ndarray, wtype: int, k: int, n: int) -> np.ndarray:
+    """Super-block stream -> FP16 bits, row-major [n][k]."""
+    out = np.zeros((n, k), np.uint16)
+    lib().orc_qk0_dequant(_p(out), _p(np.ascontiguousarray(src, np.uint8)), wtype, k, n)
+    return out
+
+
+def qk0_linear(x, src, wtype, k, n, round_acc_f16=False, rows=None, kind="st"):
+    m = x.shape[0]
+    x = np.ascontiguousarray(x, np.float32)
+    rows_arr = None if rows is None else np.ascontiguousarray(rows, np.int32)
+    nrows = m if rows is None else len(rows_arr)
+    out = np.zeros((nrows, n), np.float32)
+    lib(kind).orc_qk0_linear_rows(_p(out), _p(x), _p(np.ascontiguousarray(src, np.uint8)), wtype, m, k, n,
+                                  int(round_acc_f16), _p(rows_arr), nrows)
     return out
 
 

@@ -192,6 +192,32 @@ def test_w16a32_payload_and_mapping(L):
     b.release()
 
 
+# ------------------------------------------------------------------ opcodes 2-4
+def _mm(fo, fa, fw, m, k, n, out_off=0):
+    return struct.pack("<iiiiiiiii", fo, out_off, fa, 0, fw, 0, m, k, n) + b"\0" * 56
+
+
+@pytest.mark.parametrize("op,block", [(2, 144), (3, 272), (4, 144)])
+def test_qk0_payload_and_mapping(L, op, block):
+    """op_executor.cc:771-790 sizes the operands from m, k, n and the block
+    size of the opcode's type; mat_mul.c:1604-1613 answers -1 for the rest."""
+    assert run(L, op, b"\0" * 91)[0] == -1                        # shorter than MatMulParams
+    assert run(L, op, _mm(50, 51, 52, 0, 32, 64))[0] == -1         # zero size
+    assert run(L, op, _mm(50, 51, 52, 4, 32, 64))[0] == -2         # unmapped buffers
+    b = Buffers(L, 2100 + 10 * op)
+    m, k, n = 4, 64, 64
+    out = np.zeros(m * n + 64, np.float32)
+    act = np.zeros(m * k + 64, np.float32)
+    wt = np.zeros(k * n // 256 * block, np.uint8)
+    fo, fa, fw = b.add(out), b.add(act), b.add(wt)
+    assert run(L, op, _mm(fo, fa, fw, m, k, n + 32))[0] == -2      # weight shorter than k*n/256 blocks
+    assert run(L, op, _mm(fo, fa, fw, m, 48, 32))[0] == -1         # k % 32
+    assert run(L, op, _mm(fo, fa, fw, m, 32, 16))[0] == -1         # n % 32
+    off = (128 - out.ctypes.data % 128) % 128 + 4                   # output not 128-byte aligned
+    assert run(L, op, _mm(fo, fa, fw, m, k, n - 32, out_off=off))[0] == -1
+    b.release()
+
+
 def test_unknown_and_foreign_opcodes(L):
     assert run(L, 200, b"\0" * 16)[0] == 0                  # ignored like the reference
     assert run(L, 0, b"\0" * 24)[0] == AEE_EUNSUPPORTED       # rms_norm: not on this path

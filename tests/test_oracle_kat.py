@@ -430,3 +430,131 @@ def test_model_aux_oracle(case):
     ref = np.asarray(ref, np.float64).reshape(-1)
     assert got.shape == ref.shape
     assert np.max(np.abs(got - ref)) <= 2e-5 * max(1.0, np.max(np.abs(ref))), name
+
+
+# ----------------------------------------------------------------- opcodes 2-4
+# Instruction-level restatement of the reference's per-super-block
+# dequantisation (mat_mul.c:389-424 for Q4_0 / IQ4_NL, :488-525 for Q8_0) on
+# 128-byte HVX vectors, written from the HVX instruction definitions:
+#   vlut16(u.b, v.h, 0) "nomatch": pair.lo.h[i] = v.h[2*(u.b[2i] & 15)],
+#                                  pair.hi.h[i] = v.h[2*(u.b[2i+1] & 15)]
+#   vunpack (ub->uh, uh->uw, b->h): elements widened in order, first half in lo
+#   vlsr(ub, 4):                   each byte shifted right by four
+#   qf16 multiply + conversion:    modelled as FP16 rounding of the exact product
+# It checks the closed form of the C oracle (orc_qk0_element) element by element.
+def _vlut16(u, table):
+    return table[2 * (u[0::2] & 15)], table[2 * (u[1::2] & 15)]
+
+
+def _hvx_superblock(block: np.ndarray, wtype: int) -> np.ndarray:
+    ext = np.zeros(512, np.uint8)
+    ext[:block.size] = block                       # vmemu reads a full vector past the block
+    halves = ext[:128].view(np.uint16)             # vmemu(src[i].scales)
+    table = np.zeros(64, np.uint16)
+    table[0::2] = halves[:32]                      # lo of vunpack(uh -> uw)
+    idx0 = np.array([0, 2] * 32 + [1, 3] * 32, np.uint8)
+    s0 = _vlut16(idx0, table)
+    s1 = _vlut16(idx0 + 4, table)
+    scales = [s0[0], s0[1], s1[0], s1[1]]
+    if wtype == O.GGML_Q8_0:
+        q = ext[16:16 + 256].view(np.int8)
+        vecs = [q[0:64], q[64:128], q[128:192], q[192:256]]
+        vecs = [v.astype(np.float32) for v in vecs]
+    else:
+        levels = (np.arange(16) - 8) if wtype == O.GGML_Q4_0 else np.array(
+            [-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113])
+        lut = np.zeros(64, np.float16)
+        lut[0:32:2] = levels
+        lut = lut.view(np.uint16)
+        qs = ext[16:144]
+        lo = _vlut16(qs, lut)
+        hi = _vlut16(qs >> 4, lut)
+        vecs = [x.view(np.float16).astype(np.float32) for x in (lo[0], lo[1], hi[0], hi[1])]
+    with np.errstate(over="ignore"):              # the largest scale times -127 overflows to -inf
+        out = [(vecs[j] * scales[j].view(np.float16).astype(np.float32)).astype(np.float16) for j in range(4)]
+    return np.concatenate(out).view(np.uint16)
+
+
+@pytest.mark.parametrize("wtype", [O.GGML_Q4_0, O.GGML_Q8_0, O.GGML_IQ4_NL])
+def test_qk0_superblock_matches_hvx_sequence(wtype):
+    L = O.lib()
+    bb = O.qk0_block_bytes(wtype)
+    assert bb == (272 if wtype == O.GGML_Q8_0 else 144)
+    rng = np.random.default_rng(wtype)
+    special = np.array([0x0001, 0x03FF, 0x0400, 0x7BFF, 0x8001, 0x3C00, 0xBC00, 0x0000, 0x2E66, 0x1400],
+                       np.uint16)                  # subnormals, the largest normal, +-1, zero
+    for trial in range(60):
+        block = rng.integers(0, 256, bb, dtype=np.uint8)
+        sc = rng.normal(0, 0.01, 8).astype(np.float16).view(np.uint16)
+        if trial % 3 == 0:
+            sc = rng.choice(special, 8)
+        block[:16] = sc.view(np.uint8)
+        want = _hvx_superblock(block, wtype)
+        got = np.array([L.orc_qk0_element(block.ctypes.data, wtype, e) for e in range(256)], np.uint16)
+        np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("wtype", [O.GGML_Q4_0, O.GGML_Q8_0, O.GGML_IQ4_NL])
+def test_qk0_stream_is_the_packed_f16_weight(wtype):
+    """Super-block i dequantises to packed-FP16 elements [256i, 256i+256)
+    (mat_mul.c:1700-1709 dequantises chunk nc*k into the FP16 weight buffer
+    that core_dot_chunk_fp16 reads in the permuted tile layout)."""
+    k, n = 96, 64
+    bb = O.qk0_block_bytes(wtype)
+    rng = np.random.default_rng(3)
+    for _ in range(12):
+        src = np.zeros(k * n // 256 * bb, np.uint8)
+        blocks = src.reshape(-1, bb)
+        sb, e = int(rng.integers(0, blocks.shape[0])), int(rng.integers(0, 256))
+        blocks[sb, :16] = np.full(8, 0x3C00, np.uint16).view(np.uint8)     # all scales 1.0
+        if wtype == O.GGML_Q8_0:
+            blocks[sb, 16 + e] = 3
+        else:
+            # every other code at level 0 (Q4_0: nibble 8); IQ4_NL has no zero
+            # level, so compare against the level of nibble 0 there
+            fill = 0x88 if wtype == O.GGML_Q4_0 else 0x00
+            blocks[:, 16:] = fill
+            v, i = e // 64, e % 64
+            byte = 16 + 2 * i + (v & 1)
+            nib = 11                                                       # Q4_0: 3, IQ4_NL: 38
+            blocks[sb, byte] = (blocks[sb, byte] & 0xF0) | nib if v < 2 else (blocks[sb, byte] & 0x0F) | (nib << 4)
+        w = O.qk0_dequant(src, wtype, k, n).view(np.float16).astype(np.float32)   # [n][k]
+        f = sb * 256 + e
+        tile, o = divmod(f, 1024)
+        kk = (tile % (k // 32)) * 32 + (o // 64) * 2 + (o & 1)
+        nn = (tile // (k // 32)) * 32 + (o % 64) // 2
+        assert O.lib().orc_f16_perm_offset(k, kk, nn) == f
+        base = 0.0 if wtype != O.GGML_IQ4_NL else None
+        if base is None:
+            other = w[(np.arange(n)[:, None] != nn) | (np.arange(k)[None, :] != kk)]
+            assert np.all((other == -127.0) | (other == 0.0))
+            assert w[nn, kk] == 38.0
+        else:
+            hit = np.argwhere(w != 0)
+            assert hit.tolist() == [[nn, kk]] and w[nn, kk] == 3.0
+
+
+@pytest.mark.parametrize("wtype", [O.GGML_Q4_0, O.GGML_Q8_0, O.GGML_IQ4_NL])
+def test_qk0_quantise_round_trip(wtype):
+    k, n = 128, 96
+    w = O.normal(k * n, 0.02, seed=11).reshape(k, n)
+    q = O.qk0_quantize(w, wtype)
+    assert q.size == O.qk0_weight_bytes(wtype, k, n)
+    d = O.qk0_dequant(q, wtype, k, n).view(np.float16).astype(np.float32).T
+    # scale d = the group's extreme / (-8 | 127 | -127): Q4_0 and IQ4_NL clip the
+    # opposite extreme at 7d (113d), Q8_0 rounds to half a step
+    bound = {O.GGML_Q4_0: 1.0 / 8, O.GGML_Q8_0: 0.5 / 127, O.GGML_IQ4_NL: 14 / 127}[wtype]
+    assert np.max(np.abs(d - w)) <= bound * np.max(np.abs(w)) * 1.01
+
+
+def test_qk0_linear_uses_the_dequantised_weight():
+    k, n, m = 64, 96, 5
+    src = O.qk0_random(O.GGML_Q4_0, k, n, seed=2)
+    x = O.normal(m * k, 1.0, seed=4).reshape(m, k)
+    w = O.qk0_dequant(src, O.GGML_Q4_0, k, n).view(np.float16).astype(np.float64)   # [n][k]
+    xh = x.astype(np.float16).astype(np.float64)
+    want = xh @ w.T
+    got = O.qk0_linear(x, src, O.GGML_Q4_0, k, n)
+    assert O.max_abs_rel(got, want) <= 1e-6
+    got16 = O.qk0_linear(x, src, O.GGML_Q4_0, k, n, round_acc_f16=True)
+    assert O.max_abs_rel(got16, want) <= 1e-3

@@ -66,3 +66,14 @@ def test_headline_shapes():
     assert not c1["swap"] and c1["units"] >= 0.85 * 148
     c2 = htpg.plan_info(1, 77, 3072, 768)
     assert not c2["swap"] and c2["splits"] == 1
+
+
+def test_qk0_plan():
+    """Fused opcode 2-4 kernel: 16/32 activation rows per tile, stream-K grid of
+    at most one CTA per SM with at least four k-blocks each."""
+    p = htpg.qk0_plan_info(2, 1, 14336, 4096)
+    assert p["bn"] == 16 and p["tiles_a"] == 112 and p["kb_total"] == 64 and p["grid"] == 148
+    p = htpg.qk0_plan_info(8, 32, 128, 64)
+    assert p["bn"] == 32 and p["grid"] == 1 and p["smem"] <= 232448
+    p = htpg.qk0_plan_info(20, 17, 384, 96)
+    assert p["bn"] == 32 and p["tiles_b"] == 1 and p["kb_total"] == 2 and p["grid"] == 1
