@@ -1124,17 +1124,11 @@ extern "C" int htpg_qk0_run(const htpg_weights *w, float *out, const float *x, i
   const QGemmPlan plan = plan_qgemm(qt, m, n, k, d->sms);
   if (qgemm_counter_bytes(plan) > kQCounterBytes) return HTPG_ENOPLAN;
   const size_t part = align_up(qgemm_partial_bytes(plan), 1024);
-  const size_t act = align_up(static_cast<size_t>(m) * k * 2u, 1024);
   uint8_t *base = nullptr;
-  rc = qworkspace(d, st, kQCounterBytes + part + act, &base);
-  if (rc) return rc;
-  uint16_t *act16 = reinterpret_cast<uint16_t *>(base + kQCounterBytes + part);
-  cudaError_t e = launch_to_f16(act16, x, static_cast<long long>(m) * k, st);
-  if (e != cudaSuccess) return record_cuda(e);
-  CUtensorMap tmB;
-  rc = make_map(&tmB, act16, Kind::F16, k, m, static_cast<size_t>(k) * 2u, plan.bn);
+  rc = qworkspace(d, st, kQCounterBytes + part, &base);
   if (rc) return rc;
   QGemmArgs a;
+  a.x = x;
   a.M = m;
   a.N = n;
   a.K = k;
@@ -1143,7 +1137,7 @@ extern "C" int htpg_qk0_run(const htpg_weights *w, float *out, const float *x, i
   a.partials = reinterpret_cast<float *>(base + kQCounterBytes);
   a.counters = reinterpret_cast<uint32_t *>(base);
   a.watchdog = d->watchdog;
-  return record_cuda(launch_qgemm(qt, plan, records, tmB, a, st));
+  return record_cuda(launch_qgemm(qt, plan, records, a, st));
 }
 
 extern "C" int htpg_qk0_plan_info(int weight_type, int m, int n, int k, int sms, int64_t out[6]) {

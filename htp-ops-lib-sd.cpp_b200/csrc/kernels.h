@@ -149,16 +149,15 @@ inline size_t qgemm_counter_bytes(const QGemmPlan &p) {
 }
 struct QGemmArgs {
   int M = 0, N = 0, K = 0;
+  const float *x = nullptr;      // FP32 activations [M][K], 16-byte aligned
   float *out = nullptr;
   long long ldo = 0;
   float *partials = nullptr;     // qgemm_partial_bytes
   uint32_t *counters = nullptr;  // zero before the launch, left zero
   uint32_t *watchdog = nullptr;
 };
-// w: the stage records (launch_qk0_repack); tmB: FP16 activations [M][K],
-// box 64 x bn, 128-byte swizzle.
-cudaError_t launch_qgemm(int qt, const QGemmPlan &p, const uint8_t *w, const CUtensorMap &tmB,
-                         const QGemmArgs &a, cudaStream_t st);
+// w: the stage records (launch_qk0_repack).
+cudaError_t launch_qgemm(int qt, const QGemmPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st);
 
 // Kernel launches issued since load (all launchers above count themselves).
 uint64_t launches();

@@ -250,8 +250,11 @@ cudaError_t launch_qk0_repack(uint8_t *dst, const uint8_t *src, int qt, int k, i
 // The MMA issuer commits once per kCommit iterations: a tcgen05.commit costs
 // about as much as a dozen N=16 MMAs on this part, so the FP16 operand ring is
 // released kCommit slots at a time (one commit barrier per half of the ring).
-// The activation tile of an iteration lives with its operand slot and is
-// loaded by the converting group; the super-block ring is released by the
+// The activation tile of an iteration (BN rows x 64 k) lives with its operand
+// slot: the converting group's 128 threads read it from the FP32 activations
+// (one 8-element chunk each, 16 rows; two for 32) and round it to FP16, so no
+// copy-engine request sits behind the super-block prefetch and no separate
+// conversion kernel runs.  The super-block ring is released by the
 // dequantisers alone.
 constexpr int kQGroups = 4;
 constexpr int kQDeqWarps = 4 * kQGroups;
@@ -276,7 +279,7 @@ __host__ __device__ constexpr size_t qgemm_smem(int qt, int bn) {
   return 1024 + static_cast<size_t>(kAStages) * (16384 + bn * 128) +
          static_cast<size_t>(q_stages(qt, bn)) * q_stage_bytes(qt) + kQBarBytes;
 }
-static_assert((2 * kQMaxStages + 3 * kAStages + 7) * 8 + 16 <= kQBarBytes, "barrier block");
+static_assert((2 * kQMaxStages + kAStages + 7) * 8 + 16 <= kQBarBytes, "barrier block");
 static_assert(kQGroups <= q_stages(kGgmlQ8_0, 32), "super-block slots advance by kQGroups");
 static_assert(qgemm_smem(kGgmlQ8_0, 32) <= kQSmemLimit && qgemm_smem(kGgmlQ4_0, 32) <= kQSmemLimit,
               "shared memory budget");
@@ -311,7 +314,7 @@ __device__ __forceinline__ void qgemm_store(const QGemmArgs &g, const float (&v)
 
 template <int QT, int BN>
 __global__ void __launch_bounds__(kQThreads, 1)
-    qgemm_swap_kernel(const __grid_constant__ CUtensorMap tmB, const QGemmParams P) {
+    qgemm_swap_kernel(const QGemmParams P) {
   constexpr int QS = q_stages(QT, BN);
   constexpr uint32_t QSB = q_stage_bytes(QT);
   constexpr uint32_t BB = BN * 128;
@@ -319,16 +322,17 @@ __global__ void __launch_bounds__(kQThreads, 1)
   constexpr uint32_t TCOLS = 2 * BN <= 32 ? 32 : 64;
   constexpr uint32_t kIdesc = idesc_f16(128, BN);
   static_assert(BN == 16 || BN == 32, "activation rows per tile");
+  static_assert(BN * 8 % 128 == 0, "activation chunks per group thread");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sA = base;                    // kAStages x 128 rows x 128 B (FP16 weight, swizzled)
-  uint8_t *sB = sA + kAStages * 16384;   // kAStages x BN rows x 128 B (FP16 activations, swizzled by TMA)
+  uint8_t *sB = sA + kAStages * 16384;   // kAStages x BN rows x 128 B (FP16 activations, swizzled)
   uint8_t *sQ = sB + kAStages * BB;      // QS x one stage record
   uint64_t *bars = reinterpret_cast<uint64_t *>(sQ + QS * QSB);
   uint64_t *qfull = bars, *qempty = qfull + QS;
-  uint64_t *afull = qempty + QS, *bfull = afull + kAStages;
-  uint64_t *mdone = bfull + kAStages;    // [2]: the MMAs of a commit group have completed
+  uint64_t *afull = qempty + QS;
+  uint64_t *mdone = afull + kAStages;    // [2]: the MMAs of a commit group have completed
   uint64_t *tfull = mdone + 2, *tempty = tfull + 2, *mma_done = tempty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
   volatile uint32_t *flag = tmem_slot + 1;
@@ -344,10 +348,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
       mbar_init(smem_u32(&qfull[s]), 1);
       mbar_init(smem_u32(&qempty[s]), 4);  // the converting group's four warps
     }
-    for (int s = 0; s < kAStages; ++s) {
-      mbar_init(smem_u32(&afull[s]), 4);
-      mbar_init(smem_u32(&bfull[s]), 1);
-    }
+    for (int s = 0; s < kAStages; ++s) mbar_init(smem_u32(&afull[s]), 4);
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&mdone[b]), 1);
       mbar_init(smem_u32(&tfull[b]), 1);
@@ -439,7 +440,6 @@ __global__ void __launch_bounds__(kQThreads, 1)
           const int sa = static_cast<int>((t - i0) % kAStages);
           const uint32_t aph = static_cast<uint32_t>(((t - i0) / kAStages) & 1);
           ok = mbar_wait(smem_u32(&afull[sa]), aph, wd, kWatchMma, abort);
-          ok = ok && mbar_wait(smem_u32(&bfull[sa]), aph, wd, kWatchMma, abort);
         }
         if (!ok) break;
         tc_fence_after();
@@ -540,10 +540,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
     // ------------------------------------------------ dequantisers
     const int dw = warp - 2 - kQEpiWarps;
     const int grp = dw >> 2, nt = warp & 3;  // group; column tile = this warp's lane quadrant
-    const bool issuer = nt == 0 && lane == 0;  // loads the group's activation tiles
-    if (issuer) tma_prefetch_desc(&tmB);
+    const int gt = nt * 32 + lane;  // thread of the group: activation chunks gt, gt + 128, ...
     grid_dependency_wait();  // the activations come from the kernel before this one
-    const uint32_t sQs = smem_u32(sQ), sAs = smem_u32(sA);
+    const uint32_t sQs = smem_u32(sQ), sAs = smem_u32(sA), sBs = smem_u32(sB);
     const int row = nt * 32 + lane;
     const uint32_t row_off = static_cast<uint32_t>(row) * 128u;
     // ring slots and phases of iteration j = grp, grp + kQGroups, ...
@@ -554,21 +553,27 @@ __global__ void __launch_bounds__(kQThreads, 1)
       const long long ig = i0 + grp;
       if (ig < i1) tb = static_cast<int>((ig / KB) % P.tiles_b), kb = static_cast<int>(ig % KB);
     }
-    int last_b[kAStages];
-#pragma unroll
-    for (int s = 0; s < kAStages; ++s) last_b[s] = -1;
     for (long long i = i0 + grp; i < i1; i += kQGroups) {
       const long long j = i - i0;
       const int sa = static_cast<int>(j % kAStages);
       // the operand slot is free once the MMAs of iteration j - kAStages completed
       const uint32_t md_par = static_cast<uint32_t>(((j / kAStages) & 1) ^ 1);
-      bool ok = mbar_wait(smem_u32(&mdone[(j / kCommit) & 1]), md_par, wd, kWatchDequant, abort);
-      if (issuer && ok) {
-        const uint32_t fb = smem_u32(&bfull[sa]);
-        mbar_arrive_expect_tx(fb, BB);
-        tma_load_2d(smem_u32(sB + sa * BB), &tmB, fb, kb * 64, tb * BN);
-        last_b[sa] = static_cast<int>((j / kAStages) & 1);
+      // activation chunks of this iteration: FP32 loads issued before the waits
+      constexpr int kChunks = BN * 8 / 128;
+      float4 xa[kChunks][2];
+#pragma unroll
+      for (int u = 0; u < kChunks; ++u) {
+        const int q = gt + 128 * u, r = q >> 3, c = q & 7;
+        const int m = tb * BN + r, k0 = kb * 64 + c * 8;
+        if (m < g.M && k0 < g.K) {
+          const float4 *src = reinterpret_cast<const float4 *>(g.x + static_cast<long long>(m) * g.K + k0);
+          xa[u][0] = __ldg(src);
+          xa[u][1] = __ldg(src + 1);
+        } else {
+          xa[u][0] = xa[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
+      bool ok = mbar_wait(smem_u32(&mdone[(j / kCommit) & 1]), md_par, wd, kWatchDequant, abort);
       ok = ok && mbar_wait(smem_u32(&qfull[sq]), qph, wd, kWatchDequant, abort);
       if (!__all_sync(0xffffffffu, ok)) break;
       const uint32_t qs = sQs + sq * QSB + nt * 8 * BLK;  // this column tile's 2 k-tiles x 4 super-blocks
@@ -578,6 +583,22 @@ __global__ void __launch_bounds__(kQThreads, 1)
       for (int c = 0; c < 8; ++c) cw[c] = chunk_words_shared<QT>(qs + c * BLK, lane);
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&qempty[sq]));  // the record has been read
+      // the activation tile (FP16, round to nearest even, like the reference's
+      // conversion mat_mul.c:114-148), 128-byte swizzled
+#pragma unroll
+      for (int u = 0; u < kChunks; ++u) {
+        const int q = gt + 128 * u, r = q >> 3, c = q & 7;
+        const float f[8] = {xa[u][0].x, xa[u][0].y, xa[u][0].z, xa[u][0].w,
+                            xa[u][1].x, xa[u][1].y, xa[u][1].z, xa[u][1].w};
+        uint32_t h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          h[e] = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(f[2 * e]))) |
+                 static_cast<uint32_t>(__half_as_ushort(__float2half_rn(f[2 * e + 1]))) << 16;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sBs + sa * BB + r * 128 + ((c ^ (r & 7)) << 4)),
+                     "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
+                     : "memory");
+      }
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 val = dq_decode<QT>(cw[c], lane);
@@ -595,10 +616,6 @@ __global__ void __launch_bounds__(kQThreads, 1)
         if (++tb == P.tiles_b) tb = 0;
       }
     }
-    // no activation copy may still be landing when the CTA exits
-    if (issuer)
-      for (int s = 0; s < kAStages; ++s)
-        if (last_b[s] >= 0) mbar_wait(smem_u32(&bfull[s]), static_cast<uint32_t>(last_b[s]), wd, kWatchDequant, abort);
   }
 
   tc_fence_before();
@@ -625,8 +642,7 @@ QGemmPlan plan_qgemm(int qt, int M, int N, int K, int num_sms) {
 }
 
 template <int QT, int BN>
-static cudaError_t launch_qgemm_t(const QGemmPlan &p, const uint8_t *w, const CUtensorMap &tmB,
-                                  const QGemmArgs &a, cudaStream_t st) {
+static cudaError_t launch_qgemm_t(const QGemmPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st) {
   auto fn = qgemm_swap_kernel<QT, BN>;
   static bool configured[64] = {};
   int dev = 0;
@@ -654,19 +670,19 @@ static cudaError_t launch_qgemm_t(const QGemmPlan &p, const uint8_t *w, const CU
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, tmB, P);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, P);
   return counted(e != cudaSuccess ? e : cudaGetLastError());
 }
 
-cudaError_t launch_qgemm(int qt, const QGemmPlan &p, const uint8_t *w, const CUtensorMap &tmB,
+cudaError_t launch_qgemm(int qt, const QGemmPlan &p, const uint8_t *w,
                          const QGemmArgs &a, cudaStream_t st) {
   if (p.grid < 1 || p.iters < p.grid) return cudaErrorInvalidConfiguration;
-  if (qt == kGgmlQ4_0) return p.bn == 16 ? launch_qgemm_t<kGgmlQ4_0, 16>(p, w, tmB, a, st)
-                                         : launch_qgemm_t<kGgmlQ4_0, 32>(p, w, tmB, a, st);
-  if (qt == kGgmlQ8_0) return p.bn == 16 ? launch_qgemm_t<kGgmlQ8_0, 16>(p, w, tmB, a, st)
-                                         : launch_qgemm_t<kGgmlQ8_0, 32>(p, w, tmB, a, st);
-  if (qt == kGgmlIQ4_NL) return p.bn == 16 ? launch_qgemm_t<kGgmlIQ4_NL, 16>(p, w, tmB, a, st)
-                                           : launch_qgemm_t<kGgmlIQ4_NL, 32>(p, w, tmB, a, st);
+  if (qt == kGgmlQ4_0) return p.bn == 16 ? launch_qgemm_t<kGgmlQ4_0, 16>(p, w, a, st)
+                                         : launch_qgemm_t<kGgmlQ4_0, 32>(p, w, a, st);
+  if (qt == kGgmlQ8_0) return p.bn == 16 ? launch_qgemm_t<kGgmlQ8_0, 16>(p, w, a, st)
+                                         : launch_qgemm_t<kGgmlQ8_0, 32>(p, w, a, st);
+  if (qt == kGgmlIQ4_NL) return p.bn == 16 ? launch_qgemm_t<kGgmlIQ4_NL, 16>(p, w, a, st)
+                                           : launch_qgemm_t<kGgmlIQ4_NL, 32>(p, w, a, st);
   return cudaErrorInvalidValue;
 }
 
