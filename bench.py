@@ -632,6 +632,30 @@ def main():
     if dist:
         dist.barrier()
     L.htpg_phase_timing(0)
+    shard_ms = None
+    if world > 1:
+        # the GEMM phase alone: each rank computes its column shard (what a
+        # row-parallel next layer consumes), no exchange; same timing rules
+        def shard_step():
+            htpg.check(L.htpg_w8a8_run(w.handle, htpg.ptr(out_loc), 0, htpg.ptr(x), htpg.ptr(bias_loc), m, n_loc,
+                                       1, sp), "htpg_w8a8_run")
+        for _ in range(3):
+            flush()
+            shard_step()
+        dist.barrier()
+        torch.cuda.synchronize()
+        s_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(args.steps)]
+        torch.cuda._sleep(SLEEP_CYCLES)
+        for a, b in s_ev:
+            flush()
+            a.record(stream)
+            shard_step()
+            b.record(stream)
+        torch.cuda.synchronize()
+        ts = torch.tensor([sum(a.elapsed_time(b) for a, b in s_ev)], dtype=torch.float64, device=dev)
+        dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+        shard_ms = float(ts.item()) / args.steps
     act_ms, gemm_ms, runs = htpg.phase_timing_read()
     total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
@@ -690,6 +714,11 @@ def main():
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
     }
+    if shard_ms is not None:
+        line["shard_only"] = {"value": ops / (shard_ms * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": shard_ms,
+                              "note": "the same steps without the output exchange: every rank computes its "
+                                      "[M][N/world] column shard (the input of a row-parallel next layer); "
+                                      "max over ranks; not the headline value"}
 
     if rank == 0 and world == 1 and not args.no_e2e:
         dt, h2d, d2h = e2e_channel(torch, L, htpg, m, k, n, x, blob_host, bias, max(3, args.steps // 4), 2)
