@@ -539,17 +539,23 @@ constexpr int kMaxStages = 12;      // the 256-byte barrier block holds 2 x 12 +
 __host__ __device__ constexpr int epi_smem_for(bool swap) {
   return swap ? kEpiWarps * kWarpParams * 4 : kEpiSmem;
 }
+// k-blocks per pipeline stage.  Swapped (small-M) tiles move 16 KB of weights
+// per k-block behind only four N = 16/32 MMAs; a stage's MMA group and its
+// release commit cost about 0.4 us however small, so a stage of one k-block
+// caps the weight stream near 3.4 TB/s and two k-blocks per stage raise that
+// to about 4.9 TB/s (stream + MMA + commit loop measured in isolation).
+__host__ __device__ constexpr int kbs_for(bool swap) { return swap ? 2 : 1; }
 // As many pipeline stages as fit beside the epilogue's shared memory.
 __host__ __device__ constexpr int stages_for(int bn, bool swap = false) {
-  return (kSmemLimit - 1024 - 256 - epi_smem_for(swap)) / ((128 + bn) * kRowBytes) < kMaxStages
-             ? (kSmemLimit - 1024 - 256 - epi_smem_for(swap)) / ((128 + bn) * kRowBytes)
+  return (kSmemLimit - 1024 - 256 - epi_smem_for(swap)) / (kbs_for(swap) * (128 + bn) * kRowBytes) < kMaxStages
+             ? (kSmemLimit - 1024 - 256 - epi_smem_for(swap)) / (kbs_for(swap) * (128 + bn) * kRowBytes)
              : kMaxStages;
 }
 __host__ __device__ constexpr int tmem_cols_for(int bn) {
   return 2 * bn <= 32 ? 32 : 2 * bn <= 64 ? 64 : 2 * bn <= 128 ? 128 : 2 * bn <= 256 ? 256 : 512;
 }
 __host__ __device__ constexpr size_t smem_bytes_for(int bn, bool swap = false) {
-  return 1024 /* alignment slack */ + static_cast<size_t>(stages_for(bn, swap)) * (128 + bn) * kRowBytes +
+  return 1024 /* alignment slack */ + static_cast<size_t>(stages_for(bn, swap)) * kbs_for(swap) * (128 + bn) * kRowBytes +
          static_cast<size_t>(epi_smem_for(swap)) + 256 /* barriers, tmem slot, flags */;
 }
 static_assert((2 * kMaxStages + 5) * 8 + 12 <= 256, "barrier block");
@@ -559,8 +565,8 @@ static_assert(smem_bytes_for(256) <= kSmemLimit && smem_bytes_for(128) <= kSmemL
               "shared memory budget");
 
 struct SmemLayout {
-  uint8_t *a;          // STAGES x 128 rows x 128 B
-  uint8_t *b;          // STAGES x BN rows x 128 B
+  uint8_t *a;          // STAGES x KBS x 128 rows x 128 B
+  uint8_t *b;          // STAGES x KBS x BN rows x 128 B
   float *scratch;      // per epilogue warp: the 32 x 32 staging tile (1024-byte aligned)
   float *params;       // per epilogue warp: 96 floats of column parameters
   uint64_t *full, *empty, *tfull, *tempty, *mma_done;
@@ -574,9 +580,9 @@ __device__ __forceinline__ SmemLayout carve(uint8_t *raw) {
   SmemLayout L;
   uint8_t *p = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   L.a = p;
-  p += STAGES * 128 * kRowBytes;
+  p += STAGES * kbs_for(SWAP) * 128 * kRowBytes;
   L.b = p;
-  p += STAGES * BN * kRowBytes;
+  p += STAGES * kbs_for(SWAP) * BN * kRowBytes;
   L.scratch = reinterpret_cast<float *>(p);  // swapped tiles stage nothing
   if (!SWAP) p += kEpiWarps * kWarpScratch * 4;
   L.params = reinterpret_cast<float *>(p);
@@ -915,7 +921,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const __grid_constant__ OutMaps tmOut, const KernelParams P) {
   constexpr int STAGES = stages_for(BN, SWAP);
   constexpr int TCOLS = tmem_cols_for(BN);
-  constexpr uint32_t kStageBytes = (128 + BN) * kRowBytes;
+  constexpr int KBS = kbs_for(SWAP);                       // k-blocks per stage
+  constexpr uint32_t kKbBytes = (128 + BN) * kRowBytes;    // both operands of one k-block
   constexpr int kElemsPerRow = KIND == Kind::I8 ? 128 : 64;
   constexpr uint32_t kIdesc = KIND == Kind::I8 ? idesc_i8(128, BN) : idesc_f16(128, BN);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
@@ -961,22 +968,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The weights do not depend on the activation pass that may still be
       // running: put this CTA's first weight tiles into the ring (and warm the
       // L2 with the next ones) before waiting for it.
-      int pre = 0;  // leading stages of the first unit whose weight tile is in flight
+      // A stage holds KBS k-blocks (sub-tile j of stage s at s*KBS + j); the
+      // last stage of a unit may hold fewer.
+      int pre = 0;  // leading stages of the first unit whose weight tiles are in flight
       if (blockIdx.x < P.units) {
         const Unit w = decode_unit(blockIdx.x, P.tiles_b, P.splits);
         const int kb0 = w.ks * P.kb_per_split;
         const int kb1 = min(kb0 + P.kb_per_split, P.kb_total);
-        pre = g.late_weights ? 0 : min(STAGES, kb1 - kb0);
+        pre = g.late_weights ? 0 : min(STAGES, (kb1 - kb0 + KBS - 1) / KBS);
         for (int i = 0; i < pre; ++i) {
           const uint32_t fb = smem_u32(&L.full[i]);
-          mbar_arrive_expect_tx(fb, kStageBytes);
-          if (SWAP)
-            tma_load_2d(smem_u32(L.a + i * 128 * kRowBytes), &tmA, fb, 0, (kb0 + i) * g.N + w.ta * 128);
-          else
-            tma_load_2d(smem_u32(L.b + i * BN * kRowBytes), &tmB, fb, 0, (kb0 + i) * g.N + w.tb * BN);
+          const int kbi = kb0 + i * KBS, nk = min(KBS, kb1 - kbi);
+          mbar_arrive_expect_tx(fb, nk * kKbBytes);
+          for (int j = 0; j < nk; ++j) {
+            if (SWAP)
+              tma_load_2d(smem_u32(L.a + (i * KBS + j) * 128 * kRowBytes), &tmA, fb, 0, (kbi + j) * g.N + w.ta * 128);
+            else
+              tma_load_2d(smem_u32(L.b + (i * KBS + j) * BN * kRowBytes), &tmB, fb, 0, (kbi + j) * g.N + w.tb * BN);
+          }
         }
         const int kb2 = min(kb1, kb0 + kPrefetchBytes / ((SWAP ? 128 : BN) * kRowBytes));
-        for (int kb = kb0 + pre; kb < kb2; ++kb) {
+        for (int kb = kb0 + pre * KBS; kb < kb2; ++kb) {
           if (SWAP)
             tma_prefetch_l2_2d(&tmA, 0, kb * g.N + w.ta * 128);
           else
@@ -995,22 +1007,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Unit w = decode_unit(u, P.tiles_b, P.splits);
         const int kb0 = w.ks * P.kb_per_split;
         const int kb1 = min(kb0 + P.kb_per_split, P.kb_total);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kbs = kb0; kbs < kb1; kbs += KBS) {
           if (!mbar_wait(smem_u32(&L.empty[s]), ph ^ 1u, wd, kWatchProducer, L.abort)) {
             ok = false;
             break;
           }
           const uint32_t fb = smem_u32(&L.full[s]);
+          const int nk = min(KBS, kb1 - kbs);
           // the weight operand (A when swapped, else B) is k-block-major:
           // its box starts at row kb * N + first column
-          const bool weight_done = first && kb - kb0 < pre;
-          if (!weight_done) mbar_arrive_expect_tx(fb, kStageBytes);
-          if (SWAP) {
-            if (!weight_done) tma_load_2d(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, 0, kb * g.N + w.ta * 128);
-            tma_load_2d(smem_u32(L.b + s * BN * kRowBytes), &tmB, fb, kb * kElemsPerRow, w.tb * BN);
-          } else {
-            tma_load_2d(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, kb * kElemsPerRow, w.ta * 128);
-            if (!weight_done) tma_load_2d(smem_u32(L.b + s * BN * kRowBytes), &tmB, fb, 0, kb * g.N + w.tb * BN);
+          const bool weight_done = first && (kbs - kb0) / KBS < pre;
+          if (!weight_done) mbar_arrive_expect_tx(fb, nk * kKbBytes);
+          for (int j = 0; j < nk; ++j) {
+            const int kb = kbs + j, sub = s * KBS + j;
+            if (SWAP) {
+              if (!weight_done)
+                tma_load_2d(smem_u32(L.a + sub * 128 * kRowBytes), &tmA, fb, 0, kb * g.N + w.ta * 128);
+              tma_load_2d(smem_u32(L.b + sub * BN * kRowBytes), &tmB, fb, kb * kElemsPerRow, w.tb * BN);
+            } else {
+              tma_load_2d(smem_u32(L.a + sub * 128 * kRowBytes), &tmA, fb, kb * kElemsPerRow, w.ta * 128);
+              if (!weight_done)
+                tma_load_2d(smem_u32(L.b + sub * BN * kRowBytes), &tmB, fb, 0, kb * g.N + w.tb * BN);
+            }
           }
           last_phase[s] = static_cast<int>(ph);
           if (++s == STAGES) {
@@ -1042,23 +1060,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(smem_u32(&L.tempty[buf]), acc_ph ^ 1u, wd, kWatchMma, L.abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kbs = kb0; kbs < kb1; kbs += KBS) {
           if (!mbar_wait(smem_u32(&L.full[s]), ph, wd, kWatchMma, L.abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(L.a + s * 128 * kRowBytes);
-          const uint32_t b_addr = smem_u32(L.b + s * BN * kRowBytes);
+          const int nk = min(KBS, kb1 - kbs);
+          for (int j = 0; j < nk; ++j) {
+            const uint32_t a_addr = smem_u32(L.a + (s * KBS + j) * 128 * kRowBytes);
+            const uint32_t b_addr = smem_u32(L.b + (s * KBS + j) * BN * kRowBytes);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t da = umma_desc_sw128(a_addr + kk * 32);
-            const uint64_t db = umma_desc_sw128(b_addr + kk * 32);
-            const uint32_t accumulate = (kb > kb0 || kk > 0) ? 1u : 0u;
-            if (KIND == Kind::I8)
-              umma_i8(d_tmem, da, db, kIdesc, accumulate);
-            else
-              umma_f16(d_tmem, da, db, kIdesc, accumulate);
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t da = umma_desc_sw128(a_addr + kk * 32);
+              const uint64_t db = umma_desc_sw128(b_addr + kk * 32);
+              const uint32_t accumulate = (kbs > kb0 || j > 0 || kk > 0) ? 1u : 0u;
+              if (KIND == Kind::I8)
+                umma_i8(d_tmem, da, db, kIdesc, accumulate);
+              else
+                umma_f16(d_tmem, da, db, kIdesc, accumulate);
+            }
           }
           tc_commit(smem_u32(&L.empty[s]));
           if (++s == STAGES) {
