@@ -15,6 +15,7 @@
 // buffers are used in place.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <cstdio>
@@ -306,6 +307,75 @@ int sync_status(int rc) {
   return htpg_check_device(nullptr, nullptr);
 }
 
+// Host-memory activation and output: rows go through in chunks on three
+// streams (copy in, GEMM, copy out, ordered per chunk by events) so that the
+// copies of different chunks overlap each other and the GEMMs; PCIe carries
+// both directions at once.  Returns the first error.
+struct ChunkStreams {
+  bool ready = false;
+  cudaStream_t in = nullptr, cmp = nullptr, out = nullptr;
+  std::vector<cudaEvent_t> ev;  // 2 per chunk
+};
+ChunkStreams g_chunk;
+
+int w8a8_chunked(htpg_weights *w, Operand &out, Operand &act, Operand &bias, int m, int k, int n, int channels,
+                 int mode) {
+  if (!g_chunk.ready) {
+    if (cudaStreamCreateWithFlags(&g_chunk.in, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&g_chunk.cmp, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&g_chunk.out, cudaStreamNonBlocking) != cudaSuccess) {
+      cudaGetLastError();
+      return HTPG_ELAUNCH;
+    }
+    g_chunk.ready = true;
+  }
+  const int chunks_target = 12;
+  int rows = (m + chunks_target - 1) / chunks_target;
+  rows = (rows + 127) / 128 * 128;
+  const int chunks = (m + rows - 1) / rows;
+  while (static_cast<int>(g_chunk.ev.size()) < 2 * chunks) {
+    cudaEvent_t e;
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      return HTPG_ELAUNCH;
+    }
+    g_chunk.ev.push_back(e);
+  }
+  const uint8_t *xh = static_cast<const uint8_t *>(act.host);
+  uint8_t *xd = static_cast<uint8_t *>(act.device);
+  uint8_t *oh = static_cast<uint8_t *>(out.host);
+  uint8_t *od = static_cast<uint8_t *>(out.device);
+  int rc = 0;
+  for (int c = 0; c < chunks && !rc; ++c) {
+    const int r0 = c * rows, nr = std::min(rows, m - r0);
+    const size_t xoff = static_cast<size_t>(r0) * k * 4, xbytes = static_cast<size_t>(nr) * k * 4;
+    const size_t ooff = static_cast<size_t>(r0) * n * 4, obytes = static_cast<size_t>(nr) * n * 4;
+    cudaEvent_t e_in = g_chunk.ev[2 * c], e_cmp = g_chunk.ev[2 * c + 1];
+    if (cudaMemcpyAsync(xd + xoff, xh + xoff, xbytes, cudaMemcpyHostToDevice, g_chunk.in) != cudaSuccess ||
+        cudaEventRecord(e_in, g_chunk.in) != cudaSuccess || cudaStreamWaitEvent(g_chunk.cmp, e_in, 0) != cudaSuccess) {
+      cudaGetLastError();
+      rc = HTPG_ELAUNCH;
+      break;
+    }
+    rc = htpg_w8a8_run(w, reinterpret_cast<float *>(od + ooff), n, reinterpret_cast<const float *>(xd + xoff),
+                       bias.present ? static_cast<const float *>(bias.device) : nullptr, nr, channels, mode,
+                       g_chunk.cmp);
+    if (rc) break;
+    if (cudaEventRecord(e_cmp, g_chunk.cmp) != cudaSuccess || cudaStreamWaitEvent(g_chunk.out, e_cmp, 0) != cudaSuccess ||
+        cudaMemcpyAsync(oh + ooff, od + ooff, obytes, cudaMemcpyDeviceToHost, g_chunk.out) != cudaSuccess) {
+      cudaGetLastError();
+      rc = HTPG_ELAUNCH;
+    }
+  }
+  const cudaError_t e1 = cudaStreamSynchronize(g_chunk.in), e2 = cudaStreamSynchronize(g_chunk.cmp),
+                    e3 = cudaStreamSynchronize(g_chunk.out);
+  if (!rc && (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess)) {
+    cudaGetLastError();
+    rc = HTPG_ELAUNCH;
+  }
+  return rc ? rc : htpg_check_device(nullptr, nullptr);
+}
+
 // ---- opcode 15: native W8A8 linear (op_executor.cc:314-353) -----------------
 int exec_w8a8(uint8_t *payload, size_t payload_size) {
   const bool profiled = payload_size == sizeof(NativeW8A8ProfileParams);
@@ -397,6 +467,14 @@ int exec_w8a8(uint8_t *payload, size_t payload_size) {
   int rc = exec_weights(cst, true, k, n, &w);
   if (rc) return rc;
   const double setup_ms = std::chrono::duration<double, std::milli>(Clock::now() - t_setup).count();
+  if (!profiled && mode != 3 && m >= 1024 && act.buf.kind == HTPG_BUF_HOST && out.buf.kind == HTPG_BUF_HOST) {
+    // the activation gets a device region here and is copied chunk by chunk
+    if ((rc = stage_in({&bias}, {&act, &out}))) return rc;
+    const auto t0 = Clock::now();
+    rc = w8a8_chunked(w, out, act, bias, m, k, n, channels, mode);
+    p->elapsed_us = elapsed_us(t0);
+    return rc;
+  }
   if ((rc = stage_in({&act, &bias}, {&out}))) return rc;
   const auto t0 = Clock::now();
   if (profiled) htpg_set_profiling(1);

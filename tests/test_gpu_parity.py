@@ -177,3 +177,43 @@ def test_f16_epilogue_modes(gpu, lib, m, k, n, mode, with_bias):
 
 def test_watchdog_clear(gpu, lib):
     assert htpg.check_device() == 0
+
+
+@pytest.mark.parametrize("m,mode,with_bias", [(1500, 0, False), (1500, 1, True), (300, 0, False)])
+def test_w8a8_executor_host_buffers(gpu, lib, m, mode, with_bias):
+    """Opcode 15 through the executor with host (pinned) buffers: from 1024 rows
+    the rows go through in chunks whose copies in, GEMMs and copies out overlap
+    on three streams (the last chunk ragged); below, one staged run."""
+    import ctypes
+    import struct
+    k, n = 256, 192
+    c = O.make_w8a8(7, "exec", m, k, n, 0.01, with_bias, mode)
+    ref = O.w8a8_linear(c.x, c.blob, k, n, bias=c.bias if with_bias else None, mode=mode)
+    fds, ptrs = {}, {}
+
+    def alloc(name, arr):
+        fd, p = ctypes.c_int(), ctypes.c_void_p()
+        htpg.check(lib.htpg_buffer_alloc(arr.nbytes, htpg.BUF_HOST, ctypes.byref(fd), ctypes.byref(p)), name)
+        ctypes.memmove(p.value, arr.ctypes.data, arr.nbytes)
+        fds[name], ptrs[name] = fd.value, p.value
+
+    try:
+        alloc("out", np.full(m * n, np.nan, np.float32))
+        alloc("x", np.ascontiguousarray(c.x))
+        alloc("cst", c.blob)
+        payload = struct.pack("<iiiiiiiiii", fds["out"], 0, fds["x"], 0, fds["cst"], 0, m, k, n, 0)
+        if with_bias:
+            alloc("bias", np.ascontiguousarray(c.bias))
+            payload += struct.pack("<iiii", fds["bias"], 0, n, mode)
+        req = np.frombuffer(struct.pack("<I", 15) + payload, np.uint8).copy()
+        assert lib.execute_op_simple(req.ctypes.data, req.nbytes) == 0
+        got = np.empty(m * n, np.float32)
+        ctypes.memmove(got.ctypes.data, ptrs["out"], got.nbytes)
+        got = got.reshape(m, n)
+        if mode == 0:
+            np.testing.assert_array_equal(got, ref)
+        else:
+            assert O.max_abs_rel(got, ref) <= W8A8_TOL
+    finally:
+        for fd in fds.values():
+            lib.htpg_buffer_release(fd)
