@@ -304,9 +304,15 @@ extern "C" int htpg_phase_timing_read(double *act_ms, double *gemm_ms, int *runs
 extern "C" int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]) {
   if (!out || m < 1 || n < 1 || k < 1 || sms < 1 || (kind != 0 && kind != 1)) return HTPG_EARGS;
   const GemmPlan p = plan_gemm(kind == 0 ? Kind::I8 : Kind::F16, m, n, k, sms);
-  const int64_t v[10] = {p.swap ? 1 : 0, p.bn, p.splits, p.tiles_a, p.tiles_b, p.kb_total,
+  const int64_t v[10] = {p.reg ? 2 : p.swap ? 1 : 0, p.bn, p.splits, p.tiles_a, p.tiles_b, p.kb_total,
                          p.kb_per_split, p.units, p.grid, static_cast<int64_t>(p.smem)};
   for (int i = 0; i < 10; ++i) out[i] = v[i];
+  return HTPG_OK;
+}
+
+extern "C" int htpg_set_decode_kernel(int which) {
+  if (which != 0 && which != 1) return HTPG_EARGS;
+  g_decode_kernel.store(which);
   return HTPG_OK;
 }
 
@@ -559,6 +565,8 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
   a.ws = wsk;
   a.ws_count = cnt;
   a.watchdog = d->watchdog;
+  a.wk = w->wk;
+  a.act = act;
   a.late_weights = late_weights ? 1 : 0;
   // row-major outputs of the normal orientation leave the SM through TMA stores
   OutMaps out_maps;
@@ -888,7 +896,7 @@ int htpg::w8a8_run_in_scratch(const htpg_weights *w, float *out, int ldo, const 
   // The array keeps whatever the previous call (or an aborted launch) left:
   // the split-K partial sums and tile counters must start at zero.
   cudaError_t e = cudaSuccess;
-  if (plan.splits > 1) e = cudaMemsetAsync(base, 0, splitk_bytes, st);
+  if (plan.splits > 1 || plan.reg) e = cudaMemsetAsync(base, 0, splitk_bytes, st);
   if (e != cudaSuccess) return record_cuda(e);
   e = launch_quantize_rows(act, scales, x, w->inverse, m, k, st);
   if (e != cudaSuccess) return record_cuda(e);
@@ -915,6 +923,8 @@ int htpg::w8a8_run_in_scratch(const htpg_weights *w, float *out, int ldo, const 
   a.ws = wsk;
   a.ws_count = cnt;
   a.watchdog = d->watchdog;
+  a.wk = w->wk;
+  a.act = act;
   OutMaps out_maps;
   if (!plan.swap && mode != 3 && tma_store_ok(out, ldo)) {
     rc = make_out_map(&out_maps.map[0], out, m, n, ldo);
@@ -1211,9 +1221,10 @@ extern "C" int hmx_mat_mul_native_w8a8_profiled(float *dst, const float *activat
       const uint32_t cols64 = static_cast<uint32_t>(p.swap ? 2 : (p.bn >= 64 ? p.bn / 64 : 1));
       profile->reserved = rows64 | (cols64 << 16) | (p.swap ? 0x80000000u : 0u);
       profile->mac_ticks = static_cast<uint64_t>(p.units);  // weight tiles streamed
-      profile->readout_ticks = static_cast<uint64_t>(p.units) *
-                               static_cast<uint64_t>(p.swap ? 128 : p.bn) *
-                               static_cast<uint64_t>(p.kb_per_split) * 128u;  // weight bytes streamed
+      profile->readout_ticks = p.reg ? static_cast<uint64_t>(p.tiles_a) * 16u * p.kb_total * 128u
+                                     : static_cast<uint64_t>(p.units) *
+                                           static_cast<uint64_t>(p.swap ? 128 : p.bn) *
+                                           static_cast<uint64_t>(p.kb_per_split) * 128u;  // weight bytes streamed
     }
   }
   return rc;

@@ -1,0 +1,364 @@
+// Register-fed decode GEMM for the W8A8 linear at M <= 16 (opcode 15 decode
+// shapes, linear_w8a8.c:130-227): out[m][n] = epilogue(sum_k a[m][k] w[n][k]).
+//
+// At M <= 16 the weight stream is the whole cost: every weight byte meets at
+// most 16 activation rows.  Here each warp streams its weight bytes from HBM
+// straight into registers (16-byte loads, no shared-memory staging, no
+// tensor-memory round trip, no per-stage MMA commit) and feeds them to warp
+// MMAs (m16n8k32, INT8 x INT8 -> INT32, exact).
+//
+// Operand layout.  The prepared weight is k-block-major: the 128 K-bytes of
+// k-block kb of column n are row kb*N + n.  A warp's unit of work (an "atom")
+// is one k-block of one 16-column group: rows n0..n0+15 of k-block kb, 2 KB
+// contiguous in HBM.  Lane (g, t) (g = lane/4, t = lane%4) loads 16-byte
+// chunks t and t+4 of rows n0+g and n0+g+8.  The MMA fragments then hold, for
+// the lanes of index t, the K bytes 16t + 4s .. +3 (chunk t, word s) and
+// 64 + 16t + 4s .. +3 (chunk t+4, word s) at step s: a fixed permutation of K
+// inside the k-block.  The activation fragment of token m is loaded with the
+// same chunk pattern from row m of the codes, so both operands see the same
+// permutation and the INT32 sum is the plain dot product (integer addition
+// is order-free: bit-exact against any summation order).
+//
+// Work split.  The atoms, ordered (column group, k-block), are cut into
+// `chunks` contiguous ranges (one per CTA pass) and each range into 16
+// contiguous warp ranges.  A warp accumulates while its atoms stay in one
+// column group and adds the sums into the CTA's shared-memory tile of that
+// group.  A column group covered by one chunk is finished by the CTA
+// directly; a group that straddles chunks is published as INT32 partial
+// tiles and finished by the last chunk to arrive (counter per group).  The
+// partial tiles and the counters are left zeroed.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "epilogue.cuh"
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace htpg {
+
+namespace {
+
+// Sixteen warps per SM with four atoms in flight each.  Measured on the C5
+// decode shapes: two atoms in flight per warp stream as fast as four; eight
+// warps per SM are 35-40% slower; the load cache flavour (.nc / .cs /
+// L1::no_allocate) and L2 prefetches further ahead change nothing or cost.
+constexpr int kDecWarps = 16;
+constexpr int kDecThreads = 32 * kDecWarps;
+constexpr int kDecDepth = 4;   // weight atoms in flight per warp
+constexpr int kDecMaxCg = 32;  // column groups of one chunk held in shared memory
+
+struct DecParams {
+  GemmArgs a;
+  long long atoms;  // column groups x k-blocks
+  int KB, CG, chunks;
+};
+
+__device__ __forceinline__ long long dec_start(const DecParams &P, int c) { return P.atoms * c / P.chunks; }
+// the chunk whose range holds `atom` (every chunk holds at least one atom)
+__device__ __forceinline__ int dec_owner(const DecParams &P, long long atom) {
+  return static_cast<int>(((atom + 1) * P.chunks - 1) / P.atoms);
+}
+
+// Weight bytes are read once: no L1 allocation; an L2 miss fetches the whole
+// 256-byte pair of rows (both halves are this warp's next loads).
+__device__ __forceinline__ uint4 ld_weight16(const int8_t *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+__device__ __forceinline__ uint32_t word(const uint4 &v, int s) {
+  return s == 0 ? v.x : s == 1 ? v.y : s == 2 ? v.z : v.w;
+}
+
+__device__ __forceinline__ void mma_s8(int32_t (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                       uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Rows n0+g and n0+g+8 of one k-block, chunks t and t+4.
+struct WFrag {
+  uint4 lo0, lo1, hi0, hi1;  // row g: chunk t, chunk t+4; row g+8: chunk t, chunk t+4
+};
+
+// N is a multiple of 16 (the plan requires it): every row of a group exists.
+// The activation rows of the same k-block are pulled into L1 now, so the
+// fragment loads at MMA time (kDecDepth atoms later) hit.
+__device__ __forceinline__ void load_atom(WFrag &f, const int8_t *wk, const int8_t *act_row, int N, int cg, int kb,
+                                          int g, int t) {
+  const int8_t *p = wk + (static_cast<size_t>(kb) * N + cg * 16 + g) * 128u + 16 * t;
+  f.lo0 = ld_weight16(p);
+  f.lo1 = ld_weight16(p + 64);
+  f.hi0 = ld_weight16(p + 8 * 128);
+  f.hi1 = ld_weight16(p + 8 * 128 + 64);
+  if (act_row != nullptr) prefetch_l1(act_row + kb * 128);
+}
+
+
+template <int NT>
+__device__ __forceinline__ void mma_atom(int32_t (&acc)[NT][4], const WFrag &f, const int8_t *act, int M, int K,
+                                         int kb, int g, int t) {
+  uint4 x[2 * NT];
+  const int k0 = kb * 128 + 16 * t;
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const int m = 8 * j + g;
+    const uint4 *q = reinterpret_cast<const uint4 *>(act + static_cast<size_t>(m) * K + k0);
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    x[2 * j] = (m < M && k0 < K) ? __ldg(q) : z;
+    x[2 * j + 1] = (m < M && k0 + 64 < K) ? __ldg(q + 4) : z;
+  }
+#pragma unroll
+  for (int s = 0; s < 4; ++s)
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+      mma_s8(acc[j], word(f.lo0, s), word(f.hi0, s), word(f.lo1, s), word(f.hi1, s), word(x[2 * j], s),
+             word(x[2 * j + 1], s));
+}
+
+// Accumulator fragment -> the group's shared tile [token][16 columns].
+template <int NT>
+__device__ __forceinline__ void flush(int32_t *tile, int32_t (&acc)[NT][4], int g, int t) {
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const int m = 8 * j + 2 * t;
+    atomicAdd(tile + m * 16 + g, acc[j][0]);
+    atomicAdd(tile + (m + 1) * 16 + g, acc[j][1]);
+    atomicAdd(tile + m * 16 + g + 8, acc[j][2]);
+    atomicAdd(tile + (m + 1) * 16 + g + 8, acc[j][3]);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[j][r] = 0;
+  }
+}
+
+// One finished column group: lane holds column lane%16 and tokens lane/16 + 2i.
+template <int BN, int MODE, bool BIAS>
+__device__ __forceinline__ void finish_group(const GemmArgs &g, int cg, int lane, const int32_t (&v)[BN / 2]) {
+  const int n = cg * 16 + (lane & 15);
+  if (n >= g.N) return;
+  const float sw = __ldg(g.col_scale + n);
+  const int32_t cr = __ldg((MODE == 5 ? g.col_sum7 : g.col_corr) + n);
+  const float bn = BIAS ? __ldg(g.bias + n) : 0.0f;
+#pragma unroll
+  for (int i = 0; i < BN / 2; ++i) {
+    const int m = (lane >> 4) + 2 * i;
+    if (m >= g.M) break;
+    const float val = finish<Kind::I8, MODE, BIAS>(static_cast<uint32_t>(v[i]), cr, sw, __ldg(g.row_scale + m), bn);
+    if (MODE == 5) {
+      const uint32_t u = __float_as_uint(val);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) *plane_dst(g.out, g.ldo, g.M, m, n, p) = static_cast<uint8_t>(u >> (8 * p));
+    } else if (MODE == 3) {
+      if (n < g.channels) g.out[static_cast<long long>(n) * g.ldo + m] = val;
+    } else {
+      g.out[static_cast<long long>(m) * g.ldo + n] = val;
+    }
+  }
+}
+
+template <int BN>
+__device__ __forceinline__ void finish_dispatch(const GemmArgs &g, int cg, int lane, const int32_t (&v)[BN / 2]) {
+  switch (g.mode * 2 + (g.bias != nullptr ? 1 : 0)) {
+    case 0: finish_group<BN, 0, false>(g, cg, lane, v); break;
+    case 1: finish_group<BN, 0, true>(g, cg, lane, v); break;
+    case 2: finish_group<BN, 1, false>(g, cg, lane, v); break;
+    case 3: finish_group<BN, 1, true>(g, cg, lane, v); break;
+    case 4: finish_group<BN, 2, false>(g, cg, lane, v); break;
+    case 5: finish_group<BN, 2, true>(g, cg, lane, v); break;
+    case 6: finish_group<BN, 3, false>(g, cg, lane, v); break;
+    case 7: finish_group<BN, 3, true>(g, cg, lane, v); break;
+    case 10: finish_group<BN, 5, false>(g, cg, lane, v); break;
+    default: finish_group<BN, 4, false>(g, cg, lane, v); break;
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kDecThreads, 1) decode_i8_kernel(const DecParams P) {
+  constexpr int BN = 8 * NT;     // activation rows held (tokens)
+  constexpr int TILE = 16 * BN;  // INT32 per column group
+  extern __shared__ int32_t dtile[];  // [kDecMaxCg][BN][16]
+  const GemmArgs &g = P.a;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int8_t *wk = static_cast<const int8_t *>(g.wk);
+  const int8_t *act = static_cast<const int8_t *>(g.act);
+  const int KB = P.KB;
+  // lane (g, t < NT) keeps activation row 8t + g warm in L1 (one line per k-block)
+  const int8_t *act_pf = (tq < NT && 8 * tq + gq < g.M) ? act + static_cast<size_t>(8 * tq + gq) * g.K : nullptr;
+  // the next operator's kernels may be scheduled now (they wait for this one
+  // before they read anything it writes)
+  grid_dependents_launch();
+  bool waited = false;
+  if (g.late_weights) {
+    grid_dependency_wait();
+    waited = true;
+  }
+
+  for (int c = blockIdx.x; c < P.chunks; c += gridDim.x) {
+    const long long a0 = dec_start(P, c), a1 = dec_start(P, c + 1);
+    const int cg0 = static_cast<int>(a0 / KB);
+    const int ncg = static_cast<int>((a1 - 1) / KB) - cg0 + 1;
+    for (int i = threadIdx.x; i < ncg * TILE; i += kDecThreads) dtile[i] = 0;
+    const long long b0 = a0 + (a1 - a0) * warp / kDecWarps;
+    const long long b1 = a0 + (a1 - a0) * (warp + 1) / kDecWarps;
+
+    // weight atoms b0 .. b0+depth-1 in flight (the weights do not depend on
+    // the previous kernel: these loads overlap its tail)
+    WFrag f[kDecDepth];
+    int lcg = static_cast<int>(b0 / KB), lkb = static_cast<int>(b0 - static_cast<long long>(lcg) * KB);
+#pragma unroll
+    for (int i = 0; i < kDecDepth; ++i) {
+      if (b0 + i < b1) {
+        load_atom(f[i], wk, waited ? act_pf : nullptr, g.N, lcg, lkb, gq, tq);
+        if (++lkb == KB) {
+          lkb = 0;
+          ++lcg;
+        }
+      }
+    }
+    if (!waited) {
+      grid_dependency_wait();  // activation codes and row scales come from the previous kernel
+      waited = true;
+    }
+    __syncthreads();  // tile zeroed
+
+    int ccg = static_cast<int>(b0 / KB), ckb = static_cast<int>(b0 - static_cast<long long>(ccg) * KB);
+    int32_t acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[j][r] = 0;
+    for (long long base = b0; base < b1; base += kDecDepth) {
+#pragma unroll
+      for (int i = 0; i < kDecDepth; ++i) {
+        const long long a = base + i;
+        if (a < b1) {
+          mma_atom<NT>(acc, f[i], act, g.M, g.K, ckb, gq, tq);
+          if (a + kDecDepth < b1) {
+            load_atom(f[i], wk, act_pf, g.N, lcg, lkb, gq, tq);
+            if (++lkb == KB) {
+              lkb = 0;
+              ++lcg;
+            }
+          }
+          const bool group_end = ++ckb == KB;
+          if (group_end || a + 1 == b1) flush<NT>(dtile + (ccg - cg0) * TILE, acc, gq, tq);
+          if (group_end) {
+            ckb = 0;
+            ++ccg;
+          }
+        }
+      }
+    }
+    __syncthreads();
+
+    // finish this chunk's column groups, one warp per group
+    for (int j = warp; j < ncg; j += kDecWarps) {
+      const int cg = cg0 + j;
+      const long long ga0 = static_cast<long long>(cg) * KB, ga1 = ga0 + KB;
+      int32_t v[BN / 2];
+#pragma unroll
+      for (int i = 0; i < BN / 2; ++i) v[i] = dtile[j * TILE + ((lane >> 4) + 2 * i) * 16 + (lane & 15)];
+      bool fin = true;
+      if (ga0 < a0 || ga1 > a1) {
+        // the group straddles chunks: publish this chunk's partial tile; the
+        // chunk whose arrival completes the group finishes it
+        int32_t *slot = g.ws + (static_cast<size_t>(c) * 2 + (cg == cg0 ? 0 : 1)) * TILE;
+#pragma unroll
+        for (int i = 0; i < BN / 2; ++i) slot[((lane >> 4) + 2 * i) * 16 + (lane & 15)] = v[i];
+        __threadfence();
+        __syncwarp();
+        const int first = dec_owner(P, ga0), last = dec_owner(P, ga1 - 1);
+        uint32_t prev = 0u;
+        if (lane == 0) prev = atomicAdd(g.ws_count + cg, 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        fin = prev == static_cast<uint32_t>(last - first);
+        if (fin) {
+          __threadfence();
+#pragma unroll
+          for (int i = 0; i < BN / 2; ++i) v[i] = 0;
+          for (int o = first; o <= last; ++o) {
+            const int side = dec_start(P, o) / KB == cg ? 0 : 1;
+            int32_t *sl = g.ws + (static_cast<size_t>(o) * 2 + side) * TILE;
+#pragma unroll
+            for (int i = 0; i < BN / 2; ++i) {
+              const int idx = ((lane >> 4) + 2 * i) * 16 + (lane & 15);
+              v[i] += __ldcg(sl + idx);
+              sl[idx] = 0;
+            }
+          }
+          if (lane == 0) g.ws_count[cg] = 0u;
+        }
+      }
+      if (fin) finish_dispatch<BN>(g, cg, lane, v);
+    }
+    __syncthreads();  // the tile is reused by the next chunk
+  }
+}
+
+template <int NT>
+cudaError_t launch_nt(const GemmPlan &p, const GemmArgs &a, cudaStream_t st) {
+  auto fn = decode_i8_kernel<NT>;
+  DecParams P;
+  P.a = a;
+  P.KB = p.kb_total;
+  P.CG = p.tiles_a;
+  P.chunks = p.chunks;
+  P.atoms = static_cast<long long>(p.kb_total) * p.tiles_a;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+  cfg.blockDim = dim3(kDecThreads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, P);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+}  // namespace
+
+void plan_decode_i8(GemmPlan &p, int M, int N, int K, int num_sms) {
+  p.kind = Kind::I8;
+  p.reg = true;
+  p.swap = true;
+  p.pair = false;
+  p.bn = M <= 8 ? 8 : 16;
+  p.kb_total = (K + 127) / 128;
+  p.kb_per_split = p.kb_total;
+  p.splits = 1;
+  p.tiles_a = (N + 15) / 16;  // column groups
+  p.tiles_b = 1;
+  const long long atoms = static_cast<long long>(p.kb_total) * p.tiles_a;
+  long long chunks = std::min<long long>(atoms, num_sms);
+  // a chunk may span at most kDecMaxCg column groups (its shared tiles)
+  const long long cap = static_cast<long long>(kDecMaxCg - 2) * p.kb_total;
+  if ((atoms + chunks - 1) / chunks > cap) chunks = (atoms + cap - 1) / cap;
+  p.chunks = static_cast<int>(chunks);
+  p.units = p.chunks;
+  p.grid = static_cast<int>(std::min<long long>(chunks, num_sms));
+  p.smem = static_cast<size_t>(kDecMaxCg) * 16 * p.bn * 4;
+}
+
+size_t decode_ws_bytes(const GemmPlan &p) { return static_cast<size_t>(p.chunks) * 2 * 16 * p.bn * 4; }
+
+cudaError_t launch_decode_i8(const GemmPlan &p, const GemmArgs &a, cudaStream_t st) {
+  if (!p.reg || !a.wk || !a.act || a.M > 16) return cudaErrorInvalidConfiguration;
+  if (p.bn == 8) return counted(launch_nt<1>(p, a, st));
+  return counted(launch_nt<2>(p, a, st));
+}
+
+}  // namespace htpg

@@ -17,6 +17,7 @@
 
 #include "kernels.h"
 #include "ptx.cuh"
+#include "epilogue.cuh"
 
 namespace htpg {
 
@@ -467,55 +468,6 @@ cudaError_t launch_im2col_f16(uint16_t *a, const float *x, const ConvGeom &g, in
 }
 
 // ====================================================================== GEMM
-// Optional epilogue activation (mat_mul.c:788-826): GELU(tanh) as
-// x*sigmoid(z), z = 1.5957691216057308*(x + 0.044715 x^3), QuickGELU as
-// x*sigmoid(1.702 x).  x*sigmoid(z) is evaluated as 0.5x*(1 + tanh(z/2)) with
-// the hardware tanh (one MUFU operation instead of a 2^x and a reciprocal; the
-// epilogue, not the tensor pipe, bounds short-K layers).  The tanh's relative
-// error of about 2^-11 becomes an absolute error below 2.5e-4*|x| in the
-// output, largest where 1 + tanh cancels (z near -6); against the tensor's
-// absolute maximum that stays far inside the 2e-3 / 1e-2 output tolerances.
-// Saturation is exact: tanh = -1 gives 0, tanh = 1 gives x.  MODE is a
-// template parameter so the per-element code is branch-free and the 32
-// elements of a chunk interleave.
-template <int MODE>
-__device__ __forceinline__ float epilogue_act(float x) {
-  if constexpr (MODE != 1 && MODE != 2) {
-    return x;
-  } else {
-    // x * sigmoid(z) = 0.5x * (1 + tanh(z / 2)): one MUFU operation per element
-    float h;
-    if constexpr (MODE == 1) {
-      constexpr float c1 = 0.5f * 1.5957691216057308f, c3 = 0.5f * 1.5957691216057308f * 0.044715f;
-      h = x * fmaf(x * x, c3, c1);
-    } else {
-      h = x * (0.5f * 1.702f);
-    }
-    const float t = tanh_approx(h);
-    const float hx = 0.5f * x;
-    return fmaf(hx, t, hx);
-  }
-}
-
-// One accumulator element -> output value.
-//  I8:  v = fl(fl(float(acc + corr) * sw) * rs) (linear_w8a8.c:168-179), bias, act
-//  F16: v = acc (FP32 accumulate), bias, act (mat_mul.c:864-882)
-//  MODE 4 (diagnostic): the raw accumulator bits.
-template <Kind KIND, int MODE, bool BIAS>
-__device__ __forceinline__ float finish(uint32_t acc, int32_t corr, float sw, float rs, float bias) {
-  float v;
-  if constexpr (KIND == Kind::I8) {
-    const int32_t y = static_cast<int32_t>(acc + static_cast<uint32_t>(corr));
-    if constexpr (MODE == 4 || MODE == 5) return __int_as_float(y);  // 5: corr holds (sum w) << 7
-    v = __fmul_rn(__fmul_rn(__int2float_rn(y), sw), rs);
-  } else {
-    v = __uint_as_float(acc);
-    if constexpr (MODE == 4 || MODE == 5) return v;
-  }
-  if constexpr (BIAS) v = __fadd_rn(v, bias);
-  return epilogue_act<MODE>(v);
-}
-
 // Sixteen epilogue warps: four per TMEM lane quadrant, so each SM sub-partition
 // interleaves four independent chunk pipelines (the epilogue is latency-bound).
 constexpr int kEpiWarps = 16;
@@ -633,19 +585,6 @@ struct EpiCtx {
   int q, part, lane, epi_t;        // part: which of the quadrant's four warps
 };
 
-// Plane export (the opcode-15 CPU-epilogue form, linear_w8a8.c:205-227): the
-// unsigned-code INT32 accumulator of (m, n) is split into its four bytes.  In
-// the 64-row tile of m (rows = the tile's valid rows) and the 32-column half of
-// n, byte p sits at position p*rows*32 + (m%64)*32 + n%32 of the half's byte
-// stream, and that stream fills the half's 128 output bytes of the tile's rows
-// in order.  Returns where byte p of (m, n) goes.
-__device__ __forceinline__ uint8_t *plane_dst(float *out, long long ldo, int M, int m, int n, int p) {
-  const int t = m >> 6;
-  const int rows = min(64, M - (t << 6));
-  const int o = p * rows * 32 + (m & 63) * 32 + (n & 31);
-  return reinterpret_cast<uint8_t *>(out + (static_cast<long long>(t) * 64 + o / 128) * ldo + (n & ~31)) +
-         (o & 127);
-}
 
 // Normal orientation: TMEM lane = activation row m, column = weight column n.
 // The four warps of a lane quadrant take every fourth 32-column chunk.  The row
@@ -1362,7 +1301,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 // --------------------------------------------------------------- planning
+// 0: INT8 shapes with M <= 16 run the register-fed decode kernel (decode.cu);
+// 1: they run the swapped tcgen05 kernel like 16 < M <= 32.
+std::atomic<int> g_decode_kernel{0};
+
 // Tile plan keyed on M:
+//  * I8, M <= 16 and (M <= 8 or a K-split swapped plan): the register-fed
+//    decode kernel (decode.cu): weights stream from HBM into registers and
+//    warp MMAs, in (column group, k-block) ranges balanced over the SMs.
 //  * I8 and M <= 32: swapped orientation (weights fill the 128-row MMA
 //    dimension, the activation rows are the MMA N = 16 or 32); the K range is
 //    split over CTAs until the grid covers the SMs, with an exact INT32
@@ -1409,6 +1355,13 @@ GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms) {
     splits = splits > max_splits ? max_splits : splits;
     p.kb_per_split = (p.kb_total + splits - 1) / splits;
     p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
+    // The register-fed kernel streams faster where the swapped plan splits K
+    // (its INT32 partials meet in HBM) and at M <= 8 (one MMA per k-step);
+    // with 16 rows and whole-K tiles the tcgen05 kernel is faster.
+    if (M <= 16 && N % 16 == 0 && g_decode_kernel.load() == 0 && (M <= 8 || p.splits > 1)) {
+      plan_decode_i8(p, M, N, K, num_sms);
+      return p;
+    }
   } else {
     p.swap = false;
     p.tiles_a = (M + 127) / 128;
@@ -1432,9 +1385,11 @@ GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms) {
 }
 
 size_t splitk_ws_bytes(const GemmPlan &p) {
+  if (p.reg) return decode_ws_bytes(p);
   return p.splits > 1 ? static_cast<size_t>(p.tiles_a) * p.tiles_b * 128 * p.bn * 4 : 0;
 }
 size_t splitk_count_bytes(const GemmPlan &p) {
+  if (p.reg) return static_cast<size_t>(p.tiles_a) * 4;
   return p.splits > 1 ? static_cast<size_t>(p.tiles_a) * p.tiles_b * 4 : 0;
 }
 
@@ -1512,6 +1467,7 @@ static cudaError_t launch_pair(const GemmPlan &p, const CUtensorMap &tmA, const 
 
 cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
                         const OutMaps &tmOut, const GemmArgs &a, cudaStream_t st) {
+  if (p.reg) return launch_decode_i8(p, a, st);
   if (p.pair) {
     if (p.grid % 2) return cudaErrorInvalidConfiguration;
     if (p.kind == Kind::I8) {

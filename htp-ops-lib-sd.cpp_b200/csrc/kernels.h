@@ -2,6 +2,7 @@
 // libhtp_ops_b200.so; the public surface is include/htp_ops_b200.h.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -18,6 +19,8 @@ struct GemmPlan {
   Kind kind = Kind::I8;
   bool swap = false;
   bool pair = false;     // CTA-pair tiles of 256 rows (tcgen05.mma.cta_group::2)
+  bool reg = false;      // register-fed decode kernel (decode.cu); swap is also set
+  int chunks = 0;        // reg: contiguous (column group, k-block) ranges, one per CTA pass
   int bn = 256;          // MMA N (rows of B per tile)
   int splits = 1;        // K splits (I8 swapped only; exact INT32 reduction)
   int tiles_a = 0, tiles_b = 0;
@@ -41,6 +44,8 @@ struct GemmArgs {
   uint32_t *ws_count = nullptr;      // split-K arrival counters (self-resetting)
   uint32_t *watchdog = nullptr;
   int tma_store = 0;                 // row-major output written by TMA through tmOut
+  const void *wk = nullptr;          // the weight rows [KB][N][128 B] (register-fed decode)
+  const void *act = nullptr;         // the activation codes [M][K] (register-fed decode)
   int late_weights = 0;              // the weight is written by the kernels just before this
                                      // launch: no weight tile is loaded before the
                                      // programmatic-dependency wait (L2 prefetches only)
@@ -57,6 +62,11 @@ inline bool tma_store_ok(const float *out, long long ldo) {
 GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms);
 // Bytes of split-K workspace (ws) and counters the plan needs.
 size_t splitk_ws_bytes(const GemmPlan &p);
+// Register-fed decode plan and launch (decode.cu).
+void plan_decode_i8(GemmPlan &p, int M, int N, int K, int num_sms);
+size_t decode_ws_bytes(const GemmPlan &p);
+cudaError_t launch_decode_i8(const GemmPlan &p, const GemmArgs &a, cudaStream_t st);
+extern std::atomic<int> g_decode_kernel;  // 0: register-fed decode for I8 M <= 16; 1: swapped tcgen05
 size_t splitk_count_bytes(const GemmPlan &p);
 // Box rows of the A and B tensor maps for this plan.
 // (swapped plans use the weight as A and the activation as B)

@@ -89,6 +89,7 @@ def lib() -> ctypes.CDLL:
         "htpg_weight_cache_drop": (None, [P]),
         "htpg_weight_cache_clear": (None, []),
         "htpg_set_profiling": (I, [I]),
+        "htpg_set_decode_kernel": (I, [I]),
         "htpg_last_phase_ms": (I, [ctypes.POINTER(ctypes.c_float)] * 3),
         "htpg_launch_count": (U64, []),
         "htpg_plan_info": (I, [I, I, I, I, I, ctypes.POINTER(I64)]),
@@ -236,6 +237,12 @@ def plan_info(kind: int, m: int, n: int, k: int, sms: int = 148) -> dict:
     out = (ctypes.c_int64 * 10)()
     check(lib().htpg_plan_info(kind, m, n, k, sms, out), "htpg_plan_info")
     return dict(zip(PLAN_FIELDS, list(out)))
+
+
+def set_decode_kernel(which: int) -> None:
+    """0: W8A8 problems with m <= 16 run the register-fed decode kernel (the
+    default); 1: they run the swapped tcgen05 kernel.  Results are identical."""
+    check(lib().htpg_set_decode_kernel(which), "htpg_set_decode_kernel")
 
 
 def qk0_plan_info(weight_type: int, m: int, n: int, k: int, sms: int = 148) -> dict:

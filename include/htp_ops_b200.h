@@ -271,8 +271,15 @@ uint64_t htpg_launch_count(void);
 
 /* Tile plan the library uses for an m x n x k problem (kind 0 = W8A8,
  * 1 = FP16) on a device with `sms` SMs.  out[0..9] = swap, bn, splits,
- * tiles_a, tiles_b, kb_total, kb_per_split, units, grid, smem bytes. */
+ * tiles_a, tiles_b, kb_total, kb_per_split, units, grid, smem bytes.
+ * swap = 2: the register-fed decode kernel (W8A8, m <= 16); then bn = 8 or
+ * 16 activation rows, tiles_a = 16-column groups, units = work chunks. */
 int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]);
+
+/* Which kernel runs W8A8 problems with m <= 16: 0 (default) the register-fed
+ * decode kernel, 1 the swapped tcgen05 kernel that also serves 16 < m <= 32.
+ * Both give identical results; the switch exists for measurement. */
+int htpg_set_decode_kernel(int which);
 
 /* ---- reference kernel-level names (reference: include/dsp/ops.h:20-31) ---
  * Same arguments and return codes as the DSP kernels, on device pointers;

@@ -217,3 +217,44 @@ def test_w8a8_executor_host_buffers(gpu, lib, m, mode, with_bias):
     finally:
         for fd in fds.values():
             lib.htpg_buffer_release(fd)
+
+
+# Register-fed decode kernel (M <= 16): ragged K (k-blocks with 32/64/96 valid
+# bytes), odd M (1..16 with 8 or 16 rows held), column groups that straddle
+# work chunks (small and large K relative to N), and N from 64 to 16384.
+DECODE_SHAPES = [(1, 32, 64), (2, 96, 64), (8, 160, 128), (9, 14336, 4096), (13, 14336, 4096),
+                 (16, 16384, 1536), (5, 1024, 16384), (3, 224, 4608), (11, 6144, 192), (4, 4096, 14336)]
+
+
+@pytest.mark.parametrize("m,k,n", DECODE_SHAPES)
+def test_decode_int32_and_output_bitexact(gpu, lib, m, k, n):
+    plan = htpg.plan_info(0, m, n, k)
+    assert plan["swap"] == 2                       # the register-fed decode kernel
+    # (shapes with M > 8 here all take a K-split swapped plan otherwise)
+    c = _w8a8_case(m, k, n, seed=3 * m + k, inverse=(m % 2 == 0))
+    _, codes, scales, acc = O.w8a8_linear(c.x, c.blob, k, n, want_intermediates=True)
+    np.testing.assert_array_equal(_run_w8a8(lib, gpu, c, 0, raw=True), acc)
+    ref = O.w8a8_linear(c.x, c.blob, k, n)
+    got = _run_w8a8(lib, gpu, c, 0)
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 14336), (16, 14336, 4096), (7, 1152, 4608)])
+@pytest.mark.parametrize("mode,with_bias", [(0, False), (1, True), (2, False), (3, True)])
+def test_decode_kernels_give_identical_bits(gpu, lib, m, k, n, mode, with_bias):
+    """The register-fed decode kernel and the swapped tcgen05 kernel share the
+    epilogue and sum INT32 exactly: their outputs agree bit for bit."""
+    c = _w8a8_case(m, k, n, seed=m + mode, outliers=0.005)
+    bias = O.normal(n, 0.01, 0, 1, 5 + n) if with_bias else None
+    channels = n - 64 + 5 if mode == 3 else n
+    outs = []
+    try:
+        for which in (0, 1):
+            htpg.set_decode_kernel(which)
+            outs.append(_run_w8a8(lib, gpu, c, mode, bias=bias, channels=channels))
+    finally:
+        htpg.set_decode_kernel(0)
+    assert not np.isnan(outs[0]).any()
+    np.testing.assert_array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    ref = O.w8a8_linear(c.x, c.blob, k, n, bias=bias, channels=channels, mode=mode)
+    assert O.max_abs_rel(outs[0], ref) <= W8A8_TOL

@@ -31,6 +31,17 @@ def test_plans_are_legal(kind, sms):
         kb_total = -(-k // elems)
         assert p["kb_total"] == kb_total
         assert p["smem"] <= SMEM_LIMIT
+        if p["swap"] == 2:
+            # register-fed decode: 16-column groups x k-blocks cut into `units`
+            # contiguous chunks, each spanning at most 32 groups
+            assert kind == 0 and m <= 16 and p["bn"] == (8 if m <= 8 else 16)
+            assert p["tiles_a"] * 16 >= n and p["tiles_b"] == 1 and p["splits"] == 1
+            atoms = p["tiles_a"] * kb_total
+            assert p["grid"] == min(p["units"], sms) and 1 <= p["units"] <= atoms
+            assert -(-atoms // p["units"]) <= 30 * kb_total
+            assert p["units"] * 2 * 16 * p["bn"] * 4 + p["tiles_a"] * 4 <= 2 * 1024 * 1024 + 4096
+            checked += 1
+            continue
         assert p["units"] == p["tiles_a"] * p["tiles_b"] * p["splits"]
         assert 1 <= p["grid"] <= sms and p["grid"] <= (2 * p["units"] if p["bn"] else p["units"])
         # K ranges: every split non-empty, together exactly [0, kb_total)
@@ -54,14 +65,25 @@ def test_plans_are_legal(kind, sms):
 
 def test_headline_shapes():
     # C4 and the C3 linears take CTA-pair 256-row tiles; C5 decode shapes the
-    # swapped, K-split plan; C1/C2 single-CTA tiles that still fill the SMs.
+    # register-fed decode kernel over all SMs (or, switched, the swapped K-split
+    # tcgen05 plan); C1/C2 single-CTA tiles that still fill the SMs.
     c4 = htpg.plan_info(0, 16384, 6144, 1536)
     assert c4["bn"] == 256 and c4["tiles_a"] == 64 and c4["grid"] == 148
     for m in (1, 4, 16):
         up = htpg.plan_info(0, m, 14336, 4096)
         down = htpg.plan_info(0, m, 4096, 14336)
-        assert up["swap"] and down["swap"] and down["splits"] > 1
-        assert down["units"] <= 148 and up["units"] <= 148
+        # register-fed where the swapped plan would split K, and at M <= 8
+        assert up["swap"] == (2 if m <= 8 else 1) and down["swap"] == 2 and down["grid"] == 148
+    try:
+        htpg.set_decode_kernel(1)
+        for m in (1, 4, 16):
+            up = htpg.plan_info(0, m, 14336, 4096)
+            down = htpg.plan_info(0, m, 4096, 14336)
+            assert up["swap"] == 1 and down["swap"] == 1 and down["splits"] > 1
+            assert down["units"] <= 148 and up["units"] <= 148
+    finally:
+        htpg.set_decode_kernel(0)
+    assert htpg.plan_info(0, 17, 4096, 14336)["swap"] == 1
     c1 = htpg.plan_info(0, 256, 4608, 1152)
     assert not c1["swap"] and c1["units"] >= 0.85 * 148
     c2 = htpg.plan_info(1, 77, 3072, 768)
@@ -77,3 +99,44 @@ def test_qk0_plan():
     assert p["bn"] == 32 and p["grid"] == 1 and p["smem"] <= 232448
     p = htpg.qk0_plan_info(20, 17, 384, 96)
     assert p["bn"] == 32 and p["tiles_b"] == 1 and p["kb_total"] == 2 and p["grid"] == 1
+
+
+def _decode_slots(atoms, chunks, kb):
+    """Restatement of decode.cu's chunk arithmetic: which (chunk, side) partial
+    tiles each column group's finisher reads, and which ones chunks write."""
+    start = [atoms * c // chunks for c in range(chunks + 1)]
+    owner = lambda a: ((a + 1) * chunks - 1) // atoms
+    written, read = {}, {}
+    for c in range(chunks):
+        a0, a1 = start[c], start[c + 1]
+        assert a1 > a0
+        cg0, cg1 = a0 // kb, (a1 - 1) // kb
+        assert cg1 - cg0 + 1 <= 32
+        for cg in range(cg0, cg1 + 1):
+            if cg * kb < a0 or (cg + 1) * kb > a1:
+                key = (c, 0 if cg == cg0 else 1)
+                assert key not in written
+                written[key] = cg
+    for cg in range(-(-atoms // kb)):
+        first, last = owner(cg * kb), owner((cg + 1) * kb - 1)
+        assert start[first] <= cg * kb < start[first + 1]
+        if first == last:
+            continue
+        for o in range(first, last + 1):
+            key = (o, 0 if start[o] // kb == cg else 1)
+            assert key not in read
+            read[key] = cg
+    return written, read
+
+
+@pytest.mark.parametrize("m,n,k,sms", [(1, 14336, 4096, 148), (16, 4096, 14336, 148), (3, 64, 32, 148),
+                                       (9, 64, 16384, 148), (16, 1536, 6144, 132), (1, 128, 16384, 16),
+                                       (2, 192, 1152, 148), (7, 65536, 32, 148), (1, 6144, 160, 148)])
+def test_decode_partial_tiles_are_consistent(m, n, k, sms):
+    """Every partial tile a chunk publishes is read by exactly the finisher of
+    its column group, and the arrival count equals the number of writers."""
+    p = htpg.plan_info(0, m, n, k, sms)
+    assert p["swap"] == 2
+    kb = p["kb_total"]
+    written, read = _decode_slots(p["tiles_a"] * kb, p["units"], kb)
+    assert written == read
