@@ -692,7 +692,10 @@ def main():
             roof["traffic"] = tr
     except Exception:
         pass
-    roof["kernel"] = "gemm_kernel<I8,256,false> (tcgen05 kind::i8 + fused dequant/bias/GELU)"
+    plan = htpg.plan_info(0, m, n_loc, k)
+    pair = plan["swap"] == 0 and plan["tiles_a"] == (m + 255) // 256   # 256-row CTA-pair tiles
+    roof["kernel"] = (f"gemm2_kernel<I8,{plan['bn']}> (CTA-pair tcgen05 kind::i8 + fused dequant/bias/GELU)" if pair
+                      else f"gemm_kernel<I8,{plan['bn']},false> (tcgen05 kind::i8 + fused dequant/bias/GELU)")
     roof["peak_source"] = f"hbm {peak_kind} burst copy; tensor = 2 x {peak_kind} dense BF16 burst"
     roof["hbm_frac"] = gemm_bytes / (gemm_avg_ms * 1e-3) / 1e9 / hbm
     roof["tensor_frac"] = gemm_ops / (gemm_avg_ms * 1e-3) / 1e12 / int8_peak
