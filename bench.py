@@ -47,6 +47,7 @@ M_C4, K_C4, N_C4 = 16384, 1536, 6144
 FLUSH_BYTES = 256 << 20
 L2_NOTE = ("256 MiB buffer written then read back between steps (outside the timed events): "
            "the next step starts from a cold L2 holding only clean lines")
+NVLINK_GBS = 770.0   # measured peer copy per direction on this pool's B200s (nominal 900)
 SLEEP_CYCLES = 20_000_000   # ~10 ms of torch's bounded sleep kernel ahead of a timed loop
 
 
@@ -679,12 +680,23 @@ def main():
     gemm_ops = 2.0 * m * n_loc * k
     t_hbm = gemm_bytes / (hbm * 1e9)
     t_tc = gemm_ops / (int8_peak * 1e12)
-    if t_tc >= t_hbm:
+    # with the fused exchange the GEMM phase also stores every tile into the
+    # world-1 peers: each rank sends (and receives) (world-1)/world of the FP32
+    # output over NVLink, against the measured 770 GB/s per direction
+    link_bytes = (world - 1) * 4 * m * n_loc if (world > 1 and fused) else 0
+    t_link = link_bytes / (NVLINK_GBS * 1e9)
+    if t_link > max(t_tc, t_hbm):
+        roof = {"bound": "nvlink", "achieved": link_bytes / (gemm_avg_ms * 1e-3) / 1e9, "peak": NVLINK_GBS,
+                "unit": "GB/s"}
+    elif t_tc >= t_hbm:
         roof = {"bound": "tensor", "achieved": gemm_ops / (gemm_avg_ms * 1e-3) / 1e12, "peak": int8_peak,
                 "unit": "TFLOP/s"}
     else:
         roof = {"bound": "hbm", "achieved": gemm_bytes / (gemm_avg_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
+    if link_bytes:
+        roof["nvlink_bytes_per_rank"] = link_bytes
+        roof["nvlink_frac"] = link_bytes / (gemm_avg_ms * 1e-3) / 1e9 / NVLINK_GBS
     roof["traffic"] = None
     try:
         with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
