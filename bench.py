@@ -281,6 +281,30 @@ def suite(torch, L, htpg, dev, flush, reps=20, only=None):
         w8a8_case(name, 4096, k, n, 0x5EED0002 + k + n, 0.005, mode, b)
     if not only:
         res["C3_stack_us"] = sum(res[c]["us"] for c in ("C3_qkv", "C3_out", "C3_fc1", "C3_fc2"))
+    if not only or only == "C3_stack":
+        # the four DiT linears back to back, as a block's forward pass runs them,
+        # over two blocks' operands (~0.9 GB, more than the L2): per-stack time
+        layers = ((1536, 4608, 0, False), (1536, 1536, 0, False), (1536, 6144, 1, True), (6144, 1536, 0, True))
+        sets = []
+        for si in range(2):
+            ops = []
+            for j, (k, n, mode, b) in enumerate(layers):
+                x, w, bb, blob = _w8a8_operands(torch, htpg, dev, 4096, k, n, 0x5EED0102 + 0x100 * si + j, 0.005, b)
+                ops.append((x, w, bb, blob, torch.empty(4096, n, dtype=torch.float32, device=dev), mode))
+            sets.append(ops)
+
+        def run_stack(ops):
+            for x, w, bb, _, out, mode in ops:
+                htpg.check(htpg.w8a8_run(w, out, x, bb, mode=mode), "C3 stack")
+
+        t = stream_us([lambda o=o: run_stack(o) for o in sets])
+        ops_total = sum(2.0 * 4096 * n * k for k, n, _, _ in layers)
+        bytes_total = sum(4 * 4096 * k + k * n + 4 * n + 4 * 4096 * n + (4 * n if b else 0) for k, n, _, b in layers)
+        res["C3_stack_stream"] = {"us": t, "TOPS": ops_total / t / 1e6, "tensor_frac": ops_total / t / 1e6 / int8_peak,
+                                  "hbm_frac": bytes_total / t / 1e3 / hbm,
+                                  "note": "qkv, out, fc1 (bias+GELU), fc2 (bias) back to back, each with its own "
+                                          "activation pass, rotating two blocks' operands (no L2 flush)"}
+        del sets
     # opcode 17: SD-VAE-decoder-shaped convolutions (512 -> 512 channels, 3x3,
     # pad 1) at 64x64, and after a nearest 2x upsample (128x128 output)
     sys.path.insert(0, os.path.join(REPO, "oracle"))
