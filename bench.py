@@ -543,6 +543,8 @@ def main():
                     help="N>1: how the column blocks reach every rank")
     ap.add_argument("--suite-only", default=None,
                     help="run only this suite config (e.g. C5_up_M16) and print its timings; for profiling")
+    ap.add_argument("--tmem-weights", type=int, default=0, choices=[0, 1],
+                    help="1: CTA-pair W8A8 problems with k <= 1536 keep the weight columns in tensor memory")
     ap.add_argument("--decode-kernel", default="reg", choices=["reg", "tc"],
                     help="kernel for W8A8 m <= 16: register-fed decode (default) or swapped tcgen05")
     ap.add_argument("--m", type=int, default=M_C4,
@@ -567,6 +569,7 @@ def main():
     L = htpg.lib()
     htpg.check(L.htpg_init(local), "htpg_init")
     htpg.set_decode_kernel(0 if args.decode_kernel == "reg" else 1)
+    htpg.set_tmem_weights(bool(args.tmem_weights))
     if args.suite_only:
         res = suite(torch, L, htpg, dev, L2Flush(torch, dev), only=args.suite_only)
         htpg.check(htpg.check_device(), "watchdog")

@@ -310,6 +310,12 @@ extern "C" int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t ou
   return HTPG_OK;
 }
 
+extern "C" int htpg_set_tmem_weights(int on) {
+  if (on != 0 && on != 1) return HTPG_EARGS;
+  g_tmem_weights.store(on);
+  return HTPG_OK;
+}
+
 extern "C" int htpg_set_decode_kernel(int which) {
   if (which != 0 && which != 1) return HTPG_EARGS;
   g_decode_kernel.store(which);
@@ -543,10 +549,11 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
 
   CUtensorMap act_map;
   const CUtensorMap *wmap = nullptr;
+  const bool tw = !act_f16 && g_tmem_weights.load() != 0 && tw_eligible(plan, mode, n_outs);
   rc = make_map(&act_map, act, w->kind, k, m, static_cast<size_t>(k) * act_elem,
-                plan.swap ? plan.bn : 128);
+                tw ? tw_box_rows() : plan.swap ? plan.bn : 128);
   if (rc) return rc;
-  rc = weight_map(w, plan.swap ? 128 : box_rows_b(plan), &wmap);
+  rc = weight_map(w, tw ? 128 : plan.swap ? 128 : box_rows_b(plan), &wmap);
   if (rc) return rc;
 
   GemmArgs a;
@@ -581,8 +588,9 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
     out_maps.count = n_outs;
     a.tma_store = 1;
   }
-  e = plan.swap ? launch_gemm(plan, *wmap, act_map, out_maps, a, st)
-                : launch_gemm(plan, act_map, *wmap, out_maps, a, st);
+  e = tw ? launch_gemm_tw(plan, act_map, *wmap, a, st)
+     : plan.swap ? launch_gemm(plan, *wmap, act_map, out_maps, a, st)
+                 : launch_gemm(plan, act_map, *wmap, out_maps, a, st);
   if (e != cudaSuccess) return record_cuda(e);
   if (phase) {
     cudaEventRecord(pe.e[2], st);

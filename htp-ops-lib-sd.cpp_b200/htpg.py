@@ -90,6 +90,7 @@ def lib() -> ctypes.CDLL:
         "htpg_weight_cache_clear": (None, []),
         "htpg_set_profiling": (I, [I]),
         "htpg_set_decode_kernel": (I, [I]),
+        "htpg_set_tmem_weights": (I, [I]),
         "htpg_last_phase_ms": (I, [ctypes.POINTER(ctypes.c_float)] * 3),
         "htpg_launch_count": (U64, []),
         "htpg_plan_info": (I, [I, I, I, I, I, ctypes.POINTER(I64)]),
@@ -243,6 +244,13 @@ def set_decode_kernel(which: int) -> None:
     """0: W8A8 problems with m <= 16 run the register-fed decode kernel (the
     default); 1: they run the swapped tcgen05 kernel.  Results are identical."""
     check(lib().htpg_set_decode_kernel(which), "htpg_set_decode_kernel")
+
+
+def set_tmem_weights(on: bool) -> None:
+    """True: W8A8 CTA-pair problems with k <= 1536 (modes 0-2, 4) run the kernel that
+    keeps the weight columns in tensor memory; False: the CTA-pair kernel that
+    streams both operands.  Results are identical."""
+    check(lib().htpg_set_tmem_weights(1 if on else 0), "htpg_set_tmem_weights")
 
 
 def qk0_plan_info(weight_type: int, m: int, n: int, k: int, sms: int = 148) -> dict:

@@ -281,6 +281,13 @@ int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]);
  * Both give identical results; the switch exists for measurement. */
 int htpg_set_decode_kernel(int which);
 
+/* Which kernel runs W8A8 problems planned as CTA-pair tiles with k <= 1536, one
+ * row-major output and modes 0-2 or 4: 1 the kernel that keeps each CTA's
+ * weight columns in tensor memory and streams only activation tiles through
+ * shared memory, 0 the CTA-pair kernel that streams both.  Both give identical
+ * results; the switch exists for measurement. */
+int htpg_set_tmem_weights(int on);
+
 /* ---- reference kernel-level names (reference: include/dsp/ops.h:20-31) ---
  * Same arguments and return codes as the DSP kernels, on device pointers;
  * synchronous (they return once the output is written).  The FP16 weight
