@@ -19,8 +19,9 @@
 // The epilogue needs no staging: TMEM lane = output column, so for each token
 // a warp stores 32 consecutive FP32 outputs (one 128-byte line) from registers.
 //
-// Measured on C4 (one B200, bit-exact against the streaming kernel): 224-232
-// us against 156-162 us.  Each 128-token sub-tile costs about 5.4 us
+// Measured on C4 (one B200, bit-exact against the streaming kernel): 195 us
+// against 156-162 us (232 us before the epilogue read its row scales as
+// shared-memory broadcasts and dropped per-element bounds checks).  Each 128-token sub-tile costs about 5.4 us
 // (48 pair MMAs of N = 128, about 115 ns each) whether A comes from tensor
 // or shared memory, and the same with one accumulator buffer; N = 64 was
 // slower still (296 us with four k-blocks per commit, 367 us with one).  Pair
@@ -59,8 +60,9 @@ constexpr int kTwSmemKb = 4;
 constexpr uint32_t kTwACol = 256;
 constexpr uint32_t kTwWKbBytes = 128 * 128;               // one k-block of this CTA's 128 weight rows
 constexpr uint32_t kTwIdesc = idesc_i8(256, kTwBM);
+// tail: barriers (first 512 bytes), then one 32-float row-scale slot per epilogue warp
 constexpr size_t kTwSmem = 1024 + static_cast<size_t>(kTwStages) * kTwStageBytes +
-                           static_cast<size_t>(kTwSmemKb) * kTwWKbBytes + 1024;
+                           static_cast<size_t>(kTwSmemKb) * kTwWKbBytes + 512 + kTwEpiWarps * 128;
 
 struct TwParams {
   GemmArgs a;
@@ -93,16 +95,30 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// One epilogue warp's 32 tokens x 32 columns of a finished sub-tile.
+// One epilogue warp's 32 tokens x 32 columns of a finished sub-tile.  rs: the
+// 32 row scales of those tokens in this warp's shared-memory slot (read as
+// broadcast float4).  A full slice stores without per-element checks.
 template <int MODE, bool BIAS>
 __device__ __forceinline__ void tw_store(const GemmArgs &g, const uint32_t (&r)[32], int m0, int n, float sw,
-                                         int32_t cr, float bv, float rs_lane, int lane) {
+                                         int32_t cr, float bv, const float *rs) {
+  if (n >= g.N) return;
+  float *p = g.out + static_cast<long long>(m0) * g.ldo + n;
+  const long long ldo = g.ldo;
+  if (m0 + 32 <= g.M) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
-    const int m = m0 + j;
-    const float v = finish<Kind::I8, MODE, BIAS>(r[j], cr, sw, rs, bv);
-    if (m < g.M && n < g.N) g.out[static_cast<long long>(m) * g.ldo + n] = v;
+    for (int j4 = 0; j4 < 8; ++j4) {
+      const float4 s4 = *reinterpret_cast<const float4 *>(rs + 4 * j4);
+      p[0] = finish<Kind::I8, MODE, BIAS>(r[4 * j4], cr, sw, s4.x, bv);
+      p[ldo] = finish<Kind::I8, MODE, BIAS>(r[4 * j4 + 1], cr, sw, s4.y, bv);
+      p[2 * ldo] = finish<Kind::I8, MODE, BIAS>(r[4 * j4 + 2], cr, sw, s4.z, bv);
+      p[3 * ldo] = finish<Kind::I8, MODE, BIAS>(r[4 * j4 + 3], cr, sw, s4.w, bv);
+      p += 4 * ldo;
+    }
+  } else {
+    for (int j = 0; j < 32 && m0 + j < g.M; ++j) {
+      *p = finish<Kind::I8, MODE, BIAS>(r[j], cr, sw, rs[j], bv);
+      p += ldo;
+    }
   }
 }
 
@@ -118,6 +134,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTwThreads, 1)
            *afree = bars + 2 * kTwStages + 5, *mma_done = bars + 2 * kTwStages + 6,
            *sready = bars + 2 * kTwStages + 7;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * kTwStages + 8);
+  float *rs_slots = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + 512);
   const int KT = min(P.KB, kTwTmemKb);  // weight k-blocks in TMEM; [KT, KB) in shared memory
   volatile uint32_t *abort = tmem_slot + 1;
 
@@ -335,7 +352,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTwThreads, 1)
         ++loads;
       }
       const int m0 = static_cast<int>(st % P.MS) * kTwBM + part * 32;
-      const float rs_lane = m0 + lane < g.M ? __ldg(g.row_scale + m0 + lane) : 0.f;
+      float *rs_slot = rs_slots + (warp - 2) * 32;
+      __syncwarp();  // the previous sub-tile's reads of the slot are done
+      rs_slot[lane] = m0 + lane < g.M ? __ldg(g.row_scale + m0 + lane) : 0.f;
+      __syncwarp();
       const uint32_t buf = iter & 1u;
       if (!mbar_wait(smem_u32(&tfull[buf]), (iter >> 1) & 1u, wd, kWatchEpilogue, abort)) {
         st_shared_cluster(peer_abort, 1u);
@@ -349,13 +369,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTwThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[buf]);
       switch (mode * 2 + (has_bias ? 1 : 0)) {
-        case 0: tw_store<0, false>(g, r, m0, n, sw, cr, bv, rs_lane, lane); break;
-        case 1: tw_store<0, true>(g, r, m0, n, sw, cr, bv, rs_lane, lane); break;
-        case 2: tw_store<1, false>(g, r, m0, n, sw, cr, bv, rs_lane, lane); break;
-        case 3: tw_store<1, true>(g, r, m0, n, sw, cr, bv, rs_lane, lane); break;
-        case 4: tw_store<2, false>(g, r, m0, n, sw, cr, bv, rs_lane, lane); break;
-        case 5: tw_store<2, true>(g, r, m0, n, sw, cr, bv, rs_lane, lane); break;
-        default: tw_store<4, false>(g, r, m0, n, sw, cr, bv, rs_lane, lane); break;
+        case 0: tw_store<0, false>(g, r, m0, n, sw, cr, bv, rs_slot); break;
+        case 1: tw_store<0, true>(g, r, m0, n, sw, cr, bv, rs_slot); break;
+        case 2: tw_store<1, false>(g, r, m0, n, sw, cr, bv, rs_slot); break;
+        case 3: tw_store<1, true>(g, r, m0, n, sw, cr, bv, rs_slot); break;
+        case 4: tw_store<2, false>(g, r, m0, n, sw, cr, bv, rs_slot); break;
+        case 5: tw_store<2, true>(g, r, m0, n, sw, cr, bv, rs_slot); break;
+        default: tw_store<4, false>(g, r, m0, n, sw, cr, bv, rs_slot); break;
       }
     }
   }
