@@ -19,9 +19,10 @@
 // The epilogue needs no staging: TMEM lane = output column, so for each token
 // a warp stores 32 consecutive FP32 outputs (one 128-byte line) from registers.
 //
-// Measured on C4 (one B200, bit-exact against the streaming kernel): 195 us
-// against 156-162 us (232 us before the epilogue read its row scales as
-// shared-memory broadcasts and dropped per-element bounds checks).  Each 128-token sub-tile costs about 5.4 us
+// Measured on C4 (one B200, bit-exact against the streaming kernel): 179 us
+// against 153-162 us (232 us before the epilogue read its row scales as
+// shared-memory broadcasts, dropped per-element bounds checks and moved to
+// packed FP32x2 arithmetic).  Each 128-token sub-tile costs about 5.4 us
 // (48 pair MMAs of N = 128, about 115 ns each) whether A comes from tensor
 // or shared memory, and the same with one accumulator buffer; N = 64 was
 // slower still (296 us with four k-blocks per commit, 367 us with one).  Pair
@@ -95,6 +96,64 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Packed FP32x2 arithmetic (two tokens of one output column per instruction).
+// Each lane is the IEEE round-to-nearest operation of the scalar form, so
+// finish2 gives the bits of finish (epilogue.cuh) for both elements.  The bias
+// add stays scalar (__fadd_rn): a packed add after a packed multiply was
+// measured to be contracted into one fused multiply-add (one rounding instead
+// of two), which changes the bits.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float &a, float &b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// finish<Kind::I8, MODE, BIAS> for two accumulators of the same column.
+template <int MODE, bool BIAS>
+__device__ __forceinline__ void finish2(uint32_t a0, uint32_t a1, int32_t cr, uint64_t sw2, float rs0, float rs1,
+                                        uint64_t b2, float &o0, float &o1) {
+  const int32_t y0 = static_cast<int32_t>(a0 + static_cast<uint32_t>(cr));
+  const int32_t y1 = static_cast<int32_t>(a1 + static_cast<uint32_t>(cr));
+  if constexpr (MODE == 4) {
+    o0 = __int_as_float(y0);
+    o1 = __int_as_float(y1);
+    return;
+  } else {
+    uint64_t v = mul2(mul2(pk2(__int2float_rn(y0), __int2float_rn(y1)), sw2), pk2(rs0, rs1));
+    if constexpr (BIAS) {
+      float v0, v1;
+      upk2(v, v0, v1);
+      v = pk2(__fadd_rn(v0, __uint_as_float(static_cast<uint32_t>(b2))), __fadd_rn(v1, __uint_as_float(static_cast<uint32_t>(b2))));
+    }
+    if constexpr (MODE == 1 || MODE == 2) {
+      uint64_t h;
+      if constexpr (MODE == 1) {
+        constexpr float c1 = 0.5f * 1.5957691216057308f, c3 = 0.5f * 1.5957691216057308f * 0.044715f;
+        h = mul2(v, fma2(mul2(v, v), pk2(c3, c3), pk2(c1, c1)));
+      } else {
+        h = mul2(v, pk2(0.5f * 1.702f, 0.5f * 1.702f));
+      }
+      float h0, h1;
+      upk2(h, h0, h1);
+      const uint64_t hx = mul2(pk2(0.5f, 0.5f), v);
+      v = fma2(hx, pk2(tanh_approx(h0), tanh_approx(h1)), hx);
+    }
+    upk2(v, o0, o1);
+  }
+}
+
 // One epilogue warp's 32 tokens x 32 columns of a finished sub-tile.  rs: the
 // 32 row scales of those tokens in this warp's shared-memory slot (read as
 // broadcast float4).  A full slice stores without per-element checks.
@@ -105,13 +164,17 @@ __device__ __forceinline__ void tw_store(const GemmArgs &g, const uint32_t (&r)[
   float *p = g.out + static_cast<long long>(m0) * g.ldo + n;
   const long long ldo = g.ldo;
   if (m0 + 32 <= g.M) {
+    const uint64_t sw2 = pk2(sw, sw), b2 = pk2(bv, bv);
 #pragma unroll
     for (int j4 = 0; j4 < 8; ++j4) {
       const float4 s4 = *reinterpret_cast<const float4 *>(rs + 4 * j4);
-      p[0] = finish<Kind::I8, MODE, BIAS>(r[4 * j4], cr, sw, s4.x, bv);
-      p[ldo] = finish<Kind::I8, MODE, BIAS>(r[4 * j4 + 1], cr, sw, s4.y, bv);
-      p[2 * ldo] = finish<Kind::I8, MODE, BIAS>(r[4 * j4 + 2], cr, sw, s4.z, bv);
-      p[3 * ldo] = finish<Kind::I8, MODE, BIAS>(r[4 * j4 + 3], cr, sw, s4.w, bv);
+      float o0, o1, o2, o3;
+      finish2<MODE, BIAS>(r[4 * j4], r[4 * j4 + 1], cr, sw2, s4.x, s4.y, b2, o0, o1);
+      finish2<MODE, BIAS>(r[4 * j4 + 2], r[4 * j4 + 3], cr, sw2, s4.z, s4.w, b2, o2, o3);
+      p[0] = o0;
+      p[ldo] = o1;
+      p[2 * ldo] = o2;
+      p[3 * ldo] = o3;
       p += 4 * ldo;
     }
   } else {
