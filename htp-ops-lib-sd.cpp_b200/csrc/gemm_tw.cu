@@ -123,7 +123,7 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
 // finish<Kind::I8, MODE, BIAS> for two accumulators of the same column.
 template <int MODE, bool BIAS>
 __device__ __forceinline__ void finish2(uint32_t a0, uint32_t a1, int32_t cr, uint64_t sw2, float rs0, float rs1,
-                                        uint64_t b2, float &o0, float &o1) {
+                                        float bias, float &o0, float &o1) {
   const int32_t y0 = static_cast<int32_t>(a0 + static_cast<uint32_t>(cr));
   const int32_t y1 = static_cast<int32_t>(a1 + static_cast<uint32_t>(cr));
   if constexpr (MODE == 4) {
@@ -135,7 +135,7 @@ __device__ __forceinline__ void finish2(uint32_t a0, uint32_t a1, int32_t cr, ui
     if constexpr (BIAS) {
       float v0, v1;
       upk2(v, v0, v1);
-      v = pk2(__fadd_rn(v0, __uint_as_float(static_cast<uint32_t>(b2))), __fadd_rn(v1, __uint_as_float(static_cast<uint32_t>(b2))));
+      v = pk2(__fadd_rn(v0, bias), __fadd_rn(v1, bias));
     }
     if constexpr (MODE == 1 || MODE == 2) {
       uint64_t h;
@@ -164,13 +164,13 @@ __device__ __forceinline__ void tw_store(const GemmArgs &g, const uint32_t (&r)[
   float *p = g.out + static_cast<long long>(m0) * g.ldo + n;
   const long long ldo = g.ldo;
   if (m0 + 32 <= g.M) {
-    const uint64_t sw2 = pk2(sw, sw), b2 = pk2(bv, bv);
+    const uint64_t sw2 = pk2(sw, sw);
 #pragma unroll
     for (int j4 = 0; j4 < 8; ++j4) {
       const float4 s4 = *reinterpret_cast<const float4 *>(rs + 4 * j4);
       float o0, o1, o2, o3;
-      finish2<MODE, BIAS>(r[4 * j4], r[4 * j4 + 1], cr, sw2, s4.x, s4.y, b2, o0, o1);
-      finish2<MODE, BIAS>(r[4 * j4 + 2], r[4 * j4 + 3], cr, sw2, s4.z, s4.w, b2, o2, o3);
+      finish2<MODE, BIAS>(r[4 * j4], r[4 * j4 + 1], cr, sw2, s4.x, s4.y, bv, o0, o1);
+      finish2<MODE, BIAS>(r[4 * j4 + 2], r[4 * j4 + 3], cr, sw2, s4.z, s4.w, bv, o2, o3);
       p[0] = o0;
       p[ldo] = o1;
       p[2 * ldo] = o2;
@@ -357,7 +357,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTwThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;          // TMEM lane quadrant
-    const int part = (warp - 2) / 4;  // 16-token slice of the sub-tile; k-blocks part, part + 4, ...
+    const int part = (warp - 2) / 4;  // 32-token slice of the sub-tile; k-blocks part, part + 4, ...
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t wready_leader = mapa_shared(smem_u32(wready), 0);
     const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0), mapa_shared(smem_u32(&tempty[1]), 0)};
