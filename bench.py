@@ -3,11 +3,14 @@
 
 Workload (default, every N): configuration C4 — W8A8 MLP fc1 with bias +
 GELU(tanh) epilogue, M=16384 tokens, K=1536, N=6144, column-sharded over the
-N GPUs (N/world columns per GPU); for N > 1 each step ends with an NCCL
-all-gather of the output slices over NVLink and the reassembly of the
-row-major [M][N] output.  One step = quantise the activation rows, the tcgen05
-INT8 GEMM with the fused dequant/bias/GELU epilogue, (gather).  Metric: whole-
-job INT8 TOPS (2*M*N*K per step / device time, max over ranks).
+N GPUs (N/world columns per GPU).  For N > 1 the output exchange is fused into
+the GEMM (default, --exchange fused): the epilogue stores every finished tile
+into every rank's row-major [M][N] output over NVLink, and a stream-ordered
+NCCL all-reduce of one token orders the step; --exchange nccl keeps the NCCL
+all-gather + reassembly baseline.  One step = quantise the activation rows,
+the tcgen05 INT8 GEMM with the fused dequant/bias/GELU epilogue (and its
+stores to the peers).  Metric: whole-job INT8 TOPS (2*M*N*K per step / device
+time, max over ranks).
 
 * value        device-resident inputs; per-step CUDA-event time (L2 flushed
                between steps by a 256 MiB write + read-back outside the timed
@@ -404,6 +407,38 @@ def suite(torch, L, htpg, dev, flush, reps=20, only=None):
     return res
 
 
+def suite_summary(res):
+    """Short form of the suite: per config the device time and the fraction of
+    its roofline (tensor or HBM, whichever bounds it), decode shapes also back to
+    back; ordered so the C1, C2 and C3 entries come last."""
+    out = {}
+
+    def r(v, nd=3):
+        return None if v is None else round(float(v), nd)
+
+    order = sorted(res, key=lambda name: (0 if not name.startswith(("C1", "C2", "C3")) else 1, name))
+    for name in order:
+        v = res[name]
+        if not isinstance(v, dict):
+            out[name] = r(v, 1)
+            continue
+        e = {"us": r(v.get("us"), 1)}
+        if "roofline_frac" in v:
+            e["frac"] = r(v["roofline_frac"])
+            e["bound"] = v.get("bound")
+        elif "tensor_frac" in v:
+            e["tensor_frac"] = r(v["tensor_frac"])
+        if "hbm_frac" in v and "roofline_frac" not in v:
+            e["hbm_frac"] = r(v["hbm_frac"])
+        if "stream_us" in v:
+            e["stream_us"] = r(v["stream_us"], 1)
+            e["stream_hbm_frac"] = r(v["stream_hbm_frac"])
+        if "TOPS" in v:
+            e["TOPS"] = r(v["TOPS"], 1)
+        out[name] = e
+    return out
+
+
 # ------------------------------------------------------------------ CPU leg
 _CPU_CASES = {}
 
@@ -543,8 +578,6 @@ def main():
                     help="N>1: how the column blocks reach every rank")
     ap.add_argument("--suite-only", default=None,
                     help="run only this suite config (e.g. C5_up_M16) and print its timings; for profiling")
-    ap.add_argument("--tmem-weights", type=int, default=0, choices=[0, 1],
-                    help="1: CTA-pair W8A8 problems with k <= 1536 keep the weight columns in tensor memory")
     ap.add_argument("--decode-kernel", default="reg", choices=["reg", "tc"],
                     help="kernel for W8A8 m <= 16: register-fed decode (default) or swapped tcgen05")
     ap.add_argument("--m", type=int, default=M_C4,
@@ -569,7 +602,6 @@ def main():
     L = htpg.lib()
     htpg.check(L.htpg_init(local), "htpg_init")
     htpg.set_decode_kernel(0 if args.decode_kernel == "reg" else 1)
-    htpg.set_tmem_weights(bool(args.tmem_weights))
     if args.suite_only:
         res = suite(torch, L, htpg, dev, L2Flush(torch, dev), only=args.suite_only)
         htpg.check(htpg.check_device(), "watchdog")
@@ -798,8 +830,9 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         line["e2e"] = {"value": ops / (float(t.item()) * 1e-3) / 1e12, "unit": "TOPS",
                        "h2d_bytes_per_step": m * k * 4, "d2h_bytes_per_step": m * n * 4,
-                       "path": "C ABI htpg_w8a8_run per rank + NCCL all-gather; pinned host activation in "
-                               "(every rank), full output out (rank 0)"}
+                       "path": ("C ABI htpg_w8a8_run_gather per rank (fused output exchange over NVLink)"
+                                if fused else "C ABI htpg_w8a8_run per rank + NCCL all-gather") +
+                               "; pinned host activation in (every rank), full output out (rank 0)"}
     if world == 1 and not args.no_suite:
         line["suite"] = suite(torch, L, htpg, dev, flush)
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -821,6 +854,12 @@ def main():
         dist.barrier()
         for q in peers:
             htpg.check(L.htpg_ipc_close(q), "htpg_ipc_close")
+    if "suite" in line:
+        # the per-config figures in short form, last on the line so that a
+        # reader keeping only the line's tail still sees them (C1-C3 last)
+        full = line.pop("suite")
+        line["suite"] = full
+        line["suite_summary"] = suite_summary(full)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:

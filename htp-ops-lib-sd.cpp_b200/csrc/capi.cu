@@ -84,6 +84,16 @@ int current_device(Device **out) {
   return HTPG_OK;
 }
 
+// Zero every stream workspace of the device (W8A8/FP16 split-K areas and the
+// opcode 2-4 stream-K scratch); the device is idle when this is called.
+void clear_workspaces(Device *d) {
+  for (auto *m : {&d->ws, &d->qws})
+    for (auto &kv : *m)
+      if (kv.second.base && cudaMemset(kv.second.base, 0, kv.second.bytes) != cudaSuccess) cudaGetLastError();
+  cudaDeviceSynchronize();
+  cudaGetLastError();
+}
+
 // NULL is the CUDA default stream (the stream torch and most callers use
 // unless they create their own).
 cudaStream_t pick_stream(Device *, void *stream) { return static_cast<cudaStream_t>(stream); }
@@ -264,12 +274,45 @@ extern "C" int htpg_check_device(void *stream, uint32_t *flags) {
   if (v) {
     const uint32_t zero = 0;
     cudaMemcpyToSymbol(g_watchdog, &zero, sizeof(zero));
-    // a launch that gave up may have left split-K partials behind
-    for (auto &kv : d->ws)
-      if (kv.second.base) cudaMemset(kv.second.base, 0, kv.second.bytes);
+    // A launch that gave up may have left split-K partial sums and arrival
+    // counters behind, in the W8A8/FP16 workspaces and in the opcode 2-4
+    // stream-K scratch alike; both rely on "left zero by every launch".
+    // Other streams of this device may still run: wait for them first.
+    cudaDeviceSynchronize();
+    cudaGetLastError();
+    clear_workspaces(d);
   }
   if (flags) *flags = v;
   return v ? HTPG_EWATCHDOG : HTPG_OK;
+}
+
+// Test hook: leave the state an aborted launch can leave (every stream
+// workspace of the current device filled with `fill`, the split-K watchdog
+// bit set), so a test can check that htpg_check_device restores it.
+extern "C" int htpg_debug_simulate_abort(uint32_t fill) {
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  if (cudaDeviceSynchronize() != cudaSuccess) return record_cuda(cudaGetLastError());
+  for (auto *m : {&d->ws, &d->qws})
+    for (auto &kv : *m)
+      if (kv.second.base && cudaMemset(kv.second.base, static_cast<int>(fill & 0xffu), kv.second.bytes) != cudaSuccess)
+        return record_cuda(cudaGetLastError());
+  const uint32_t bit = 8u;  // the split-K role bit of the watchdog word
+  if (cudaMemcpyToSymbol(g_watchdog, &bit, sizeof(bit)) != cudaSuccess) return record_cuda(cudaGetLastError());
+  return HTPG_OK;
+}
+
+extern "C" int htpg_debug_workspaces(size_t *ws_bytes, size_t *qws_bytes) {
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  size_t a = 0, b = 0;
+  for (auto &kv : d->ws) a += kv.second.bytes;
+  for (auto &kv : d->qws) b += kv.second.bytes;
+  if (ws_bytes) *ws_bytes = a;
+  if (qws_bytes) *qws_bytes = b;
+  return HTPG_OK;
 }
 
 extern "C" uint64_t htpg_launch_count(void) { return htpg::launches(); }
@@ -310,11 +353,6 @@ extern "C" int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t ou
   return HTPG_OK;
 }
 
-extern "C" int htpg_set_tmem_weights(int on) {
-  if (on != 0 && on != 1) return HTPG_EARGS;
-  g_tmem_weights.store(on);
-  return HTPG_OK;
-}
 
 extern "C" int htpg_set_decode_kernel(int which) {
   if (which != 0 && which != 1) return HTPG_EARGS;
@@ -549,11 +587,9 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
 
   CUtensorMap act_map;
   const CUtensorMap *wmap = nullptr;
-  const bool tw = !act_f16 && g_tmem_weights.load() != 0 && tw_eligible(plan, mode, n_outs);
-  rc = make_map(&act_map, act, w->kind, k, m, static_cast<size_t>(k) * act_elem,
-                tw ? tw_box_rows() : plan.swap ? plan.bn : 128);
+  rc = make_map(&act_map, act, w->kind, k, m, static_cast<size_t>(k) * act_elem, plan.swap ? plan.bn : 128);
   if (rc) return rc;
-  rc = weight_map(w, tw ? 128 : plan.swap ? 128 : box_rows_b(plan), &wmap);
+  rc = weight_map(w, plan.swap ? 128 : box_rows_b(plan), &wmap);
   if (rc) return rc;
 
   GemmArgs a;
@@ -588,9 +624,8 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
     out_maps.count = n_outs;
     a.tma_store = 1;
   }
-  e = tw ? launch_gemm_tw(plan, act_map, *wmap, a, st)
-     : plan.swap ? launch_gemm(plan, *wmap, act_map, out_maps, a, st)
-                 : launch_gemm(plan, act_map, *wmap, out_maps, a, st);
+  e = plan.swap ? launch_gemm(plan, *wmap, act_map, out_maps, a, st)
+                : launch_gemm(plan, act_map, *wmap, out_maps, a, st);
   if (e != cudaSuccess) return record_cuda(e);
   if (phase) {
     cudaEventRecord(pe.e[2], st);
@@ -1198,9 +1233,8 @@ extern "C" int hmx_mat_mul_native_w8a8_profiled(float *dst, const float *activat
   if (!dst || !activation || !constants || m < 1 || m > HTPG_W8A8_MAX_M || k < 32 ||
       k > HTPG_W8A8_MAX_K || k % 32 || n < 64 || n > HTPG_W8A8_MAX_N || n % 64)
     return HTPG_EARGS;
-  uint32_t mode = 0;
-  if (profile) {
-    mode = profile->mode;
+  if (profile) {  // the caller's mode survives; every other field is rewritten
+    const uint32_t mode = profile->mode;
     std::memset(profile, 0, sizeof(*profile));
     profile->mode = mode;
   }
@@ -1213,29 +1247,41 @@ extern "C" int hmx_mat_mul_native_w8a8_profiled(float *dst, const float *activat
   if (profile) g_profiling = 1;
   rc = finish_sync(run_common(w, &dst, 1, 0, activation, nullptr, m, 0, 0, nullptr));
   g_profiling = prev;
-  if (profile && rc == HTPG_OK) {
-    const double tick_per_ms = 19200.0;  // the reference reports 19.2 MHz qtimer ticks
-    profile->setup_ticks =
-        static_cast<uint64_t>(std::chrono::duration<double, std::milli>(t1 - t0).count() * tick_per_ms);
-    profile->activation_ticks = static_cast<uint64_t>(t_phase_ms[0] * tick_per_ms);
-    profile->hmx_ticks = static_cast<uint64_t>(t_phase_ms[1] * tick_per_ms);
-    profile->output_ticks = 0;  // the epilogue is fused into the GEMM
-    if (mode == 2) profile->mac_ticks = profile->hmx_ticks;
-    if (mode == 3) {
-      int dev = 0;
-      cudaGetDevice(&dev);
-      const GemmPlan p = plan_gemm(Kind::I8, m, n, k, g_dev[dev].sms);
-      const uint32_t rows64 = p.swap ? 2u : 2u;
-      const uint32_t cols64 = static_cast<uint32_t>(p.swap ? 2 : (p.bn >= 64 ? p.bn / 64 : 1));
-      profile->reserved = rows64 | (cols64 << 16) | (p.swap ? 0x80000000u : 0u);
-      profile->mac_ticks = static_cast<uint64_t>(p.units);  // weight tiles streamed
-      profile->readout_ticks = p.reg ? static_cast<uint64_t>(p.tiles_a) * 16u * p.kb_total * 128u
-                                     : static_cast<uint64_t>(p.units) *
-                                           static_cast<uint64_t>(p.swap ? 128 : p.bn) *
-                                           static_cast<uint64_t>(p.kb_per_split) * 128u;  // weight bytes streamed
-    }
-  }
+  if (profile && rc == HTPG_OK)
+    htpg_w8a8_profile_fill(m, k, n, std::chrono::duration<double, std::milli>(t1 - t0).count(), profile);
   return rc;
+}
+
+// The trailer of a profiled opcode-15 request (reference op_reg.h:91-101,
+// linear_w8a8.c:328-335, 396-399, 421-508), from the last run's phase events.
+extern "C" int htpg_w8a8_profile_fill(int m, int k, int n, double setup_ms, struct NativeW8A8Profile *profile) {
+  if (!profile) return HTPG_EARGS;
+  const uint32_t mode = profile->mode;
+  std::memset(profile, 0, sizeof(*profile));
+  profile->mode = mode;
+  const double tick_per_ms = 19200.0;  // the reference reports 19.2 MHz qtimer ticks
+  profile->setup_ticks = static_cast<uint64_t>(setup_ms * tick_per_ms);
+  profile->activation_ticks = static_cast<uint64_t>(t_phase_ms[0] * tick_per_ms);
+  profile->hmx_ticks = static_cast<uint64_t>(t_phase_ms[1] * tick_per_ms);
+  // weight loads and the output stores happen inside the GEMM launch: the
+  // weight and output phases have no time of their own (0)
+  if (mode == 2) profile->mac_ticks = profile->hmx_ticks;  // accumulation and readout are one launch
+  if (mode == 3) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const GemmPlan p = plan_gemm(Kind::I8, m, n, k, dev >= 0 && dev < 16 && g_dev[dev].sms ? g_dev[dev].sms : 148);
+    // low 16 bits: 64-row activation tiles per output tile; high 16 bits:
+    // 64-column weight groups per output tile; bit 31 (table hit) stays 0,
+    // every plan here comes from the shape-keyed planner
+    const uint32_t rows64 = p.swap ? 1u : p.pair ? 4u : 2u;
+    const uint32_t cols64 = static_cast<uint32_t>(p.swap ? 2 : (p.bn >= 64 ? p.bn / 64 : 1));
+    profile->reserved = rows64 | (cols64 << 16);
+    profile->mac_ticks = static_cast<uint64_t>(p.units);  // weight tiles loaded
+    profile->readout_ticks = p.reg ? static_cast<uint64_t>(p.tiles_a) * 16u * p.kb_total * 128u
+                                   : static_cast<uint64_t>(p.units) * static_cast<uint64_t>(p.swap ? 128 : p.bn) *
+                                         static_cast<uint64_t>(p.kb_per_split) * 128u;  // weight bytes loaded
+  }
+  return HTPG_OK;
 }
 
 extern "C" int hmx_mat_mul_native_w8a8(float *dst, const float *activation, const uint8_t *constants,
@@ -1243,10 +1289,10 @@ extern "C" int hmx_mat_mul_native_w8a8(float *dst, const float *activation, cons
   return hmx_mat_mul_native_w8a8_profiled(dst, activation, constants, m, k, n, nullptr);
 }
 
-// The raw INT32 byte-plane export of the reference (linear_w8a8.c:205-227,
-// 512-526) is a property of the Hexagon HMX readout; this device has no byte
-// planes, so the request is answered like the reference answers it on a DSP
-// without the feature (-75).
+// The reference's CPU-epilogue form (linear_w8a8.c:205-227, 512-526): the
+// unsigned-code INT32 accumulators leave as raw byte planes in the HMX export
+// layout, the row scales and one batch descriptor go into the control block
+// (htpg_w8a8_run_planes does both).
 extern "C" int hmx_mat_mul_native_w8a8_cpu(float *dst, const float *activation,
                                            const uint8_t *constants, int m, int k, int n,
                                            struct W8A8CpuControl *control) {

@@ -58,6 +58,65 @@ __device__ __forceinline__ float finish(uint32_t acc, int32_t corr, float sw, fl
   return epilogue_act<MODE>(v);
 }
 
+// Packed FP32x2 arithmetic (two output elements per instruction).  Each lane
+// is the IEEE round-to-nearest operation of the scalar form, so finish2 gives
+// the bits of finish for both elements.  The bias add stays scalar
+// (__fadd_rn): a packed add after a packed multiply was measured to be
+// contracted into one fused multiply-add (one rounding instead of two), which
+// changes the bits.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float &a, float &b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// finish<Kind::I8, MODE, BIAS> for two accumulators of the same column
+// (column scale sw2 = {sw, sw}, row scales rs0 and rs1).
+template <int MODE, bool BIAS>
+__device__ __forceinline__ void finish2(uint32_t a0, uint32_t a1, int32_t cr, uint64_t sw2, float rs0, float rs1,
+                                        float bias, float &o0, float &o1) {
+  const int32_t y0 = static_cast<int32_t>(a0 + static_cast<uint32_t>(cr));
+  const int32_t y1 = static_cast<int32_t>(a1 + static_cast<uint32_t>(cr));
+  if constexpr (MODE == 4) {
+    o0 = __int_as_float(y0);
+    o1 = __int_as_float(y1);
+    return;
+  } else {
+    uint64_t v = mul2(mul2(pk2(__int2float_rn(y0), __int2float_rn(y1)), sw2), pk2(rs0, rs1));
+    if constexpr (BIAS) {
+      float v0, v1;
+      upk2(v, v0, v1);
+      v = pk2(__fadd_rn(v0, bias), __fadd_rn(v1, bias));
+    }
+    if constexpr (MODE == 1 || MODE == 2) {
+      uint64_t h;
+      if constexpr (MODE == 1) {
+        constexpr float c1 = 0.5f * 1.5957691216057308f, c3 = 0.5f * 1.5957691216057308f * 0.044715f;
+        h = mul2(v, fma2(mul2(v, v), pk2(c3, c3), pk2(c1, c1)));
+      } else {
+        h = mul2(v, pk2(0.5f * 1.702f, 0.5f * 1.702f));
+      }
+      float h0, h1;
+      upk2(h, h0, h1);
+      const uint64_t hx = mul2(pk2(0.5f, 0.5f), v);
+      v = fma2(hx, pk2(tanh_approx(h0), tanh_approx(h1)), hx);
+    }
+    upk2(v, o0, o1);
+  }
+}
+
 // Plane export (the opcode-15 CPU-epilogue form, linear_w8a8.c:205-227): the
 // unsigned-code INT32 accumulator of (m, n) is split into its four bytes.  In
 // the 64-row tile of m (rows = the tile's valid rows) and the 32-column half of

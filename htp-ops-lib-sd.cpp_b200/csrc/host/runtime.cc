@@ -485,16 +485,8 @@ int exec_w8a8(uint8_t *payload, size_t payload_size) {
   if (profiled) htpg_set_profiling(0);
   p->elapsed_us = elapsed_us(t0);
   if (profiled) {
-    float q = 0, g = 0, t = 0;
-    htpg_last_phase_ms(&q, &g, &t);
-    const double tick = 19200.0;  // 19.2 MHz qtimer ticks per ms, as the reference reports
-    const uint32_t mode_keep = prof.mode;
-    std::memset(&prof, 0, sizeof(prof));
-    prof.mode = mode_keep;
-    prof.setup_ticks = static_cast<uint64_t>(setup_ms * tick);
-    prof.activation_ticks = static_cast<uint64_t>(q * tick);
-    prof.hmx_ticks = static_cast<uint64_t>(g * tick);
-    if (mode_keep == 2) prof.mac_ticks = prof.hmx_ticks;
+    // the trailer is written back like the reference's (op_executor.cc:344-346)
+    htpg_w8a8_profile_fill(m, k, n, setup_ms, &prof);
     std::memcpy(payload + sizeof(NativeW8A8Params), &prof, sizeof(prof));
   }
   if (rc) return rc;

@@ -1304,7 +1304,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // 0: INT8 shapes with M <= 16 run the register-fed decode kernel (decode.cu);
 // 1: they run the swapped tcgen05 kernel like 16 < M <= 32.
 std::atomic<int> g_decode_kernel{0};
-std::atomic<int> g_tmem_weights{0};
 
 // Tile plan keyed on M:
 //  * I8, M <= 16 and (M <= 8 or a K-split swapped plan): the register-fed

@@ -85,15 +85,6 @@ struct OutMaps {
 
 cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
                         const OutMaps &tmOut, const GemmArgs &a, cudaStream_t st);
-// CTA-pair W8A8 GEMM with the weight tile resident in tensor memory
-// (gemm_tw.cu): CTA-pair plans with K <= 1536, one row-major output, modes
-// 0-2 and 4.  tmB: the activation codes with boxes of tw_box_rows() rows;
-// tmW: the prepared weight with boxes of 128 rows.
-bool tw_eligible(const GemmPlan &p, int mode, int n_outs);
-int tw_box_rows();
-cudaError_t launch_gemm_tw(const GemmPlan &p, const CUtensorMap &tmB, const CUtensorMap &tmW, const GemmArgs &a,
-                           cudaStream_t st);
-extern std::atomic<int> g_tmem_weights;  // 1: eligible plans run gemm_tw
 
 cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
                                  const float *inverse, int m, int k, cudaStream_t st);

@@ -3,8 +3,10 @@
 // that owns the device, or a loop that cannot absorb cudaMalloc's implicit
 // device synchronisation).  Its scratch -- split-K area, activation codes, row
 // scales -- is the file-scope static array below, one per device; nothing is
-// allocated by any call.  The array lives in this translation unit alone, so
-// its module (and the 32 MiB) is loaded only by callers of this entry point.
+// allocated by any call.  The array lives in this translation unit alone; with
+// CUDA's lazy module loading (the default, CUDA_MODULE_LOADING=LAZY) its module,
+// and so the 32 MiB, is loaded on a device only once this entry point runs
+// there, while eager loading places it on every device at start-up.
 #include <cuda_runtime.h>
 
 #include <mutex>

@@ -90,9 +90,11 @@ def lib() -> ctypes.CDLL:
         "htpg_weight_cache_clear": (None, []),
         "htpg_set_profiling": (I, [I]),
         "htpg_set_decode_kernel": (I, [I]),
-        "htpg_set_tmem_weights": (I, [I]),
         "htpg_last_phase_ms": (I, [ctypes.POINTER(ctypes.c_float)] * 3),
         "htpg_launch_count": (U64, []),
+        "htpg_debug_simulate_abort": (I, [U32]),
+        "htpg_debug_workspaces": (I, [ctypes.POINTER(S), ctypes.POINTER(S)]),
+        "htpg_w8a8_profile_fill": (I, [I, I, I, ctypes.c_double, P]),
         "htpg_plan_info": (I, [I, I, I, I, I, ctypes.POINTER(I64)]),
         "htpg_phase_timing": (I, [I]),
         "htpg_phase_timing_read": (I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
@@ -154,6 +156,8 @@ def lib() -> ctypes.CDLL:
         "destroy_htp_message_channel": (I, []),
         "htp_ops_rpc_rms_norm_f32": (I, [I] * 6),
         "htp_ops_rpc_mat_mul_permuted_w16a32": (I, [I] * 9),
+        "htp_ops_rpc_mat_mul_permuted_w16a32_session": (I, [P] + [I] * 9),
+        "htp_ops_rpc_mat_mul_permuted_w16a32_trace_session": (I, [P] + [I] * 9 + [ctypes.POINTER(U64)] * 3),
         "htp_ops_f16_epilogue_version": (I, []),
         "htp_ops_native_model_version": (I, []),
         "htp_ops_dit_aux_version": (I, []),
@@ -244,13 +248,6 @@ def set_decode_kernel(which: int) -> None:
     """0: W8A8 problems with m <= 16 run the register-fed decode kernel (the
     default); 1: they run the swapped tcgen05 kernel.  Results are identical."""
     check(lib().htpg_set_decode_kernel(which), "htpg_set_decode_kernel")
-
-
-def set_tmem_weights(on: bool) -> None:
-    """True: W8A8 CTA-pair problems with k <= 1536 (modes 0-2, 4) run the kernel that
-    keeps the weight columns in tensor memory; False: the CTA-pair kernel that
-    streams both operands.  Results are identical."""
-    check(lib().htpg_set_tmem_weights(1 if on else 0), "htpg_set_tmem_weights")
 
 
 def qk0_plan_info(weight_type: int, m: int, n: int, k: int, sms: int = 148) -> dict:

@@ -92,6 +92,7 @@ int htpg_quantize_rows(int8_t *codes, float *row_scales, const float *x, const f
 /* ---- prepared weights ------------------------------------------------- */
 typedef struct htpg_weights htpg_weights;
 struct W8A8CpuControl; /* include/op_reg.h */
+struct NativeW8A8Profile; /* include/op_reg.h */
 
 /* Repack a W8A8 constants blob (device memory, reference layout:
  * include/op_reg.h W8A8Header) into the tensor-core layout; columns
@@ -214,7 +215,8 @@ int htpg_ipc_close(void *dev_ptr);
  * under a fixed memory budget or a caching allocator that owns all device
  * memory, real-time loops where cudaMalloc's implicit device synchronisation
  * is not acceptable, and hosts that prepare every buffer up front.  Same
- * arguments, checks and results as htpg_w8a8_run, but the activation codes,
+ * arguments, checks and results as htpg_w8a8_run for modes 0-4 (mode 5, the
+ * plane export, is refused with HTPG_ECAPACITY), but the activation codes,
  * row scales and split-K partial sums live in one fixed static device array
  * of HTPG_STATIC_SCRATCH_BYTES per device instead of the per-stream
  * workspace, and no call allocates: no cudaMalloc, cudaFree or allocating
@@ -225,8 +227,10 @@ int htpg_ipc_close(void *dev_ptr);
  * (m*k up to 31,453,184 - 4*m: e.g. M = 16384 at K = 1536).  The prepared
  * weight `w` is made beforehand with htpg_w8a8_weights_create, which does
  * allocate.  The first call on each device does that device's one-time set-up
- * (device properties, the array's device address, kernel attributes), so make
- * it before any stream capture.  Every call on a device shares the one array,
+ * (device properties and the array's device address), so make it before any
+ * stream capture; each tile plan's kernel also sets its launch attributes on
+ * its first use, and under CUDA's lazy module loading (the default) loads its
+ * module then, so run each shape once before a capture.  Every call on a device shares the one array,
  * which keeps the previous call's contents: calls whose executions overlap on
  * the GPU (different streams, or host threads racing on one device) race on
  * it; order them on one stream. */
@@ -257,6 +261,18 @@ void htpg_weight_cache_clear(void);
  * profile trailer. */
 int htpg_set_profiling(int on);
 int htpg_last_phase_ms(float *quant_ms, float *gemm_ms, float *total_ms);
+/* Fill the opcode-15 profile trailer (include/op_reg.h NativeW8A8Profile;
+ * reference op_reg.h:91-101, linear_w8a8.c:328-335, 396-399, 421-508) for an
+ * m x k x n run that just finished with profiling on: profile->mode (1, 2 or 3)
+ * is kept, every other field rewritten.  setup_ticks = setup_ms, and
+ * activation_ticks / hmx_ticks = this thread's last phase times, all in
+ * 19.2 MHz ticks; weight_ticks and output_ticks stay 0 (the weight stream and
+ * the output stores run inside the GEMM launch); mode 2: mac_ticks =
+ * hmx_ticks; mode 3: reserved = 64-row activation tiles | 64-column weight
+ * groups << 16 of one output tile (bit 31, the reference's table hit, stays 0),
+ * mac_ticks = weight tiles loaded, readout_ticks = weight bytes loaded.  Used
+ * by both hmx_mat_mul_native_w8a8_profiled and the 104-byte executor request. */
+int htpg_w8a8_profile_fill(int m, int k, int n, double setup_ms, struct NativeW8A8Profile *profile);
 
 /* Phase timing for benchmarks: while on, every run records CUDA events on its
  * stream before the activation pass, between it and the GEMM, and after the
@@ -268,6 +284,16 @@ int htpg_phase_timing_read(double *act_ms, double *gemm_ms, int *runs);
 
 /* Kernel launches issued by this library since load (for launch accounting). */
 uint64_t htpg_launch_count(void);
+
+/* Test hooks (no counterpart in the reference).  htpg_debug_simulate_abort
+ * leaves, on the current device, the state a launch that gave up can leave:
+ * every stream workspace (W8A8/FP16 split-K areas, opcode 2-4 stream-K
+ * scratch) filled with the byte `fill` and the watchdog word set.  The next
+ * htpg_check_device must then answer HTPG_EWATCHDOG and restore the zeroed
+ * scratch that later launches rely on.  htpg_debug_workspaces reports the
+ * bytes held by the stream workspaces of the current device. */
+int htpg_debug_simulate_abort(uint32_t fill);
+int htpg_debug_workspaces(size_t *ws_bytes, size_t *qws_bytes);
 
 /* Tile plan the library uses for an m x n x k problem (kind 0 = W8A8,
  * 1 = FP16) on a device with `sms` SMs.  out[0..9] = swap, bn, splits,
@@ -281,18 +307,11 @@ int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]);
  * Both give identical results; the switch exists for measurement. */
 int htpg_set_decode_kernel(int which);
 
-/* Which kernel runs W8A8 problems planned as CTA-pair tiles with k <= 1536, one
- * row-major output and modes 0-2 or 4: 1 the kernel that keeps each CTA's
- * weight columns in tensor memory and streams only activation tiles through
- * shared memory, 0 the CTA-pair kernel that streams both.  Both give identical
- * results; the switch exists for measurement. */
-int htpg_set_tmem_weights(int on);
 
 /* ---- reference kernel-level names (reference: include/dsp/ops.h:20-31) ---
  * Same arguments and return codes as the DSP kernels, on device pointers;
  * synchronous (they return once the output is written).  The FP16 weight
  * type __fp16 of the reference is passed as its 16-bit pattern. */
-struct NativeW8A8Profile;
 int hmx_mat_mul_native_w8a8(float *dst, const float *activation, const uint8_t *constants, int m,
                             int k, int n);
 int hmx_mat_mul_native_w8a8_profiled(float *dst, const float *activation, const uint8_t *constants,
