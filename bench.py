@@ -578,6 +578,9 @@ def main():
                     help="N>1: how the column blocks reach every rank")
     ap.add_argument("--suite-only", default=None,
                     help="run only this suite config (e.g. C5_up_M16) and print its timings; for profiling")
+    ap.add_argument("--pair-direct", type=int, default=1, choices=[0, 1],
+                    help="W8A8 CTA-pair problems: 1 swapped orientation with register stores (default), "
+                         "0 normal orientation with staged TMA stores")
     ap.add_argument("--decode-kernel", default="reg", choices=["reg", "tc"],
                     help="kernel for W8A8 m <= 16: register-fed decode (default) or swapped tcgen05")
     ap.add_argument("--m", type=int, default=M_C4,
@@ -602,6 +605,7 @@ def main():
     L = htpg.lib()
     htpg.check(L.htpg_init(local), "htpg_init")
     htpg.set_decode_kernel(0 if args.decode_kernel == "reg" else 1)
+    htpg.set_pair_direct(bool(args.pair_direct))
     if args.suite_only:
         res = suite(torch, L, htpg, dev, L2Flush(torch, dev), only=args.suite_only)
         htpg.check(htpg.check_device(), "watchdog")
@@ -763,10 +767,17 @@ def main():
             roof["traffic"] = tr
     except Exception:
         pass
-    plan = htpg.plan_info(0, m, n_loc, k)
-    pair = plan["swap"] == 0 and plan["tiles_a"] == (m + 255) // 256   # 256-row CTA-pair tiles
-    roof["kernel"] = (f"gemm2_kernel<I8,{plan['bn']}> (CTA-pair tcgen05 kind::i8 + fused dequant/bias/GELU)" if pair
-                      else f"gemm_kernel<I8,{plan['bn']},false> (tcgen05 kind::i8 + fused dequant/bias/GELU)")
+    plan = htpg.plan_info(0, m, n_loc, k) if not (world > 1 and fused) else None
+    if plan is None:
+        roof["kernel"] = "gemm2_kernel<I8,256,false> (CTA-pair tcgen05 kind::i8, TMA stores to every rank)"
+    elif plan["swap"] == 3:
+        roof["kernel"] = (f"gemm2_kernel<I8,{plan['bn']},true> (CTA-pair tcgen05 kind::i8, swapped orientation, "
+                          "fused dequant/bias/GELU, stores from registers)")
+    elif plan["swap"] == 0 and plan["tiles_a"] == (m + 255) // 256:
+        roof["kernel"] = (f"gemm2_kernel<I8,{plan['bn']},false> (CTA-pair tcgen05 kind::i8 + fused "
+                          "dequant/bias/GELU, TMA stores)")
+    else:
+        roof["kernel"] = f"gemm_kernel<I8,{plan['bn']},false> (tcgen05 kind::i8 + fused dequant/bias/GELU)"
     roof["peak_source"] = f"hbm {peak_kind} burst copy; tensor = 2 x {peak_kind} dense BF16 burst"
     roof["hbm_frac"] = gemm_bytes / (gemm_avg_ms * 1e-3) / 1e9 / hbm
     roof["tensor_frac"] = gemm_ops / (gemm_avg_ms * 1e-3) / 1e12 / int8_peak

@@ -346,10 +346,16 @@ extern "C" int htpg_phase_timing_read(double *act_ms, double *gemm_ms, int *runs
 
 extern "C" int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]) {
   if (!out || m < 1 || n < 1 || k < 1 || sms < 1 || (kind != 0 && kind != 1)) return HTPG_EARGS;
-  const GemmPlan p = plan_gemm(kind == 0 ? Kind::I8 : Kind::F16, m, n, k, sms);
-  const int64_t v[10] = {p.reg ? 2 : p.swap ? 1 : 0, p.bn, p.splits, p.tiles_a, p.tiles_b, p.kb_total,
-                         p.kb_per_split, p.units, p.grid, static_cast<int64_t>(p.smem)};
+  const GemmPlan p = plan_for(kind == 0 ? Kind::I8 : Kind::F16, m, n, k, sms, 0, 1);
+  const int64_t v[10] = {p.reg ? 2 : p.swap ? 1 : p.pair_sw ? 3 : 0, p.bn, p.splits, p.tiles_a, p.tiles_b,
+                         p.kb_total, p.kb_per_split, p.units, p.grid, static_cast<int64_t>(p.smem)};
   for (int i = 0; i < 10; ++i) out[i] = v[i];
+  return HTPG_OK;
+}
+
+extern "C" int htpg_set_pair_direct(int on) {
+  if (on != 0 && on != 1) return HTPG_EARGS;
+  g_pair_direct.store(on);
   return HTPG_OK;
 }
 
@@ -542,9 +548,11 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
   cudaStream_t st = pick_stream(d, stream);
   std::lock_guard<std::mutex> lk(g_mu);
 
-  const GemmPlan plan = plan_gemm(w->kind, m, n, k, d->sms);
+  const GemmPlan plan = plan_for(w->kind, m, n, k, d->sms, mode, n_outs);
   // several destinations need the TMA-store epilogue (normal orientation, row-major, aligned)
-  if (n_outs > 1 && (plan.swap || mode == 3 || !tma_store_ok(out, ldo))) return HTPG_ECAPACITY;
+  if (n_outs > 1 && (plan.swap || plan.pair_sw || mode == 3 || !tma_store_ok(out, ldo))) return HTPG_ECAPACITY;
+  // the weight is the A operand of swapped plans (small M and swapped CTA pairs)
+  const bool w_is_a = plan.swap || plan.pair_sw;
   // Workspace: [split-K accumulators + counters | activation codes / FP16 | row scales].
   // The split-K region sits at a fixed offset and is kept all-zero (zeroed at
   // allocation, left zeroed by every launch), so no per-call clear is needed.
@@ -587,9 +595,10 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
 
   CUtensorMap act_map;
   const CUtensorMap *wmap = nullptr;
-  rc = make_map(&act_map, act, w->kind, k, m, static_cast<size_t>(k) * act_elem, plan.swap ? plan.bn : 128);
+  rc = make_map(&act_map, act, w->kind, k, m, static_cast<size_t>(k) * act_elem,
+                plan.pair_sw ? plan.bn / 2 : plan.swap ? plan.bn : 128);
   if (rc) return rc;
-  rc = weight_map(w, plan.swap ? 128 : box_rows_b(plan), &wmap);
+  rc = weight_map(w, w_is_a ? 128 : box_rows_b(plan), &wmap);
   if (rc) return rc;
 
   GemmArgs a;
@@ -615,7 +624,7 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
   OutMaps out_maps;
   if (mode == HTPG_MODE_PLANES) {
     a.tma_store = tma_store_ok(out, ldo) ? 1 : 0;  // 16-byte aligned rows: vector plane stores
-  } else if (!plan.swap && mode != 3 && tma_store_ok(out, ldo)) {
+  } else if (!w_is_a && mode != 3 && tma_store_ok(out, ldo)) {
     for (int i = 0; i < n_outs; ++i) {
       if (!tma_store_ok(outs[i], ldo)) return HTPG_ECONTROL;
       rc = make_out_map(&out_maps.map[i], outs[i], m, n, ldo);
@@ -624,8 +633,8 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
     out_maps.count = n_outs;
     a.tma_store = 1;
   }
-  e = plan.swap ? launch_gemm(plan, *wmap, act_map, out_maps, a, st)
-                : launch_gemm(plan, act_map, *wmap, out_maps, a, st);
+  e = w_is_a ? launch_gemm(plan, *wmap, act_map, out_maps, a, st)
+             : launch_gemm(plan, act_map, *wmap, out_maps, a, st);
   if (e != cudaSuccess) return record_cuda(e);
   if (phase) {
     cudaEventRecord(pe.e[2], st);
@@ -928,7 +937,8 @@ int htpg::w8a8_run_in_scratch(const htpg_weights *w, float *out, int ldo, const 
   cudaStream_t st = pick_stream(d, stream);
   std::lock_guard<std::mutex> lk(g_mu);
 
-  const GemmPlan plan = plan_gemm(Kind::I8, m, n, k, d->sms);
+  const GemmPlan plan = plan_for(Kind::I8, m, n, k, d->sms, mode, 1);
+  const bool w_is_a = plan.swap || plan.pair_sw;
   const size_t splitk_bytes = splitk_ws_bytes(plan) + splitk_count_bytes(plan);
   if (splitk_bytes > kSplitKRegion) return HTPG_ENOPLAN;
   uint8_t *base = static_cast<uint8_t *>(scratch);
@@ -946,9 +956,10 @@ int htpg::w8a8_run_in_scratch(const htpg_weights *w, float *out, int ldo, const 
 
   CUtensorMap act_map;
   const CUtensorMap *wmap = nullptr;
-  rc = make_map(&act_map, act, Kind::I8, k, m, static_cast<size_t>(k), plan.swap ? plan.bn : 128);
+  rc = make_map(&act_map, act, Kind::I8, k, m, static_cast<size_t>(k),
+                plan.pair_sw ? plan.bn / 2 : plan.swap ? plan.bn : 128);
   if (rc) return rc;
-  rc = weight_map(const_cast<htpg_weights *>(w), plan.swap ? 128 : box_rows_b(plan), &wmap);
+  rc = weight_map(const_cast<htpg_weights *>(w), w_is_a ? 128 : box_rows_b(plan), &wmap);
   if (rc) return rc;
   GemmArgs a;
   a.M = m;
@@ -969,14 +980,14 @@ int htpg::w8a8_run_in_scratch(const htpg_weights *w, float *out, int ldo, const 
   a.wk = w->wk;
   a.act = act;
   OutMaps out_maps;
-  if (!plan.swap && mode != 3 && tma_store_ok(out, ldo)) {
+  if (!w_is_a && mode != 3 && tma_store_ok(out, ldo)) {
     rc = make_out_map(&out_maps.map[0], out, m, n, ldo);
     if (rc) return rc;
     out_maps.count = 1;
     a.tma_store = 1;
   }
-  e = plan.swap ? launch_gemm(plan, *wmap, act_map, out_maps, a, st)
-                : launch_gemm(plan, act_map, *wmap, out_maps, a, st);
+  e = w_is_a ? launch_gemm(plan, *wmap, act_map, out_maps, a, st)
+             : launch_gemm(plan, act_map, *wmap, out_maps, a, st);
   return record_cuda(e);
 }
 
@@ -1269,16 +1280,19 @@ extern "C" int htpg_w8a8_profile_fill(int m, int k, int n, double setup_ms, stru
   if (mode == 3) {
     int dev = 0;
     cudaGetDevice(&dev);
-    const GemmPlan p = plan_gemm(Kind::I8, m, n, k, dev >= 0 && dev < 16 && g_dev[dev].sms ? g_dev[dev].sms : 148);
+    const GemmPlan p =
+        plan_for(Kind::I8, m, n, k, dev >= 0 && dev < 16 && g_dev[dev].sms ? g_dev[dev].sms : 148, 0, 1);
     // low 16 bits: 64-row activation tiles per output tile; high 16 bits:
     // 64-column weight groups per output tile; bit 31 (table hit) stays 0,
     // every plan here comes from the shape-keyed planner
-    const uint32_t rows64 = p.swap ? 1u : p.pair ? 4u : 2u;
-    const uint32_t cols64 = static_cast<uint32_t>(p.swap ? 2 : (p.bn >= 64 ? p.bn / 64 : 1));
+    const int act_rows = p.swap ? 64 : p.pair_sw ? p.bn : p.pair ? 256 : 128;
+    const int w_cols = p.swap ? 128 : p.pair_sw ? 256 : p.bn;
+    const uint32_t rows64 = static_cast<uint32_t>(act_rows / 64);
+    const uint32_t cols64 = static_cast<uint32_t>(w_cols >= 64 ? w_cols / 64 : 1);
     profile->reserved = rows64 | (cols64 << 16);
     profile->mac_ticks = static_cast<uint64_t>(p.units);  // weight tiles loaded
     profile->readout_ticks = p.reg ? static_cast<uint64_t>(p.tiles_a) * 16u * p.kb_total * 128u
-                                   : static_cast<uint64_t>(p.units) * static_cast<uint64_t>(p.swap ? 128 : p.bn) *
+                                   : static_cast<uint64_t>(p.units) * static_cast<uint64_t>(w_cols) *
                                          static_cast<uint64_t>(p.kb_per_split) * 128u;  // weight bytes loaded
   }
   return HTPG_OK;

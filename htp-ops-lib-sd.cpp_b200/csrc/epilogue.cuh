@@ -60,10 +60,7 @@ __device__ __forceinline__ float finish(uint32_t acc, int32_t corr, float sw, fl
 
 // Packed FP32x2 arithmetic (two output elements per instruction).  Each lane
 // is the IEEE round-to-nearest operation of the scalar form, so finish2 gives
-// the bits of finish for both elements.  The bias add stays scalar
-// (__fadd_rn): a packed add after a packed multiply was measured to be
-// contracted into one fused multiply-add (one rounding instead of two), which
-// changes the bits.
+// the bits of finish for both elements.
 __device__ __forceinline__ uint64_t pk2(float a, float b) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
@@ -83,10 +80,14 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
   return d;
 }
 // finish<Kind::I8, MODE, BIAS> for two accumulators of the same column
-// (column scale sw2 = {sw, sw}, row scales rs0 and rs1).
+// (column scale sw2 = {sw, sw}, row scales rs0 and rs1, bias2 = {b, b}).  The
+// bias add is fma(v, one, b): with one = 1.0 that is the single rounding of
+// v + b, the bits of __fadd_rn, in one packed instruction.  `one` must come
+// from kernel arguments: a literal 1.0 lets ptxas fold the multiplication and
+// contract the add into the preceding multiply, which rounds differently.
 template <int MODE, bool BIAS>
 __device__ __forceinline__ void finish2(uint32_t a0, uint32_t a1, int32_t cr, uint64_t sw2, float rs0, float rs1,
-                                        float bias, float &o0, float &o1) {
+                                        uint64_t bias2, uint64_t one2, float &o0, float &o1) {
   const int32_t y0 = static_cast<int32_t>(a0 + static_cast<uint32_t>(cr));
   const int32_t y1 = static_cast<int32_t>(a1 + static_cast<uint32_t>(cr));
   if constexpr (MODE == 4) {
@@ -95,11 +96,7 @@ __device__ __forceinline__ void finish2(uint32_t a0, uint32_t a1, int32_t cr, ui
     return;
   } else {
     uint64_t v = mul2(mul2(pk2(__int2float_rn(y0), __int2float_rn(y1)), sw2), pk2(rs0, rs1));
-    if constexpr (BIAS) {
-      float v0, v1;
-      upk2(v, v0, v1);
-      v = pk2(__fadd_rn(v0, bias), __fadd_rn(v1, bias));
-    }
+    if constexpr (BIAS) v = fma2(v, one2, bias2);
     if constexpr (MODE == 1 || MODE == 2) {
       uint64_t h;
       if constexpr (MODE == 1) {

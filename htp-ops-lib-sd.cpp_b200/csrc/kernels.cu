@@ -608,7 +608,7 @@ __device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
     tc_fence_after();
     if (ok && c.lane == 0) {
       if (c.empty_remote)
-        mbar_arrive_cluster(c.empty_bar);
+        mbar_arrive_cluster_relaxed(c.empty_bar);
       else
         mbar_arrive(c.empty_bar);
     }
@@ -650,7 +650,7 @@ __device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
   __syncwarp();
   if (c.lane == 0) {
     if (c.empty_remote)
-      mbar_arrive_cluster(c.empty_bar);
+      mbar_arrive_cluster_relaxed(c.empty_bar);
     else
       mbar_arrive(c.empty_bar);
   }
@@ -1091,24 +1091,181 @@ __global__ void __launch_bounds__(kThreads, 1)
 // operands through shared memory per 128 x 256 x 32 MMA step, which is what
 // lets the tensor pipe run past the shared-memory bandwidth ceiling of the
 // single-CTA tile.
-__host__ __device__ constexpr int stages2_for(int bn) {
-  return (kSmemLimit - 1024 - 256 - kEpiSmem) / ((128 + bn / 2) * kRowBytes) < 10
-             ? (kSmemLimit - 1024 - 256 - kEpiSmem) / ((128 + bn / 2) * kRowBytes)
+// Epilogue shared memory of the pair kernel: the staging tiles and column
+// parameters of the TMA-store epilogue, or (swapped orientation, stores from
+// registers) only the per-warp row-scale slots.
+__host__ __device__ constexpr int epi2_smem_for(bool sw) { return sw ? kEpiWarps * kWarpParams * 4 : kEpiSmem; }
+__host__ __device__ constexpr int stages2_for(int bn, bool sw = false) {
+  return (kSmemLimit - 1024 - 256 - epi2_smem_for(sw)) / ((128 + bn / 2) * kRowBytes) < 10
+             ? (kSmemLimit - 1024 - 256 - epi2_smem_for(sw)) / ((128 + bn / 2) * kRowBytes)
              : 10;
 }
-__host__ __device__ constexpr size_t smem2_bytes_for(int bn) {
-  return 1024 + static_cast<size_t>(stages2_for(bn)) * (128 + bn / 2) * kRowBytes +
-         static_cast<size_t>(kEpiSmem) + 256;
+__host__ __device__ constexpr size_t smem2_bytes_for(int bn, bool sw = false) {
+  return 1024 + static_cast<size_t>(stages2_for(bn, sw)) * (128 + bn / 2) * kRowBytes +
+         static_cast<size_t>(epi2_smem_for(sw)) + 256;
 }
-static_assert(smem2_bytes_for(256) <= kSmemLimit && smem2_bytes_for(128) <= kSmemLimit,
+static_assert(smem2_bytes_for(256) <= kSmemLimit && smem2_bytes_for(128) <= kSmemLimit &&
+                  smem2_bytes_for(256, true) <= kSmemLimit && smem2_bytes_for(128, true) <= kSmemLimit,
               "shared memory budget (pair)");
 
+// Shared-memory carve-up of the pair kernel (one k-block per stage).
+template <int BH, int STAGES, bool SW>
+__device__ __forceinline__ SmemLayout carve2(uint8_t *raw) {
+  SmemLayout L;
+  uint8_t *p = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  L.a = p;
+  p += STAGES * 128 * kRowBytes;
+  L.b = p;
+  p += STAGES * BH * kRowBytes;
+  L.scratch = reinterpret_cast<float *>(p);  // the swapped orientation stages nothing
+  if (!SW) p += kEpiWarps * kWarpScratch * 4;
+  L.params = reinterpret_cast<float *>(p);
+  p += kEpiWarps * kWarpParams * 4;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(p);
+  L.full = bars;
+  L.empty = bars + STAGES;
+  L.tfull = bars + 2 * STAGES;
+  L.tempty = bars + 2 * STAGES + 2;
+  L.mma_done = bars + 2 * STAGES + 4;
+  L.tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
+  L.flag = L.tmem_slot + 1;
+  L.abort = L.tmem_slot + 2;
+  return L;
+}
+
+// Swapped orientation of the pair tile (weights are the 256-row MMA operand,
+// activations the MMA N): TMEM lane = output column n, TMEM column = activation
+// row m.  Each epilogue warp owns 32 columns (its lane quadrant) and BN/4 rows
+// (its part) of every unit.  Per row, the warp's 32 lanes store 32
+// consecutive FP32 outputs: one 128-byte line per store instruction, straight
+// from registers, so the output never passes through shared memory.  Column
+// scale, correction and bias are per-thread constants, the rows' scales are
+// read as shared-memory broadcasts, and both are fetched one unit ahead so
+// their global-load latency hides behind the current unit's arithmetic.  The
+// whole unit loop lives here (one dispatch on the epilogue mode per launch).
+template <Kind KIND, int BN, int MODE, bool BIAS>
+__device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const KernelParams &P, const SmemLayout &L,
+                                                 float *rs, uint32_t tmem_base, int q, int part, int lane,
+                                                 int pair, int npairs, uint32_t rank, uint32_t peer_abort) {
+  constexpr int kTok = BN / kEpiPerQuadrant;  // rows (TMEM columns) per warp and unit: 64 or 32
+  constexpr int kCh = kTok / 32;
+  static_assert(kTok <= kWarpParams, "row-scale slot per warp");
+  const uint32_t ldo4 = static_cast<uint32_t>(g.ldo) * 4u;  // bytes per output row (< 2^31 by the shape limits)
+  const uint64_t one2 = pk2(g.one, g.one);
+  float f_sw = 0.0f, f_bv = 0.0f, f_rs[kCh];
+  int32_t f_cr = 0;
+  auto fetch = [&](int u) {
+    const Unit w = decode_unit(u, P.tiles_b, 1);
+    const int n = w.ta * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+    const int m0 = w.tb * BN + part * kTok;
+    const bool ok = n < g.N;
+    f_sw = (KIND == Kind::I8 && ok) ? __ldg(g.col_scale + n) : 0.0f;
+    f_cr = (KIND == Kind::I8 && ok) ? __ldg(g.col_corr + n) : 0;
+    f_bv = (BIAS && ok) ? __ldg(g.bias + n) : 0.0f;
+#pragma unroll
+    for (int i = 0; i < kCh; ++i) {
+      const int m = m0 + 32 * i + lane;
+      f_rs[i] = (KIND == Kind::I8 && m < g.M) ? __ldg(g.row_scale + m) : 0.0f;
+    }
+  };
+  if (pair < P.units) fetch(pair);
+  uint32_t iter = 0;
+  for (int u = pair; u < P.units; u += npairs, ++iter) {
+    const Unit w = decode_unit(u, P.tiles_b, 1);
+    const uint32_t buf = iter & 1u;
+    const int n = w.ta * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+    const bool n_ok = n < g.N;
+    const int m0 = w.tb * BN + part * kTok;
+    // this unit's parameters (the f_ registers are refilled for the next unit below)
+    const float sw = f_sw, bv = f_bv;
+    const uint64_t bias2 = pk2(bv, bv);
+    const int32_t cr = f_cr;
+    __syncwarp();  // the previous unit's reads of the row-scale slot are complete
+#pragma unroll
+    for (int i = 0; i < kCh; ++i) rs[32 * i + lane] = f_rs[i];
+    __syncwarp();
+    if (u + npairs < P.units) fetch(u + npairs);
+    const bool ok = mbar_wait(smem_u32(&L.tfull[buf]), (iter >> 1) & 1u, g.watchdog, kWatchEpilogue, L.abort);
+    tc_fence_after();
+    if (!ok) {
+      st_shared_cluster(peer_abort, 1u);
+      return;
+    }
+    uint32_t r[kCh][32];
+    const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN + part * kTok;
+#pragma unroll
+    for (int i = 0; i < kCh; ++i) tmem_ld32(t_row + 32 * i, r[i]);
+    tmem_ld_wait();
+    tc_fence_before();
+    __syncwarp();
+    // the accumulator goes back to the pair leader's MMA issuer
+    if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&L.tempty[buf]), 0));
+    if (!n_ok) continue;
+#pragma unroll
+    for (int i = 0; i < kCh; ++i) {
+      const int mb = m0 + 32 * i;
+      if (mb >= g.M) break;
+      char *base = reinterpret_cast<char *>(g.out + static_cast<long long>(mb) * g.ldo + n);
+      const float *rsi = rs + 32 * i;
+      auto row = [&](int j) {
+        return reinterpret_cast<float *>(base + static_cast<unsigned long long>(ldo4) * static_cast<unsigned>(j));
+      };
+      if (mb + 32 <= g.M) {
+        if constexpr (KIND == Kind::I8) {
+          const uint64_t sw2 = pk2(sw, sw);
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 s4 = *reinterpret_cast<const float4 *>(rsi + 4 * j4);
+            float o0, o1, o2, o3;
+            finish2<MODE, BIAS>(r[i][4 * j4], r[i][4 * j4 + 1], cr, sw2, s4.x, s4.y, bias2, one2, o0, o1);
+            finish2<MODE, BIAS>(r[i][4 * j4 + 2], r[i][4 * j4 + 3], cr, sw2, s4.z, s4.w, bias2, one2, o2, o3);
+            *row(4 * j4) = o0;
+            *row(4 * j4 + 1) = o1;
+            *row(4 * j4 + 2) = o2;
+            *row(4 * j4 + 3) = o3;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) *row(j) = finish<KIND, MODE, BIAS>(r[i][j], 0, 0.0f, 0.0f, bv);
+        }
+      } else {
+        for (int j = 0; j < 32 && mb + j < g.M; ++j)
+          *row(j) = finish<KIND, MODE, BIAS>(r[i][j], cr, sw, KIND == Kind::I8 ? rsi[j] : 0.0f, bv);
+      }
+    }
+  }
+}
+
 template <Kind KIND, int BN>
+__device__ __forceinline__ void epilogue_loop_sw_dispatch(const GemmArgs &g, const KernelParams &P,
+                                                          const SmemLayout &L, float *rs, uint32_t tmem_base, int q,
+                                                          int part, int lane, int pair, int npairs, uint32_t rank,
+                                                          uint32_t peer_abort) {
+#define HTPG_SW_LOOP(M_, B_) \
+  epilogue_loop_sw<KIND, BN, M_, B_>(g, P, L, rs, tmem_base, q, part, lane, pair, npairs, rank, peer_abort)
+  switch (g.mode * 2 + (g.bias ? 1 : 0)) {
+    case 0: HTPG_SW_LOOP(0, false); break;
+    case 1: HTPG_SW_LOOP(0, true); break;
+    case 2: HTPG_SW_LOOP(1, false); break;
+    case 3: HTPG_SW_LOOP(1, true); break;
+    case 4: HTPG_SW_LOOP(2, false); break;
+    case 5: HTPG_SW_LOOP(2, true); break;
+    default: HTPG_SW_LOOP(4, false); break;
+  }
+#undef HTPG_SW_LOOP
+}
+
+// SW (swapped orientation): A = the weight (tile ta: columns ta*256 + r*128
+// in CTA r), B = the activation codes (tile tb: rows tb*BN + r*BN/2), and the
+// epilogue stores from registers (epilogue_pair_sw).  Otherwise A = the
+// activation codes (rows ta*256 + r*128), B = the weight (columns tb*BN +
+// r*BN/2) and the epilogue leaves through TMA stores.
+template <Kind KIND, int BN, bool SW>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ OutMaps tmOut, const KernelParams P) {
   constexpr int BH = BN / 2;  // B rows held by each CTA
-  constexpr int STAGES = stages2_for(BN);
+  constexpr int STAGES = stages2_for(BN, SW);
   constexpr int TCOLS = tmem_cols_for(BN);
   constexpr uint32_t kStageBytes = (128 + BH) * kRowBytes;  // per CTA
   constexpr int kElemsPerRow = KIND == Kind::I8 ? 128 : 64;
@@ -1116,7 +1273,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
 
   extern __shared__ uint8_t smem_raw[];
-  const SmemLayout L = carve<BH, STAGES>(smem_raw);
+  const SmemLayout L = carve2<BH, STAGES, SW>(smem_raw);
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   const GemmArgs &g = P.a;
@@ -1161,7 +1318,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
-      // this CTA's half of its first weight tile goes into the ring (the next
+      // this CTA's part of the weight tile of k-block kb and unit w (into ring
+      // stage s), and its part of the activation tile
+      auto load_weight = [&](int s, int kb, const Unit &w, uint32_t fb) {
+        if (SW)
+          tma_load_2d_pair(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, 0,
+                           kb * g.N + w.ta * 256 + static_cast<int>(rank) * 128);
+        else
+          tma_load_2d_pair(smem_u32(L.b + s * BH * kRowBytes), &tmB, fb, 0,
+                           kb * g.N + w.tb * BN + static_cast<int>(rank) * BH);
+      };
+      auto load_act = [&](int s, int kb, const Unit &w, uint32_t fb) {
+        if (SW)
+          tma_load_2d_pair(smem_u32(L.b + s * BH * kRowBytes), &tmB, fb, kb * kElemsPerRow,
+                           w.tb * BN + static_cast<int>(rank) * BH);
+        else
+          tma_load_2d_pair(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, kb * kElemsPerRow,
+                           w.ta * 256 + static_cast<int>(rank) * 128);
+      };
+      // this CTA's part of its first weight tile goes into the ring (the next
       // k-blocks into the L2) before waiting for the activation pass
       int pre = 0;
       if (pair < P.units) {
@@ -1170,12 +1345,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int i = 0; i < pre; ++i) {
           const uint32_t fb_local = smem_u32(&L.full[i]);
           if (leader) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);
-          tma_load_2d_pair(smem_u32(L.b + i * BH * kRowBytes), &tmB, mapa_shared(fb_local, 0), 0,
-                           i * g.N + w.tb * BN + static_cast<int>(rank) * BH);
+          load_weight(i, i, w, mapa_shared(fb_local, 0));
         }
-        const int kb2 = min(P.kb_total, kPrefetchBytes / (BH * kRowBytes));
-        for (int kb = pre; kb < kb2; ++kb)
-          tma_prefetch_l2_2d(&tmB, 0, kb * g.N + w.tb * BN + static_cast<int>(rank) * BH);
+        constexpr int kWRows = SW ? 128 : BH;  // weight rows this CTA loads per k-block
+        const int kb2 = min(P.kb_total, kPrefetchBytes / (kWRows * kRowBytes));
+        for (int kb = pre; kb < kb2; ++kb) {
+          if (SW)
+            tma_prefetch_l2_2d(&tmA, 0, kb * g.N + w.ta * 256 + static_cast<int>(rank) * 128);
+          else
+            tma_prefetch_l2_2d(&tmB, 0, kb * g.N + w.tb * BN + static_cast<int>(rank) * BH);
+        }
       }
       grid_dependency_wait();
       int s = 0;
@@ -1196,11 +1375,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const bool weight_done = first && kb < pre;
           if (leader && !weight_done) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);
           const uint32_t fb = mapa_shared(fb_local, 0);
-          tma_load_2d_pair(smem_u32(L.a + s * 128 * kRowBytes), &tmA, fb, kb * kElemsPerRow,
-                           w.ta * 256 + static_cast<int>(rank) * 128);
-          if (!weight_done)
-            tma_load_2d_pair(smem_u32(L.b + s * BH * kRowBytes), &tmB, fb, 0,
-                             kb * g.N + w.tb * BN + static_cast<int>(rank) * BH);
+          load_act(s, kb, w, fb);
+          if (!weight_done) load_weight(s, kb, w, fb);
           last_phase[s] = static_cast<int>(ph);
           if (++s == STAGES) {
             s = 0;
@@ -1273,21 +1449,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     c.prm = L.params + (warp - 2) * kWarpParams;
     const bool has_bias = g.bias != nullptr;
     grid_dependency_wait();  // row scales come from the activation pass
-    uint32_t iter = 0;
-    for (int u = pair; u < P.units; u += npairs, ++iter) {
-      c.w = decode_unit(u, P.tiles_b, 1);
-      const uint32_t buf = iter & 1u;
-      c.full_bar = smem_u32(&L.tfull[buf]);
-      c.full_parity = (iter >> 1) & 1u;
-      c.row0 = c.w.ta * 256 + static_cast<int>(rank) * 128;
-      c.t_row = tmem_base + (static_cast<uint32_t>(c.q * 32) << 16) + buf * BN;
-      c.empty_bar = mapa_shared(smem_u32(&L.tempty[buf]), 0);
-      c.empty_remote = true;
-      // the epilogue hands the buffer back to the leader once its TMEM reads are done
-      const bool ok = epilogue_dispatch<KIND, BN, false>(c, g.mode, has_bias);
-      if (!ok) st_shared_cluster(peer_abort, 1u);
+    if constexpr (SW) {
+      epilogue_loop_sw_dispatch<KIND, BN>(g, P, L, c.prm, tmem_base, c.q, c.part, lane, pair, npairs, rank,
+                                          peer_abort);
+    } else {
+      uint32_t iter = 0;
+      for (int u = pair; u < P.units; u += npairs, ++iter) {
+        c.w = decode_unit(u, P.tiles_b, 1);
+        const uint32_t buf = iter & 1u;
+        c.full_bar = smem_u32(&L.tfull[buf]);
+        c.full_parity = (iter >> 1) & 1u;
+        c.row0 = c.w.ta * 256 + static_cast<int>(rank) * 128;
+        c.t_row = tmem_base + (static_cast<uint32_t>(c.q * 32) << 16) + buf * BN;
+        c.empty_bar = mapa_shared(smem_u32(&L.tempty[buf]), 0);
+        c.empty_remote = true;
+        // the epilogue hands the buffer back to the leader once its TMEM reads are done
+        const bool ok = epilogue_dispatch<KIND, BN, false>(c, g.mode, has_bias);
+        if (!ok) st_shared_cluster(peer_abort, 1u);
+      }
+      if (lane == 0) bulk_wait_all();
     }
-    if (lane == 0) bulk_wait_all();
   }
 
   // the leader's MMAs (which read both CTAs' shared memory) are complete and
@@ -1384,6 +1565,41 @@ GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms) {
   return p;
 }
 
+// The swapped orientation of a CTA-pair plan: 256-column weight tiles (the
+// pair's MMA M) by BN-row activation tiles (MMA N), BN in {256, 128} by the
+// same wave cost as the normal orientation.  Its epilogue stores from
+// registers, which serves row-major outputs (modes 0-2 and the raw mode 4) of
+// one destination; the channel-major store (mode 3), the plane export (mode 5)
+// and the multi-destination run keep the normal orientation.
+std::atomic<int> g_pair_direct{1};
+
+bool pair_sw_eligible(const GemmPlan &p, int mode, int n_outs) {
+  return p.pair && p.kind == Kind::I8 && n_outs == 1 && (mode == 0 || mode == 1 || mode == 2 || mode == 4) &&
+         g_pair_direct.load() != 0;
+}
+
+GemmPlan plan_pair_sw(const GemmPlan &normal, int M, int N, int num_sms) {
+  GemmPlan p = normal;
+  const int pairs = num_sms / 2;
+  const long long tw = (N + 255) / 256;
+  const long long u256 = tw * ((M + 255) / 256), u128 = tw * ((M + 127) / 128);
+  const long long cost256 = (u256 + pairs - 1) / pairs * 256;
+  const long long cost128 = (u128 + pairs - 1) / pairs * 128;
+  p.pair_sw = true;
+  p.bn = cost256 <= cost128 ? 256 : 128;
+  p.tiles_a = static_cast<int>(tw);
+  p.tiles_b = (M + p.bn - 1) / p.bn;
+  p.units = p.tiles_a * p.tiles_b;
+  p.grid = 2 * (p.units < pairs ? p.units : pairs);
+  p.smem = smem2_bytes_for(p.bn, true);
+  return p;
+}
+
+GemmPlan plan_for(Kind kind, int M, int N, int K, int num_sms, int mode, int n_outs) {
+  const GemmPlan p = plan_gemm(kind, M, N, K, num_sms);
+  return pair_sw_eligible(p, mode, n_outs) ? plan_pair_sw(p, M, N, num_sms) : p;
+}
+
 size_t splitk_ws_bytes(const GemmPlan &p) {
   if (p.reg) return decode_ws_bytes(p);
   return p.splits > 1 ? static_cast<size_t>(p.tiles_a) * p.tiles_b * 128 * p.bn * 4 : 0;
@@ -1438,14 +1654,14 @@ static cudaError_t launch_one(const GemmPlan &p, const CUtensorMap &tmA, const C
   return counted(launch_dependent(fn, p.grid, smem, st, tmA, tmB, tmOut, P));
 }
 
-template <Kind KIND, int BN>
+template <Kind KIND, int BN, bool SW>
 static cudaError_t launch_pair(const GemmPlan &p, const CUtensorMap &tmA, const CUtensorMap &tmB,
                                const OutMaps &tmOut, const GemmArgs &a, cudaStream_t st) {
-  auto fn = gemm2_kernel<KIND, BN>;
+  auto fn = gemm2_kernel<KIND, BN, SW>;
   static bool configured[64] = {};  // per instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
-  const size_t smem = smem2_bytes_for(BN);
+  const size_t smem = smem2_bytes_for(BN, SW);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1471,11 +1687,16 @@ cudaError_t launch_gemm(const GemmPlan &p, const CUtensorMap &tmA, const CUtenso
   if (p.pair) {
     if (p.grid % 2) return cudaErrorInvalidConfiguration;
     if (p.kind == Kind::I8) {
-      if (p.bn == 256) return launch_pair<Kind::I8, 256>(p, tmA, tmB, tmOut, a, st);
-      if (p.bn == 128) return launch_pair<Kind::I8, 128>(p, tmA, tmB, tmOut, a, st);
-    } else {
-      if (p.bn == 256) return launch_pair<Kind::F16, 256>(p, tmA, tmB, tmOut, a, st);
-      if (p.bn == 128) return launch_pair<Kind::F16, 128>(p, tmA, tmB, tmOut, a, st);
+      if (p.pair_sw) {
+        if (p.bn == 256) return launch_pair<Kind::I8, 256, true>(p, tmA, tmB, tmOut, a, st);
+        if (p.bn == 128) return launch_pair<Kind::I8, 128, true>(p, tmA, tmB, tmOut, a, st);
+      } else {
+        if (p.bn == 256) return launch_pair<Kind::I8, 256, false>(p, tmA, tmB, tmOut, a, st);
+        if (p.bn == 128) return launch_pair<Kind::I8, 128, false>(p, tmA, tmB, tmOut, a, st);
+      }
+    } else if (!p.pair_sw) {
+      if (p.bn == 256) return launch_pair<Kind::F16, 256, false>(p, tmA, tmB, tmOut, a, st);
+      if (p.bn == 128) return launch_pair<Kind::F16, 128, false>(p, tmA, tmB, tmOut, a, st);
     }
     return cudaErrorInvalidConfiguration;
   }

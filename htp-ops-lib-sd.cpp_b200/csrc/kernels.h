@@ -19,6 +19,8 @@ struct GemmPlan {
   Kind kind = Kind::I8;
   bool swap = false;
   bool pair = false;     // CTA-pair tiles of 256 rows (tcgen05.mma.cta_group::2)
+  bool pair_sw = false;  // pair tiles in the swapped orientation: A = the weight
+                         // (256 columns per tile), B = the activation (bn rows)
   bool reg = false;      // register-fed decode kernel (decode.cu); swap is also set
   int chunks = 0;        // reg: contiguous (column group, k-block) ranges, one per CTA pass
   int bn = 256;          // MMA N (rows of B per tile)
@@ -46,6 +48,7 @@ struct GemmArgs {
   int tma_store = 0;                 // row-major output written by TMA through tmOut
   const void *wk = nullptr;          // the weight rows [KB][N][128 B] (register-fed decode)
   const void *act = nullptr;         // the activation codes [M][K] (register-fed decode)
+  float one = 1.0f;                  // 1.0 as a runtime value (packed bias add, see finish2)
   int late_weights = 0;              // the weight is written by the kernels just before this
                                      // launch: no weight tile is loaded before the
                                      // programmatic-dependency wait (L2 prefetches only)
@@ -60,6 +63,10 @@ inline bool tma_store_ok(const float *out, long long ldo) {
 
 // Plan for an M x N x K problem (see plan_gemm in kernels.cu for the rules).
 GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms);
+// plan_gemm, with CTA-pair plans turned to the swapped orientation where the
+// register-store epilogue serves the output (mode, number of destinations).
+GemmPlan plan_for(Kind kind, int M, int N, int K, int num_sms, int mode, int n_outs);
+extern std::atomic<int> g_pair_direct;  // 0: CTA-pair plans keep the normal orientation
 // Bytes of split-K workspace (ws) and counters the plan needs.
 size_t splitk_ws_bytes(const GemmPlan &p);
 // Register-fed decode plan and launch (decode.cu).

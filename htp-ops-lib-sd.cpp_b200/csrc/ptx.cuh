@@ -315,6 +315,15 @@ __device__ __forceinline__ void st_shared_cluster(uint32_t cluster_addr, uint32_
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// The same arrive without release semantics.  For handing a TMEM accumulator
+// back to the MMA issuer after this thread's tcgen05.ld of it completed
+// (tcgen05.wait::ld, then tcgen05.fence::before_thread_sync): the loaded
+// values are already in registers, so nothing the arrive would release is
+// needed by the waiter, and a cluster-scope release would instead stall until
+// this thread's earlier global stores are performed.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 // 2-D tiled load into this CTA's shared memory whose transaction bytes are
 // counted on the pair leader's mbarrier (`bar` is a shared::cluster address).
 // No multicast: each CTA loads only its own operand halves.

@@ -90,6 +90,7 @@ def lib() -> ctypes.CDLL:
         "htpg_weight_cache_clear": (None, []),
         "htpg_set_profiling": (I, [I]),
         "htpg_set_decode_kernel": (I, [I]),
+        "htpg_set_pair_direct": (I, [I]),
         "htpg_last_phase_ms": (I, [ctypes.POINTER(ctypes.c_float)] * 3),
         "htpg_launch_count": (U64, []),
         "htpg_debug_simulate_abort": (I, [U32]),
@@ -248,6 +249,13 @@ def set_decode_kernel(which: int) -> None:
     """0: W8A8 problems with m <= 16 run the register-fed decode kernel (the
     default); 1: they run the swapped tcgen05 kernel.  Results are identical."""
     check(lib().htpg_set_decode_kernel(which), "htpg_set_decode_kernel")
+
+
+def set_pair_direct(on: bool) -> None:
+    """True (default): W8A8 CTA-pair problems with a row-major output run in the
+    swapped orientation with stores straight from registers; False: the normal
+    orientation with staged TMA stores.  Results are identical."""
+    check(lib().htpg_set_pair_direct(1 if on else 0), "htpg_set_pair_direct")
 
 
 def qk0_plan_info(weight_type: int, m: int, n: int, k: int, sms: int = 148) -> dict:

@@ -296,11 +296,24 @@ int htpg_debug_simulate_abort(uint32_t fill);
 int htpg_debug_workspaces(size_t *ws_bytes, size_t *qws_bytes);
 
 /* Tile plan the library uses for an m x n x k problem (kind 0 = W8A8,
- * 1 = FP16) on a device with `sms` SMs.  out[0..9] = swap, bn, splits,
- * tiles_a, tiles_b, kb_total, kb_per_split, units, grid, smem bytes.
- * swap = 2: the register-fed decode kernel (W8A8, m <= 16); then bn = 8 or
- * 16 activation rows, tiles_a = 16-column groups, units = work chunks. */
+ * 1 = FP16) with a row-major output on a device with `sms` SMs.  out[0..9] =
+ * swap, bn, splits, tiles_a, tiles_b, kb_total, kb_per_split, units, grid,
+ * smem bytes.  swap = 0: activation rows are the MMA M (128-row tiles, or
+ * 256-row CTA-pair tiles when tiles_a = ceil(m/256)), bn weight columns per
+ * tile; 1: small-M swapped tiles (weights are the MMA M); 2: the register-fed
+ * decode kernel (W8A8, m <= 16), bn = 8 or 16 activation rows, tiles_a =
+ * 16-column groups, units = work chunks; 3: CTA-pair tiles in the swapped
+ * orientation, tiles_a = 256-column weight tiles, bn activation rows per
+ * tile, stores straight from registers. */
 int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]);
+
+/* W8A8 CTA-pair plans with a row-major output of one destination (modes 0-2
+ * and 4): 1 (default) run them in the swapped orientation, whose epilogue
+ * writes each output row's 32 columns from registers as one 128-byte line;
+ * 0 keep the normal orientation, whose epilogue stages 32 x 32 tiles in shared
+ * memory for TMA stores.  Both give identical results; the switch exists for
+ * measurement. */
+int htpg_set_pair_direct(int on);
 
 /* Which kernel runs W8A8 problems with m <= 16: 0 (default) the register-fed
  * decode kernel, 1 the swapped tcgen05 kernel that also serves 16 < m <= 32.

@@ -381,9 +381,14 @@ def test_opcode15_profiled_trailer(lib, bufs, mode, m, k, n):
         assert reserved == 0 and mac == hmx and readout == 0
     else:
         assert reserved & 0x80000000 == 0          # no allocation table: never a "table hit"
-        # 64-row activation tiles per output tile: 1 (swapped), 2 (128 rows) or 4 (CTA pair)
-        assert reserved & 0xffff == 1 if plan["swap"] else reserved & 0xffff in (2, 4)
-        assert (reserved >> 16) == (2 if plan["swap"] else max(1, plan["bn"] // 64))
+        # low half: 64-row activation tiles per output tile; high half: 64-column weight groups
+        rows64, cols64 = reserved & 0xffff, reserved >> 16
+        if plan["swap"] in (1, 2):                 # small-M swapped tiles / register-fed decode
+            assert (rows64, cols64) == (1, 2)
+        elif plan["swap"] == 3:                    # CTA pair, swapped: 256 weight columns x bn rows
+            assert (rows64, cols64) == (plan["bn"] // 64, 4)
+        else:                                      # 128-row tiles or 256-row CTA-pair tiles
+            assert rows64 in (2, 4) and cols64 == max(1, plan["bn"] // 64)
         assert mac == plan["units"]
         assert readout >= k * n                    # every weight byte loaded at least once
 

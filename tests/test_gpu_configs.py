@@ -94,14 +94,14 @@ def test_c2(gpu, lib):
 def test_c3_dit_linears(gpu, layer):
     c = O.config_c3()[layer]
     plan = htpg.plan_info(0, c.m, c.n, c.k)
-    assert plan["swap"] == 0 and c.m == 4096
+    assert plan["swap"] in (0, 3) and c.m == 4096     # CTA-pair tiles, either orientation
     _check_w8a8(gpu, c)
 
 
 def test_c4_every_row(gpu):
     c = O.config_c4()
     plan = htpg.plan_info(0, c.m, c.n, c.k)
-    assert plan["swap"] == 0 and plan["bn"] == 256
+    assert plan["swap"] == 3 and plan["bn"] == 256    # 256 x 256 CTA-pair tiles, swapped orientation
     _check_w8a8(gpu, c)
 
 

@@ -47,7 +47,11 @@ def test_plans_are_legal(kind, sms):
         # K ranges: every split non-empty, together exactly [0, kb_total)
         assert p["splits"] * p["kb_per_split"] >= kb_total
         assert (p["splits"] - 1) * p["kb_per_split"] < kb_total
-        if p["swap"]:
+        if p["swap"] == 3:
+            # CTA pair in the swapped orientation: 256-column weight tiles x bn rows
+            assert kind == 0 and m > 128 and p["bn"] in (128, 256) and p["splits"] == 1
+            assert p["tiles_a"] == -(-n // 256) and p["tiles_b"] == -(-m // p["bn"]) and p["grid"] % 2 == 0
+        elif p["swap"]:
             assert kind == 0 and m <= 32 and p["bn"] in (16, 32)
             assert p["tiles_a"] * 128 >= n and p["tiles_b"] * p["bn"] >= m
         else:
@@ -68,7 +72,14 @@ def test_headline_shapes():
     # register-fed decode kernel over all SMs (or, switched, the swapped K-split
     # tcgen05 plan); C1/C2 single-CTA tiles that still fill the SMs.
     c4 = htpg.plan_info(0, 16384, 6144, 1536)
-    assert c4["bn"] == 256 and c4["tiles_a"] == 64 and c4["grid"] == 148
+    assert c4["swap"] == 3 and c4["bn"] == 256 and c4["tiles_a"] == 24 and c4["tiles_b"] == 64
+    assert c4["grid"] == 148
+    try:
+        htpg.set_pair_direct(False)
+        c4 = htpg.plan_info(0, 16384, 6144, 1536)
+        assert c4["swap"] == 0 and c4["bn"] == 256 and c4["tiles_a"] == 64 and c4["grid"] == 148
+    finally:
+        htpg.set_pair_direct(True)
     for m in (1, 4, 16):
         up = htpg.plan_info(0, m, 14336, 4096)
         down = htpg.plan_info(0, m, 4096, 14336)
