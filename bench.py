@@ -560,6 +560,56 @@ def e2e_channel(torch, L, htpg, m, k, n, x_dev, blob_host, bias_dev, steps, warm
     return dt, m * k * 4 + n * 4, m * n * 4
 
 
+def peer_copy(gib: int = 1, reps: int = 10):
+    """Copy-engine bandwidth over NVLink between GPUs 0 and 1: 1 GiB from
+    GPU 0 to GPU 1 (one direction), and both directions at once (one stream
+    per direction); best of `reps`, CUDA events.  One JSON line."""
+    import torch
+    assert torch.cuda.device_count() >= 2, "needs two visible GPUs"
+    nbytes = gib << 30
+    a0 = torch.empty(nbytes, dtype=torch.uint8, device="cuda:0")
+    b1 = torch.empty(nbytes, dtype=torch.uint8, device="cuda:1")
+    a1 = torch.empty(nbytes, dtype=torch.uint8, device="cuda:1")
+    b0 = torch.empty(nbytes, dtype=torch.uint8, device="cuda:0")
+    s0 = torch.cuda.Stream(device="cuda:0")
+    s1 = torch.cuda.Stream(device="cuda:1")
+
+    def one_way():
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        with torch.cuda.stream(s0):
+            e[0].record(s0)
+            b1.copy_(a0, non_blocking=True)
+            e[1].record(s0)
+        torch.cuda.synchronize("cuda:0")
+        torch.cuda.synchronize("cuda:1")
+        return nbytes / (e[0].elapsed_time(e[1]) * 1e-3) / 1e9
+
+    def both_ways():
+        e0 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        e1 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        with torch.cuda.stream(s0):
+            e0[0].record(s0)
+            b1.copy_(a0, non_blocking=True)
+            e0[1].record(s0)
+        with torch.cuda.stream(s1):
+            e1[0].record(s1)
+            b0.copy_(a1, non_blocking=True)
+            e1[1].record(s1)
+        torch.cuda.synchronize("cuda:0")
+        torch.cuda.synchronize("cuda:1")
+        return min(nbytes / (e0[0].elapsed_time(e0[1]) * 1e-3) / 1e9, nbytes / (e1[0].elapsed_time(e1[1]) * 1e-3) / 1e9)
+
+    for _ in range(2):
+        one_way()
+        both_ways()
+    uni = max(one_way() for _ in range(reps))
+    bi = max(both_ways() for _ in range(reps))
+    print(json.dumps({"peer_copy": {"bytes": nbytes, "one_direction_GBps": uni,
+                                    "each_direction_when_both_GBps": bi,
+                                    "how": "torch copy_ between cuda:0 and cuda:1 (copy engine, NVLink), "
+                                           f"best of {reps}, CUDA events"}}), flush=True)
+
+
 # ------------------------------------------------------------------ main arm
 def main():
     faulthandler.enable()
@@ -587,8 +637,13 @@ def main():
                     help="token rows; smaller values only for profiling captures (workload C4-M<m>)")
     ap.add_argument("--settle", type=float, default=1.5,
                     help="seconds of untimed load before timing (clock sampling); 0 under ncu")
+    ap.add_argument("--peer-copy", action="store_true",
+                    help="measure the NVLink peer-copy bandwidth between GPUs 0 and 1 (one process) and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.peer_copy:
+        peer_copy()
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

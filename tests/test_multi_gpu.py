@@ -2,7 +2,10 @@
 
 Each rank prepares its column block of the weight, maps every rank's [M][N]
 output through CUDA IPC and runs htpg_w8a8_run_gather: its epilogue stores
-each tile into all of them.  After a stream-ordered all-reduce of a token the
+each tile into all of them.  The single-destination CTA-pair shapes of this
+test run the swapped orientation in the single-GPU reference run and the
+normal orientation (TMA stores) in the exchange, so the comparison also
+checks the two orientations against each other.  After a stream-ordered all-reduce of a token the
 assembled output must equal, bit for bit, one GPU computing all N columns.
 Skipped when fewer than two GPUs are visible.
 """
@@ -45,7 +48,8 @@ def _worker(rank, world, port, q):
     results = {}
     peers = []
     try:
-        for (m, k, n, mode) in ((1000, 512, 1280, 1), (300, 768, 1024, 0), (4100, 256, 4608, 2)):
+        cases = [(1000, 512, 1280, 1), (300, 768, 1024, 0), (4100, 256, 4608, 2), (2048, 1536, 3072, 1)]
+        for (m, k, n, mode) in cases:
             x, blob, bias, _ = bench.make_c4_inputs(torch, dev, m, k, n, seed=0x5EED0100 + m)
             n0, nl = htpg.column_range(n, world, rank)
             w = htpg.w8a8_weights(blob, k, n, n0=n0, n_cols=nl)
