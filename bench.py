@@ -50,7 +50,7 @@ M_C4, K_C4, N_C4 = 16384, 1536, 6144
 FLUSH_BYTES = 256 << 20
 L2_NOTE = ("256 MiB buffer written then read back between steps (outside the timed events): "
            "the next step starts from a cold L2 holding only clean lines")
-NVLINK_GBS = 770.0   # measured peer copy per direction on this pool's B200s (nominal 900)
+NVLINK_GBS = 770.0   # peer copy per direction measured with `bench.py --peer-copy` (771-775 GB/s; nominal 900)
 SLEEP_CYCLES = 20_000_000   # ~10 ms of torch's bounded sleep kernel ahead of a timed loop
 
 
@@ -400,6 +400,26 @@ def suite(torch, L, htpg, dev, flush, reps=20, only=None):
             # the one-call entry point caches the prepared weight by address
             L.htpg_weight_cache_drop(htpg.ptr(src))
             del src
+    # C5 read ceiling: a read-only stream (the decode kernels' 32-byte loads,
+    # data discarded) over one linear's weight bytes (4096 x 14336 = 58.7 MB)
+    # from a cold L2, the same back to back over six buffers (352 MB, more
+    # than the L2), and one launch over all 352 MB
+    if not only or only == "C5_read":
+        nb = 4096 * 14336
+        big = torch.ones(6 * nb, dtype=torch.uint8, device=dev)
+        parts = [big[i * nb:(i + 1) * nb] for i in range(6)]
+
+        def rd(b, nbytes=nb):
+            htpg.check(L.htpg_stream_read(htpg.ptr(b), nbytes, htpg.stream_ptr()), "htpg_stream_read")
+
+        tm = timed(lambda: rd(parts[0]))
+        t = stream_us([lambda b=b: rd(b) for b in parts])
+        tb = timed(lambda: rd(big, 6 * nb))[0]
+        res["C5_read_ceiling"] = {"bytes": nb, "us": tm[0], "GBps": nb / tm[0] / 1e3, "hbm_frac": nb / tm[0] / 1e3 / hbm,
+                                  "stream_us": t, "stream_GBps": nb / t / 1e3, "stream_hbm_frac": nb / t / 1e3 / hbm,
+                                  "one_launch_352MB_us": tb, "one_launch_352MB_GBps": 6 * nb / tb / 1e3,
+                                  "one_launch_352MB_hbm_frac": 6 * nb / tb / 1e3 / hbm}
+        del big, parts
     # C5: decode shapes, no epilogue
     for m in (1, 4, 16):
         for name, k, n in (("up", 4096, 14336), ("down", 14336, 4096)):
@@ -433,6 +453,9 @@ def suite_summary(res):
         if "stream_us" in v:
             e["stream_us"] = r(v["stream_us"], 1)
             e["stream_hbm_frac"] = r(v["stream_hbm_frac"])
+        if "one_launch_352MB_hbm_frac" in v:
+            e["hbm_frac"] = r(v["hbm_frac"])
+            e["one_launch_352MB_hbm_frac"] = r(v["one_launch_352MB_hbm_frac"])
         if "TOPS" in v:
             e["TOPS"] = r(v["TOPS"], 1)
         out[name] = e

@@ -353,6 +353,14 @@ extern "C" int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t ou
   return HTPG_OK;
 }
 
+extern "C" int htpg_stream_read(const void *src, size_t bytes, void *stream) {
+  Device *d;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  if (!src || !bytes || bytes % 32 || (reinterpret_cast<uintptr_t>(src) & 31u)) return HTPG_EARGS;
+  return record_cuda(launch_stream_read(src, bytes, d->sms, pick_stream(d, stream)));
+}
+
 extern "C" int htpg_set_pair_direct(int on) {
   if (on != 0 && on != 1) return HTPG_EARGS;
   g_pair_direct.store(on);

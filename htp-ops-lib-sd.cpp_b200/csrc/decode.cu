@@ -329,7 +329,43 @@ cudaError_t launch_nt(const GemmPlan &p, const GemmArgs &a, cudaStream_t st) {
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
+// Read-only HBM stream (diagnostic): every thread reads 32-byte pieces with
+// the weight loads' cache policy, eight in flight, and folds them into one
+// word that is stored only if it equals a value it never takes, so the loads
+// cannot be dropped.  It measures the read ceiling the decode kernels are
+// compared with.
+__device__ uint32_t g_stream_sink;
+
+__global__ void __launch_bounds__(256) stream_read_kernel(const int8_t *src, long long pieces) {
+  uint32_t acc = 0u;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + 7 * stride < pieces; i += 8 * stride) {
+    uint32_t v[8][8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) ld_weight32(v[u], src + (i + u * stride) * 32);
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+#pragma unroll
+      for (int w = 0; w < 8; ++w) acc ^= v[u][w];
+  }
+  for (; i < pieces; i += stride) {
+    uint32_t v[8];
+    ld_weight32(v, src + i * 32);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) acc ^= v[w];
+  }
+  if (acc == 0x9e3779b9u) g_stream_sink = acc;
+}
+
 }  // namespace
+
+cudaError_t launch_stream_read(const void *src, size_t bytes, int num_sms, cudaStream_t st) {
+  if (!src || bytes % 32 || (reinterpret_cast<uintptr_t>(src) & 31u)) return cudaErrorInvalidValue;
+  stream_read_kernel<<<num_sms * 8, 256, 0, st>>>(static_cast<const int8_t *>(src),
+                                                   static_cast<long long>(bytes / 32));
+  return counted(cudaGetLastError());
+}
 
 void plan_decode_i8(GemmPlan &p, int M, int N, int K, int num_sms) {
   p.kind = Kind::I8;

@@ -1495,12 +1495,19 @@ std::atomic<int> g_decode_kernel{0};
 //    split over CTAs until the grid covers the SMs, with an exact INT32
 //    reduction.  These shapes stream the weight once and are HBM-bound.
 //  * large M: CTA-pair tiles of 256 rows x BN in {256, 128}, whichever needs
-//    fewer tile-rounds x BN over the SM pairs (wave quantisation), as long as
-//    the tiles fill at least half of the pairs.
+//    less time over the SM pairs: tile rounds (wave quantisation) x the cost
+//    of one round of that width (kPairCost*), as long as the tiles fill at
+//    least half of the pairs.
 //  * otherwise: activation rows in 128-row tiles and the widest weight tile
 //    N in {256, 128, 64, 32} that still gives one CTA per SM.
 //  In the normal orientation K stays whole inside a CTA (no split), so the
 //  FP16 accumulation order never depends on the plan.
+// Relative time of one CTA-pair tile wave by tile width: a 256 x 128 tile
+// does half the work of a 256 x 256 tile but its N = 128 pair MMAs issue at
+// about 0.72 of the N = 256 rate (C4 measured 1.38x slower with 128-wide
+// tiles), so it costs 128 / 0.72 ~ 178 against 256.
+constexpr long long kPairCost256 = 256, kPairCost128 = 178;
+
 GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms) {
   GemmPlan p;
   p.kind = kind;
@@ -1511,8 +1518,8 @@ GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms) {
     const long long u256 = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
     const long long u128 = static_cast<long long>((M + 255) / 256) * ((N + 127) / 128);
     if (u128 * 2 >= pairs) {
-      const long long cost256 = (u256 + pairs - 1) / pairs * 256;
-      const long long cost128 = (u128 + pairs - 1) / pairs * 128;
+      const long long cost256 = (u256 + pairs - 1) / pairs * kPairCost256;
+      const long long cost128 = (u128 + pairs - 1) / pairs * kPairCost128;
       p.pair = true;
       p.bn = cost256 <= cost128 ? 256 : 128;
       p.tiles_a = (M + 255) / 256;
@@ -1583,8 +1590,8 @@ GemmPlan plan_pair_sw(const GemmPlan &normal, int M, int N, int num_sms) {
   const int pairs = num_sms / 2;
   const long long tw = (N + 255) / 256;
   const long long u256 = tw * ((M + 255) / 256), u128 = tw * ((M + 127) / 128);
-  const long long cost256 = (u256 + pairs - 1) / pairs * 256;
-  const long long cost128 = (u128 + pairs - 1) / pairs * 128;
+  const long long cost256 = (u256 + pairs - 1) / pairs * kPairCost256;
+  const long long cost128 = (u128 + pairs - 1) / pairs * kPairCost128;
   p.pair_sw = true;
   p.bn = cost256 <= cost128 ? 256 : 128;
   p.tiles_a = static_cast<int>(tw);

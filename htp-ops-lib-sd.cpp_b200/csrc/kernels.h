@@ -74,6 +74,9 @@ void plan_decode_i8(GemmPlan &p, int M, int N, int K, int num_sms);
 size_t decode_ws_bytes(const GemmPlan &p);
 cudaError_t launch_decode_i8(const GemmPlan &p, const GemmArgs &a, cudaStream_t st);
 extern std::atomic<int> g_decode_kernel;  // 0: register-fed decode for I8 M <= 16; 1: swapped tcgen05
+// Read-only stream of `bytes` (a multiple of 32, 32-byte aligned) with the
+// decode kernels' load policy (diagnostic: the HBM read ceiling).
+cudaError_t launch_stream_read(const void *src, size_t bytes, int num_sms, cudaStream_t st);
 size_t splitk_count_bytes(const GemmPlan &p);
 // Box rows of the A and B tensor maps for this plan.
 // (swapped plans use the weight as A and the activation as B)

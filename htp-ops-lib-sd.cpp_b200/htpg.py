@@ -93,6 +93,7 @@ def lib() -> ctypes.CDLL:
         "htpg_set_pair_direct": (I, [I]),
         "htpg_last_phase_ms": (I, [ctypes.POINTER(ctypes.c_float)] * 3),
         "htpg_launch_count": (U64, []),
+        "htpg_stream_read": (I, [P, S, P]),
         "htpg_debug_simulate_abort": (I, [U32]),
         "htpg_debug_workspaces": (I, [ctypes.POINTER(S), ctypes.POINTER(S)]),
         "htpg_w8a8_profile_fill": (I, [I, I, I, ctypes.c_double, P]),

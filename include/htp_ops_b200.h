@@ -285,6 +285,12 @@ int htpg_phase_timing_read(double *act_ms, double *gemm_ms, int *runs);
 /* Kernel launches issued by this library since load (for launch accounting). */
 uint64_t htpg_launch_count(void);
 
+/* Diagnostic (no counterpart in the reference): one kernel that reads `bytes`
+ * of device memory at `src` (a multiple of 32 bytes, 32-byte aligned) with the
+ * decode kernels' 32-byte streaming loads and discards the data: the HBM read
+ * ceiling that the weight-streaming decode kernels are measured against. */
+int htpg_stream_read(const void *src, size_t bytes, void *stream);
+
 /* Test hooks (no counterpart in the reference).  htpg_debug_simulate_abort
  * leaves, on the current device, the state a launch that gave up can leave:
  * every stream workspace (W8A8/FP16 split-K areas, opcode 2-4 stream-K

@@ -25,11 +25,11 @@ pytestmark = pytest.mark.gpu
 W8A8_TOL = 2e-3
 
 SHAPES = [  # (m, k, n)
-    (1000, 512, 1280),      # ragged M
+    (1000, 512, 1280),      # ragged M, 128-row activation tiles
     (2100, 800, 1344),      # K = 6.25 k-blocks, N = 5.25 weight tiles
     (4100, 256, 4608),      # 4 rows in the last activation tile
     (4096, 6144, 1536),     # C3 fc2 shape (48 k-blocks)
-    (4096, 1536, 1536),     # C3 out-projection shape (128-row activation tiles)
+    (4096, 1536, 1536),     # C3 out-projection shape (96 tiles on 74 SM pairs)
     (257, 1152, 4608),
 ]
 
