@@ -251,11 +251,13 @@ static cudaError_t launch_reg(int8_t *codes, float *scales, const float *x, cons
 cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
                                  const float *inverse, int m, int k, cudaStream_t st) {
   // Many rows of at most 2048 elements: a register-resident warp per row.
-  // Long rows or few rows: a 256-thread block per row (two passes, the
-  // second from L1/L2).
+  // Few rows, or rows longer than 2048 elements (up to 16384): a 512-thread
+  // block per row that keeps the row in registers (one read from HBM).
+  // Otherwise (fewer than 1184 rows of at most 2048): two passes per row,
+  // the second from L1/L2.
   cudaError_t e;
-  if (m <= 64) {
-    // decode shapes: one block per row, the row in registers
+  if (m <= 64 || (k > 2048 && k <= 8 * 2048)) {
+    // decode shapes and long rows: one block per row, the row in registers
     const unsigned g = static_cast<unsigned>(m);
     switch ((k + 2047) / 2048) {
       case 1: e = launch_pdl(quantize_rows_wide_kernel<1>, g, kWideThreads, st, codes, scales, x, inverse, m, k); break;
@@ -278,11 +280,8 @@ cudaError_t launch_quantize_rows(int8_t *codes, float *scales, const float *x,
       case 7: e = launch_reg<7>(codes, scales, x, inverse, m, k, st); break;
       default: e = launch_reg<8>(codes, scales, x, inverse, m, k, st); break;
     }
-  } else if (k >= 4096 || m < 1184) {
-    e = launch_pdl(quantize_rows_kernel<256, 1>, static_cast<unsigned>(m), 256, st, codes, scales, x, inverse, m, k);
   } else {
-    e = launch_pdl(quantize_rows_kernel<32, 8>, static_cast<unsigned>((m + 7) / 8), 256, st, codes, scales, x,
-                   inverse, m, k);
+    e = launch_pdl(quantize_rows_kernel<256, 1>, static_cast<unsigned>(m), 256, st, codes, scales, x, inverse, m, k);
   }
   return counted(e != cudaSuccess ? e : cudaGetLastError());
 }
