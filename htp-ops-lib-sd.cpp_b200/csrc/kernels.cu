@@ -1190,20 +1190,22 @@ __device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const Kernel
       st_shared_cluster(peer_abort, 1u);
       return;
     }
-    uint32_t r[kCh][32];
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN + part * kTok;
-#pragma unroll
-    for (int i = 0; i < kCh; ++i) tmem_ld32(t_row + 32 * i, r[i]);
-    tmem_ld_wait();
-    tc_fence_before();
-    __syncwarp();
-    // the accumulator goes back to the pair leader's MMA issuer
-    if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&L.tempty[buf]), 0));
-    if (!n_ok) continue;
-#pragma unroll
+    // One 32-row chunk at a time (the code of one chunk stays small next to
+    // the MMA issuer's loop in the instruction caches); the accumulator goes
+    // back to the pair leader's MMA issuer once the last chunk is in registers.
+#pragma unroll 1
     for (int i = 0; i < kCh; ++i) {
+      uint32_t r[32];
+      tmem_ld32(t_row + 32 * i, r);
+      tmem_ld_wait();
+      if (i == kCh - 1) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&L.tempty[buf]), 0));
+      }
       const int mb = m0 + 32 * i;
-      if (mb >= g.M) break;
+      if (!n_ok || mb >= g.M) continue;
       char *base = reinterpret_cast<char *>(g.out + static_cast<long long>(mb) * g.ldo + n);
       const float *rsi = rs + 32 * i;
       auto row = [&](int j) {
@@ -1216,8 +1218,8 @@ __device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const Kernel
           for (int j4 = 0; j4 < 8; ++j4) {
             const float4 s4 = *reinterpret_cast<const float4 *>(rsi + 4 * j4);
             float o0, o1, o2, o3;
-            finish2<MODE, BIAS>(r[i][4 * j4], r[i][4 * j4 + 1], cr, sw2, s4.x, s4.y, bias2, one2, o0, o1);
-            finish2<MODE, BIAS>(r[i][4 * j4 + 2], r[i][4 * j4 + 3], cr, sw2, s4.z, s4.w, bias2, one2, o2, o3);
+            finish2<MODE, BIAS>(r[4 * j4], r[4 * j4 + 1], cr, sw2, s4.x, s4.y, bias2, one2, o0, o1);
+            finish2<MODE, BIAS>(r[4 * j4 + 2], r[4 * j4 + 3], cr, sw2, s4.z, s4.w, bias2, one2, o2, o3);
             *row(4 * j4) = o0;
             *row(4 * j4 + 1) = o1;
             *row(4 * j4 + 2) = o2;
@@ -1225,11 +1227,11 @@ __device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const Kernel
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) *row(j) = finish<KIND, MODE, BIAS>(r[i][j], 0, 0.0f, 0.0f, bv);
+          for (int j = 0; j < 32; ++j) *row(j) = finish<KIND, MODE, BIAS>(r[j], 0, 0.0f, 0.0f, bv);
         }
       } else {
         for (int j = 0; j < 32 && mb + j < g.M; ++j)
-          *row(j) = finish<KIND, MODE, BIAS>(r[i][j], cr, sw, KIND == Kind::I8 ? rsi[j] : 0.0f, bv);
+          *row(j) = finish<KIND, MODE, BIAS>(r[j], cr, sw, KIND == Kind::I8 ? rsi[j] : 0.0f, bv);
       }
     }
   }
@@ -1394,10 +1396,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer (leader)
     if (lane == 0 && leader) {
       grid_dependency_wait();  // bounded waits start once the operands can exist
+      // This thread shares its SM sub-partition with four epilogue warps whose
+      // arithmetic competes for issue: per k-block it only waits for the
+      // stage, advances two precomputed descriptors by a constant and issues
+      // the four MMAs as one block.
       int s = 0;
       uint32_t ph = 0;
       uint32_t iter = 0;
       bool ok = true;
+      const uint64_t a_desc0 = umma_desc_sw128(smem_u32(L.a)), b_desc0 = umma_desc_sw128(smem_u32(L.b));
+      constexpr uint64_t kAStep = (128 * kRowBytes) >> 4, kBStep = (BH * kRowBytes) >> 4;  // per stage
+      uint64_t da = a_desc0, db = b_desc0;
+      const uint32_t full0 = smem_u32(&L.full[0]), empty0 = smem_u32(&L.empty[0]);
       for (int u = pair; ok && u < P.units; u += npairs, ++iter) {
         const uint32_t buf = iter & 1u;
         const uint32_t acc_ph = (iter >> 1) & 1u;
@@ -1405,27 +1415,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = 0; kb < P.kb_total; ++kb) {
-          if (!wait(smem_u32(&L.full[s]), ph, kWatchMma)) {
+          if (!wait(full0 + 8u * s, ph, kWatchMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(L.a + s * 128 * kRowBytes);
-          const uint32_t b_addr = smem_u32(L.b + s * BH * kRowBytes);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t da = umma_desc_sw128(a_addr + kk * 32);
-            const uint64_t db = umma_desc_sw128(b_addr + kk * 32);
-            const uint32_t accumulate = (kb > 0 || kk > 0) ? 1u : 0u;
-            if (KIND == Kind::I8)
-              umma_i8_pair(d_tmem, da, db, kIdesc, accumulate);
-            else
-              umma_f16_pair(d_tmem, da, db, kIdesc, accumulate);
-          }
-          tc_commit_pair_mc(smem_u32(&L.empty[s]), 0x3);
+          umma_pair_kblock<KIND == Kind::I8>(d_tmem, da, db, kIdesc, kb > 0 ? 1u : 0u);
+          tc_commit_pair_mc(empty0 + 8u * s, 0x3);
           if (++s == STAGES) {
             s = 0;
             ph ^= 1u;
+            da = a_desc0;
+            db = b_desc0;
+          } else {
+            da += kAStep;
+            db += kBStep;
           }
         }
         if (ok) tc_commit_pair_mc(smem_u32(&L.tfull[buf]), 0x3);

@@ -379,6 +379,40 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, 
       : "memory");
 }
 
+// The four pair MMAs over the K of one 128-byte swizzled k-block (kind::i8:
+// K = 32 per MMA; kind::f16: K = 16), in one asm block: descriptors advance
+// by 32 bytes (2 in the start-address field) per MMA, one predicate set.
+// accumulate applies to the first MMA; the other three always accumulate.
+template <bool I8>
+__device__ __forceinline__ void umma_pair_kblock(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  if constexpr (I8) {
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.eq.b32 q, %4, %4;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %5, %6, %3, q;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %7, %8, %3, q;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %9, %10, %3, q;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "l"(a_desc + 2), "l"(b_desc + 2), "l"(a_desc + 4),
+        "l"(b_desc + 4), "l"(a_desc + 6), "l"(b_desc + 6)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.eq.b32 q, %4, %4;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %5, %6, %3, q;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %7, %8, %3, q;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %9, %10, %3, q;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "l"(a_desc + 2), "l"(b_desc + 2), "l"(a_desc + 4),
+        "l"(b_desc + 4), "l"(a_desc + 6), "l"(b_desc + 6)
+        : "memory");
+  }
+}
+
 // Named barrier among `nthreads` threads (whole warps) of the CTA.
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
