@@ -15,6 +15,7 @@
 #include <atomic>
 #include <cstdio>
 
+
 #include "kernels.h"
 #include "ptx.cuh"
 #include "epilogue.cuh"
@@ -875,6 +876,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the next operator's kernels may be scheduled now (they wait for this one
   // before they read anything it writes)
   grid_dependents_launch();
+  if (threadIdx.x == 32) {  // the descriptor fetch overlaps the set-up below
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -1284,6 +1289,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const uint32_t peer_abort = mapa_shared(smem_u32(const_cast<uint32_t *>(L.abort)), rank ^ 1u);
   grid_dependents_launch();  // the next operator's kernels may be scheduled now
+  if (threadIdx.x == 32) {     // the descriptor fetch overlaps the set-up below
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
   // a failed wait also tells the peer CTA, whose waits then return at once
   auto wait = [&](uint32_t bar, uint32_t parity, uint32_t bit) {
     const bool ok = mbar_wait(bar, parity, wd, bit, L.abort);
