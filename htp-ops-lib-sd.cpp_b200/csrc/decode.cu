@@ -29,8 +29,12 @@
 // column group and adds the sums into the CTA's shared-memory tile of that
 // group.  A column group covered by one chunk is finished by the CTA
 // directly; a group that straddles chunks is published as INT32 partial
-// tiles and finished by the last chunk to arrive (counter per group).  The
-// partial tiles and the counters are left zeroed.
+// tiles and finished by the last chunk to arrive (counter per group, one
+// acquire-release arrival per partial tile instead of full fences).  The
+// partial tiles and the counters are left zeroed.  The epilogue parameters of
+// a chunk's columns (scale, correction, bias) and the row scales are staged
+// in shared memory while the weight streams, so the tail after the main loop
+// carries no global parameter loads.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -126,6 +130,15 @@ __device__ __forceinline__ void mma_atom(int32_t (&acc)[NT][4], const WFrag &f, 
       mma_s8(acc[j], f.lo[s], f.hi[s], f.lo[4 + s], f.hi[4 + s], word(x[2 * j], s), word(x[2 * j + 1], s));
 }
 
+// Arrival on a group's counter, ordered after the warp's partial-tile stores
+// (release, made cumulative by the warp barrier before it) and before the
+// finisher's reads of the other partial tiles (acquire).
+__device__ __forceinline__ uint32_t arrive_acq_rel(uint32_t *count) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(count) : "memory");
+  return old;
+}
+
 // Accumulator fragment -> the group's shared tile [token][16 columns].
 template <int NT>
 __device__ __forceinline__ void flush(int32_t *tile, int32_t (&acc)[NT][4], int g, int t) {
@@ -141,19 +154,31 @@ __device__ __forceinline__ void flush(int32_t *tile, int32_t (&acc)[NT][4], int 
   }
 }
 
-// One finished column group: lane holds column lane%16 and tokens lane/16 + 2i.
+// Per-chunk parameters in shared memory (after the INT32 tiles): the column
+// scale, correction and bias of each of the chunk's columns and the row scales.
+struct DecPrm {
+  float *sw;
+  int32_t *cr;
+  float *bias;
+  float *rs;
+};
+
+// One finished column group (j-th of its chunk): lane holds column lane%16 and
+// tokens lane/16 + 2i.
 template <int BN, int MODE, bool BIAS>
-__device__ __forceinline__ void finish_group(const GemmArgs &g, int cg, int lane, const int32_t (&v)[BN / 2]) {
+__device__ __forceinline__ void finish_group(const GemmArgs &g, const DecPrm &q, int cg, int j, int lane,
+                                             const int32_t (&v)[BN / 2]) {
   const int n = cg * 16 + (lane & 15);
   if (n >= g.N) return;
-  const float sw = __ldg(g.col_scale + n);
-  const int32_t cr = __ldg((MODE == 5 ? g.col_sum7 : g.col_corr) + n);
-  const float bn = BIAS ? __ldg(g.bias + n) : 0.0f;
+  const int c = j * 16 + (lane & 15);
+  const float sw = q.sw[c];
+  const int32_t cr = q.cr[c];
+  const float bn = BIAS ? q.bias[c] : 0.0f;
 #pragma unroll
   for (int i = 0; i < BN / 2; ++i) {
     const int m = (lane >> 4) + 2 * i;
     if (m >= g.M) break;
-    const float val = finish<Kind::I8, MODE, BIAS>(static_cast<uint32_t>(v[i]), cr, sw, __ldg(g.row_scale + m), bn);
+    const float val = finish<Kind::I8, MODE, BIAS>(static_cast<uint32_t>(v[i]), cr, sw, q.rs[m], bn);
     if (MODE == 5) {
       const uint32_t u = __float_as_uint(val);
 #pragma unroll
@@ -167,26 +192,37 @@ __device__ __forceinline__ void finish_group(const GemmArgs &g, int cg, int lane
 }
 
 template <int BN>
-__device__ __forceinline__ void finish_dispatch(const GemmArgs &g, int cg, int lane, const int32_t (&v)[BN / 2]) {
+__device__ __forceinline__ void finish_dispatch(const GemmArgs &g, const DecPrm &q, int cg, int j, int lane,
+                                                const int32_t (&v)[BN / 2]) {
   switch (g.mode * 2 + (g.bias != nullptr ? 1 : 0)) {
-    case 0: finish_group<BN, 0, false>(g, cg, lane, v); break;
-    case 1: finish_group<BN, 0, true>(g, cg, lane, v); break;
-    case 2: finish_group<BN, 1, false>(g, cg, lane, v); break;
-    case 3: finish_group<BN, 1, true>(g, cg, lane, v); break;
-    case 4: finish_group<BN, 2, false>(g, cg, lane, v); break;
-    case 5: finish_group<BN, 2, true>(g, cg, lane, v); break;
-    case 6: finish_group<BN, 3, false>(g, cg, lane, v); break;
-    case 7: finish_group<BN, 3, true>(g, cg, lane, v); break;
-    case 10: finish_group<BN, 5, false>(g, cg, lane, v); break;
-    default: finish_group<BN, 4, false>(g, cg, lane, v); break;
+    case 0: finish_group<BN, 0, false>(g, q, cg, j, lane, v); break;
+    case 1: finish_group<BN, 0, true>(g, q, cg, j, lane, v); break;
+    case 2: finish_group<BN, 1, false>(g, q, cg, j, lane, v); break;
+    case 3: finish_group<BN, 1, true>(g, q, cg, j, lane, v); break;
+    case 4: finish_group<BN, 2, false>(g, q, cg, j, lane, v); break;
+    case 5: finish_group<BN, 2, true>(g, q, cg, j, lane, v); break;
+    case 6: finish_group<BN, 3, false>(g, q, cg, j, lane, v); break;
+    case 7: finish_group<BN, 3, true>(g, q, cg, j, lane, v); break;
+    case 10: finish_group<BN, 5, false>(g, q, cg, j, lane, v); break;
+    default: finish_group<BN, 4, false>(g, q, cg, j, lane, v); break;
   }
+}
+
+// Shared memory of the decode kernel: INT32 tiles, then the parameters.
+__host__ __device__ constexpr size_t dec_smem_bytes(int bn) {
+  return static_cast<size_t>(kDecMaxCg) * 16 * bn * 4 + static_cast<size_t>(kDecMaxCg) * 16 * 12 + 16 * 4;
 }
 
 template <int NT>
 __global__ void __launch_bounds__(kDecThreads, 1) decode_i8_kernel(const DecParams P) {
   constexpr int BN = 8 * NT;     // activation rows held (tokens)
   constexpr int TILE = 16 * BN;  // INT32 per column group
-  extern __shared__ int32_t dtile[];  // [kDecMaxCg][BN][16]
+  extern __shared__ int32_t dtile[];  // [kDecMaxCg][BN][16], then the DecPrm arrays
+  DecPrm q;
+  q.sw = reinterpret_cast<float *>(dtile + kDecMaxCg * TILE);
+  q.cr = reinterpret_cast<int32_t *>(q.sw + kDecMaxCg * 16);
+  q.bias = reinterpret_cast<float *>(q.cr + kDecMaxCg * 16);
+  q.rs = q.bias + kDecMaxCg * 16;
   const GemmArgs &g = P.a;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 2, tq = lane & 3;
@@ -226,10 +262,22 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_i8_kernel(const DecPara
         }
       }
     }
+    // the weight's column parameters come with the weight (read before the
+    // wait when the weight loads are); the bias and the row scales after it
+    for (int i = threadIdx.x; i < ncg * 16; i += kDecThreads) {
+      const int n = cg0 * 16 + i;
+      q.sw[i] = n < g.N ? __ldg(g.col_scale + n) : 0.0f;
+      q.cr[i] = n < g.N ? __ldg((g.mode == 5 ? g.col_sum7 : g.col_corr) + n) : 0;
+    }
     if (!waited) {
       grid_dependency_wait();  // activation codes and row scales come from the previous kernel
       waited = true;
     }
+    // held in registers through the main loop, stored after it (their load
+    // latency stays off the loop's start)
+    const int pi = threadIdx.x, pn = cg0 * 16 + pi;
+    const float p_bias = (g.bias != nullptr && pi < ncg * 16 && pn < g.N) ? __ldg(g.bias + pn) : 0.0f;
+    const float p_rs = pi < g.M ? __ldg(g.row_scale + pi) : 0.0f;
     __syncthreads();  // tile zeroed
 
     int ccg = static_cast<int>(b0 / KB), ckb = static_cast<int>(b0 - static_cast<long long>(ccg) * KB);
@@ -260,6 +308,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_i8_kernel(const DecPara
         }
       }
     }
+    if (pi < ncg * 16) q.bias[pi] = p_bias;
+    if (pi < BN) q.rs[pi] = p_rs;
     __syncthreads();
 
     // finish this chunk's column groups, one warp per group
@@ -276,15 +326,14 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_i8_kernel(const DecPara
         int32_t *slot = g.ws + (static_cast<size_t>(c) * 2 + (cg == cg0 ? 0 : 1)) * TILE;
 #pragma unroll
         for (int i = 0; i < BN / 2; ++i) slot[((lane >> 4) + 2 * i) * 16 + (lane & 15)] = v[i];
-        __threadfence();
         __syncwarp();
         const int first = dec_owner(P, ga0), last = dec_owner(P, ga1 - 1);
         uint32_t prev = 0u;
-        if (lane == 0) prev = atomicAdd(g.ws_count + cg, 1u);
+        if (lane == 0) prev = arrive_acq_rel(g.ws_count + cg);
         prev = __shfl_sync(0xffffffffu, prev, 0);
         fin = prev == static_cast<uint32_t>(last - first);
         if (fin) {
-          __threadfence();
+          __syncwarp();  // lane 0's acquire orders every lane's reads below
 #pragma unroll
           for (int i = 0; i < BN / 2; ++i) v[i] = 0;
           for (int o = first; o <= last; ++o) {
@@ -300,7 +349,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_i8_kernel(const DecPara
           if (lane == 0) g.ws_count[cg] = 0u;
         }
       }
-      if (fin) finish_dispatch<BN>(g, cg, lane, v);
+      if (fin) finish_dispatch<BN>(g, q, cg, j, lane, v);
     }
     __syncthreads();  // the tile is reused by the next chunk
   }
@@ -386,7 +435,7 @@ void plan_decode_i8(GemmPlan &p, int M, int N, int K, int num_sms) {
   p.chunks = static_cast<int>(chunks);
   p.units = p.chunks;
   p.grid = static_cast<int>(std::min<long long>(chunks, num_sms));
-  p.smem = static_cast<size_t>(kDecMaxCg) * 16 * p.bn * 4;
+  p.smem = dec_smem_bytes(p.bn);
 }
 
 size_t decode_ws_bytes(const GemmPlan &p) { return static_cast<size_t>(p.chunks) * 2 * 16 * p.bn * 4; }
