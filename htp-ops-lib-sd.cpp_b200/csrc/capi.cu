@@ -344,12 +344,22 @@ extern "C" int htpg_phase_timing_read(double *act_ms, double *gemm_ms, int *runs
   return HTPG_OK;
 }
 
-extern "C" int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]) {
+extern "C" int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[12]) {
   if (!out || m < 1 || n < 1 || k < 1 || sms < 1 || (kind != 0 && kind != 1)) return HTPG_EARGS;
   const GemmPlan p = plan_for(kind == 0 ? Kind::I8 : Kind::F16, m, n, k, sms, 0, 1);
-  const int64_t v[10] = {p.reg ? 2 : p.swap ? 1 : p.pair_sw ? 3 : 0, p.bn, p.splits, p.tiles_a, p.tiles_b,
-                         p.kb_total, p.kb_per_split, p.units, p.grid, static_cast<int64_t>(p.smem)};
-  for (int i = 0; i < 10; ++i) out[i] = v[i];
+  const int64_t v[12] = {p.reg ? 2 : p.swap ? 1 : p.pair_sw ? 3 : 0,
+                         p.bn,
+                         p.splits,
+                         p.tiles_a,
+                         p.tiles_b,
+                         p.kb_total,
+                         p.kb_per_split,
+                         p.units,
+                         p.grid,
+                         static_cast<int64_t>(p.smem),
+                         p.tail_s > 1 ? p.full_units : p.units,
+                         p.tail_s};
+  for (int i = 0; i < 12; ++i) out[i] = v[i];
   return HTPG_OK;
 }
 
@@ -359,6 +369,12 @@ extern "C" int htpg_stream_read(const void *src, size_t bytes, void *stream) {
   if (rc) return rc;
   if (!src || !bytes || bytes % 32 || (reinterpret_cast<uintptr_t>(src) & 31u)) return HTPG_EARGS;
   return record_cuda(launch_stream_read(src, bytes, d->sms, pick_stream(d, stream)));
+}
+
+extern "C" int htpg_set_pair_tail_split(int on) {
+  if (on != 0 && on != 1) return HTPG_EARGS;
+  g_pair_tail.store(on);
+  return HTPG_OK;
 }
 
 extern "C" int htpg_set_pair_direct(int on) {
@@ -569,10 +585,14 @@ int run_common(htpg_weights *w, float *const *outs, int n_outs, int ldo, const f
   const size_t act_elem = w->kind == Kind::I8 ? 1 : 2;
   const size_t act_bytes = act_f16 ? 0 : align_up(static_cast<size_t>(m) * k * act_elem, 1024);
   const size_t scale_bytes = align_up(4u * static_cast<size_t>(m), 1024);
+  // the tail pieces' INT32 sums (written before they are read: no clearing)
+  const size_t slot_bytes = tail_slot_bytes(plan);
   void *base = nullptr;
-  rc = workspace(d, st, wsk_bytes + act_bytes + scale_bytes, &base);
+  rc = workspace(d, st, wsk_bytes + act_bytes + scale_bytes + slot_bytes, &base);
   if (rc) return rc;
-  int32_t *wsk = static_cast<int32_t *>(base);
+  int32_t *wsk = slot_bytes ? reinterpret_cast<int32_t *>(static_cast<uint8_t *>(base) + wsk_bytes + act_bytes +
+                                                          scale_bytes)
+                            : static_cast<int32_t *>(base);
   uint32_t *cnt = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(base) + splitk_ws_bytes(plan));
   uint8_t *act = act_f16 ? reinterpret_cast<uint8_t *>(const_cast<uint16_t *>(act_f16))
                          : static_cast<uint8_t *>(base) + wsk_bytes;
@@ -945,7 +965,8 @@ int htpg::w8a8_run_in_scratch(const htpg_weights *w, float *out, int ldo, const 
   cudaStream_t st = pick_stream(d, stream);
   std::lock_guard<std::mutex> lk(g_mu);
 
-  const GemmPlan plan = plan_for(Kind::I8, m, n, k, d->sms, mode, 1);
+  // the documented scratch layout has no room for tail-piece sums: whole tiles only
+  const GemmPlan plan = plan_for(Kind::I8, m, n, k, d->sms, mode, 1, false);
   const bool w_is_a = plan.swap || plan.pair_sw;
   const size_t splitk_bytes = splitk_ws_bytes(plan) + splitk_count_bytes(plan);
   if (splitk_bytes > kSplitKRegion) return HTPG_ENOPLAN;
@@ -1298,10 +1319,11 @@ extern "C" int htpg_w8a8_profile_fill(int m, int k, int n, double setup_ms, stru
     const uint32_t rows64 = static_cast<uint32_t>(act_rows / 64);
     const uint32_t cols64 = static_cast<uint32_t>(w_cols >= 64 ? w_cols / 64 : 1);
     profile->reserved = rows64 | (cols64 << 16);
-    profile->mac_ticks = static_cast<uint64_t>(p.units);  // weight tiles loaded
+    profile->mac_ticks = static_cast<uint64_t>(p.units);  // weight tiles (or tile pieces) loaded
+    // weight bytes loaded: every k-block of every tile's weight columns once
     profile->readout_ticks = p.reg ? static_cast<uint64_t>(p.tiles_a) * 16u * p.kb_total * 128u
-                                   : static_cast<uint64_t>(p.units) * static_cast<uint64_t>(w_cols) *
-                                         static_cast<uint64_t>(p.kb_per_split) * 128u;  // weight bytes loaded
+                                   : static_cast<uint64_t>(p.tiles_a) * p.tiles_b * p.splits *
+                                         static_cast<uint64_t>(w_cols) * static_cast<uint64_t>(p.kb_per_split) * 128u;
   }
   return HTPG_OK;
 }

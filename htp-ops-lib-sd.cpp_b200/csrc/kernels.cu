@@ -566,7 +566,67 @@ __device__ __forceinline__ Unit decode_unit(int u, int tiles_b, int splits) {
 struct KernelParams {
   GemmArgs a;
   int tiles_a, tiles_b, splits, kb_total, kb_per_split, units;
+  int full_units = 0, tail_s = 1;  // CTA-pair plans: whole-tile units, then pieces of the tail tiles
 };
+
+// A CTA-pair unit: the tile and its k-block range.  Units below full_units are
+// whole tiles; the rest cut each remaining (tail) tile into tail_s pieces of
+// consecutive k-blocks, piece `part` of tile t at unit full_units + (t -
+// full_units) * tail_s + part.  Units go round-robin to the pairs, and
+// full_units is a multiple of the pair count, so every piece is its pair's
+// last unit and all pieces of the tail run side by side.
+struct PairUnit {
+  int tile, kb0, kb1, part;
+};
+__device__ __forceinline__ PairUnit pair_unit(const KernelParams &P, int u) {
+  PairUnit r;
+  if (u < P.full_units) {
+    r.tile = u;
+    r.kb0 = 0;
+    r.kb1 = P.kb_total;
+    r.part = 0;
+    return r;
+  }
+  const int j = u - P.full_units;
+  const int t = j / P.tail_s;
+  r.tile = P.full_units + t;
+  r.part = j - t * P.tail_s;
+  r.kb0 = P.kb_total * r.part / P.tail_s;
+  r.kb1 = P.kb_total * (r.part + 1) / P.tail_s;
+  return r;
+}
+
+// Tail-piece hand-off counters: a piece publishes the INT32 sums of the
+// chunks other pieces own and then arrives on their counters (release, made
+// cumulative by the epilogue barrier before it); it waits for the other
+// pieces' arrivals on its own counter (acquire) before reading their sums.
+__device__ __forceinline__ void arrive_release(uint32_t *count) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(count) : "memory");
+}
+__device__ __forceinline__ uint32_t load_acquire(const uint32_t *count) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(count) : "memory");
+  return v;
+}
+// Bounded wait for *count to reach `target` (the time limit and the CTA's
+// abort flag as in mbar_wait).
+__device__ __forceinline__ bool wait_count(const uint32_t *count, uint32_t target, uint32_t *watchdog,
+                                           volatile uint32_t *abort) {
+  if (load_acquire(count) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t spin = 1;; ++spin) {
+    __nanosleep(32);
+    if (load_acquire(count) >= target) return true;
+    if ((spin & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        atomicOr(watchdog, kWatchSplitK);
+        *abort = 1u;
+        return false;
+      }
+    }
+  }
+}
 
 // Everything an epilogue warp needs for one unit.
 struct EpiCtx {
@@ -1159,7 +1219,7 @@ __device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const Kernel
   float f_sw = 0.0f, f_bv = 0.0f, f_rs[kCh];
   int32_t f_cr = 0;
   auto fetch = [&](int u) {
-    const Unit w = decode_unit(u, P.tiles_b, 1);
+    const Unit w = decode_unit(pair_unit(P, u).tile, P.tiles_b, 1);
     const int n = w.ta * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
     const int m0 = w.tb * BN + part * kTok;
     const bool ok = n < g.N;
@@ -1173,13 +1233,30 @@ __device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const Kernel
     }
   };
   if (pair < P.units) fetch(pair);
+  const int epi_t = static_cast<int>(threadIdx.x) - 64;  // among the CTA's epilogue threads
   uint32_t iter = 0;
   for (int u = pair; u < P.units; u += npairs, ++iter) {
-    const Unit w = decode_unit(u, P.tiles_b, 1);
+    const PairUnit pu = pair_unit(P, u);
+    const Unit w = decode_unit(pu.tile, P.tiles_b, 1);
     const uint32_t buf = iter & 1u;
     const int n = w.ta * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
     const bool n_ok = n < g.N;
     const int m0 = w.tb * BN + part * kTok;
+    // Tail pieces (reduce-scatter of their INT32 sums): piece k owns the
+    // tile's 32-row chunks c with c % tail_s == k, so each warp owns at most
+    // one of its two chunks.  Every piece stores the chunks it does not own in
+    // its slot [BN rows][128 columns] per (tail tile, piece, CTA), arrives on
+    // the owners' counters (per tail tile, owner piece and CTA), waits for the
+    // other pieces' arrivals on its own counter, adds their slots' rows of
+    // its chunks to its accumulator and finishes those rows.
+    const bool piece = u >= P.full_units;
+    const int tt = pu.tile - P.full_units;
+    auto count = [&](int owner) { return g.ws_count + (tt * P.tail_s + owner) * 2 + static_cast<int>(rank); };
+    auto slot = [&](int k) {
+      return g.ws + (static_cast<size_t>((tt * P.tail_s + k) * 2 + static_cast<int>(rank)) * BN + part * kTok) * 128 +
+             q * 32 + lane;
+    };
+    auto owner_of = [&](int i) { return (part * kCh + i) % P.tail_s; };  // chunk i of this warp
     // this unit's parameters (the f_ registers are refilled for the next unit below)
     const float sw = f_sw, bv = f_bv;
     const uint64_t bias2 = pk2(bv, bv);
@@ -1193,21 +1270,62 @@ __device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const Kernel
     tc_fence_after();
     if (!ok) {
       st_shared_cluster(peer_abort, 1u);
-      return;
+      if (!piece) return;  // a piece's warps all meet at its barrier below, failed or not
     }
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN + part * kTok;
+    if (piece) {
+      if (ok) {
+        int32_t *sl = slot(pu.part);
+#pragma unroll 1
+        for (int i = 0; i < kCh; ++i) {
+          if (owner_of(i) == pu.part) continue;
+          uint32_t r[32];
+          tmem_ld32(t_row + 32 * i, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) __stcg(sl + (32 * i + j) * 128, static_cast<int32_t>(r[j]));
+        }
+      }
+      named_bar_sync(1, kEpiThreads);  // every slot store of this CTA precedes the arrivals
+      if (epi_t == 0) {
+        bool got = *L.abort == 0u;
+        if (got)
+          for (int o = 0; o < P.tail_s; ++o)
+            if (o != pu.part) arrive_release(count(o));
+        got = got && wait_count(count(pu.part), static_cast<uint32_t>(P.tail_s - 1), g.watchdog, L.abort);
+        if (got) *count(pu.part) = 0u;  // left zero for the next launch (every arrival is in)
+        *L.flag = got ? 1u : 0u;
+      }
+      named_bar_sync(1, kEpiThreads);
+      if (!ok || *L.flag == 0u) {
+        st_shared_cluster(peer_abort, 1u);
+        return;
+      }
+    }
     // One 32-row chunk at a time (the code of one chunk stays small next to
     // the MMA issuer's loop in the instruction caches); the accumulator goes
     // back to the pair leader's MMA issuer once the last chunk is in registers.
 #pragma unroll 1
     for (int i = 0; i < kCh; ++i) {
+      const bool mine = !piece || owner_of(i) == pu.part;
       uint32_t r[32];
-      tmem_ld32(t_row + 32 * i, r);
-      tmem_ld_wait();
+      if (mine) {
+        tmem_ld32(t_row + 32 * i, r);
+        tmem_ld_wait();
+      }
       if (i == kCh - 1) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&L.tempty[buf]), 0));
+      }
+      if (!mine) continue;
+      if (piece) {
+        for (int k = 0; k < P.tail_s; ++k) {
+          if (k == pu.part) continue;
+          const int32_t *sl = slot(k) + 32 * i * 128;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = static_cast<uint32_t>(static_cast<int32_t>(r[j]) + __ldcg(sl + j * 128));
+        }
       }
       const int mb = m0 + 32 * i;
       if (!n_ok || mb >= g.M) continue;
@@ -1235,8 +1353,10 @@ __device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const Kernel
           for (int j = 0; j < 32; ++j) *row(j) = finish<KIND, MODE, BIAS>(r[j], 0, 0.0f, 0.0f, bv);
         }
       } else {
-        for (int j = 0; j < 32 && mb + j < g.M; ++j)
-          *row(j) = finish<KIND, MODE, BIAS>(r[j], cr, sw, KIND == Kind::I8 ? rsi[j] : 0.0f, bv);
+        const int valid = g.M - mb;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)  // constant indices keep r[] in registers
+          if (j < valid) *row(j) = finish<KIND, MODE, BIAS>(r[j], cr, sw, KIND == Kind::I8 ? rsi[j] : 0.0f, bv);
       }
     }
   }
@@ -1350,16 +1470,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // k-blocks into the L2) before waiting for the activation pass
       int pre = 0;
       if (pair < P.units) {
-        const Unit w = decode_unit(pair, P.tiles_b, 1);
-        pre = g.late_weights ? 0 : min(STAGES, P.kb_total);
+        const PairUnit pu = pair_unit(P, pair);
+        const Unit w = decode_unit(pu.tile, P.tiles_b, 1);
+        pre = g.late_weights ? 0 : min(STAGES, pu.kb1 - pu.kb0);
         for (int i = 0; i < pre; ++i) {
           const uint32_t fb_local = smem_u32(&L.full[i]);
           if (leader) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);
-          load_weight(i, i, w, mapa_shared(fb_local, 0));
+          load_weight(i, pu.kb0 + i, w, mapa_shared(fb_local, 0));
         }
         constexpr int kWRows = SW ? 128 : BH;  // weight rows this CTA loads per k-block
-        const int kb2 = min(P.kb_total, kPrefetchBytes / (kWRows * kRowBytes));
-        for (int kb = pre; kb < kb2; ++kb) {
+        const int kb2 = min(pu.kb1, pu.kb0 + kPrefetchBytes / (kWRows * kRowBytes));
+        for (int kb = pu.kb0 + pre; kb < kb2; ++kb) {
           if (SW)
             tma_prefetch_l2_2d(&tmA, 0, kb * g.N + w.ta * 256 + static_cast<int>(rank) * 128);
           else
@@ -1375,14 +1496,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       bool first = true;
       for (int u = pair; ok && u < P.units; u += npairs, first = false) {
-        const Unit w = decode_unit(u, P.tiles_b, 1);
-        for (int kb = 0; kb < P.kb_total; ++kb) {
+        const PairUnit pu = pair_unit(P, u);
+        const Unit w = decode_unit(pu.tile, P.tiles_b, 1);
+        for (int kb = pu.kb0; kb < pu.kb1; ++kb) {
           if (!wait(smem_u32(&L.empty[s]), ph ^ 1u, kWatchProducer)) {
             ok = false;
             break;
           }
           const uint32_t fb_local = smem_u32(&L.full[s]);
-          const bool weight_done = first && kb < pre;
+          const bool weight_done = first && kb - pu.kb0 < pre;
           if (leader && !weight_done) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);
           const uint32_t fb = mapa_shared(fb_local, 0);
           load_act(s, kb, w, fb);
@@ -1423,13 +1545,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (!wait(smem_u32(&L.tempty[buf]), acc_ph ^ 1u, kWatchMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < P.kb_total; ++kb) {
+        const PairUnit pu = pair_unit(P, u);
+        for (int kb = pu.kb0; kb < pu.kb1; ++kb) {
           if (!wait(full0 + 8u * s, ph, kWatchMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          umma_pair_kblock<KIND == Kind::I8>(d_tmem, da, db, kIdesc, kb > 0 ? 1u : 0u);
+          umma_pair_kblock<KIND == Kind::I8>(d_tmem, da, db, kIdesc, kb > pu.kb0 ? 1u : 0u);
           tc_commit_pair_mc(empty0 + 8u * s, 0x3);
           if (++s == STAGES) {
             s = 0;
@@ -1609,14 +1732,45 @@ GemmPlan plan_pair_sw(const GemmPlan &normal, int M, int N, int num_sms) {
   p.tiles_a = static_cast<int>(tw);
   p.tiles_b = (M + p.bn - 1) / p.bn;
   p.units = p.tiles_a * p.tiles_b;
+  p.full_units = p.units;
+  p.tail_s = 1;
   p.grid = 2 * (p.units < pairs ? p.units : pairs);
   p.smem = smem2_bytes_for(p.bn, true);
   return p;
 }
 
-GemmPlan plan_for(Kind kind, int M, int N, int K, int num_sms, int mode, int n_outs) {
+// Tail split of a swapped pair plan.  With T tiles on P pairs the last round
+// holds T mod P tiles and leaves the other pairs idle for a whole tile time.
+// When that round is at most half full, its tiles are cut into S = P / (T mod
+// P) pieces of consecutive k-blocks (at least kTailMinKb each), one per pair,
+// so the round takes about 1/S of a tile plus the exchange of the pieces'
+// INT32 sums (each piece stores the (S-1)/S of the tile it does not own,
+// waits for the others and finishes its own rows: ~4 us).  Measured on the
+// C3 shapes: fc2 (48 k-blocks per tile) gains; 12-k-block tiles (out
+// projection, fc1) lose, hence kTailMinTileKb.
+constexpr int kTailMinKb = 4, kTailMinTileKb = 24;
+std::atomic<int> g_pair_tail{1};
+
+static void split_tail(GemmPlan &p, int num_sms) {
+  const int pairs = num_sms / 2;
+  const int tail = p.units % pairs;
+  if (g_pair_tail.load() == 0 || tail == 0 || p.kb_total < kTailMinTileKb) return;
+  int pieces = pairs / tail;
+  if (pieces > p.kb_total / kTailMinKb) pieces = p.kb_total / kTailMinKb;
+  if (pieces > p.bn / 32) pieces = p.bn / 32;  // every piece owns a 32-row chunk
+  if (pieces < 2) return;
+  p.full_units = p.units - tail;
+  p.tail_s = pieces;
+  p.units = p.full_units + tail * pieces;
+  p.grid = 2 * (p.units < pairs ? p.units : pairs);
+}
+
+GemmPlan plan_for(Kind kind, int M, int N, int K, int num_sms, int mode, int n_outs, bool tail_split) {
   const GemmPlan p = plan_gemm(kind, M, N, K, num_sms);
-  return pair_sw_eligible(p, mode, n_outs) ? plan_pair_sw(p, M, N, num_sms) : p;
+  if (!pair_sw_eligible(p, mode, n_outs)) return p;
+  GemmPlan q = plan_pair_sw(p, M, N, num_sms);
+  if (tail_split) split_tail(q, num_sms);
+  return q;
 }
 
 size_t splitk_ws_bytes(const GemmPlan &p) {
@@ -1625,7 +1779,12 @@ size_t splitk_ws_bytes(const GemmPlan &p) {
 }
 size_t splitk_count_bytes(const GemmPlan &p) {
   if (p.reg) return static_cast<size_t>(p.tiles_a) * 4;
+  if (p.tail_s > 1) return static_cast<size_t>(p.units - p.full_units) * 2 * 4;  // per tail tile, piece, CTA
   return p.splits > 1 ? static_cast<size_t>(p.tiles_a) * p.tiles_b * 4 : 0;
+}
+size_t tail_slot_bytes(const GemmPlan &p) {
+  if (p.tail_s < 2) return 0;
+  return static_cast<size_t>(p.units - p.full_units) * 2 * static_cast<size_t>(p.bn) * 128 * 4;
 }
 
 // GEMM launch with programmatic stream serialisation: its prologue (barriers,
@@ -1696,6 +1855,8 @@ static cudaError_t launch_pair(const GemmPlan &p, const CUtensorMap &tmA, const 
   P.kb_total = p.kb_total;
   P.kb_per_split = p.kb_total;
   P.units = p.units;
+  P.tail_s = SW && p.tail_s > 1 ? p.tail_s : 1;
+  P.full_units = P.tail_s > 1 ? p.full_units : p.units;
   // grid is a multiple of the pair (cluster dimensions are compiled in)
   return counted(launch_dependent(fn, p.grid, smem, st, tmA, tmB, tmOut, P));
 }

@@ -27,7 +27,9 @@ struct GemmPlan {
   int splits = 1;        // K splits (I8 swapped only; exact INT32 reduction)
   int tiles_a = 0, tiles_b = 0;
   int kb_total = 0, kb_per_split = 0;
-  int units = 0;         // tiles_a * tiles_b * splits
+  int units = 0;         // tiles_a * tiles_b * splits, or full_units + tail tiles x tail_s
+  int full_units = 0;    // swapped pair plans: units that are whole tiles (tail_s > 1)
+  int tail_s = 1;        // swapped pair plans: pieces (K ranges) of each tile after full_units
   int grid = 0;          // persistent CTAs
   size_t smem = 0;       // dynamic shared memory bytes
 };
@@ -65,8 +67,11 @@ inline bool tma_store_ok(const float *out, long long ldo) {
 GemmPlan plan_gemm(Kind kind, int M, int N, int K, int num_sms);
 // plan_gemm, with CTA-pair plans turned to the swapped orientation where the
 // register-store epilogue serves the output (mode, number of destinations).
-GemmPlan plan_for(Kind kind, int M, int N, int K, int num_sms, int mode, int n_outs);
+GemmPlan plan_for(Kind kind, int M, int N, int K, int num_sms, int mode, int n_outs, bool tail_split = true);
 extern std::atomic<int> g_pair_direct;  // 0: CTA-pair plans keep the normal orientation
+extern std::atomic<int> g_pair_tail;    // 0: swapped pair plans never cut their last round's tiles
+// INT32 partial tiles of the pieces of a plan's split tail tiles (tail_s > 1).
+size_t tail_slot_bytes(const GemmPlan &p);
 // Bytes of split-K workspace (ws) and counters the plan needs.
 size_t splitk_ws_bytes(const GemmPlan &p);
 // Register-fed decode plan and launch (decode.cu).

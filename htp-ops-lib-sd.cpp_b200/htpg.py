@@ -91,6 +91,7 @@ def lib() -> ctypes.CDLL:
         "htpg_set_profiling": (I, [I]),
         "htpg_set_decode_kernel": (I, [I]),
         "htpg_set_pair_direct": (I, [I]),
+        "htpg_set_pair_tail_split": (I, [I]),
         "htpg_last_phase_ms": (I, [ctypes.POINTER(ctypes.c_float)] * 3),
         "htpg_launch_count": (U64, []),
         "htpg_stream_read": (I, [P, S, P]),
@@ -237,11 +238,11 @@ def f16_run(w: Weights, out, x, bias=None, m=None, channels=0, mode=0, ldo=0, st
 
 
 PLAN_FIELDS = ("swap", "bn", "splits", "tiles_a", "tiles_b", "kb_total", "kb_per_split",
-               "units", "grid", "smem")
+               "units", "grid", "smem", "full_units", "tail_s")
 
 
 def plan_info(kind: int, m: int, n: int, k: int, sms: int = 148) -> dict:
-    out = (ctypes.c_int64 * 10)()
+    out = (ctypes.c_int64 * 12)()
     check(lib().htpg_plan_info(kind, m, n, k, sms, out), "htpg_plan_info")
     return dict(zip(PLAN_FIELDS, list(out)))
 
@@ -250,6 +251,13 @@ def set_decode_kernel(which: int) -> None:
     """0: W8A8 problems with m <= 16 run the register-fed decode kernel (the
     default); 1: they run the swapped tcgen05 kernel.  Results are identical."""
     check(lib().htpg_set_decode_kernel(which), "htpg_set_decode_kernel")
+
+
+def set_pair_tail_split(on: bool) -> None:
+    """True (default): swapped CTA-pair plans cut the tiles of a mostly idle
+    last round into K pieces (exact INT32 hand-off); False: whole tiles only.
+    Results are identical."""
+    check(lib().htpg_set_pair_tail_split(1 if on else 0), "htpg_set_pair_tail_split")
 
 
 def set_pair_direct(on: bool) -> None:

@@ -302,16 +302,22 @@ int htpg_debug_simulate_abort(uint32_t fill);
 int htpg_debug_workspaces(size_t *ws_bytes, size_t *qws_bytes);
 
 /* Tile plan the library uses for an m x n x k problem (kind 0 = W8A8,
- * 1 = FP16) with a row-major output on a device with `sms` SMs.  out[0..9] =
+ * 1 = FP16) with a row-major output on a device with `sms` SMs.  out[0..11] =
  * swap, bn, splits, tiles_a, tiles_b, kb_total, kb_per_split, units, grid,
- * smem bytes.  swap = 0: activation rows are the MMA M (128-row tiles, or
- * 256-row CTA-pair tiles when tiles_a = ceil(m/256)), bn weight columns per
- * tile; 1: small-M swapped tiles (weights are the MMA M); 2: the register-fed
- * decode kernel (W8A8, m <= 16), bn = 8 or 16 activation rows, tiles_a =
- * 16-column groups, units = work chunks; 3: CTA-pair tiles in the swapped
- * orientation, tiles_a = 256-column weight tiles, bn activation rows per
- * tile, stores straight from registers. */
-int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]);
+ * smem bytes, full_units, tail_s.  swap = 0: activation rows are the MMA M
+ * (128-row tiles, or 256-row CTA-pair tiles when tiles_a = ceil(m/256)), bn
+ * weight columns per tile; 1: small-M swapped tiles (weights are the MMA M);
+ * 2: the register-fed decode kernel (W8A8, m <= 16), bn = 8 or 16 activation
+ * rows, tiles_a = 16-column groups, units = work chunks; 3: CTA-pair tiles in
+ * the swapped orientation, tiles_a = 256-column weight tiles, bn activation
+ * rows per tile, stores straight from registers.  For swap = 3, tail_s > 1
+ * means the tiles after the first full_units (a last round of tiles that would
+ * leave at least half of the SM pairs idle) are each cut into tail_s pieces of
+ * consecutive k-blocks, one piece per pair, which exchange their exact INT32
+ * sums so that each finishes a share of the tile's rows: units = full_units
+ * + tail tiles x tail_s.
+ * Otherwise full_units = units and tail_s = 1. */
+int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[12]);
 
 /* W8A8 CTA-pair plans with a row-major output of one destination (modes 0-2
  * and 4): 1 (default) run them in the swapped orientation, whose epilogue
@@ -320,6 +326,12 @@ int htpg_plan_info(int kind, int m, int n, int k, int sms, int64_t out[10]);
  * memory for TMA stores.  Both give identical results; the switch exists for
  * measurement. */
 int htpg_set_pair_direct(int on);
+
+/* Swapped CTA-pair plans whose last round of tiles would leave at least half
+ * of the SM pairs idle: 1 (default) cut those tiles into K pieces (see
+ * htpg_plan_info), 0 keep whole tiles.  Results are identical (the pieces'
+ * INT32 sums are exact); the switch exists for measurement and tests. */
+int htpg_set_pair_tail_split(int on);
 
 /* Which kernel runs W8A8 problems with m <= 16: 0 (default) the register-fed
  * decode kernel, 1 the swapped tcgen05 kernel that also serves 16 < m <= 32.

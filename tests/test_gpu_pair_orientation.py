@@ -116,3 +116,46 @@ def test_ldo_padded_output(gpu, lib):
         htpg.set_pair_direct(True)
     np.testing.assert_array_equal(res[0].view(np.uint32), res[1].view(np.uint32))
     assert (res[0][:, n:] == 123.0).all()
+
+
+@pytest.mark.parametrize("m,k,n", [(4096, 3200, 1536), (4100, 4096, 1536), (4096, 6144, 1536), (4096, 6144, 1280)])
+@pytest.mark.parametrize("mode,with_bias", [(4, False), (1, True), (2, False), (0, True)])
+def test_tail_split_identical(gpu, m, k, n, mode, with_bias):
+    """A last round of tiles cut into K pieces (the pieces exchange their INT32
+    sums, each finishing the 32-row chunks it owns) gives the bits of whole
+    tiles: ragged K pieces (25 k-blocks in 3), two pieces with a ragged last
+    activation tile, the C3 fc2 shape (48 k-blocks in 3) and eight pieces of
+    six k-blocks (one chunk per piece)."""
+    import torch
+    c = O.make_w8a8(25, f"ts{m}", m, k, n, 0.01, with_bias, mode if mode != 4 else 0)
+    hw = htpg.w8a8_weights(_t(c.blob, gpu), k, n)
+    x = _t(c.x, gpu)
+    b = _t(c.bias, gpu) if with_bias else None
+    outs = []
+    try:
+        for split in (True, False):
+            htpg.set_pair_tail_split(split)
+            plan = htpg.plan_info(0, m, n, k)
+            assert plan["swap"] == 3 and (plan["tail_s"] > 1) == split
+            if mode == 4:
+                o = torch.full((m, n), -7, dtype=torch.int32, device=gpu)
+            else:
+                o = torch.full((m, n), float("nan"), device=gpu)
+            htpg.check(htpg.w8a8_run(hw, o, x, b, mode=mode), "run")
+            htpg.check(htpg.check_device(), "device watchdog")
+            outs.append(o.cpu().numpy())
+    finally:
+        htpg.set_pair_tail_split(True)
+    a, w = outs
+    np.testing.assert_array_equal(a.view(np.uint32), w.view(np.uint32))
+    rows = np.unique(np.concatenate([np.arange(0, m, 211), np.arange(max(0, m - 8), m)])).astype(np.int32)
+    if mode == 4:
+        _, _, _, acc = O.w8a8_linear(c.x[rows], c.blob, k, n, want_intermediates=True)
+        np.testing.assert_array_equal(a[rows], acc)
+    else:
+        assert not np.isnan(a).any()
+        ref = O.w8a8_linear(c.x, c.blob, k, n, bias=c.bias if with_bias else None, mode=mode, rows=rows)
+        if mode == 0:
+            np.testing.assert_array_equal(a[rows].view(np.uint32), ref.view(np.uint32))
+        else:
+            assert O.max_abs_rel(a[rows], ref) <= W8A8_TOL

@@ -42,7 +42,17 @@ def test_plans_are_legal(kind, sms):
             assert p["units"] * 2 * 16 * p["bn"] * 4 + p["tiles_a"] * 4 <= 2 * 1024 * 1024 + 4096
             checked += 1
             continue
-        assert p["units"] == p["tiles_a"] * p["tiles_b"] * p["splits"]
+        tiles = p["tiles_a"] * p["tiles_b"] * p["splits"]
+        if p["tail_s"] > 1:
+            # swapped pair plan with its sparse last round cut into K pieces
+            pairs = sms // 2
+            assert p["swap"] == 3 and p["full_units"] % pairs == 0 and p["full_units"] < tiles
+            tail = tiles - p["full_units"]
+            assert tail <= pairs // 2 and tail * p["tail_s"] <= pairs
+            assert p["units"] == p["full_units"] + tail * p["tail_s"] and kb_total >= max(24, 4 * p["tail_s"])
+            assert p["tail_s"] <= p["bn"] // 32
+        else:
+            assert p["units"] == tiles and p["full_units"] == p["units"]
         assert 1 <= p["grid"] <= sms and p["grid"] <= (2 * p["units"] if p["bn"] else p["units"])
         # K ranges: every split non-empty, together exactly [0, kb_total)
         assert p["splits"] * p["kb_per_split"] >= kb_total
@@ -99,6 +109,44 @@ def test_headline_shapes():
     assert not c1["swap"] and c1["units"] >= 0.85 * 148
     c2 = htpg.plan_info(1, 77, 3072, 768)
     assert not c2["swap"] and c2["splits"] == 1
+
+
+def _tail_split(tiles, kb_total, bn, pairs=74):
+    """Restatement of the planner's tail split: (full_units, tail_s)."""
+    tail = tiles % pairs
+    if tail == 0 or kb_total < 24:
+        return tiles, 1
+    pieces = min(pairs // tail, kb_total // 4, bn // 32)
+    if pieces < 2:
+        return tiles, 1
+    return tiles - tail, pieces
+
+
+@pytest.mark.parametrize("m,n,k", [(4096, 1536, 1536), (4096, 1536, 6144), (4096, 6144, 1536), (4096, 4608, 1536),
+                                   (16384, 6144, 1536), (1000, 1280, 1536), (4096, 1536, 3200), (4100, 1536, 4096),
+                                   (4096, 1280, 6144)])
+def test_tail_split(m, n, k):
+    """Swapped pair plans cut a last round that would leave at least half of the
+    74 SM pairs idle into K pieces of tiles with at least 24 k-blocks; the C3
+    fc2 (96 tiles of 48 k-blocks: 74 whole, 22 tail tiles x 3 pieces) takes
+    it, C4, the other C3 shapes (fuller last rounds or 12 k-blocks) keep
+    whole tiles."""
+    p = htpg.plan_info(0, m, n, k)
+    assert p["swap"] == 3
+    tiles = p["tiles_a"] * p["tiles_b"]
+    full, s = _tail_split(tiles, p["kb_total"], p["bn"])
+    assert (p["full_units"], p["tail_s"]) == (full, s)
+    assert p["units"] == full + (tiles - full) * s
+    if (m, n, k) == (4096, 1536, 6144):
+        assert (full, s, p["units"]) == (74, 3, 140)
+    if (m, n, k) in ((16384, 6144, 1536), (4096, 4608, 1536)):
+        assert s == 1
+    try:
+        htpg.set_pair_tail_split(False)
+        q = htpg.plan_info(0, m, n, k)
+        assert q["tail_s"] == 1 and q["units"] == tiles and q["bn"] == p["bn"]
+    finally:
+        htpg.set_pair_tail_split(True)
 
 
 def test_qk0_plan():
