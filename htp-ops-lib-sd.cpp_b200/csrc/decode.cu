@@ -120,8 +120,8 @@ __device__ __forceinline__ void mma_atom(int32_t (&acc)[NT][4], const WFrag &f, 
     const uint4 *q = reinterpret_cast<const uint4 *>(act + static_cast<size_t>(m) * K + k0);
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
     const bool ok = m < M && k0 < K;
-    x[2 * j] = ok ? __ldg(q) : z;
-    x[2 * j + 1] = ok ? __ldg(q + 1) : z;
+    x[2 * j] = ok ? ld_dep(q) : z;  // written by the activation pass
+    x[2 * j + 1] = ok ? ld_dep(q + 1) : z;
   }
 #pragma unroll
   for (int s = 0; s < 4; ++s)
@@ -276,8 +276,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_i8_kernel(const DecPara
     // held in registers through the main loop, stored after it (their load
     // latency stays off the loop's start)
     const int pi = threadIdx.x, pn = cg0 * 16 + pi;
-    const float p_bias = (g.bias != nullptr && pi < ncg * 16 && pn < g.N) ? __ldg(g.bias + pn) : 0.0f;
-    const float p_rs = pi < g.M ? __ldg(g.row_scale + pi) : 0.0f;
+    const float p_bias = (g.bias != nullptr && pi < ncg * 16 && pn < g.N) ? ld_dep(g.bias + pn) : 0.0f;
+    const float p_rs = pi < g.M ? ld_dep(g.row_scale + pi) : 0.0f;
     __syncthreads();  // tile zeroed
 
     int ccg = static_cast<int>(b0 / KB), ckb = static_cast<int>(b0 - static_cast<long long>(ccg) * KB);

@@ -18,6 +18,7 @@
 
 #include "kernels.h"
 #include "ptx.cuh"
+#include "quant.cuh"
 #include "epilogue.cuh"
 
 namespace htpg {
@@ -30,25 +31,8 @@ cudaError_t counted(cudaError_t e) {
 }
 
 // ===================================================================== quant
-// Shared per-element steps.  Every FP32 operation is an explicit IEEE
-// round-to-nearest intrinsic so the compiler cannot contract or reorder.
-__device__ __forceinline__ float scaled_input(float x, const float *inverse, int c) {
-  return inverse ? __fmul_rn(x, __ldg(inverse + c)) : x;
-}
-// u = x'*s + 128 (two roundings), clamped to [1,255] by integer max/min on the
-// IEEE bits (linear_w8a8.c:44-49), then rounded half to even; returned as the
-// signed code u-128 in [-127, 127].
-__device__ __forceinline__ int quant_code(float xs, float s) {
-  const float u = __fadd_rn(__fmul_rn(xs, s), 128.0f);
-  int b = __float_as_int(u);
-  b = max(b, 0x3f800000);
-  b = min(b, 0x437f0000);
-  return __float2int_rn(__int_as_float(b)) - 128;
-}
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-  return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
-         ((static_cast<uint32_t>(c) & 0xffu) << 16) | ((static_cast<uint32_t>(d) & 0xffu) << 24);
-}
+// The per-element steps (scaled_input, quant_code, pack4, row_scale_of) are in
+// quant.cuh.
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -78,8 +62,8 @@ __global__ void __launch_bounds__(TPR *ROWS) quantize_rows_kernel(int8_t *__rest
   float amax = 0.0f;
   if (valid) {
     for (int c = t * 8; c < k; c += TPR * 8) {
-      const float4 a = __ldg(reinterpret_cast<const float4 *>(xr + c));
-      const float4 b = __ldg(reinterpret_cast<const float4 *>(xr + c + 4));
+      const float4 a = ld_dep(reinterpret_cast<const float4 *>(xr + c));
+      const float4 b = ld_dep(reinterpret_cast<const float4 *>(xr + c + 4));
       const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(scaled_input(v[i], inverse, c + i)));
@@ -94,13 +78,13 @@ __global__ void __launch_bounds__(TPR *ROWS) quantize_rows_kernel(int8_t *__rest
     for (int w = 0; w < kWarps; ++w) amax = fmaxf(amax, red[local_row][w]);
   }
   if (!valid) return;
-  const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
-  const float s = __fdiv_rn(1.0f, scale);
+  const float scale = row_scale_of(amax);
+  const float s = row_inverse_of(scale);
   if (t == 0) scales[row] = scale;
   int8_t *cr = codes + static_cast<size_t>(row) * k;
   for (int c = t * 8; c < k; c += TPR * 8) {
-    const float4 a = __ldg(reinterpret_cast<const float4 *>(xr + c));
-    const float4 b = __ldg(reinterpret_cast<const float4 *>(xr + c + 4));
+    const float4 a = ld_dep(reinterpret_cast<const float4 *>(xr + c));
+    const float4 b = ld_dep(reinterpret_cast<const float4 *>(xr + c + 4));
     const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     int q[8];
 #pragma unroll
@@ -132,8 +116,8 @@ __global__ void __launch_bounds__(256) quantize_rows_reg_kernel(int8_t *__restri
     const int c = s * 256 + lane * 8;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
     if (c < k) {
-      a = __ldg(reinterpret_cast<const float4 *>(xr + c));
-      b = __ldg(reinterpret_cast<const float4 *>(xr + c + 4));
+      a = ld_dep(reinterpret_cast<const float4 *>(xr + c));
+      b = ld_dep(reinterpret_cast<const float4 *>(xr + c + 4));
     }
     v[s][0] = a.x; v[s][1] = a.y; v[s][2] = a.z; v[s][3] = a.w;
     v[s][4] = b.x; v[s][5] = b.y; v[s][6] = b.z; v[s][7] = b.w;
@@ -151,8 +135,8 @@ __global__ void __launch_bounds__(256) quantize_rows_reg_kernel(int8_t *__restri
     }
   }
   amax = warp_max(amax);
-  const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
-  const float inv_scale = __fdiv_rn(1.0f, scale);
+  const float scale = row_scale_of(amax);
+  const float inv_scale = row_inverse_of(scale);
   if (lane == 0) scales[row] = scale;
   int8_t *cr = codes + static_cast<size_t>(row) * k;
 #pragma unroll
@@ -190,7 +174,7 @@ __global__ void __launch_bounds__(kWideThreads) quantize_rows_wide_kernel(int8_t
   for (int j = 0; j < J; ++j) {
     const int c = (j * kWideThreads + t) * 4;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (c < k) a = __ldg(reinterpret_cast<const float4 *>(xr + c));
+    if (c < k) a = ld_dep(reinterpret_cast<const float4 *>(xr + c));
     v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
   }
   float amax = 0.0f;
@@ -211,8 +195,8 @@ __global__ void __launch_bounds__(kWideThreads) quantize_rows_wide_kernel(int8_t
   amax = 0.0f;
 #pragma unroll
   for (int w = 0; w < kWideThreads / 32; ++w) amax = fmaxf(amax, red[w]);
-  const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
-  const float inv_scale = __fdiv_rn(1.0f, scale);
+  const float scale = row_scale_of(amax);
+  const float inv_scale = row_inverse_of(scale);
   if (t == 0) scales[row] = scale;
   int8_t *cr = codes + static_cast<size_t>(row) * k;
 #pragma unroll
@@ -293,8 +277,8 @@ __global__ void to_f16_kernel(uint16_t *__restrict__ dst, const float *__restric
   grid_dependency_wait();
   const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   if (i >= count) return;
-  const float4 a = __ldg(reinterpret_cast<const float4 *>(x + i));
-  const float4 b = __ldg(reinterpret_cast<const float4 *>(x + i + 4));
+  const float4 a = ld_dep(reinterpret_cast<const float4 *>(x + i));
+  const float4 b = ld_dep(reinterpret_cast<const float4 *>(x + i + 4));
   const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
   uint32_t w[4];
 #pragma unroll
@@ -444,7 +428,7 @@ __global__ void __launch_bounds__(256) im2col_f16_kernel(uint16_t *__restrict__ 
   for (int cc = tc; cc < kI2cCols; cc += 2) {
     const int ci = col_ci[cc], xx = xbase + col_kx[cc], yy = ybase + col_ky[cc];
     const float v = (row_ok && ci < g.ic && xx >= 0 && xx < wu && yy >= 0 && yy < hu)
-                        ? __ldg(x + (static_cast<size_t>(ci) * g.ih + (yy >> ush)) * g.iw + (xx >> ush))
+                        ? ld_dep(x + (static_cast<size_t>(ci) * g.ih + (yy >> ush)) * g.iw + (xx >> ush))
                         : 0.0f;
     tile[tr * kI2cPitch + cc] = __half_as_ushort(__float2half_rn(v));
   }
@@ -676,7 +660,7 @@ __device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
   }
   const int m = c.row0 + c.q * 32 + c.lane;
   const bool m_ok = m < g.M;
-  const float rs = (KIND == Kind::I8 && m_ok) ? __ldg(g.row_scale + m) : 0.0f;
+  const float rs = (KIND == Kind::I8 && m_ok) ? ld_dep(g.row_scale + m) : 0.0f;
   float psw[kMine], pb[kMine];
   int pcr[kMine];
 #pragma unroll
@@ -685,7 +669,7 @@ __device__ __forceinline__ bool epilogue_normal(const EpiCtx &c) {
     const bool ok = nl < g.N;
     psw[i] = (KIND == Kind::I8 && ok) ? __ldg(g.col_scale + nl) : 0.0f;
     pcr[i] = (KIND == Kind::I8 && ok) ? __ldg((MODE == 5 ? g.col_sum7 : g.col_corr) + nl) : 0;
-    pb[i] = (BIAS && ok) ? __ldg(g.bias + nl) : 0.0f;
+    pb[i] = (BIAS && ok) ? ld_dep(g.bias + nl) : 0.0f;
   }
   const bool ok = mbar_wait(c.full_bar, c.full_parity, g.watchdog, kWatchEpilogue, c.L.abort);
   tc_fence_after();
@@ -862,7 +846,7 @@ __device__ __forceinline__ bool epilogue_swap(const EpiCtx &c) {
   if (!fin || !owner) return c_ok;
   float *scr = c.prm;  // the row scales of this tile's (at most 32) activation rows
   const int mrow = c.w.tb * BN + c.lane;
-  scr[c.lane] = (KIND == Kind::I8 && mrow < g.M) ? __ldg(g.row_scale + mrow) : 0.0f;
+  scr[c.lane] = (KIND == Kind::I8 && mrow < g.M) ? ld_dep(g.row_scale + mrow) : 0.0f;
   __syncwarp();
   if (!n_ok) return c_ok;
   float sw = 0.0f, bn_ = 0.0f;
@@ -871,7 +855,7 @@ __device__ __forceinline__ bool epilogue_swap(const EpiCtx &c) {
     sw = __ldg(g.col_scale + n);
     cr = __ldg((MODE == 5 ? g.col_sum7 : g.col_corr) + n);
   }
-  if (BIAS) bn_ = __ldg(g.bias + n);
+  if (BIAS) bn_ = ld_dep(g.bias + n);
 #pragma unroll
   for (int j = 0; j < BN; ++j) {
     const int m = c.w.tb * BN + j;
@@ -1225,11 +1209,11 @@ __device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const Kernel
     const bool ok = n < g.N;
     f_sw = (KIND == Kind::I8 && ok) ? __ldg(g.col_scale + n) : 0.0f;
     f_cr = (KIND == Kind::I8 && ok) ? __ldg(g.col_corr + n) : 0;
-    f_bv = (BIAS && ok) ? __ldg(g.bias + n) : 0.0f;
+    f_bv = (BIAS && ok) ? ld_dep(g.bias + n) : 0.0f;
 #pragma unroll
     for (int i = 0; i < kCh; ++i) {
       const int m = m0 + 32 * i + lane;
-      f_rs[i] = (KIND == Kind::I8 && m < g.M) ? __ldg(g.row_scale + m) : 0.0f;
+      f_rs[i] = (KIND == Kind::I8 && m < g.M) ? ld_dep(g.row_scale + m) : 0.0f;
     }
   };
   if (pair < P.units) fetch(pair);

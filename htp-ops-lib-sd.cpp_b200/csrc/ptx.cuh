@@ -159,6 +159,39 @@ __device__ __forceinline__ float ex2_approx(float x) {
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Loads of data that an earlier kernel in the stream writes: the activations,
+// codes, row scales and biases.  Kernels here are launched as programmatic
+// dependents, so they start while earlier kernels still write; the
+// non-coherent path (ld.global.nc, __ldg) is valid only for data that stays
+// unchanged for a kernel's whole life and can return lines cached before
+// those writes.  Ordinary loads issued after griddepcontrol.wait observe them.
+// (asm volatile: never moved above the wait, which is asm volatile too.)
+__device__ __forceinline__ float ld_dep(const float *p) {
+  float v;
+  asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ld_dep(const float4 *p) {
+  float4 v;
+  asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_dep(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint16_t ld_dep(const uint16_t *p) {
+  uint16_t v;
+  asm volatile("ld.global.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_dep(const uint4 *p) {
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
 // Hardware tanh approximation (PTX tanh.approx.f32, relative error about 2^-11).
 __device__ __forceinline__ float tanh_approx(float x) {
   float y;

@@ -80,12 +80,12 @@ struct ChunkWords {
 template <int QT>
 __device__ __forceinline__ ChunkWords chunk_words_global(const uint8_t *blk, int m) {
   ChunkWords w;
-  w.sc = __ldg(reinterpret_cast<const uint4 *>(blk));
+  w.sc = ld_dep(reinterpret_cast<const uint4 *>(blk));
   if constexpr (QT == kGgmlQ8_0) {
 #pragma unroll
-    for (int v = 0; v < 4; ++v) w.q[v] = __ldg(reinterpret_cast<const uint16_t *>(blk + 16 + 2 * m + 64 * v));
+    for (int v = 0; v < 4; ++v) w.q[v] = ld_dep(reinterpret_cast<const uint16_t *>(blk + 16 + 2 * m + 64 * v));
   } else {
-    w.q[0] = __ldg(reinterpret_cast<const uint32_t *>(blk + 16 + 4 * m));
+    w.q[0] = ld_dep(reinterpret_cast<const uint32_t *>(blk + 16 + 4 * m));
   }
   return w;
 }
@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(256) qk0_repack_kernel(uint4 *__restrict__ dst
   const int nt = 4 * ta + r, kt = 2 * kb + e;
   uint4 v = make_uint4(0u, 0u, 0u, 0u);
   if (nt < ntiles && kt < ktiles)
-    v = __ldg(src + ((static_cast<long long>(nt) * ktiles + kt) * 4 + j) * blk16 + part);
+    v = ld_dep(src + ((static_cast<long long>(nt) * ktiles + kt) * 4 + j) * blk16 + part);
   dst[u] = v;
 }
 
@@ -567,8 +567,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
         const int m = tb * BN + r, k0 = kb * 64 + c * 8;
         if (m < g.M && k0 < g.K) {
           const float4 *src = reinterpret_cast<const float4 *>(g.x + static_cast<long long>(m) * g.K + k0);
-          xa[u][0] = __ldg(src);
-          xa[u][1] = __ldg(src + 1);
+          xa[u][0] = ld_dep(src);  // written by the kernel before this one
+          xa[u][1] = ld_dep(src + 1);
         } else {
           xa[u][0] = xa[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
