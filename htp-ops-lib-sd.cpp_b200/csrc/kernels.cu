@@ -62,8 +62,8 @@ __global__ void __launch_bounds__(TPR *ROWS) quantize_rows_kernel(int8_t *__rest
   float amax = 0.0f;
   if (valid) {
     for (int c = t * 8; c < k; c += TPR * 8) {
-      const float4 a = ld_dep(reinterpret_cast<const float4 *>(xr + c));
-      const float4 b = ld_dep(reinterpret_cast<const float4 *>(xr + c + 4));
+      const float4 a = ld_dep_stream(reinterpret_cast<const float4 *>(xr + c));
+      const float4 b = ld_dep_stream(reinterpret_cast<const float4 *>(xr + c + 4));
       const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(scaled_input(v[i], inverse, c + i)));
@@ -83,8 +83,8 @@ __global__ void __launch_bounds__(TPR *ROWS) quantize_rows_kernel(int8_t *__rest
   if (t == 0) scales[row] = scale;
   int8_t *cr = codes + static_cast<size_t>(row) * k;
   for (int c = t * 8; c < k; c += TPR * 8) {
-    const float4 a = ld_dep(reinterpret_cast<const float4 *>(xr + c));
-    const float4 b = ld_dep(reinterpret_cast<const float4 *>(xr + c + 4));
+    const float4 a = ld_dep_stream(reinterpret_cast<const float4 *>(xr + c));
+    const float4 b = ld_dep_stream(reinterpret_cast<const float4 *>(xr + c + 4));
     const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     int q[8];
 #pragma unroll
@@ -116,8 +116,8 @@ __global__ void __launch_bounds__(256) quantize_rows_reg_kernel(int8_t *__restri
     const int c = s * 256 + lane * 8;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
     if (c < k) {
-      a = ld_dep(reinterpret_cast<const float4 *>(xr + c));
-      b = ld_dep(reinterpret_cast<const float4 *>(xr + c + 4));
+      a = ld_dep_stream(reinterpret_cast<const float4 *>(xr + c));
+      b = ld_dep_stream(reinterpret_cast<const float4 *>(xr + c + 4));
     }
     v[s][0] = a.x; v[s][1] = a.y; v[s][2] = a.z; v[s][3] = a.w;
     v[s][4] = b.x; v[s][5] = b.y; v[s][6] = b.z; v[s][7] = b.w;
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(kWideThreads) quantize_rows_wide_kernel(int8_t
   for (int j = 0; j < J; ++j) {
     const int c = (j * kWideThreads + t) * 4;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (c < k) a = ld_dep(reinterpret_cast<const float4 *>(xr + c));
+    if (c < k) a = ld_dep_stream(reinterpret_cast<const float4 *>(xr + c));
     v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
   }
   float amax = 0.0f;
@@ -277,8 +277,8 @@ __global__ void to_f16_kernel(uint16_t *__restrict__ dst, const float *__restric
   grid_dependency_wait();
   const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   if (i >= count) return;
-  const float4 a = ld_dep(reinterpret_cast<const float4 *>(x + i));
-  const float4 b = ld_dep(reinterpret_cast<const float4 *>(x + i + 4));
+  const float4 a = ld_dep_stream(reinterpret_cast<const float4 *>(x + i));
+  const float4 b = ld_dep_stream(reinterpret_cast<const float4 *>(x + i + 4));
   const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
   uint32_t w[4];
 #pragma unroll
@@ -1191,6 +1191,14 @@ __device__ __forceinline__ SmemLayout carve2(uint8_t *raw) {
 // read as shared-memory broadcasts, and both are fetched one unit ahead so
 // their global-load latency hides behind the current unit's arithmetic.  The
 // whole unit loop lives here (one dispatch on the epilogue mode per launch).
+// Output stores marked as streaming (evict-first in the L2): the output is
+// written once and not read by this kernel, and with the default policy its
+// stream (403 MB for C4) evicts the activation-code tiles that later tiles
+// read again.  Measured on C4: operator 158.2 -> 154.1 us (interleaved
+// medians); no change where the output fits in the L2.
+__device__ __forceinline__ void st_stream(float *p, float v) {
+  asm volatile("st.global.cs.f32 [%0], %1;" ::"l"(p), "f"(v));
+}
 template <Kind KIND, int BN, int MODE, bool BIAS>
 __device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const KernelParams &P, const SmemLayout &L,
                                                  float *rs, uint32_t tmem_base, int q, int part, int lane,
@@ -1327,10 +1335,10 @@ __device__ __forceinline__ void epilogue_loop_sw(const GemmArgs &g, const Kernel
             float o0, o1, o2, o3;
             finish2<MODE, BIAS>(r[4 * j4], r[4 * j4 + 1], cr, sw2, s4.x, s4.y, bias2, one2, o0, o1);
             finish2<MODE, BIAS>(r[4 * j4 + 2], r[4 * j4 + 3], cr, sw2, s4.z, s4.w, bias2, one2, o2, o3);
-            *row(4 * j4) = o0;
-            *row(4 * j4 + 1) = o1;
-            *row(4 * j4 + 2) = o2;
-            *row(4 * j4 + 3) = o3;
+            st_stream(row(4 * j4), o0);
+            st_stream(row(4 * j4 + 1), o1);
+            st_stream(row(4 * j4 + 2), o2);
+            st_stream(row(4 * j4 + 3), o3);
           }
         } else {
 #pragma unroll

@@ -176,6 +176,14 @@ __device__ __forceinline__ float4 ld_dep(const float4 *p) {
   asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
   return v;
 }
+// The same for data read exactly once (the activation passes' x): marked as
+// streaming (evict-first in the L2), so reading it does not push out the
+// codes the activation pass writes for the GEMM that follows.
+__device__ __forceinline__ float4 ld_dep_stream(const float4 *p) {
+  float4 v;
+  asm volatile("ld.global.cs.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
 __device__ __forceinline__ uint32_t ld_dep(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
