@@ -371,6 +371,12 @@ extern "C" int htpg_stream_read(const void *src, size_t bytes, void *stream) {
   return record_cuda(launch_stream_read(src, bytes, d->sms, pick_stream(d, stream)));
 }
 
+extern "C" int htpg_set_qk0_decode(int which) {
+  if (which != 0 && which != 1) return HTPG_EARGS;
+  g_qdec.store(which == 0 ? 1 : 0);
+  return HTPG_OK;
+}
+
 extern "C" int htpg_set_pair_tail_split(int on) {
   if (on != 0 && on != 1) return HTPG_EARGS;
   g_pair_tail.store(on);
@@ -1214,6 +1220,25 @@ extern "C" int htpg_qk0_run(const htpg_weights *w, float *out, const float *x, i
     return run_common(&f, &out, 1, 0, x, nullptr, m, n, 0, stream, nullptr, nullptr, true);
   }
   std::lock_guard<std::mutex> lk(g_mu);
+  if (qdec_serves(qt, m) && g_qdec.load() != 0) {
+    // decode shapes: the register-fed kernel (weights streamed into registers)
+    const QDecPlan plan = plan_qdec(qt, m, n, k, d->sms);
+    if (qdec_counter_bytes(plan) > kQCounterBytes || plan.smem > kQdMaxSlice) return HTPG_ENOPLAN;
+    uint8_t *base = nullptr;
+    rc = qworkspace(d, st, kQCounterBytes + align_up(qdec_partial_bytes(plan), 1024), &base);
+    if (rc) return rc;
+    QGemmArgs a;
+    a.x = x;
+    a.M = m;
+    a.N = n;
+    a.K = k;
+    a.out = out;
+    a.ldo = n;
+    a.partials = reinterpret_cast<float *>(base + kQCounterBytes);
+    a.counters = reinterpret_cast<uint32_t *>(base);
+    a.watchdog = d->watchdog;
+    return record_cuda(launch_qdec(qt, plan, records, a, st));
+  }
   const QGemmPlan plan = plan_qgemm(qt, m, n, k, d->sms);
   if (qgemm_counter_bytes(plan) > kQCounterBytes) return HTPG_ENOPLAN;
   const size_t part = align_up(qgemm_partial_bytes(plan), 1024);

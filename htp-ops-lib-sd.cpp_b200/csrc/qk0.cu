@@ -626,6 +626,339 @@ __global__ void __launch_bounds__(kQThreads, 1)
   }
 }
 
+// ============================================= register-fed decode (M <= 16)
+// Each CTA owns up to 16 32-column weight tiles (one per warp) and one range
+// of 32-deep k-tiles.  It first rounds its slice of x to FP16 into shared
+// memory (the reference's activation rounding).  Each warp streams its tile's
+// super-blocks from the stage records into its own shared-memory ring with
+// cp.async (a k-tile pair of one tile is 8 consecutive super-blocks, 1152 or
+// 2176 bytes; four pairs in flight), decodes only the FP16 pairs its MMA
+// fragments hold, with dq_decode's arithmetic, and accumulates with mma.sync
+// m16n8k16 (FP16 x FP16 -> FP32).  Fragment layout: lane (g, t) holds, for
+// columns g and g+8 of a 16-column group, pair t of super-blocks 2s and 2s+1
+// (k = 16s + 2t, +1 and 16s + 8 + 2t, +1 of the tile's 32); the activation
+// fragment holds the same k.  The k ranges' FP32 partial tiles meet in a
+// workspace; the last range to arrive sums them in range order
+// (deterministic) and writes the output.  No thread waits for another CTA.
+constexpr int kQdWarps = 16, kQdThreads = 32 * kQdWarps;
+constexpr int kQdStages = 4;       // k-tile pairs of a warp's tile in flight
+constexpr int kQdMaxSplits = 16;   // k ranges per tile at most (the last one sums them all)
+__host__ __device__ constexpr int qd_pair_bytes(int qt) { return 8 * (qt == kGgmlQ8_0 ? 272 : 144); }
+
+struct QDecParams {
+  const uint8_t *w;   // stage records
+  const float *x;     // [M][K]
+  float *out;         // [M][ldo]
+  float *part;        // [ntiles][S][32 columns][16 tokens]
+  uint32_t *cnt;      // [ntiles], zero before the launch, left zero
+  int M, N, K, ldo;
+  int ntiles, ktiles, kb_total, S, pitch;  // pitch: halves per activation row in shared memory
+};
+
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// The raw words one lane needs from one 32 x 32 tile (four super-blocks) in
+// shared memory: scale word t of each super-block and the codes of pair t of
+// columns g, g+8, g+16, g+24.
+struct QdWords {
+  uint32_t sc[4];
+  uint32_t q[4][4];  // [super-block][column]
+};
+
+template <int QT>
+__device__ __forceinline__ void qd_load(QdWords &w, uint32_t tile, int g, int t) {
+  constexpr int BLK = QT == kGgmlQ8_0 ? 272 : 144;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t sb = tile + j * BLK;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w.sc[j]) : "r"(sb + 4 * t));
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int m = g + 8 * c;
+      if constexpr (QT == kGgmlQ8_0) {
+        uint16_t h;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(sb + 16 + 2 * m + 64 * t));
+        w.q[j][c] = h;
+      } else {
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w.q[j][c]) : "r"(sb + 16 + 4 * m));
+      }
+    }
+  }
+}
+
+// Pair t (k = 2t, 2t+1 of the super-block's eight) of column m: the same
+// operations as dq_decode's element pair t.  sh = 4 * the nibble index of the
+// pair's first code in the word: dq_decode's pairs are (b0.lo, b2.lo),
+// (b1.lo, b3.lo), (b0.hi, b2.hi), (b1.hi, b3.hi), i.e. nibbles 0, 2, 1, 3 and
+// the same + 4 (computed without branches: ((t & 1) << 3) | ((t >> 1) << 2)).
+template <int QT>
+__device__ __forceinline__ uint32_t qd_pair(uint32_t scw, uint32_t q, int m, int sh) {
+  const uint32_t s = prmt(scw, scw, (m & 16) ? 0x3232u : 0x1010u);
+  uint32_t h, bias;
+  if constexpr (QT == kGgmlQ8_0) {
+    h = prmt(q, 0x64646464u, 0x5140u) ^ 0x00800080u;
+    bias = 0x64806480u;
+  } else if constexpr (QT == kGgmlQ4_0) {
+    h = ((q >> sh) & 0x000F000Fu) | 0x64006400u;
+    bias = 0x64086408u;
+  } else {
+    // the pair's two nibbles looked up together, levels into the two halves
+    const uint32_t y = ((q >> sh) & 0xFu) | (((q >> (sh + 16)) & 0xFu) << 4);
+    h = prmt(iq4_lookup4(y), 0u, 0x5140u) | 0x64006400u;
+    bias = 0x64806480u;
+  }
+  return hmul2_rn(hsub2_rn(h, bias), s);
+}
+
+__device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+template <int QT, int NT>
+__global__ void __launch_bounds__(kQdThreads, 1) qdec_kernel(const QDecParams P) {
+  constexpr int BLK = QT == kGgmlQ8_0 ? 272 : 144;
+  constexpr int PAIR = qd_pair_bytes(QT);
+  extern __shared__ __align__(16) uint32_t qd_smem[];  // [16 warps][stages][PAIR] rings, then the x slice
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int sh = ((t & 1) << 3) | ((t >> 1) << 2);  // see qd_pair
+  const int grp = blockIdx.x / P.S, sp = blockIdx.x - grp * P.S;
+  const int kt0 = static_cast<int>(static_cast<long long>(P.ktiles) * sp / P.S);
+  const int kt1 = static_cast<int>(static_cast<long long>(P.ktiles) * (sp + 1) / P.S);
+  const int nt = grp * kQdWarps + warp;
+  const bool active = nt < P.ntiles;
+  const uint32_t ring = smem_u32(qd_smem) + static_cast<uint32_t>(warp * kQdStages * PAIR);
+  uint32_t *qd_x = qd_smem + kQdWarps * kQdStages * PAIR / 4;  // [8 NT rows][pitch / 2] f16x2
+  // k-tile pair pp (k-tiles 2pp, 2pp+1) of this warp's tile: 8 consecutive
+  // super-blocks of record (nt/4, pp), starting at block (nt%4)*8
+  const int pp0 = kt0 >> 1, npairs = ((kt1 - 1) >> 1) - pp0 + 1;
+  auto issue_pair = [&](int i) {  // pair pp0 + i into stage i % stages (one commit group per call)
+    if (active && i < npairs) {
+      const uint8_t *src = P.w + (static_cast<size_t>(nt >> 2) * P.kb_total + (pp0 + i)) * (32u * BLK) +
+                           static_cast<size_t>((nt & 3) << 3) * BLK;
+      const uint32_t dst = ring + static_cast<uint32_t>((i % kQdStages) * PAIR);
+      for (int c = lane; c < PAIR / 16; c += 32)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16 * c), "l"(src + 16 * c) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  grid_dependents_launch();
+  // the weight is prepared once (static): its first pairs stream now
+#pragma unroll
+  for (int i = 0; i < kQdStages; ++i) issue_pair(i);
+  grid_dependency_wait();  // x may be the previous operator's output
+  // this CTA's slice of x, rounded to FP16 (rows >= M are zero)
+  const int kw = (kt1 - kt0) * 32;  // k per row of the slice
+  for (int i = threadIdx.x; i < 8 * NT * (kw / 4); i += kQdThreads) {
+    const int r = i / (kw / 4), c4 = i - r * (kw / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < P.M) v = ld_dep(reinterpret_cast<const float4 *>(P.x + static_cast<size_t>(r) * P.K + kt0 * 32) + c4);
+    qd_x[r * (P.pitch / 2) + 2 * c4] = f2_to_h2(v.x, v.y);
+    qd_x[r * (P.pitch / 2) + 2 * c4 + 1] = f2_to_h2(v.z, v.w);
+  }
+  __syncthreads();
+  if (!active) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    return;
+  }
+
+  float acc[2][NT][4];
+#pragma unroll
+  for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+    for (int jt = 0; jt < NT; ++jt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[cg][jt][r] = 0.0f;
+  for (int i = 0; i < npairs; ++i) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kQdStages - 1) : "memory");  // pair i has landed
+    __syncwarp();
+    const uint32_t stage = ring + static_cast<uint32_t>((i % kQdStages) * PAIR);
+#pragma unroll 1
+    for (int e = 0; e < 2; ++e) {
+      const int kt = 2 * (pp0 + i) + e;
+      if (kt < kt0 || kt >= kt1) continue;
+      QdWords cur;
+      qd_load<QT>(cur, stage + e * 4 * BLK, g, t);
+      const int kl = (kt - kt0) * 32;  // k of the tile within the slice
+#pragma unroll
+      for (int s2 = 0; s2 < 2; ++s2) {
+        uint32_t b[NT][2];
+#pragma unroll
+        for (int jt = 0; jt < NT; ++jt) {
+          const uint32_t *row = qd_x + (8 * jt + g) * (P.pitch / 2);
+          b[jt][0] = row[(kl + 16 * s2 + 2 * t) / 2];
+          b[jt][1] = row[(kl + 16 * s2 + 8 + 2 * t) / 2];
+        }
+#pragma unroll
+        for (int cg = 0; cg < 2; ++cg) {
+          const int c0 = 2 * cg, c1 = 2 * cg + 1;
+          const uint32_t a0 = qd_pair<QT>(cur.sc[2 * s2], cur.q[2 * s2][c0], g + 8 * c0, sh);
+          const uint32_t a1 = qd_pair<QT>(cur.sc[2 * s2], cur.q[2 * s2][c1], g + 8 * c1, sh);
+          const uint32_t a2 = qd_pair<QT>(cur.sc[2 * s2 + 1], cur.q[2 * s2 + 1][c0], g + 8 * c0, sh);
+          const uint32_t a3 = qd_pair<QT>(cur.sc[2 * s2 + 1], cur.q[2 * s2 + 1][c1], g + 8 * c1, sh);
+#pragma unroll
+          for (int jt = 0; jt < NT; ++jt) mma_f16_16816(acc[cg][jt], a0, a1, a2, a3, b[jt][0], b[jt][1]);
+        }
+      }
+    }
+    __syncwarp();  // every lane is done with the stage before it is refilled
+    issue_pair(i + kQdStages);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  // this range's partial tile, then the arrival; the last range of the tile
+  // sums all ranges' partials in range order and writes the output
+  auto elem = [&](int cg, int jt, int r) {  // accumulator element (cg, jt, r) in a [32][16] partial tile
+    return (16 * cg + g + ((r & 2) ? 8 : 0)) * 16 + 8 * jt + 2 * t + (r & 1);
+  };
+  float *mine = P.part + (static_cast<size_t>(nt) * P.S + sp) * (32 * 16);
+#pragma unroll
+  for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+    for (int jt = 0; jt < NT; ++jt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) mine[elem(cg, jt, r)] = acc[cg][jt][r];
+  __syncwarp();
+  uint32_t prev = 0u;
+  if (lane == 0)
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.cnt + nt) : "memory");
+  prev = __shfl_sync(0xffffffffu, prev, 0);
+  if (prev != static_cast<uint32_t>(P.S - 1)) return;
+  __syncwarp();  // lane 0's acquire orders every lane's reads below
+  const float *all = P.part + static_cast<size_t>(nt) * P.S * (32 * 16);
+  // the lane's elements of every range: QB ranges' loads in flight at a time,
+  // added in range order
+  constexpr int QB = NT == 1 ? 4 : 2;
+#pragma unroll
+  for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+    for (int jt = 0; jt < NT; ++jt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[cg][jt][r] = 0.0f;
+  for (int q0 = 0; q0 < P.S; q0 += QB) {
+    float u[QB][2][NT][4];
+#pragma unroll
+    for (int qq = 0; qq < QB; ++qq)
+#pragma unroll
+      for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+        for (int jt = 0; jt < NT; ++jt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r)
+            u[qq][cg][jt][r] = q0 + qq < P.S ? __ldcg(all + (q0 + qq) * (32 * 16) + elem(cg, jt, r)) : 0.0f;
+#pragma unroll
+    for (int qq = 0; qq < QB; ++qq)
+      if (q0 + qq < P.S) {
+#pragma unroll
+        for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+          for (int jt = 0; jt < NT; ++jt)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[cg][jt][r] = __fadd_rn(acc[cg][jt][r], u[qq][cg][jt][r]);
+      }
+  }
+#pragma unroll
+  for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+    for (int jt = 0; jt < NT; ++jt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int col = 16 * cg + g + ((r & 2) ? 8 : 0), tok = 8 * jt + 2 * t + (r & 1);
+        if (tok < P.M) P.out[static_cast<size_t>(tok) * P.ldo + nt * 32 + col] = acc[cg][jt][r];
+      }
+  if (lane == 0) P.cnt[nt] = 0u;
+}
+
+std::atomic<int> g_qdec{1};
+
+QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms) {
+  QDecPlan p;
+  p.nt = M <= 8 ? 1 : 2;
+  p.ntiles = N / 32;
+  p.ktiles = K / 32;
+  const int groups = (p.ntiles + kQdWarps - 1) / kQdWarps;
+  // two CTAs (32 warps) per SM where two weight rings and slices fit
+  const size_t rings = static_cast<size_t>(kQdWarps) * kQdStages * qd_pair_bytes(qt);
+  const int per_sm = 2 * (rings + 24 * 1024) <= 226 * 1024 ? 2 : 1;
+  int S = per_sm * num_sms / groups;
+  S = S < 1 ? 1 : S > kQdMaxSplits ? kQdMaxSplits : S;
+  const int maxs = p.ktiles / 2 > 0 ? p.ktiles / 2 : 1;  // at least two k-tiles per range
+  S = S > maxs ? maxs : S;
+  // the widest range's FP16 slice must fit in shared memory beside the rings
+  // (two CTAs per SM: within 24 KB each)
+  const size_t slice_max = per_sm == 2 ? 24 * 1024 : kQdMaxSlice;
+  while (static_cast<size_t>((p.ktiles + S - 1) / S) * 32 * 2 * 8 * p.nt > slice_max && S < p.ktiles) ++S;
+  p.splits = S;
+  p.grid = groups * S;
+  p.pitch = (p.ktiles + S - 1) / S * 32 + 8;  // halves; rows 4 words apart in the banks
+  p.smem = static_cast<size_t>(8 * p.nt) * p.pitch * 2;  // the slice (the rings are added per type)
+  return p;
+}
+size_t qdec_smem_bytes(int qt, const QDecPlan &p) {
+  return static_cast<size_t>(kQdWarps) * kQdStages * qd_pair_bytes(qt) + p.smem;
+}
+
+template <int QT, int NT>
+static cudaError_t launch_qdec_t(const QDecPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st) {
+  auto fn = qdec_kernel<QT, NT>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const size_t smem = qdec_smem_bytes(QT, p);
+  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+  if (!configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  QDecParams P;
+  P.w = w;
+  P.x = a.x;
+  P.out = a.out;
+  P.part = a.partials;
+  P.cnt = a.counters;
+  P.M = a.M;
+  P.N = a.N;
+  P.K = a.K;
+  P.ldo = static_cast<int>(a.ldo);
+  P.ntiles = p.ntiles;
+  P.ktiles = p.ktiles;
+  P.kb_total = (a.K + 63) / 64;
+  P.S = p.splits;
+  P.pitch = p.pitch;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+  cfg.blockDim = dim3(kQdThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, P);
+  return counted(e != cudaSuccess ? e : cudaGetLastError());
+}
+
+cudaError_t launch_qdec(int qt, const QDecPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st) {
+  if (a.M < 1 || a.M > 16 || a.N % 32 || a.K % 32 || p.smem > kQdMaxSlice) return cudaErrorInvalidConfiguration;
+  if (qt == kGgmlQ4_0)
+    return p.nt == 1 ? launch_qdec_t<kGgmlQ4_0, 1>(p, w, a, st) : launch_qdec_t<kGgmlQ4_0, 2>(p, w, a, st);
+  if (qt == kGgmlQ8_0)
+    return p.nt == 1 ? launch_qdec_t<kGgmlQ8_0, 1>(p, w, a, st) : launch_qdec_t<kGgmlQ8_0, 2>(p, w, a, st);
+  if (qt == kGgmlIQ4_NL)
+    return p.nt == 1 ? launch_qdec_t<kGgmlIQ4_NL, 1>(p, w, a, st) : launch_qdec_t<kGgmlIQ4_NL, 2>(p, w, a, st);
+  return cudaErrorInvalidValue;
+}
+
 QGemmPlan plan_qgemm(int qt, int M, int N, int K, int num_sms) {
   QGemmPlan p;
   p.bn = M <= 16 ? 16 : 32;

@@ -92,6 +92,7 @@ def lib() -> ctypes.CDLL:
         "htpg_set_decode_kernel": (I, [I]),
         "htpg_set_pair_direct": (I, [I]),
         "htpg_set_pair_tail_split": (I, [I]),
+        "htpg_set_qk0_decode": (I, [I]),
         "htpg_last_phase_ms": (I, [ctypes.POINTER(ctypes.c_float)] * 3),
         "htpg_launch_count": (U64, []),
         "htpg_stream_read": (I, [P, S, P]),
@@ -251,6 +252,12 @@ def set_decode_kernel(which: int) -> None:
     """0: W8A8 problems with m <= 16 run the register-fed decode kernel (the
     default); 1: they run the swapped tcgen05 kernel.  Results are identical."""
     check(lib().htpg_set_decode_kernel(which), "htpg_set_decode_kernel")
+
+
+def set_qk0_decode(which: int) -> None:
+    """0 (default): opcode 2-4 problems with m <= 16 run the register-fed decode
+    kernel; 1: the tcgen05 kernel."""
+    check(lib().htpg_set_qk0_decode(which), "htpg_set_qk0_decode")
 
 
 def set_pair_tail_split(on: bool) -> None:

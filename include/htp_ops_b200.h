@@ -333,6 +333,16 @@ int htpg_set_pair_direct(int on);
  * INT32 sums are exact); the switch exists for measurement and tests. */
 int htpg_set_pair_tail_split(int on);
 
+/* Which kernel runs opcode 2-4 (ggml-block weight) decode problems, Q8_0 with
+ * m <= 16 and Q4_0 with m <= 8 (IQ4_NL always runs the tcgen05 kernel, which
+ * is faster for its table-lookup decode): 0 (default) the register-fed decode
+ * kernel (each warp streams a 32-column weight tile's super-blocks through a
+ * shared-memory ring into registers and feeds mma.sync; k ranges summed in a
+ * fixed order), 1 the tcgen05 kernel that serves the other m <= 32.  Both are
+ * deterministic and within 1e-5 (relative) of the FP32-accumulating oracle;
+ * they sum in different orders. */
+int htpg_set_qk0_decode(int which);
+
 /* Which kernel runs W8A8 problems with m <= 16: 0 (default) the register-fed
  * decode kernel, 1 the swapped tcgen05 kernel that also serves 16 < m <= 32.
  * Both give identical results; the switch exists for measurement. */
