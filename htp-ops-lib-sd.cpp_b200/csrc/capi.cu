@@ -372,8 +372,8 @@ extern "C" int htpg_stream_read(const void *src, size_t bytes, void *stream) {
 }
 
 extern "C" int htpg_set_qk0_decode(int which) {
-  if (which != 0 && which != 1) return HTPG_EARGS;
-  g_qdec.store(which == 0 ? 1 : 0);
+  if (which < 0 || which > 2) return HTPG_EARGS;
+  g_qdec.store(which == 0 ? 1 : which == 1 ? 0 : 2);
   return HTPG_OK;
 }
 
@@ -1220,7 +1220,8 @@ extern "C" int htpg_qk0_run(const htpg_weights *w, float *out, const float *x, i
     return run_common(&f, &out, 1, 0, x, nullptr, m, n, 0, stream, nullptr, nullptr, true);
   }
   std::lock_guard<std::mutex> lk(g_mu);
-  if (qdec_serves(qt, m) && g_qdec.load() != 0) {
+  const int qdec_mode = g_qdec.load();
+  if (m <= 16 && (qdec_mode == 2 || (qdec_mode == 1 && qdec_serves(qt, m)))) {
     // decode shapes: the register-fed kernel (weights streamed into registers)
     const QDecPlan plan = plan_qdec(qt, m, n, k, d->sms);
     if (qdec_counter_bytes(plan) > kQCounterBytes || plan.smem > kQdMaxSlice) return HTPG_ENOPLAN;

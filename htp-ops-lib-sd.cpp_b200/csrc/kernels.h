@@ -190,6 +190,7 @@ constexpr size_t kQdMaxSlice = 64 * 1024;  // shared-memory bytes of the FP16 ac
 struct QDecPlan {
   int nt = 1;          // 8-token MMA tiles (M <= 8: 1, else 2)
   int ntiles = 0, ktiles = 0, splits = 1, grid = 0, pitch = 0;
+  int nw = 16;         // weight tiles per CTA
   size_t smem = 0;     // the activation slice
 };
 QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms);
@@ -197,14 +198,13 @@ size_t qdec_smem_bytes(int qt, const QDecPlan &p);  // the weight rings plus the
 inline size_t qdec_partial_bytes(const QDecPlan &p) { return static_cast<size_t>(p.ntiles) * p.splits * 32 * 16 * 4; }
 inline size_t qdec_counter_bytes(const QDecPlan &p) { return static_cast<size_t>(p.ntiles) * 4; }
 cudaError_t launch_qdec(int qt, const QDecPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st);
-extern std::atomic<int> g_qdec;  // 1: opcode 2-4 decode shapes may run the register-fed kernel
+extern std::atomic<int> g_qdec;  // 1: the register-fed kernel where qdec_serves; 0: never; 2: every m <= 16
 // Where the register-fed kernel is the faster one (measured on the LLM up /
 // down projections, K x N = 4096 x 14336 and 14336 x 4096, back to back):
-// Q8_0 (codes decode with one byte permute) up to 16 tokens (18.7 / 27.2 us
-// against 34.4 / 36.3 at m = 1 / 16); Q4_0 up to 8 tokens (up projection 20.5
-// against 33.9 us, down projection equal); IQ4_NL, whose table lookup makes
-// the decode the bound, keeps the tcgen05 kernel (down projection 69 against
-// 40 us).
+// Q8_0 (codes decode with one byte permute) up to 16 tokens (18.9 / 26.5 us
+// against 34.4 / 36.3 at m = 1 / 16); Q4_0 up to 8 tokens (20.7 / 26.7 us
+// against 34.0 / 35.1); IQ4_NL, whose table lookup makes the decode the
+// bound, keeps the tcgen05 kernel (down projection 49 against 40 us).
 inline bool qdec_serves(int qt, int m) {
   return (qt == kGgmlQ8_0 && m <= 16) || (qt == kGgmlQ4_0 && m <= 8);
 }

@@ -627,8 +627,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
 }
 
 // ============================================= register-fed decode (M <= 16)
-// Each CTA owns up to 16 32-column weight tiles (one per warp) and one range
-// of 32-deep k-tiles.  It first rounds its slice of x to FP16 into shared
+// Each CTA owns NW (16, 8 or 4) 32-column weight tiles and one range of
+// 32-deep k-tiles; 16 / NW warps share a tile, each a part of the range, and
+// add their FP32 sums in shared memory in a fixed order.  It first rounds its slice of x to FP16 into shared
 // memory (the reference's activation rounding).  Each warp streams its tile's
 // super-blocks from the stage records into its own shared-memory ring with
 // cp.async (a k-tile pair of one tile is 8 consecutive super-blocks, 1152 or
@@ -653,6 +654,7 @@ struct QDecParams {
   uint32_t *cnt;      // [ntiles], zero before the launch, left zero
   int M, N, K, ldo;
   int ntiles, ktiles, kb_total, S, pitch;  // pitch: halves per activation row in shared memory
+  int nw;                                  // weight tiles per CTA (16 / nw warps per tile)
 };
 
 __device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -733,13 +735,15 @@ __global__ void __launch_bounds__(kQdThreads, 1) qdec_kernel(const QDecParams P)
   const int grp = blockIdx.x / P.S, sp = blockIdx.x - grp * P.S;
   const int kt0 = static_cast<int>(static_cast<long long>(P.ktiles) * sp / P.S);
   const int kt1 = static_cast<int>(static_cast<long long>(P.ktiles) * (sp + 1) / P.S);
-  const int nt = grp * kQdWarps + warp;
-  const bool active = nt < P.ntiles;
+  const int kw_parts = kQdWarps / P.nw, ks = warp / P.nw;  // this warp's part of the range
+  const int nt = grp * P.nw + (warp - ks * P.nw);
+  const int wk0 = kt0 + (kt1 - kt0) * ks / kw_parts, wk1 = kt0 + (kt1 - kt0) * (ks + 1) / kw_parts;
+  const bool active = nt < P.ntiles && wk1 > wk0;
   const uint32_t ring = smem_u32(qd_smem) + static_cast<uint32_t>(warp * kQdStages * PAIR);
   uint32_t *qd_x = qd_smem + kQdWarps * kQdStages * PAIR / 4;  // [8 NT rows][pitch / 2] f16x2
   // k-tile pair pp (k-tiles 2pp, 2pp+1) of this warp's tile: 8 consecutive
   // super-blocks of record (nt/4, pp), starting at block (nt%4)*8
-  const int pp0 = kt0 >> 1, npairs = ((kt1 - 1) >> 1) - pp0 + 1;
+  const int pp0 = wk0 >> 1, npairs = active ? ((wk1 - 1) >> 1) - pp0 + 1 : 0;
   auto issue_pair = [&](int i) {  // pair pp0 + i into stage i % stages (one commit group per call)
     if (active && i < npairs) {
       const uint8_t *src = P.w + (static_cast<size_t>(nt >> 2) * P.kb_total + (pp0 + i)) * (32u * BLK) +
@@ -765,10 +769,6 @@ __global__ void __launch_bounds__(kQdThreads, 1) qdec_kernel(const QDecParams P)
     qd_x[r * (P.pitch / 2) + 2 * c4 + 1] = f2_to_h2(v.z, v.w);
   }
   __syncthreads();
-  if (!active) {
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    return;
-  }
 
   float acc[2][NT][4];
 #pragma unroll
@@ -784,7 +784,7 @@ __global__ void __launch_bounds__(kQdThreads, 1) qdec_kernel(const QDecParams P)
 #pragma unroll 1
     for (int e = 0; e < 2; ++e) {
       const int kt = 2 * (pp0 + i) + e;
-      if (kt < kt0 || kt >= kt1) continue;
+      if (kt < wk0 || kt >= wk1) continue;
       QdWords cur;
       qd_load<QT>(cur, stage + e * 4 * BLK, g, t);
       const int kl = (kt - kt0) * 32;  // k of the tile within the slice
@@ -813,11 +813,38 @@ __global__ void __launch_bounds__(kQdThreads, 1) qdec_kernel(const QDecParams P)
     issue_pair(i + kQdStages);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
-  // this range's partial tile, then the arrival; the last range of the tile
-  // sums all ranges' partials in range order and writes the output
   auto elem = [&](int cg, int jt, int r) {  // accumulator element (cg, jt, r) in a [32][16] partial tile
     return (16 * cg + g + ((r & 2) ? 8 : 0)) * 16 + 8 * jt + 2 * t + (r & 1);
   };
+  if (kw_parts > 1) {
+    // the tile's warps add their parts in part order, through shared memory
+    // (over the rings, which every warp has finished with)
+    float *red = reinterpret_cast<float *>(qd_smem);  // [part][nw][32 * 16]
+    __syncthreads();
+    if (nt < P.ntiles)
+#pragma unroll
+      for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+        for (int jt = 0; jt < NT; ++jt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) red[(ks * P.nw + (warp - ks * P.nw)) * 512 + elem(cg, jt, r)] = acc[cg][jt][r];
+    __syncthreads();
+    if (ks != 0 || nt >= P.ntiles) return;
+#pragma unroll
+    for (int cg = 0; cg < 2; ++cg)
+#pragma unroll
+      for (int jt = 0; jt < NT; ++jt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float v = red[warp * 512 + elem(cg, jt, r)];
+          for (int q = 1; q < kw_parts; ++q) v = __fadd_rn(v, red[(q * P.nw + warp) * 512 + elem(cg, jt, r)]);
+          acc[cg][jt][r] = v;
+        }
+  } else if (nt >= P.ntiles) {
+    return;
+  }
+  // this range's partial tile, then the arrival; the last range of the tile
+  // sums all ranges' partials in range order and writes the output
   float *mine = P.part + (static_cast<size_t>(nt) * P.S + sp) * (32 * 16);
 #pragma unroll
   for (int cg = 0; cg < 2; ++cg)
@@ -883,14 +910,23 @@ QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms) {
   p.nt = M <= 8 ? 1 : 2;
   p.ntiles = N / 32;
   p.ktiles = K / 32;
-  const int groups = (p.ntiles + kQdWarps - 1) / kQdWarps;
   // two CTAs (32 warps) per SM where two weight rings and slices fit
   const size_t rings = static_cast<size_t>(kQdWarps) * kQdStages * qd_pair_bytes(qt);
   const int per_sm = 2 * (rings + 24 * 1024) <= 226 * 1024 ? 2 : 1;
-  int S = per_sm * num_sms / groups;
-  S = S < 1 ? 1 : S > kQdMaxSplits ? kQdMaxSplits : S;
-  const int maxs = p.ktiles / 2 > 0 ? p.ktiles / 2 : 1;  // at least two k-tiles per range
-  S = S > maxs ? maxs : S;
+  const int target = per_sm * num_sms;
+  // the widest tile group (16, 8 or 4 tiles per CTA) whose CTAs still fill
+  // the SMs; narrower groups put 2 or 4 warps on each tile
+  int groups = 0, S = 1;
+  for (int nw = kQdWarps; nw >= 4; nw /= 2) {
+    p.nw = nw;
+    groups = (p.ntiles + nw - 1) / nw;
+    const int parts = kQdWarps / nw;
+    S = target / groups;
+    S = S < 1 ? 1 : S > kQdMaxSplits ? kQdMaxSplits : S;
+    const int maxs = p.ktiles / (2 * parts) > 0 ? p.ktiles / (2 * parts) : 1;  // two k-tiles per warp
+    S = S > maxs ? maxs : S;
+    if (static_cast<long long>(groups) * S * 10 >= 9LL * target) break;
+  }
   // the widest range's FP16 slice must fit in shared memory beside the rings
   // (two CTAs per SM: within 24 KB each)
   const size_t slice_max = per_sm == 2 ? 24 * 1024 : kQdMaxSlice;
@@ -934,6 +970,7 @@ static cudaError_t launch_qdec_t(const QDecPlan &p, const uint8_t *w, const QGem
   P.kb_total = (a.K + 63) / 64;
   P.S = p.splits;
   P.pitch = p.pitch;
+  P.nw = p.nw;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
   cfg.blockDim = dim3(kQdThreads, 1, 1);

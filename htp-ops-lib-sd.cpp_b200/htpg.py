@@ -255,8 +255,9 @@ def set_decode_kernel(which: int) -> None:
 
 
 def set_qk0_decode(which: int) -> None:
-    """0 (default): opcode 2-4 problems with m <= 16 run the register-fed decode
-    kernel; 1: the tcgen05 kernel."""
+    """0 (default): opcode 2-4 decode problems run the register-fed kernel
+    where it is the faster one; 1: always the tcgen05 kernel; 2: the
+    register-fed kernel for every m <= 16."""
     check(lib().htpg_set_qk0_decode(which), "htpg_set_qk0_decode")
 
 

@@ -338,9 +338,10 @@ int htpg_set_pair_tail_split(int on);
  * is faster for its table-lookup decode): 0 (default) the register-fed decode
  * kernel (each warp streams a 32-column weight tile's super-blocks through a
  * shared-memory ring into registers and feeds mma.sync; k ranges summed in a
- * fixed order), 1 the tcgen05 kernel that serves the other m <= 32.  Both are
- * deterministic and within 1e-5 (relative) of the FP32-accumulating oracle;
- * they sum in different orders. */
+ * fixed order), 1 the tcgen05 kernel that serves the other m <= 32, 2 the
+ * register-fed kernel for every type and m <= 16.  Both are deterministic and
+ * within 1e-5 (relative) of the FP32-accumulating oracle; they sum in
+ * different orders. */
 int htpg_set_qk0_decode(int which);
 
 /* Which kernel runs W8A8 problems with m <= 16: 0 (default) the register-fed

@@ -73,11 +73,11 @@ def test_qk0_linear_matches_oracle(gpu, lib, wtype, m, k, n):
     assert _rel(got, ref16) <= 1e-2
 
 
-DECODE_CASES = [  # (m, k, n): the register-fed decode kernel serves Q8_0 (m <= 16) and Q4_0 (m <= 8)
+DECODE_CASES = [  # (m, k, n) for the register-fed decode kernel (m <= 16)
     (1, 32, 64),         # one k-tile, two column tiles
     (5, 96, 160),        # odd number of k-tiles (record padding), N % 128 = 32
     (8, 4096, 14336),    # LLM up projection
-    (12, 2048, 1536),    # two 8-token MMA tiles, ragged M (Q8_0; the others compare tcgen05 with itself)
+    (12, 2048, 1536),    # two 8-token MMA tiles, ragged M
     (16, 14336, 4096),   # LLM down projection, 16 tokens (Q8_0)
     (2, 8192, 96),       # few column tiles: many k ranges per tile
     (4, 14336, 4096),    # LLM down projection, 4 tokens
@@ -89,16 +89,15 @@ DECODE_CASES = [  # (m, k, n): the register-fed decode kernel serves Q8_0 (m <= 
 def test_qk0_decode_kernels_agree(gpu, lib, wtype, m, k, n):
     """The register-fed decode kernel and the tcgen05 kernel decode the same
     FP16 weights and activations and accumulate in FP32 in different orders:
-    both within 1e-5 of the FP32-accumulating oracle and of each other.  (For
-    types and row counts the register-fed kernel does not serve, both runs
-    take the tcgen05 kernel.)"""
+    both within 1e-5 of the FP32-accumulating oracle and of each other (every
+    type, up to 16 rows, whichever kernel the library would pick)."""
     src, x = _case(wtype, m, k, n, seed=m * 11 + k + n + wtype)
     ref32 = O.qk0_linear(x, src, wtype, k, n, kind="omp")
     wd, xd = torch.from_numpy(src).to(gpu), torch.from_numpy(x).to(gpu)
     w = htpg.qk0_weights(wd, wtype, k, n)
     outs = []
     try:
-        for which in (0, 1):
+        for which in (2, 1):       # register-fed for every m <= 16, then tcgen05
             htpg.set_qk0_decode(which)
             out = torch.full((m, n), float("nan"), device=gpu)
             htpg.check(htpg.qk0_run(w, out, xd, m), "htpg_qk0_run")
