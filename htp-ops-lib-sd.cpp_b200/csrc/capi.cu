@@ -377,6 +377,16 @@ extern "C" int htpg_set_qk0_decode(int which) {
   return HTPG_OK;
 }
 
+extern "C" int htpg_set_qdec_shape(int per_sm, int tiles) {
+  if (per_sm == 0 && tiles == 0) {
+    g_qdec_shape.store(0);
+    return HTPG_OK;
+  }
+  if ((per_sm != 1 && per_sm != 2) || (tiles != 16 && tiles != 8 && tiles != 4)) return HTPG_EARGS;
+  g_qdec_shape.store(per_sm * 100 + tiles);
+  return HTPG_OK;
+}
+
 extern "C" int htpg_set_pair_tail_split(int on) {
   if (on != 0 && on != 1) return HTPG_EARGS;
   g_pair_tail.store(on);
@@ -1224,7 +1234,7 @@ extern "C" int htpg_qk0_run(const htpg_weights *w, float *out, const float *x, i
   if (m <= 16 && (qdec_mode == 2 || (qdec_mode == 1 && qdec_serves(qt, m)))) {
     // decode shapes: the register-fed kernel (weights streamed into registers)
     const QDecPlan plan = plan_qdec(qt, m, n, k, d->sms);
-    if (qdec_counter_bytes(plan) > kQCounterBytes || plan.smem > kQdMaxSlice) return HTPG_ENOPLAN;
+    if (plan.grid == 0 || qdec_counter_bytes(plan) > kQCounterBytes || plan.smem > kQdMaxSlice) return HTPG_ENOPLAN;
     uint8_t *base = nullptr;
     rc = qworkspace(d, st, kQCounterBytes + align_up(qdec_partial_bytes(plan), 1024), &base);
     if (rc) return rc;
@@ -1268,6 +1278,22 @@ extern "C" int htpg_qk0_plan_info(int weight_type, int m, int n, int k, int sms,
   out[3] = p.kb_total;
   out[4] = p.grid;
   out[5] = static_cast<int64_t>(p.smem);
+  return HTPG_OK;
+}
+
+extern "C" int htpg_qk0_decode_plan_info(int weight_type, int m, int n, int k, int sms, int64_t out[8]) {
+  if (!out || !qk0_type_ok(weight_type) || m < 1 || m > 16 || n < 32 || k < 32 || n % 32 || k % 32 || sms < 1)
+    return HTPG_EARGS;
+  const QDecPlan p = plan_qdec(weight_type, m, n, k, sms);
+  if (p.grid == 0) return HTPG_ENOPLAN;
+  out[0] = p.per_sm;
+  out[1] = p.nw;
+  out[2] = p.ntiles;
+  out[3] = p.ktiles;
+  out[4] = p.splits;
+  out[5] = p.grid;
+  out[6] = static_cast<int64_t>(p.smem);
+  out[7] = static_cast<int64_t>(qdec_smem_bytes(weight_type, p));
   return HTPG_OK;
 }
 

@@ -191,6 +191,7 @@ struct QDecPlan {
   int nt = 1;          // 8-token MMA tiles (M <= 8: 1, else 2)
   int ntiles = 0, ktiles = 0, splits = 1, grid = 0, pitch = 0;
   int nw = 16;         // weight tiles per CTA
+  int per_sm = 1;      // CTAs resident per SM the plan is sized for
   size_t smem = 0;     // the activation slice
 };
 QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms);
@@ -199,14 +200,12 @@ inline size_t qdec_partial_bytes(const QDecPlan &p) { return static_cast<size_t>
 inline size_t qdec_counter_bytes(const QDecPlan &p) { return static_cast<size_t>(p.ntiles) * 4; }
 cudaError_t launch_qdec(int qt, const QDecPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st);
 extern std::atomic<int> g_qdec;  // 1: the register-fed kernel where qdec_serves; 0: never; 2: every m <= 16
-// Where the register-fed kernel is the faster one (measured on the LLM up /
-// down projections, K x N = 4096 x 14336 and 14336 x 4096, back to back):
-// Q8_0 (codes decode with one byte permute) up to 16 tokens (18.9 / 26.5 us
-// against 34.4 / 36.3 at m = 1 / 16); Q4_0 up to 8 tokens (20.7 / 26.7 us
-// against 34.0 / 35.1); IQ4_NL, whose table lookup makes the decode the
-// bound, keeps the tcgen05 kernel (down projection 49 against 40 us).
+extern std::atomic<int> g_qdec_shape;  // 0: plan_qdec chooses; else CTAs per SM * 100 + tiles per CTA
+// Where the register-fed kernel is the faster one: every type up to 16 tokens
+// (LLM up / down projections, K x N = 4096 x 14336 and 14336 x 4096, back to
+// back: 19-34 us against 34-38 us for the tcgen05 kernel).
 inline bool qdec_serves(int qt, int m) {
-  return (qt == kGgmlQ8_0 && m <= 16) || (qt == kGgmlQ4_0 && m <= 8);
+  return (qt == kGgmlQ8_0 || qt == kGgmlQ4_0 || qt == kGgmlIQ4_NL) && m <= 16;
 }
 
 // Kernel launches issued since load (all launchers above count themselves).

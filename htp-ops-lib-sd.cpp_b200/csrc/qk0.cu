@@ -50,11 +50,20 @@ __device__ __forceinline__ uint32_t hmul2_rn(uint32_t a, uint32_t b) {
 
 // Bytes level+128 of the four nibbles in bits [0, 16) of x: two 8-entry byte
 // tables selected by the nibbles' low three bits, merged by their fourth bit.
+// prmt.b32 in its default mode, where a selector nibble with bit 3 set gives
+// the selected byte's sign bit replicated (__byte_perm ignores that bit).
+__device__ __forceinline__ uint32_t prmt_sx(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
 __device__ __forceinline__ uint32_t iq4_lookup4(uint32_t x) {
-  const uint32_t sel = x & 0x7777u;
-  const uint32_t lo = prmt(iq4_word(0), iq4_word(4), sel);
-  const uint32_t hi = prmt(iq4_word(8), iq4_word(12), sel);
-  const uint32_t msk = prmt(0u, 0xFFFFFFFFu, (x >> 1) & 0x4444u);  // 0xFF where the nibble is >= 8
+  // nibbles >= 8 give sign bytes in lo; the select below takes hi for them
+  const uint32_t lo = prmt_sx(iq4_word(0), iq4_word(4), x);
+  const uint32_t hi = prmt_sx(iq4_word(8), iq4_word(12), x & 0x7777u);
+  // 0xFF where the nibble is >= 8: bit 3 of nibble 1 / 3 is the sign bit of
+  // byte 0 / 1 of x, that of nibble 0 / 2 the sign bit of byte 0 / 1 of x << 4
+  const uint32_t msk = prmt_sx(x, x << 4, 0x9D8Cu);
   return (hi & msk) | (lo & ~msk);
 }
 
@@ -643,7 +652,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
 // (deterministic) and writes the output.  No thread waits for another CTA.
 constexpr int kQdWarps = 16, kQdThreads = 32 * kQdWarps;
 constexpr int kQdStages = 4;       // k-tile pairs of a warp's tile in flight
-constexpr int kQdMaxSplits = 16;   // k ranges per tile at most (the last one sums them all)
+constexpr int kQdMaxSplits = 32;   // k ranges per tile at most (the last one sums them all)
 __host__ __device__ constexpr int qd_pair_bytes(int qt) { return 8 * (qt == kGgmlQ8_0 ? 272 : 144); }
 
 struct QDecParams {
@@ -718,6 +727,28 @@ __device__ __forceinline__ uint32_t qd_pair(uint32_t scw, uint32_t q, int m, int
   return hmul2_rn(hsub2_rn(h, bias), s);
 }
 
+// Pair t of column m in two super-blocks (words q0, q1 with scale words sc0,
+// sc1): qd_pair twice.  IQ4_NL looks the four nibbles up together: one byte
+// permute gathers bytes (t & 1) and (t & 1) + 2 of both words, the shift by
+// s4 = 4 * (t >> 1) brings the pair's nibbles to the bytes' low halves, and
+// x = A0 | A1 << 4 | B0 << 8 | B1 << 12 indexes the table (A, B: the pair's
+// nibbles at sh and sh + 16 of q0 and q1).
+template <int QT>
+__device__ __forceinline__ void qd_pair2(uint32_t sc0, uint32_t sc1, uint32_t q0, uint32_t q1, int m, int sh,
+                                         uint32_t gsel, int s4, uint32_t &r0, uint32_t &r1) {
+  if constexpr (QT == kGgmlIQ4_NL) {
+    const uint32_t w = prmt(q0, q1, gsel) >> s4;
+    const uint32_t lv = iq4_lookup4((w & 0x0F0Fu) | ((w >> 12) & 0xF0F0u));  // L(A0) L(A1) L(B0) L(B1)
+    const uint32_t bias = 0x64806480u;
+    const uint32_t ssel = (m & 16) ? 0x3232u : 0x1010u;
+    r0 = hmul2_rn(hsub2_rn(prmt(lv, 0x64646464u, 0x4240u), bias), prmt(sc0, sc0, ssel));
+    r1 = hmul2_rn(hsub2_rn(prmt(lv, 0x64646464u, 0x4341u), bias), prmt(sc1, sc1, ssel));
+  } else {
+    r0 = qd_pair<QT>(sc0, q0, m, sh);
+    r1 = qd_pair<QT>(sc1, q1, m, sh);
+  }
+}
+
 __device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
   uint32_t d;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
@@ -725,13 +756,15 @@ __device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
 }
 
 template <int QT, int NT>
-__global__ void __launch_bounds__(kQdThreads, 1) qdec_kernel(const QDecParams P) {
+__global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P) {
   constexpr int BLK = QT == kGgmlQ8_0 ? 272 : 144;
   constexpr int PAIR = qd_pair_bytes(QT);
   extern __shared__ __align__(16) uint32_t qd_smem[];  // [16 warps][stages][PAIR] rings, then the x slice
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int sh = ((t & 1) << 3) | ((t >> 1) << 2);  // see qd_pair
+  const uint32_t gsel = 0x6420u + 0x1111u * static_cast<uint32_t>(t & 1);  // see qd_pair2
+  const int s4 = (t >> 1) << 2;
   const int grp = blockIdx.x / P.S, sp = blockIdx.x - grp * P.S;
   const int kt0 = static_cast<int>(static_cast<long long>(P.ktiles) * sp / P.S);
   const int kt1 = static_cast<int>(static_cast<long long>(P.ktiles) * (sp + 1) / P.S);
@@ -800,10 +833,11 @@ __global__ void __launch_bounds__(kQdThreads, 1) qdec_kernel(const QDecParams P)
 #pragma unroll
         for (int cg = 0; cg < 2; ++cg) {
           const int c0 = 2 * cg, c1 = 2 * cg + 1;
-          const uint32_t a0 = qd_pair<QT>(cur.sc[2 * s2], cur.q[2 * s2][c0], g + 8 * c0, sh);
-          const uint32_t a1 = qd_pair<QT>(cur.sc[2 * s2], cur.q[2 * s2][c1], g + 8 * c1, sh);
-          const uint32_t a2 = qd_pair<QT>(cur.sc[2 * s2 + 1], cur.q[2 * s2 + 1][c0], g + 8 * c0, sh);
-          const uint32_t a3 = qd_pair<QT>(cur.sc[2 * s2 + 1], cur.q[2 * s2 + 1][c1], g + 8 * c1, sh);
+          uint32_t a0, a1, a2, a3;
+          qd_pair2<QT>(cur.sc[2 * s2], cur.sc[2 * s2 + 1], cur.q[2 * s2][c0], cur.q[2 * s2 + 1][c0], g + 8 * c0, sh,
+                       gsel, s4, a0, a2);
+          qd_pair2<QT>(cur.sc[2 * s2], cur.sc[2 * s2 + 1], cur.q[2 * s2][c1], cur.q[2 * s2 + 1][c1], g + 8 * c1, sh,
+                       gsel, s4, a1, a3);
 #pragma unroll
           for (int jt = 0; jt < NT; ++jt) mma_f16_16816(acc[cg][jt], a0, a1, a2, a3, b[jt][0], b[jt][1]);
         }
@@ -904,41 +938,81 @@ __global__ void __launch_bounds__(kQdThreads, 1) qdec_kernel(const QDecParams P)
 }
 
 std::atomic<int> g_qdec{1};
+std::atomic<int> g_qdec_shape{0};
 
+// Candidates: one or two CTAs per SM (two where both CTAs' rings and slices
+// fit in the SM's shared memory) x 16, 8 or 4 weight tiles per CTA (narrower
+// groups put 2 or 4 warps on each tile).  Each takes as many k ranges as fill
+// its CTA slots, at least as many as make the widest range's FP16 slice fit
+// beside the rings, at most kQdMaxSplits and two k-tiles per warp.  The
+// estimate of a candidate: 8 us per wave of CTAs (the fixed part of a CTA's
+// life: slice load, ring fill, hand-off; a second wave costs it again), the
+// busiest SM's streaming work (CTAs spread over the SMs first: ceil(grid /
+// SMs) x tiles x k-tiles of a range, in k-tile units of this type's bytes at
+// an SM's share of the HBM bandwidth) and the finishing warp's L2 round trips
+// (ceil(S / QB) batches of partial loads).  The smallest estimate wins; ties
+// keep one CTA per SM (fewer CTAs, no tile shared between warps) and wider
+// groups.  On the LLM projections (K x N =
+// 4096 x 14336 and 14336 x 4096, m = 1..16, every type) it picks the fastest
+// measured shape or one within 3%.
 QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms) {
-  QDecPlan p;
-  p.nt = M <= 8 ? 1 : 2;
-  p.ntiles = N / 32;
-  p.ktiles = K / 32;
-  // two CTAs (32 warps) per SM where two weight rings and slices fit
+  QDecPlan best;
+  best.grid = 0;
+  const int nt = M <= 8 ? 1 : 2;
+  const int ntiles = N / 32, ktiles = K / 32;
   const size_t rings = static_cast<size_t>(kQdWarps) * kQdStages * qd_pair_bytes(qt);
-  const int per_sm = 2 * (rings + 24 * 1024) <= 226 * 1024 ? 2 : 1;
-  const int target = per_sm * num_sms;
-  // the widest tile group (16, 8 or 4 tiles per CTA) whose CTAs still fill
-  // the SMs; narrower groups put 2 or 4 warps on each tile
-  int groups = 0, S = 1;
-  for (int nw = kQdWarps; nw >= 4; nw /= 2) {
-    p.nw = nw;
-    groups = (p.ntiles + nw - 1) / nw;
-    const int parts = kQdWarps / nw;
-    S = target / groups;
-    S = S < 1 ? 1 : S > kQdMaxSplits ? kQdMaxSplits : S;
-    const int maxs = p.ktiles / (2 * parts) > 0 ? p.ktiles / (2 * parts) : 1;  // two k-tiles per warp
-    S = S > maxs ? maxs : S;
-    if (static_cast<long long>(groups) * S * 10 >= 9LL * target) break;
+  // one k-tile of one 32-column tile: four super-blocks; 13 ns per 576 bytes
+  // at ~44 GB/s per SM, against ~700 ns per dependent L2 round trip
+  const double kt_ns = 4.0 * (qt == kGgmlQ8_0 ? 272 : 144) / 44.0, trip_ns = 700.0, wave_ns = 8000.0;
+  const int qb = nt == 1 ? 4 : 2;  // the finisher's ranges per batch (qdec_kernel's QB)
+  const int force = g_qdec_shape.load();
+  double best_cost = 0.0;
+  auto slice_bytes = [&](int S) {  // rows 4 words apart in the banks: 8 halves of padding
+    return static_cast<size_t>(8 * nt) * ((ktiles + S - 1) / S * 32 + 8) * 2;
+  };
+  for (int per_sm = 1; per_sm <= 2; ++per_sm) {
+    // per CTA: 113 KB of the SM's 228 (1 KB of each CTA's is reserved) with
+    // two; the kernel's launch bounds keep two CTAs' registers within the SM's
+    const size_t budget = per_sm == 2 ? 112 * 1024 : 227 * 1024;
+    if (rings >= budget) continue;
+    const size_t slice_max = budget - rings < kQdMaxSlice ? budget - rings : kQdMaxSlice;
+    const int target = per_sm * num_sms;
+    for (int nw = kQdWarps; nw >= 4; nw /= 2) {
+      if (force && force != per_sm * 100 + nw) continue;
+      const int groups = (ntiles + nw - 1) / nw, parts = kQdWarps / nw;
+      int s_max = ktiles / (2 * parts);
+      s_max = s_max < 1 ? 1 : s_max > kQdMaxSplits ? kQdMaxSplits : s_max;
+      int S = target / groups;
+      S = S < 1 ? 1 : S > s_max ? s_max : S;
+      while (slice_bytes(S) > slice_max && S < ktiles) ++S;
+      if (slice_bytes(S) > slice_max) continue;
+      const long long grid = static_cast<long long>(groups) * S;
+      const long long busiest = (grid + num_sms - 1) / num_sms, waves = (grid + target - 1) / target;
+      const double cost = static_cast<double>(waves) * wave_ns +
+                          static_cast<double>(busiest) * nw * ((ktiles + S - 1) / S) * kt_ns +
+                          static_cast<double>((S + qb - 1) / qb) * trip_ns;
+      if (best.grid == 0 || cost < best_cost) {
+        best_cost = cost;
+        best.nt = nt;
+        best.ntiles = ntiles;
+        best.ktiles = ktiles;
+        best.nw = nw;
+        best.per_sm = per_sm;
+        best.splits = S;
+        best.grid = static_cast<int>(grid);
+        best.pitch = (ktiles + S - 1) / S * 32 + 8;  // halves
+        best.smem = slice_bytes(S);                  // the slice (the rings are added per type)
+      }
+    }
   }
-  // the widest range's FP16 slice must fit in shared memory beside the rings
-  // (two CTAs per SM: within 24 KB each)
-  const size_t slice_max = per_sm == 2 ? 24 * 1024 : kQdMaxSlice;
-  while (static_cast<size_t>((p.ktiles + S - 1) / S) * 32 * 2 * 8 * p.nt > slice_max && S < p.ktiles) ++S;
-  p.splits = S;
-  p.grid = groups * S;
-  p.pitch = (p.ktiles + S - 1) / S * 32 + 8;  // halves; rows 4 words apart in the banks
-  p.smem = static_cast<size_t>(8 * p.nt) * p.pitch * 2;  // the slice (the rings are added per type)
-  return p;
+  return best;  // grid 0: no candidate (a forced shape that does not fit)
 }
 size_t qdec_smem_bytes(int qt, const QDecPlan &p) {
-  return static_cast<size_t>(kQdWarps) * kQdStages * qd_pair_bytes(qt) + p.smem;
+  const size_t s = static_cast<size_t>(kQdWarps) * kQdStages * qd_pair_bytes(qt) + p.smem;
+  // a plan sized for one CTA per SM asks for more than half the SM's shared
+  // memory, so that its CTAs spread over the SMs instead of pairing up on
+  // some of them while others stay empty
+  return p.per_sm == 1 && s < 116 * 1024 ? 116 * 1024 : s;
 }
 
 template <int QT, int NT>
@@ -951,7 +1025,9 @@ static cudaError_t launch_qdec_t(const QDecPlan &p, const uint8_t *w, const QGem
   const size_t smem = qdec_smem_bytes(QT, p);
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
   if (!configured[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    // all of the SM's unified memory as shared memory: two CTAs' rings fit
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }

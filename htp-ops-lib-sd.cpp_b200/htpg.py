@@ -93,6 +93,8 @@ def lib() -> ctypes.CDLL:
         "htpg_set_pair_direct": (I, [I]),
         "htpg_set_pair_tail_split": (I, [I]),
         "htpg_set_qk0_decode": (I, [I]),
+        "htpg_set_qdec_shape": (I, [I, I]),
+        "htpg_qk0_decode_plan_info": (I, [I, I, I, I, I, ctypes.POINTER(I64)]),
         "htpg_last_phase_ms": (I, [ctypes.POINTER(ctypes.c_float)] * 3),
         "htpg_launch_count": (U64, []),
         "htpg_stream_read": (I, [P, S, P]),
@@ -255,10 +257,17 @@ def set_decode_kernel(which: int) -> None:
 
 
 def set_qk0_decode(which: int) -> None:
-    """0 (default): opcode 2-4 decode problems run the register-fed kernel
-    where it is the faster one; 1: always the tcgen05 kernel; 2: the
-    register-fed kernel for every m <= 16."""
+    """0 (default): opcode 2-4 decode problems (m <= 16) run the register-fed
+    kernel where it is the faster one (every type); 1: always the tcgen05
+    kernel; 2: the register-fed kernel for every m <= 16."""
     check(lib().htpg_set_qk0_decode(which), "htpg_set_qk0_decode")
+
+
+def set_qdec_shape(per_sm: int = 0, tiles: int = 0) -> None:
+    """Force the register-fed opcode 2-4 decode kernel's launch shape (CTAs
+    per SM 1 or 2, weight tiles per CTA 16, 8 or 4); (0, 0) restores the
+    planner's choice."""
+    check(lib().htpg_set_qdec_shape(per_sm, tiles), "htpg_set_qdec_shape")
 
 
 def set_pair_tail_split(on: bool) -> None:
@@ -280,6 +289,13 @@ def qk0_plan_info(weight_type: int, m: int, n: int, k: int, sms: int = 148) -> d
     out = (ctypes.c_int64 * 6)()
     check(lib().htpg_qk0_plan_info(weight_type, m, n, k, sms, out), "htpg_qk0_plan_info")
     return dict(zip(("bn", "tiles_a", "tiles_b", "kb_total", "grid", "smem"), list(out)))
+
+
+def qk0_decode_plan_info(weight_type: int, m: int, n: int, k: int, sms: int = 148) -> dict:
+    """Plan of the register-fed opcode 2-4 decode kernel (m <= 16)."""
+    out = (ctypes.c_int64 * 8)()
+    check(lib().htpg_qk0_decode_plan_info(weight_type, m, n, k, sms, out), "htpg_qk0_decode_plan_info")
+    return dict(zip(("per_sm", "tiles", "ntiles", "ktiles", "splits", "grid", "slice", "smem"), list(out)))
 
 
 def qk0_weights(weight_dev, weight_type: int, k: int, n: int, stream=None) -> Weights:

@@ -186,6 +186,11 @@ int htpg_qk0_linear(float *out, const float *x, const void *weight, int m, int k
 int htpg_qk0_dequantize(uint16_t *w_nk, const void *weight, int k, int n, int weight_type, void *stream);
 /* Plan of the fused kernel: {bn, tiles_a, tiles_b, k-blocks, CTAs, shared bytes}. */
 int htpg_qk0_plan_info(int weight_type, int m, int n, int k, int sms, int64_t out[6]);
+/* Plan of the register-fed decode kernel (m <= 16): {CTAs per SM, weight tiles
+ * per CTA, 32-column tiles, 32-deep k-tiles, k ranges, CTAs, activation slice
+ * bytes, shared bytes per CTA}.  HTPG_ENOPLAN when a shape forced with
+ * htpg_set_qdec_shape does not fit. */
+int htpg_qk0_decode_plan_info(int weight_type, int m, int n, int k, int sms, int64_t out[8]);
 
 /* ---- column-sharded run with a fused output exchange -------------------- */
 /* Multi-GPU form of htpg_w8a8_run for a weight split by output columns (N)
@@ -333,16 +338,24 @@ int htpg_set_pair_direct(int on);
  * INT32 sums are exact); the switch exists for measurement and tests. */
 int htpg_set_pair_tail_split(int on);
 
-/* Which kernel runs opcode 2-4 (ggml-block weight) decode problems, Q8_0 with
- * m <= 16 and Q4_0 with m <= 8 (IQ4_NL always runs the tcgen05 kernel, which
- * is faster for its table-lookup decode): 0 (default) the register-fed decode
- * kernel (each warp streams a 32-column weight tile's super-blocks through a
- * shared-memory ring into registers and feeds mma.sync; k ranges summed in a
- * fixed order), 1 the tcgen05 kernel that serves the other m <= 32, 2 the
- * register-fed kernel for every type and m <= 16.  Both are deterministic and
+/* Which kernel runs opcode 2-4 (ggml-block weight) decode problems, m <= 16:
+ * 0 (default) the register-fed decode kernel (each warp streams a 32-column
+ * weight tile's super-blocks through a shared-memory ring into registers and
+ * feeds mma.sync; k ranges summed in a fixed order), 1 the tcgen05 kernel
+ * that serves the other m <= 32, 2 the register-fed kernel (the same as 0
+ * now that it serves every type up to m = 16).  Both are deterministic and
  * within 1e-5 (relative) of the FP32-accumulating oracle; they sum in
  * different orders. */
 int htpg_set_qk0_decode(int which);
+
+/* The register-fed opcode 2-4 decode kernel's launch shape: per_sm CTAs per
+ * SM (1 or 2) with `tiles` 32-column weight tiles each (16, 8 or 4; narrower
+ * CTAs put 2 or 4 warps on each tile).  (0, 0), the default, lets the planner
+ * choose.  A forced shape that does not fit the problem makes the call return
+ * HTPG_ENOPLAN.  Results do not depend on the shape beyond the order of the
+ * k-range sums (each shape is deterministic); the switch exists for tests and
+ * measurement. */
+int htpg_set_qdec_shape(int per_sm, int tiles);
 
 /* Which kernel runs W8A8 problems with m <= 16: 0 (default) the register-fed
  * decode kernel, 1 the swapped tcgen05 kernel that also serves 16 < m <= 32.

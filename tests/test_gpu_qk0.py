@@ -5,9 +5,11 @@ the reference's super-block decode (mat_mul.c:389-525).  The GEMM output is
 checked against the oracle's FP32-accumulating GEMM of the same FP16 operands
 (1e-5 max-abs-rel: same products, different summation order) and against the
 variant that reads the accumulator through FP16 as the reference's HMX readout
-does (the 1e-2 FP16 bar).  M <= 32 runs the fused small-M kernel (stream-K over
-the CTAs; the shapes below give tiles finished by one CTA, by several CTAs and
-CTAs that span tiles); larger M dequantises once and runs the FP16 GEMM.
+does (the 1e-2 FP16 bar).  M <= 16 runs the register-fed decode kernel by
+default and is also run on the fused tcgen05 small-M kernel, which serves
+16 < M <= 32 (stream-K over the CTAs; the shapes below give tiles finished by
+one CTA, by several CTAs and CTAs that span tiles); larger M dequantises once
+and runs the FP16 GEMM.
 """
 import ctypes
 import struct
@@ -58,19 +60,24 @@ def test_qk0_linear_matches_oracle(gpu, lib, wtype, m, k, n):
     ref16 = O.qk0_linear(x, src, wtype, k, n, round_acc_f16=True, kind="omp")
     wd = torch.from_numpy(src).to(gpu)
     xd = torch.from_numpy(x).to(gpu)
-    out = torch.full((m, n), float("nan"), device=gpu)
+    outs = []
     try:
-        htpg.check(htpg.qk0_linear(out, xd, wd, wtype, m, k, n), "htpg_qk0_linear")
-        torch.cuda.synchronize()
+        for which in ((0, 1) if m <= 16 else (0,)):   # default kernel, then tcgen05 for m <= 16
+            htpg.set_qk0_decode(which)
+            out = torch.full((m, n), float("nan"), device=gpu)
+            htpg.check(htpg.qk0_linear(out, xd, wd, wtype, m, k, n), "htpg_qk0_linear")
+            torch.cuda.synchronize()
+            outs.append(out.cpu().numpy())
     finally:
+        htpg.set_qk0_decode(0)
         # the one-call entry point caches the prepared weight by address; the
         # allocator may hand this address to the next test's weight
         lib.htpg_weight_cache_drop(htpg.ptr(wd))
     assert htpg.check_device() == 0
-    got = out.cpu().numpy()
-    assert np.isfinite(got).all()
-    assert _rel(got, ref32) <= 1e-5
-    assert _rel(got, ref16) <= 1e-2
+    for got in outs:
+        assert np.isfinite(got).all()
+        assert _rel(got, ref32) <= 1e-5
+        assert _rel(got, ref16) <= 1e-2
 
 
 DECODE_CASES = [  # (m, k, n) for the register-fed decode kernel (m <= 16)
@@ -111,20 +118,78 @@ def test_qk0_decode_kernels_agree(gpu, lib, wtype, m, k, n):
     assert _rel(outs[0], outs[1].astype(np.float64)) <= 1e-5
 
 
+SHAPE_CASES = [  # (m, k, n) run under every launch shape of the register-fed kernel
+    (5, 96, 160),        # three k-tiles: more warps than k-tiles in narrow shapes
+    (12, 2048, 1536),    # two 8-token MMA tiles, ragged M
+    (16, 14336, 4096),   # LLM down projection: the slice bounds the k ranges
+    (1, 4096, 1024),
+]
+
+
+@pytest.mark.parametrize("wtype", TYPES)
+@pytest.mark.parametrize("m,k,n", SHAPE_CASES)
+def test_qk0_decode_every_launch_shape(gpu, lib, wtype, m, k, n):
+    """Every launch shape of the register-fed kernel (one or two CTAs per SM x
+    16, 8 or 4 weight tiles per CTA) that fits the problem gives results
+    within 1e-5 of the oracle, bit-identical on a rerun; a shape that does not
+    fit (Q8_0's rings leave no room for two CTAs per SM) is refused with
+    HTPG_ENOPLAN, by the plan query and by the run."""
+    src, x = _case(wtype, m, k, n, seed=m * 13 + k + n + wtype)
+    ref32 = O.qk0_linear(x, src, wtype, k, n, kind="omp")
+    wd, xd = torch.from_numpy(src).to(gpu), torch.from_numpy(x).to(gpu)
+    w = htpg.qk0_weights(wd, wtype, k, n)
+    ran = 0
+    try:
+        htpg.set_qk0_decode(2)
+        for per_sm in (1, 2):
+            for tiles in (16, 8, 4):
+                htpg.set_qdec_shape(per_sm, tiles)
+                out = torch.full((m, n), float("nan"), device=gpu)
+                plan = (ctypes.c_int64 * 8)()
+                rc = lib.htpg_qk0_decode_plan_info(wtype, m, n, k, 148, plan)
+                if rc == htpg.ENOPLAN:
+                    assert wtype == O.GGML_Q8_0 and per_sm == 2
+                    assert htpg.qk0_run(w, out, xd, m) == htpg.ENOPLAN
+                    continue
+                htpg.check(rc, "htpg_qk0_decode_plan_info")
+                assert (plan[0], plan[1]) == (per_sm, tiles)
+                htpg.check(htpg.qk0_run(w, out, xd, m), "htpg_qk0_run")
+                again = torch.full((m, n), float("nan"), device=gpu)
+                htpg.check(htpg.qk0_run(w, again, xd, m), "htpg_qk0_run")
+                assert htpg.check_device() == 0
+                got = out.cpu().numpy()
+                assert np.isfinite(got).all(), (per_sm, tiles)
+                assert _rel(got, ref32) <= 1e-5, (per_sm, tiles)
+                assert np.array_equal(got, again.cpu().numpy()), (per_sm, tiles)
+                ran += 1
+    finally:
+        htpg.set_qdec_shape(0, 0)
+        htpg.set_qk0_decode(0)
+    assert ran == (3 if wtype == O.GGML_Q8_0 else 6)
+
+
 @pytest.mark.parametrize("wtype", TYPES)
 def test_qk0_repeated_runs_are_identical(gpu, lib, wtype):
-    """Stream-K partial tiles are summed in a fixed order: bit-identical reruns."""
+    """Both small-M kernels sum their partial tiles (k ranges of the
+    register-fed kernel, stream-K pieces of the tcgen05 kernel) in a fixed
+    order: bit-identical reruns."""
     m, k, n = 16, 8192, 256
     src, x = _case(wtype, m, k, n, seed=5)
     wd, xd = torch.from_numpy(src).to(gpu), torch.from_numpy(x).to(gpu)
     w = htpg.qk0_weights(wd, wtype, k, n)
-    outs = []
-    for _ in range(3):
-        out = torch.empty((m, n), device=gpu)
-        htpg.check(htpg.qk0_run(w, out, xd, m), "htpg_qk0_run")
-        outs.append(out.cpu().numpy())
-    assert all(np.array_equal(outs[0], o) for o in outs[1:])
-    assert _rel(outs[0], O.qk0_linear(x, src, wtype, k, n, kind="omp")) <= 1e-5
+    ref = O.qk0_linear(x, src, wtype, k, n, kind="omp")
+    try:
+        for which in (0, 1):
+            htpg.set_qk0_decode(which)
+            outs = []
+            for _ in range(3):
+                out = torch.empty((m, n), device=gpu)
+                htpg.check(htpg.qk0_run(w, out, xd, m), "htpg_qk0_run")
+                outs.append(out.cpu().numpy())
+            assert all(np.array_equal(outs[0], o) for o in outs[1:])
+            assert _rel(outs[0], ref) <= 1e-5
+    finally:
+        htpg.set_qk0_decode(0)
 
 
 @pytest.mark.parametrize("wtype", TYPES)

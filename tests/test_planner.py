@@ -199,3 +199,56 @@ def test_decode_partial_tiles_are_consistent(m, n, k, sms):
     kb = p["kb_total"]
     written, read = _decode_slots(p["tiles_a"] * kb, p["units"], kb)
     assert written == read
+
+
+QK0_DECODE_NS = [32, 96, 160, 1536, 4096, 14336]
+QK0_DECODE_KS = [32, 96, 2048, 4096, 14336, 65536]
+
+
+@pytest.mark.parametrize("wtype", [2, 8, 20])
+@pytest.mark.parametrize("sms", [148, 16])
+def test_qk0_decode_plans_are_legal(wtype, sms):
+    """Register-fed opcode 2-4 decode plans (m <= 16): the grid is the tile
+    groups x k ranges, no range is empty, the activation slice holds the widest
+    range, a CTA's shared memory fits (two CTAs per SM within 112 KB each; a
+    one-per-SM plan asks for more than half the SM so its CTAs spread)."""
+    rings = 16 * 4 * 8 * (272 if wtype == 8 else 144)
+    for m, n, k in itertools.product([1, 4, 8, 9, 16], QK0_DECODE_NS, QK0_DECODE_KS):
+        p = htpg.qk0_decode_plan_info(wtype, m, n, k, sms)
+        nt = 1 if m <= 8 else 2
+        assert p["ntiles"] == n // 32 and p["ktiles"] == k // 32
+        assert p["tiles"] in (16, 8, 4) and p["per_sm"] in (1, 2)
+        assert 1 <= p["splits"] <= p["ktiles"]
+        assert p["grid"] == -(-p["ntiles"] // p["tiles"]) * p["splits"]
+        widest = -(-p["ktiles"] // p["splits"])
+        assert p["slice"] == 8 * nt * (widest * 32 + 8) * 2 <= 64 * 1024
+        assert p["smem"] == max(rings + p["slice"], 116 * 1024 if p["per_sm"] == 1 else 0)
+        assert p["smem"] <= (112 * 1024 if p["per_sm"] == 2 else 227 * 1024)
+        if wtype == 8:
+            assert p["per_sm"] == 1   # Q8_0's rings leave no room for two CTAs
+
+
+@pytest.mark.parametrize("m,k,n,want", [
+    (1, 4096, 14336, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
+    (16, 4096, 14336, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
+    (4, 14336, 4096, {2: (1, 4), 8: (1, 4), 20: (1, 4)}),
+    (16, 14336, 4096, {2: (1, 8), 8: (1, 8), 20: (1, 8)}),
+])
+def test_qk0_decode_plan_choices(m, k, n, want):
+    """On the LLM projections the planner picks the launch shape measured
+    fastest (back to back on a B200) or one within 3% of it; a forced shape
+    overrides it until reset."""
+    for wtype, (per_sm, tiles) in want.items():
+        p = htpg.qk0_decode_plan_info(wtype, m, n, k)
+        assert (p["per_sm"], p["tiles"]) == (per_sm, tiles), wtype
+        assert p["grid"] <= per_sm * 148
+    try:
+        htpg.set_qdec_shape(1, 16)
+        assert htpg.qk0_decode_plan_info(2, m, n, k)["tiles"] == 16
+        htpg.set_qdec_shape(2, 4)
+        with pytest.raises(RuntimeError):
+            htpg.qk0_decode_plan_info(8, m, n, k)   # Q8_0: no room for two CTAs per SM
+    finally:
+        htpg.set_qdec_shape(0, 0)
+    assert htpg.lib().htpg_set_qdec_shape(3, 4) == htpg.EARGS
+    assert htpg.lib().htpg_set_qdec_shape(1, 2) == htpg.EARGS
