@@ -638,18 +638,21 @@ __global__ void __launch_bounds__(kQThreads, 1)
 // ============================================= register-fed decode (M <= 16)
 // Each CTA owns NW (16, 8 or 4) 32-column weight tiles and one range of
 // 32-deep k-tiles; 16 / NW warps share a tile, each a part of the range, and
-// add their FP32 sums in shared memory in a fixed order.  It first rounds its slice of x to FP16 into shared
-// memory (the reference's activation rounding).  Each warp streams its tile's
-// super-blocks from the stage records into its own shared-memory ring with
-// cp.async (a k-tile pair of one tile is 8 consecutive super-blocks, 1152 or
-// 2176 bytes; four pairs in flight), decodes only the FP16 pairs its MMA
-// fragments hold, with dq_decode's arithmetic, and accumulates with mma.sync
-// m16n8k16 (FP16 x FP16 -> FP32).  Fragment layout: lane (g, t) holds, for
-// columns g and g+8 of a 16-column group, pair t of super-blocks 2s and 2s+1
-// (k = 16s + 2t, +1 and 16s + 8 + 2t, +1 of the tile's 32); the activation
-// fragment holds the same k.  The k ranges' FP32 partial tiles meet in a
-// workspace; the last range to arrive sums them in range order
-// (deterministic) and writes the output.  No thread waits for another CTA.
+// add their FP32 sums in shared memory in a fixed order.  It first rounds its
+// slice of x to FP16 into shared memory (the reference's activation rounding).
+// Each warp streams its tile's super-blocks from the stage records into its
+// own shared-memory ring with cp.async (a k-tile pair of one tile is 8
+// consecutive super-blocks, 1152 or 2176 bytes; four pairs in flight), decodes
+// only the FP16 pairs its MMA fragments hold, with dq_decode's arithmetic, and
+// accumulates with mma.sync m16n8k16 (FP16 x FP16 -> FP32).  Fragment layout:
+// lane (g, t) holds tile columns 4g .. 4g+3 (MMA rows g / g+8 of column group
+// cg are columns 4g + 2cg / 4g + 2cg + 1, so a lane's codes of one super-block
+// are adjacent in shared memory), pair t of super-blocks 2s and 2s+1 (k = 16s
+// + 2t, +1 and 16s + 8 + 2t, +1 of the tile's 32); the activation fragment
+// holds the same k.  The k ranges' FP32 partial tiles meet in a workspace
+// (lane-major: each lane's values in one 128-byte row per element); the last
+// range to arrive sums them in range order (deterministic) and writes the
+// output.  No thread waits for another CTA.
 constexpr int kQdWarps = 16, kQdThreads = 32 * kQdWarps;
 constexpr int kQdStages = 4;       // k-tile pairs of a warp's tile in flight
 constexpr int kQdMaxSplits = 32;   // k ranges per tile at most (the last one sums them all)
@@ -675,11 +678,13 @@ __device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32
 }
 
 // The raw words one lane needs from one 32 x 32 tile (four super-blocks) in
-// shared memory: scale word t of each super-block and the codes of pair t of
-// columns g, g+8, g+16, g+24.
+// shared memory: scale word t of each super-block and the codes of columns
+// 4g .. 4g+3 (Q4_0 / IQ4_NL: the columns' code words, one 16-byte load per
+// super-block; Q8_0: pair t of the four columns, one 8-byte load, two columns
+// per word: q[j][0] = q[j][1] and q[j][2] = q[j][3]).
 struct QdWords {
   uint32_t sc[4];
-  uint32_t q[4][4];  // [super-block][column]
+  uint32_t q[4][4];  // [super-block][column 4g + c]
 };
 
 template <int QT>
@@ -689,31 +694,31 @@ __device__ __forceinline__ void qd_load(QdWords &w, uint32_t tile, int g, int t)
   for (int j = 0; j < 4; ++j) {
     const uint32_t sb = tile + j * BLK;
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w.sc[j]) : "r"(sb + 4 * t));
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int m = g + 8 * c;
-      if constexpr (QT == kGgmlQ8_0) {
-        uint16_t h;
-        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(sb + 16 + 2 * m + 64 * t));
-        w.q[j][c] = h;
-      } else {
-        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w.q[j][c]) : "r"(sb + 16 + 4 * m));
-      }
+    if constexpr (QT == kGgmlQ8_0) {
+      asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w.q[j][0]), "=r"(w.q[j][2]) : "r"(sb + 16 + 8 * g + 64 * t));
+      w.q[j][1] = w.q[j][0];
+      w.q[j][3] = w.q[j][2];
+    } else {
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w.q[j][0]), "=r"(w.q[j][1]), "=r"(w.q[j][2]), "=r"(w.q[j][3])
+                   : "r"(sb + 16 + 16 * g));
     }
   }
 }
 
-// Pair t (k = 2t, 2t+1 of the super-block's eight) of column m: the same
-// operations as dq_decode's element pair t.  sh = 4 * the nibble index of the
-// pair's first code in the word: dq_decode's pairs are (b0.lo, b2.lo),
-// (b1.lo, b3.lo), (b0.hi, b2.hi), (b1.hi, b3.hi), i.e. nibbles 0, 2, 1, 3 and
-// the same + 4 (computed without branches: ((t & 1) << 3) | ((t >> 1) << 2)).
-template <int QT>
-__device__ __forceinline__ uint32_t qd_pair(uint32_t scw, uint32_t q, int m, int sh) {
-  const uint32_t s = prmt(scw, scw, (m & 16) ? 0x3232u : 0x1010u);
+// Pair t (k = 2t, 2t+1 of the super-block's eight) of one column: the same
+// operations as dq_decode's element pair t.  ssel broadcasts the column's
+// scale (scale 2v + column / 16 of the super-block's eight).  sh = 4 * the
+// nibble index of the pair's first code in the word: dq_decode's pairs are
+// (b0.lo, b2.lo), (b1.lo, b3.lo), (b0.hi, b2.hi), (b1.hi, b3.hi), i.e.
+// nibbles 0, 2, 1, 3 and the same + 4 (computed without branches:
+// ((t & 1) << 3) | ((t >> 1) << 2)).  Q8_0: HI takes the word's upper pair.
+template <int QT, bool HI>
+__device__ __forceinline__ uint32_t qd_pair(uint32_t scw, uint32_t q, uint32_t ssel, int sh) {
+  const uint32_t s = prmt(scw, scw, ssel);
   uint32_t h, bias;
   if constexpr (QT == kGgmlQ8_0) {
-    h = prmt(q, 0x64646464u, 0x5140u) ^ 0x00800080u;
+    h = prmt(q, 0x64646464u, HI ? 0x5342u : 0x5140u) ^ 0x00800080u;
     bias = 0x64806480u;
   } else if constexpr (QT == kGgmlQ4_0) {
     h = ((q >> sh) & 0x000F000Fu) | 0x64006400u;
@@ -727,27 +732,31 @@ __device__ __forceinline__ uint32_t qd_pair(uint32_t scw, uint32_t q, int m, int
   return hmul2_rn(hsub2_rn(h, bias), s);
 }
 
-// Pair t of column m in two super-blocks (words q0, q1 with scale words sc0,
-// sc1): qd_pair twice.  IQ4_NL looks the four nibbles up together: one byte
-// permute gathers bytes (t & 1) and (t & 1) + 2 of both words, the shift by
-// s4 = 4 * (t >> 1) brings the pair's nibbles to the bytes' low halves, and
-// x = A0 | A1 << 4 | B0 << 8 | B1 << 12 indexes the table (A, B: the pair's
-// nibbles at sh and sh + 16 of q0 and q1).
-template <int QT>
-__device__ __forceinline__ void qd_pair2(uint32_t sc0, uint32_t sc1, uint32_t q0, uint32_t q1, int m, int sh,
+// Pair t of one column in two super-blocks (words q0, q1 with scale words
+// sc0, sc1): qd_pair twice.  IQ4_NL looks the four nibbles up together: one
+// byte permute gathers bytes (t & 1) and (t & 1) + 2 of both words, the shift
+// by s4 = 4 * (t >> 1) brings the pair's nibbles to the bytes' low halves,
+// and x = A0 | A1 << 4 | B0 << 8 | B1 << 12 indexes the table (A, B: the
+// pair's nibbles at sh and sh + 16 of q0 and q1).
+template <int QT, bool HI>
+__device__ __forceinline__ void qd_pair2(uint32_t sc0, uint32_t sc1, uint32_t q0, uint32_t q1, uint32_t ssel, int sh,
                                          uint32_t gsel, int s4, uint32_t &r0, uint32_t &r1) {
   if constexpr (QT == kGgmlIQ4_NL) {
     const uint32_t w = prmt(q0, q1, gsel) >> s4;
     const uint32_t lv = iq4_lookup4((w & 0x0F0Fu) | ((w >> 12) & 0xF0F0u));  // L(A0) L(A1) L(B0) L(B1)
     const uint32_t bias = 0x64806480u;
-    const uint32_t ssel = (m & 16) ? 0x3232u : 0x1010u;
     r0 = hmul2_rn(hsub2_rn(prmt(lv, 0x64646464u, 0x4240u), bias), prmt(sc0, sc0, ssel));
     r1 = hmul2_rn(hsub2_rn(prmt(lv, 0x64646464u, 0x4341u), bias), prmt(sc1, sc1, ssel));
   } else {
-    r0 = qd_pair<QT>(sc0, q0, m, sh);
-    r1 = qd_pair<QT>(sc1, q1, m, sh);
+    r0 = qd_pair<QT, HI>(sc0, q0, ssel, sh);
+    r1 = qd_pair<QT, HI>(sc1, q1, ssel, sh);
   }
 }
+
+// Position of word w of an activation row in the shared-memory slice: each
+// 16-k group (8 words) holds its pairs in the order 0, 4, 1, 5, 2, 6, 3, 7,
+// so that a lane's two activation words (pairs t and t + 4) are one 8-byte load.
+__device__ __forceinline__ int qd_xpos(int w) { return (w & ~7) | ((w & 3) << 1) | ((w >> 2) & 1); }
 
 __device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
   uint32_t d;
@@ -765,6 +774,7 @@ __global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P)
   const int sh = ((t & 1) << 3) | ((t >> 1) << 2);  // see qd_pair
   const uint32_t gsel = 0x6420u + 0x1111u * static_cast<uint32_t>(t & 1);  // see qd_pair2
   const int s4 = (t >> 1) << 2;
+  const uint32_t ssel = g >= 4 ? 0x3232u : 0x1010u;  // columns 4g.. >= 16: the upper scale of each pair
   const int grp = blockIdx.x / P.S, sp = blockIdx.x - grp * P.S;
   const int kt0 = static_cast<int>(static_cast<long long>(P.ktiles) * sp / P.S);
   const int kt1 = static_cast<int>(static_cast<long long>(P.ktiles) * (sp + 1) / P.S);
@@ -773,7 +783,7 @@ __global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P)
   const int wk0 = kt0 + (kt1 - kt0) * ks / kw_parts, wk1 = kt0 + (kt1 - kt0) * (ks + 1) / kw_parts;
   const bool active = nt < P.ntiles && wk1 > wk0;
   const uint32_t ring = smem_u32(qd_smem) + static_cast<uint32_t>(warp * kQdStages * PAIR);
-  uint32_t *qd_x = qd_smem + kQdWarps * kQdStages * PAIR / 4;  // [8 NT rows][pitch / 2] f16x2
+  uint32_t *qd_x = qd_smem + kQdWarps * kQdStages * PAIR / 4;  // [8 NT rows][pitch / 2] f16x2, see qd_xpos
   // k-tile pair pp (k-tiles 2pp, 2pp+1) of this warp's tile: 8 consecutive
   // super-blocks of record (nt/4, pp), starting at block (nt%4)*8
   const int pp0 = wk0 >> 1, npairs = active ? ((wk1 - 1) >> 1) - pp0 + 1 : 0;
@@ -798,8 +808,8 @@ __global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P)
     const int r = i / (kw / 4), c4 = i - r * (kw / 4);
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (r < P.M) v = ld_dep(reinterpret_cast<const float4 *>(P.x + static_cast<size_t>(r) * P.K + kt0 * 32) + c4);
-    qd_x[r * (P.pitch / 2) + 2 * c4] = f2_to_h2(v.x, v.y);
-    qd_x[r * (P.pitch / 2) + 2 * c4 + 1] = f2_to_h2(v.z, v.w);
+    qd_x[r * (P.pitch / 2) + qd_xpos(2 * c4)] = f2_to_h2(v.x, v.y);
+    qd_x[r * (P.pitch / 2) + qd_xpos(2 * c4 + 1)] = f2_to_h2(v.z, v.w);
   }
   __syncthreads();
 
@@ -826,18 +836,19 @@ __global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P)
         uint32_t b[NT][2];
 #pragma unroll
         for (int jt = 0; jt < NT; ++jt) {
-          const uint32_t *row = qd_x + (8 * jt + g) * (P.pitch / 2);
-          b[jt][0] = row[(kl + 16 * s2 + 2 * t) / 2];
-          b[jt][1] = row[(kl + 16 * s2 + 8 + 2 * t) / 2];
+          // pairs t and t + 4 of the 16-k group: adjacent words (qd_xpos)
+          const uint2 bv = *reinterpret_cast<const uint2 *>(qd_x + (8 * jt + g) * (P.pitch / 2) + (kl + 16 * s2) / 2 + 2 * t);
+          b[jt][0] = bv.x;
+          b[jt][1] = bv.y;
         }
 #pragma unroll
         for (int cg = 0; cg < 2; ++cg) {
           const int c0 = 2 * cg, c1 = 2 * cg + 1;
           uint32_t a0, a1, a2, a3;
-          qd_pair2<QT>(cur.sc[2 * s2], cur.sc[2 * s2 + 1], cur.q[2 * s2][c0], cur.q[2 * s2 + 1][c0], g + 8 * c0, sh,
-                       gsel, s4, a0, a2);
-          qd_pair2<QT>(cur.sc[2 * s2], cur.sc[2 * s2 + 1], cur.q[2 * s2][c1], cur.q[2 * s2 + 1][c1], g + 8 * c1, sh,
-                       gsel, s4, a1, a3);
+          qd_pair2<QT, false>(cur.sc[2 * s2], cur.sc[2 * s2 + 1], cur.q[2 * s2][c0], cur.q[2 * s2 + 1][c0], ssel, sh,
+                              gsel, s4, a0, a2);
+          qd_pair2<QT, true>(cur.sc[2 * s2], cur.sc[2 * s2 + 1], cur.q[2 * s2][c1], cur.q[2 * s2 + 1][c1], ssel, sh,
+                             gsel, s4, a1, a3);
 #pragma unroll
           for (int jt = 0; jt < NT; ++jt) mma_f16_16816(acc[cg][jt], a0, a1, a2, a3, b[jt][0], b[jt][1]);
         }
@@ -847,9 +858,9 @@ __global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P)
     issue_pair(i + kQdStages);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
-  auto elem = [&](int cg, int jt, int r) {  // accumulator element (cg, jt, r) in a [32][16] partial tile
-    return (16 * cg + g + ((r & 2) ? 8 : 0)) * 16 + 8 * jt + 2 * t + (r & 1);
-  };
+  // accumulator element (cg, jt, r) of this lane in a 512-float partial tile:
+  // lane-major, so that a warp's stores and loads of one element are 128 bytes
+  auto elem = [&](int cg, int jt, int r) { return ((cg * NT + jt) * 4 + r) * 32 + lane; };
   if (kw_parts > 1) {
     // the tile's warps add their parts in part order, through shared memory
     // (over the rings, which every warp has finished with)
@@ -931,7 +942,7 @@ __global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P)
     for (int jt = 0; jt < NT; ++jt)
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const int col = 16 * cg + g + ((r & 2) ? 8 : 0), tok = 8 * jt + 2 * t + (r & 1);
+        const int col = 4 * g + 2 * cg + (r >> 1), tok = 8 * jt + 2 * t + (r & 1);
         if (tok < P.M) P.out[static_cast<size_t>(tok) * P.ldo + nt * 32 + col] = acc[cg][jt][r];
       }
   if (lane == 0) P.cnt[nt] = 0u;
@@ -967,9 +978,9 @@ QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms) {
   const int qb = nt == 1 ? 4 : 2;  // the finisher's ranges per batch (qdec_kernel's QB)
   const int force = g_qdec_shape.load();
   double best_cost = 0.0;
-  auto slice_bytes = [&](int S) {  // rows 4 words apart in the banks: 8 halves of padding
-    return static_cast<size_t>(8 * nt) * ((ktiles + S - 1) / S * 32 + 8) * 2;
-  };
+  // rows 8 words apart in the banks (16 halves of padding): a half-warp's
+  // 8-byte activation loads (4 rows x 32 bytes) hit every bank once
+  auto slice_bytes = [&](int S) { return static_cast<size_t>(8 * nt) * ((ktiles + S - 1) / S * 32 + 16) * 2; };
   for (int per_sm = 1; per_sm <= 2; ++per_sm) {
     // per CTA: 113 KB of the SM's 228 (1 KB of each CTA's is reserved) with
     // two; the kernel's launch bounds keep two CTAs' registers within the SM's
@@ -1000,7 +1011,7 @@ QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms) {
         best.per_sm = per_sm;
         best.splits = S;
         best.grid = static_cast<int>(grid);
-        best.pitch = (ktiles + S - 1) / S * 32 + 8;  // halves
+        best.pitch = (ktiles + S - 1) / S * 32 + 16;  // halves
         best.smem = slice_bytes(S);                  // the slice (the rings are added per type)
       }
     }

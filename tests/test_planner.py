@@ -221,7 +221,7 @@ def test_qk0_decode_plans_are_legal(wtype, sms):
         assert 1 <= p["splits"] <= p["ktiles"]
         assert p["grid"] == -(-p["ntiles"] // p["tiles"]) * p["splits"]
         widest = -(-p["ktiles"] // p["splits"])
-        assert p["slice"] == 8 * nt * (widest * 32 + 8) * 2 <= 64 * 1024
+        assert p["slice"] == 8 * nt * (widest * 32 + 16) * 2 <= 64 * 1024
         assert p["smem"] == max(rings + p["slice"], 116 * 1024 if p["per_sm"] == 1 else 0)
         assert p["smem"] <= (112 * 1024 if p["per_sm"] == 2 else 227 * 1024)
         if wtype == 8:
