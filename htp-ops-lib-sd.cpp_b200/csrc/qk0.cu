@@ -707,15 +707,14 @@ __device__ __forceinline__ void qd_load(QdWords &w, uint32_t tile, int g, int t)
 }
 
 // Pair t (k = 2t, 2t+1 of the super-block's eight) of one column: the same
-// operations as dq_decode's element pair t.  ssel broadcasts the column's
-// scale (scale 2v + column / 16 of the super-block's eight).  sh = 4 * the
+// operations as dq_decode's element pair t.  s: the column's scale (scale
+// 2v + column / 16 of the super-block's eight) in both halves.  sh = 4 * the
 // nibble index of the pair's first code in the word: dq_decode's pairs are
 // (b0.lo, b2.lo), (b1.lo, b3.lo), (b0.hi, b2.hi), (b1.hi, b3.hi), i.e.
 // nibbles 0, 2, 1, 3 and the same + 4 (computed without branches:
 // ((t & 1) << 3) | ((t >> 1) << 2)).  Q8_0: HI takes the word's upper pair.
 template <int QT, bool HI>
-__device__ __forceinline__ uint32_t qd_pair(uint32_t scw, uint32_t q, uint32_t ssel, int sh) {
-  const uint32_t s = prmt(scw, scw, ssel);
+__device__ __forceinline__ uint32_t qd_pair(uint32_t s, uint32_t q, int sh) {
   uint32_t h, bias;
   if constexpr (QT == kGgmlQ8_0) {
     h = prmt(q, 0x64646464u, HI ? 0x5342u : 0x5140u) ^ 0x00800080u;
@@ -732,24 +731,24 @@ __device__ __forceinline__ uint32_t qd_pair(uint32_t scw, uint32_t q, uint32_t s
   return hmul2_rn(hsub2_rn(h, bias), s);
 }
 
-// Pair t of one column in two super-blocks (words q0, q1 with scale words
-// sc0, sc1): qd_pair twice.  IQ4_NL looks the four nibbles up together: one
+// Pair t of one column in two super-blocks (words q0, q1 with broadcast
+// scales s0, s1): qd_pair twice.  IQ4_NL looks the four nibbles up together: one
 // byte permute gathers bytes (t & 1) and (t & 1) + 2 of both words, the shift
 // by s4 = 4 * (t >> 1) brings the pair's nibbles to the bytes' low halves,
 // and x = A0 | A1 << 4 | B0 << 8 | B1 << 12 indexes the table (A, B: the
 // pair's nibbles at sh and sh + 16 of q0 and q1).
 template <int QT, bool HI>
-__device__ __forceinline__ void qd_pair2(uint32_t sc0, uint32_t sc1, uint32_t q0, uint32_t q1, uint32_t ssel, int sh,
-                                         uint32_t gsel, int s4, uint32_t &r0, uint32_t &r1) {
+__device__ __forceinline__ void qd_pair2(uint32_t s0, uint32_t s1, uint32_t q0, uint32_t q1, int sh, uint32_t gsel,
+                                         int s4, uint32_t &r0, uint32_t &r1) {
   if constexpr (QT == kGgmlIQ4_NL) {
     const uint32_t w = prmt(q0, q1, gsel) >> s4;
     const uint32_t lv = iq4_lookup4((w & 0x0F0Fu) | ((w >> 12) & 0xF0F0u));  // L(A0) L(A1) L(B0) L(B1)
     const uint32_t bias = 0x64806480u;
-    r0 = hmul2_rn(hsub2_rn(prmt(lv, 0x64646464u, 0x4240u), bias), prmt(sc0, sc0, ssel));
-    r1 = hmul2_rn(hsub2_rn(prmt(lv, 0x64646464u, 0x4341u), bias), prmt(sc1, sc1, ssel));
+    r0 = hmul2_rn(hsub2_rn(prmt(lv, 0x64646464u, 0x4240u), bias), s0);
+    r1 = hmul2_rn(hsub2_rn(prmt(lv, 0x64646464u, 0x4341u), bias), s1);
   } else {
-    r0 = qd_pair<QT, HI>(sc0, q0, ssel, sh);
-    r1 = qd_pair<QT, HI>(sc1, q1, ssel, sh);
+    r0 = qd_pair<QT, HI>(s0, q0, sh);
+    r1 = qd_pair<QT, HI>(s1, q1, sh);
   }
 }
 
@@ -787,13 +786,17 @@ __global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P)
   // k-tile pair pp (k-tiles 2pp, 2pp+1) of this warp's tile: 8 consecutive
   // super-blocks of record (nt/4, pp), starting at block (nt%4)*8
   const int pp0 = wk0 >> 1, npairs = active ? ((wk1 - 1) >> 1) - pp0 + 1 : 0;
+  // this lane's first 16-byte chunk of pair pp0; records of one tile group are 32 * BLK apart
+  const uint8_t *wsrc = P.w + (static_cast<size_t>(nt >> 2) * P.kb_total + pp0) * (32u * BLK) +
+                        static_cast<size_t>((nt & 3) << 3) * BLK + 16 * lane;
   auto issue_pair = [&](int i) {  // pair pp0 + i into stage i % stages (one commit group per call)
     if (active && i < npairs) {
-      const uint8_t *src = P.w + (static_cast<size_t>(nt >> 2) * P.kb_total + (pp0 + i)) * (32u * BLK) +
-                           static_cast<size_t>((nt & 3) << 3) * BLK;
-      const uint32_t dst = ring + static_cast<uint32_t>((i % kQdStages) * PAIR);
-      for (int c = lane; c < PAIR / 16; c += 32)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16 * c), "l"(src + 16 * c) : "memory");
+      const uint8_t *src = wsrc + static_cast<size_t>(i) * (32u * BLK);
+      const uint32_t dst = ring + static_cast<uint32_t>((i % kQdStages) * PAIR) + 16 * lane;
+#pragma unroll
+      for (int c = 0; c < (PAIR / 16 + 31) / 32; ++c)
+        if (lane + 32 * c < PAIR / 16)
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 512 * c), "l"(src + 512 * c) : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
@@ -824,7 +827,7 @@ __global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P)
     asm volatile("cp.async.wait_group %0;" ::"n"(kQdStages - 1) : "memory");  // pair i has landed
     __syncwarp();
     const uint32_t stage = ring + static_cast<uint32_t>((i % kQdStages) * PAIR);
-#pragma unroll 1
+#pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int kt = 2 * (pp0 + i) + e;
       if (kt < wk0 || kt >= wk1) continue;
@@ -841,14 +844,15 @@ __global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P)
           b[jt][0] = bv.x;
           b[jt][1] = bv.y;
         }
+        // the lane's column scales of the two super-blocks, both halves
+        const uint32_t sl = prmt(cur.sc[2 * s2], cur.sc[2 * s2], ssel);
+        const uint32_t su = prmt(cur.sc[2 * s2 + 1], cur.sc[2 * s2 + 1], ssel);
 #pragma unroll
         for (int cg = 0; cg < 2; ++cg) {
           const int c0 = 2 * cg, c1 = 2 * cg + 1;
           uint32_t a0, a1, a2, a3;
-          qd_pair2<QT, false>(cur.sc[2 * s2], cur.sc[2 * s2 + 1], cur.q[2 * s2][c0], cur.q[2 * s2 + 1][c0], ssel, sh,
-                              gsel, s4, a0, a2);
-          qd_pair2<QT, true>(cur.sc[2 * s2], cur.sc[2 * s2 + 1], cur.q[2 * s2][c1], cur.q[2 * s2 + 1][c1], ssel, sh,
-                             gsel, s4, a1, a3);
+          qd_pair2<QT, false>(sl, su, cur.q[2 * s2][c0], cur.q[2 * s2 + 1][c0], sh, gsel, s4, a0, a2);
+          qd_pair2<QT, true>(sl, su, cur.q[2 * s2][c1], cur.q[2 * s2 + 1][c1], sh, gsel, s4, a1, a3);
 #pragma unroll
           for (int jt = 0; jt < NT; ++jt) mma_f16_16816(acc[cg][jt], a0, a1, a2, a3, b[jt][0], b[jt][1]);
         }
