@@ -763,8 +763,10 @@ __device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
   return d;
 }
 
-template <int QT, int NT>
-__global__ void __launch_bounds__(kQdThreads, 2) qdec_kernel(const QDecParams P) {
+// MB: the CTAs per SM the launch bounds promise (a plan for two CTAs per SM
+// keeps 64 registers per thread; one CTA per SM may use up to 128).
+template <int QT, int NT, int MB>
+__global__ void __launch_bounds__(kQdThreads, MB) qdec_kernel(const QDecParams P) {
   constexpr int BLK = QT == kGgmlQ8_0 ? 272 : 144;
   constexpr int PAIR = qd_pair_bytes(QT);
   extern __shared__ __align__(16) uint32_t qd_smem[];  // [16 warps][stages][PAIR] rings, then the x slice
@@ -1030,9 +1032,9 @@ size_t qdec_smem_bytes(int qt, const QDecPlan &p) {
   return p.per_sm == 1 && s < 116 * 1024 ? 116 * 1024 : s;
 }
 
-template <int QT, int NT>
+template <int QT, int NT, int MB>
 static cudaError_t launch_qdec_t(const QDecPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st) {
-  auto fn = qdec_kernel<QT, NT>;
+  auto fn = qdec_kernel<QT, NT, MB>;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1078,12 +1080,13 @@ static cudaError_t launch_qdec_t(const QDecPlan &p, const uint8_t *w, const QGem
 
 cudaError_t launch_qdec(int qt, const QDecPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st) {
   if (a.M < 1 || a.M > 16 || a.N % 32 || a.K % 32 || p.smem > kQdMaxSlice) return cudaErrorInvalidConfiguration;
-  if (qt == kGgmlQ4_0)
-    return p.nt == 1 ? launch_qdec_t<kGgmlQ4_0, 1>(p, w, a, st) : launch_qdec_t<kGgmlQ4_0, 2>(p, w, a, st);
-  if (qt == kGgmlQ8_0)
-    return p.nt == 1 ? launch_qdec_t<kGgmlQ8_0, 1>(p, w, a, st) : launch_qdec_t<kGgmlQ8_0, 2>(p, w, a, st);
-  if (qt == kGgmlIQ4_NL)
-    return p.nt == 1 ? launch_qdec_t<kGgmlIQ4_NL, 1>(p, w, a, st) : launch_qdec_t<kGgmlIQ4_NL, 2>(p, w, a, st);
+#define HTPG_QDEC(T)                                                                           \
+  (p.per_sm == 1 ? (p.nt == 1 ? launch_qdec_t<T, 1, 1>(p, w, a, st) : launch_qdec_t<T, 2, 1>(p, w, a, st)) \
+                 : (p.nt == 1 ? launch_qdec_t<T, 1, 2>(p, w, a, st) : launch_qdec_t<T, 2, 2>(p, w, a, st)))
+  if (qt == kGgmlQ4_0) return HTPG_QDEC(kGgmlQ4_0);
+  if (qt == kGgmlQ8_0) return HTPG_QDEC(kGgmlQ8_0);
+  if (qt == kGgmlIQ4_NL) return HTPG_QDEC(kGgmlIQ4_NL);
+#undef HTPG_QDEC
   return cudaErrorInvalidValue;
 }
 
