@@ -1231,7 +1231,7 @@ extern "C" int htpg_qk0_run(const htpg_weights *w, float *out, const float *x, i
   }
   std::lock_guard<std::mutex> lk(g_mu);
   const int qdec_mode = g_qdec.load();
-  if (m <= 16 && (qdec_mode == 2 || (qdec_mode == 1 && qdec_serves(qt, m)))) {
+  if (m <= 32 && (qdec_mode == 2 || (qdec_mode == 1 && qdec_serves(qt, m)))) {
     // decode shapes: the register-fed kernel (weights streamed into registers)
     const QDecPlan plan = plan_qdec(qt, m, n, k, d->sms);
     if (plan.grid == 0 || qdec_counter_bytes(plan) > kQCounterBytes || plan.smem > kQdMaxSlice) return HTPG_ENOPLAN;
@@ -1282,7 +1282,7 @@ extern "C" int htpg_qk0_plan_info(int weight_type, int m, int n, int k, int sms,
 }
 
 extern "C" int htpg_qk0_decode_plan_info(int weight_type, int m, int n, int k, int sms, int64_t out[8]) {
-  if (!out || !qk0_type_ok(weight_type) || m < 1 || m > 16 || n < 32 || k < 32 || n % 32 || k % 32 || sms < 1)
+  if (!out || !qk0_type_ok(weight_type) || m < 1 || m > 32 || n < 32 || k < 32 || n % 32 || k % 32 || sms < 1)
     return HTPG_EARGS;
   const QDecPlan p = plan_qdec(weight_type, m, n, k, sms);
   if (p.grid == 0) return HTPG_ENOPLAN;

@@ -183,12 +183,12 @@ struct QGemmArgs {
 };
 // w: the stage records (launch_qk0_repack).
 cudaError_t launch_qgemm(int qt, const QGemmPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st);
-// Register-fed decode for M <= 16 (qk0.cu, qdec_kernel): up to 16 32-column
+// Register-fed decode for M <= 32 (qk0.cu, qdec_kernel): up to 16 32-column
 // weight tiles x one k range per CTA, FP32 partials of the ranges summed in
-// range order.  Partials: ntiles * splits * 32 * 16 floats; counters: ntiles.
+// range order.  Partials: ntiles * splits * 32 * 8 nt floats; counters: ntiles.
 constexpr size_t kQdMaxSlice = 64 * 1024;  // shared-memory bytes of the FP16 activation slice
 struct QDecPlan {
-  int nt = 1;          // 8-token MMA tiles (M <= 8: 1, else 2)
+  int nt = 1;          // 8-token MMA tiles (M <= 8: 1, M <= 16: 2, else 4)
   int ntiles = 0, ktiles = 0, splits = 1, grid = 0, pitch = 0;
   int nw = 16;         // weight tiles per CTA
   int per_sm = 1;      // CTAs resident per SM the plan is sized for
@@ -196,16 +196,18 @@ struct QDecPlan {
 };
 QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms);
 size_t qdec_smem_bytes(int qt, const QDecPlan &p);  // the weight rings plus the activation slice
-inline size_t qdec_partial_bytes(const QDecPlan &p) { return static_cast<size_t>(p.ntiles) * p.splits * 32 * 16 * 4; }
+inline size_t qdec_partial_bytes(const QDecPlan &p) {
+  return static_cast<size_t>(p.ntiles) * p.splits * 32 * 8 * p.nt * 4;
+}
 inline size_t qdec_counter_bytes(const QDecPlan &p) { return static_cast<size_t>(p.ntiles) * 4; }
 cudaError_t launch_qdec(int qt, const QDecPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st);
-extern std::atomic<int> g_qdec;  // 1: the register-fed kernel where qdec_serves; 0: never; 2: every m <= 16
+extern std::atomic<int> g_qdec;  // 1: the register-fed kernel where qdec_serves; 0: never; 2: every m <= 32
 extern std::atomic<int> g_qdec_shape;  // 0: plan_qdec chooses; else CTAs per SM * 100 + tiles per CTA
-// Where the register-fed kernel is the faster one: every type up to 16 tokens
+// Where the register-fed kernel is the faster one: every type up to 32 tokens
 // (LLM up / down projections, K x N = 4096 x 14336 and 14336 x 4096, back to
-// back: 19-34 us against 34-38 us for the tcgen05 kernel).
+// back: 14.5-33 us against 34-43 us for the tcgen05 kernel).
 inline bool qdec_serves(int qt, int m) {
-  return (qt == kGgmlQ8_0 || qt == kGgmlQ4_0 || qt == kGgmlIQ4_NL) && m <= 16;
+  return (qt == kGgmlQ8_0 || qt == kGgmlQ4_0 || qt == kGgmlIQ4_NL) && m <= 32;
 }
 
 // Kernel launches issued since load (all launchers above count themselves).

@@ -768,6 +768,7 @@ __device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
 template <int QT, int NT, int MB>
 __global__ void __launch_bounds__(kQdThreads, MB) qdec_kernel(const QDecParams P) {
   constexpr int BLK = QT == kGgmlQ8_0 ? 272 : 144;
+  constexpr int TILEF = 256 * NT;  // floats of one partial tile: 32 columns x 8 NT tokens
   constexpr int PAIR = qd_pair_bytes(QT);
   extern __shared__ __align__(16) uint32_t qd_smem[];  // [16 warps][stages][PAIR] rings, then the x slice
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -864,13 +865,14 @@ __global__ void __launch_bounds__(kQdThreads, MB) qdec_kernel(const QDecParams P
     issue_pair(i + kQdStages);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
-  // accumulator element (cg, jt, r) of this lane in a 512-float partial tile:
-  // lane-major, so that a warp's stores and loads of one element are 128 bytes
+  // accumulator element (cg, jt, r) of this lane in a partial tile (32
+  // columns x 8 NT tokens): lane-major, so that a warp's stores and loads of
+  // one element are 128 bytes
   auto elem = [&](int cg, int jt, int r) { return ((cg * NT + jt) * 4 + r) * 32 + lane; };
   if (kw_parts > 1) {
     // the tile's warps add their parts in part order, through shared memory
     // (over the rings, which every warp has finished with)
-    float *red = reinterpret_cast<float *>(qd_smem);  // [part][nw][32 * 16]
+    float *red = reinterpret_cast<float *>(qd_smem);  // [part][nw][TILEF]
     __syncthreads();
     if (nt < P.ntiles)
 #pragma unroll
@@ -878,7 +880,7 @@ __global__ void __launch_bounds__(kQdThreads, MB) qdec_kernel(const QDecParams P
 #pragma unroll
         for (int jt = 0; jt < NT; ++jt)
 #pragma unroll
-          for (int r = 0; r < 4; ++r) red[(ks * P.nw + (warp - ks * P.nw)) * 512 + elem(cg, jt, r)] = acc[cg][jt][r];
+          for (int r = 0; r < 4; ++r) red[(ks * P.nw + (warp - ks * P.nw)) * TILEF + elem(cg, jt, r)] = acc[cg][jt][r];
     __syncthreads();
     if (ks != 0 || nt >= P.ntiles) return;
 #pragma unroll
@@ -887,8 +889,8 @@ __global__ void __launch_bounds__(kQdThreads, MB) qdec_kernel(const QDecParams P
       for (int jt = 0; jt < NT; ++jt)
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          float v = red[warp * 512 + elem(cg, jt, r)];
-          for (int q = 1; q < kw_parts; ++q) v = __fadd_rn(v, red[(q * P.nw + warp) * 512 + elem(cg, jt, r)]);
+          float v = red[warp * TILEF + elem(cg, jt, r)];
+          for (int q = 1; q < kw_parts; ++q) v = __fadd_rn(v, red[(q * P.nw + warp) * TILEF + elem(cg, jt, r)]);
           acc[cg][jt][r] = v;
         }
   } else if (nt >= P.ntiles) {
@@ -896,7 +898,7 @@ __global__ void __launch_bounds__(kQdThreads, MB) qdec_kernel(const QDecParams P
   }
   // this range's partial tile, then the arrival; the last range of the tile
   // sums all ranges' partials in range order and writes the output
-  float *mine = P.part + (static_cast<size_t>(nt) * P.S + sp) * (32 * 16);
+  float *mine = P.part + (static_cast<size_t>(nt) * P.S + sp) * TILEF;
 #pragma unroll
   for (int cg = 0; cg < 2; ++cg)
 #pragma unroll
@@ -910,10 +912,10 @@ __global__ void __launch_bounds__(kQdThreads, MB) qdec_kernel(const QDecParams P
   prev = __shfl_sync(0xffffffffu, prev, 0);
   if (prev != static_cast<uint32_t>(P.S - 1)) return;
   __syncwarp();  // lane 0's acquire orders every lane's reads below
-  const float *all = P.part + static_cast<size_t>(nt) * P.S * (32 * 16);
+  const float *all = P.part + static_cast<size_t>(nt) * P.S * TILEF;
   // the lane's elements of every range: QB ranges' loads in flight at a time,
   // added in range order
-  constexpr int QB = NT == 1 ? 4 : 2;
+  constexpr int QB = NT == 1 ? 4 : NT == 2 ? 2 : 1;
 #pragma unroll
   for (int cg = 0; cg < 2; ++cg)
 #pragma unroll
@@ -930,7 +932,7 @@ __global__ void __launch_bounds__(kQdThreads, MB) qdec_kernel(const QDecParams P
         for (int jt = 0; jt < NT; ++jt)
 #pragma unroll
           for (int r = 0; r < 4; ++r)
-            u[qq][cg][jt][r] = q0 + qq < P.S ? __ldcg(all + (q0 + qq) * (32 * 16) + elem(cg, jt, r)) : 0.0f;
+            u[qq][cg][jt][r] = q0 + qq < P.S ? __ldcg(all + (q0 + qq) * TILEF + elem(cg, jt, r)) : 0.0f;
 #pragma unroll
     for (int qq = 0; qq < QB; ++qq)
       if (q0 + qq < P.S) {
@@ -975,13 +977,13 @@ std::atomic<int> g_qdec_shape{0};
 QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms) {
   QDecPlan best;
   best.grid = 0;
-  const int nt = M <= 8 ? 1 : 2;
+  const int nt = M <= 8 ? 1 : M <= 16 ? 2 : 4;
   const int ntiles = N / 32, ktiles = K / 32;
   const size_t rings = static_cast<size_t>(kQdWarps) * kQdStages * qd_pair_bytes(qt);
   // one k-tile of one 32-column tile: four super-blocks; 13 ns per 576 bytes
   // at ~44 GB/s per SM, against ~700 ns per dependent L2 round trip
   const double kt_ns = 4.0 * (qt == kGgmlQ8_0 ? 272 : 144) / 44.0, trip_ns = 700.0, wave_ns = 8000.0;
-  const int qb = nt == 1 ? 4 : 2;  // the finisher's ranges per batch (qdec_kernel's QB)
+  const int qb = nt == 1 ? 4 : nt == 2 ? 2 : 1;  // the finisher's ranges per batch (qdec_kernel's QB)
   const int force = g_qdec_shape.load();
   double best_cost = 0.0;
   // rows 8 words apart in the banks (16 halves of padding): a half-warp's
@@ -1079,14 +1081,17 @@ static cudaError_t launch_qdec_t(const QDecPlan &p, const uint8_t *w, const QGem
 }
 
 cudaError_t launch_qdec(int qt, const QDecPlan &p, const uint8_t *w, const QGemmArgs &a, cudaStream_t st) {
-  if (a.M < 1 || a.M > 16 || a.N % 32 || a.K % 32 || p.smem > kQdMaxSlice) return cudaErrorInvalidConfiguration;
-#define HTPG_QDEC(T)                                                                           \
-  (p.per_sm == 1 ? (p.nt == 1 ? launch_qdec_t<T, 1, 1>(p, w, a, st) : launch_qdec_t<T, 2, 1>(p, w, a, st)) \
-                 : (p.nt == 1 ? launch_qdec_t<T, 1, 2>(p, w, a, st) : launch_qdec_t<T, 2, 2>(p, w, a, st)))
+  if (a.M < 1 || a.M > 32 || a.N % 32 || a.K % 32 || p.smem > kQdMaxSlice) return cudaErrorInvalidConfiguration;
+#define HTPG_QDEC_NT(T, MB)                                                 \
+  (p.nt == 1   ? launch_qdec_t<T, 1, MB>(p, w, a, st)                       \
+   : p.nt == 2 ? launch_qdec_t<T, 2, MB>(p, w, a, st)                       \
+               : launch_qdec_t<T, 4, MB>(p, w, a, st))
+#define HTPG_QDEC(T) (p.per_sm == 1 ? HTPG_QDEC_NT(T, 1) : HTPG_QDEC_NT(T, 2))
   if (qt == kGgmlQ4_0) return HTPG_QDEC(kGgmlQ4_0);
   if (qt == kGgmlQ8_0) return HTPG_QDEC(kGgmlQ8_0);
   if (qt == kGgmlIQ4_NL) return HTPG_QDEC(kGgmlIQ4_NL);
 #undef HTPG_QDEC
+#undef HTPG_QDEC_NT
   return cudaErrorInvalidValue;
 }
 

@@ -257,9 +257,9 @@ def set_decode_kernel(which: int) -> None:
 
 
 def set_qk0_decode(which: int) -> None:
-    """0 (default): opcode 2-4 decode problems (m <= 16) run the register-fed
-    kernel where it is the faster one (every type); 1: always the tcgen05
-    kernel; 2: the register-fed kernel for every m <= 16."""
+    """0 (default): opcode 2-4 problems with m <= 32 run the register-fed
+    kernel where it is the faster one, else the tcgen05 kernel; 1: always the
+    tcgen05 kernel; 2: the register-fed kernel for every m <= 32."""
     check(lib().htpg_set_qk0_decode(which), "htpg_set_qk0_decode")
 
 
@@ -292,7 +292,7 @@ def qk0_plan_info(weight_type: int, m: int, n: int, k: int, sms: int = 148) -> d
 
 
 def qk0_decode_plan_info(weight_type: int, m: int, n: int, k: int, sms: int = 148) -> dict:
-    """Plan of the register-fed opcode 2-4 decode kernel (m <= 16)."""
+    """Plan of the register-fed opcode 2-4 decode kernel (m <= 32)."""
     out = (ctypes.c_int64 * 8)()
     check(lib().htpg_qk0_decode_plan_info(weight_type, m, n, k, sms, out), "htpg_qk0_decode_plan_info")
     return dict(zip(("per_sm", "tiles", "ntiles", "ktiles", "splits", "grid", "slice", "smem"), list(out)))

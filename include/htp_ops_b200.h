@@ -186,7 +186,7 @@ int htpg_qk0_linear(float *out, const float *x, const void *weight, int m, int k
 int htpg_qk0_dequantize(uint16_t *w_nk, const void *weight, int k, int n, int weight_type, void *stream);
 /* Plan of the fused kernel: {bn, tiles_a, tiles_b, k-blocks, CTAs, shared bytes}. */
 int htpg_qk0_plan_info(int weight_type, int m, int n, int k, int sms, int64_t out[6]);
-/* Plan of the register-fed decode kernel (m <= 16): {CTAs per SM, weight tiles
+/* Plan of the register-fed decode kernel (m <= 32): {CTAs per SM, weight tiles
  * per CTA, 32-column tiles, 32-deep k-tiles, k ranges, CTAs, activation slice
  * bytes, shared bytes per CTA}.  HTPG_ENOPLAN when a shape forced with
  * htpg_set_qdec_shape does not fit. */
@@ -338,12 +338,12 @@ int htpg_set_pair_direct(int on);
  * INT32 sums are exact); the switch exists for measurement and tests. */
 int htpg_set_pair_tail_split(int on);
 
-/* Which kernel runs opcode 2-4 (ggml-block weight) decode problems, m <= 16:
+/* Which kernel runs opcode 2-4 (ggml-block weight) problems with m <= 32:
  * 0 (default) the register-fed decode kernel (each warp streams a 32-column
  * weight tile's super-blocks through a shared-memory ring into registers and
- * feeds mma.sync; k ranges summed in a fixed order), 1 the tcgen05 kernel
- * that serves the other m <= 32, 2 the register-fed kernel (the same as 0
- * now that it serves every type up to m = 16).  Both are deterministic and
+ * feeds mma.sync; k ranges summed in a fixed order) where it is the faster
+ * one, else the tcgen05 kernel; 1 always the tcgen05 kernel; 2 always the
+ * register-fed kernel.  Both are deterministic and
  * within 1e-5 (relative) of the FP32-accumulating oracle; they sum in
  * different orders. */
 int htpg_set_qk0_decode(int which);

@@ -5,11 +5,11 @@ the reference's super-block decode (mat_mul.c:389-525).  The GEMM output is
 checked against the oracle's FP32-accumulating GEMM of the same FP16 operands
 (1e-5 max-abs-rel: same products, different summation order) and against the
 variant that reads the accumulator through FP16 as the reference's HMX readout
-does (the 1e-2 FP16 bar).  M <= 16 runs the register-fed decode kernel by
-default and is also run on the fused tcgen05 small-M kernel, which serves
-16 < M <= 32 (stream-K over the CTAs; the shapes below give tiles finished by
-one CTA, by several CTAs and CTAs that span tiles); larger M dequantises once
-and runs the FP16 GEMM.
+does (the 1e-2 FP16 bar).  M <= 32 runs on both small-M kernels: the
+register-fed decode kernel and the fused tcgen05 kernel (stream-K over the
+CTAs; the shapes below give tiles finished by one CTA, by several CTAs and
+CTAs that span tiles), the default being the faster one; larger M
+dequantises once and runs the FP16 GEMM.
 """
 import ctypes
 import struct
@@ -62,7 +62,7 @@ def test_qk0_linear_matches_oracle(gpu, lib, wtype, m, k, n):
     xd = torch.from_numpy(x).to(gpu)
     outs = []
     try:
-        for which in ((0, 1) if m <= 16 else (0,)):   # default kernel, then tcgen05 for m <= 16
+        for which in ((0, 1, 2) if m <= 32 else (0,)):   # default, tcgen05, register-fed for m <= 32
             htpg.set_qk0_decode(which)
             out = torch.full((m, n), float("nan"), device=gpu)
             htpg.check(htpg.qk0_linear(out, xd, wd, wtype, m, k, n), "htpg_qk0_linear")
@@ -88,6 +88,8 @@ DECODE_CASES = [  # (m, k, n) for the register-fed decode kernel (m <= 16)
     (16, 14336, 4096),   # LLM down projection, 16 tokens (Q8_0)
     (2, 8192, 96),       # few column tiles: many k ranges per tile
     (4, 14336, 4096),    # LLM down projection, 4 tokens
+    (24, 4096, 2048),    # four 8-token MMA tiles, ragged M
+    (32, 14336, 4096),   # LLM down projection, 32 tokens
 ]
 
 
@@ -97,14 +99,14 @@ def test_qk0_decode_kernels_agree(gpu, lib, wtype, m, k, n):
     """The register-fed decode kernel and the tcgen05 kernel decode the same
     FP16 weights and activations and accumulate in FP32 in different orders:
     both within 1e-5 of the FP32-accumulating oracle and of each other (every
-    type, up to 16 rows, whichever kernel the library would pick)."""
+    type, up to 32 rows, whichever kernel the library would pick)."""
     src, x = _case(wtype, m, k, n, seed=m * 11 + k + n + wtype)
     ref32 = O.qk0_linear(x, src, wtype, k, n, kind="omp")
     wd, xd = torch.from_numpy(src).to(gpu), torch.from_numpy(x).to(gpu)
     w = htpg.qk0_weights(wd, wtype, k, n)
     outs = []
     try:
-        for which in (2, 1):       # register-fed for every m <= 16, then tcgen05
+        for which in (2, 1):       # register-fed for every m <= 32, then tcgen05
             htpg.set_qk0_decode(which)
             out = torch.full((m, n), float("nan"), device=gpu)
             htpg.check(htpg.qk0_run(w, out, xd, m), "htpg_qk0_run")
@@ -123,6 +125,7 @@ SHAPE_CASES = [  # (m, k, n) run under every launch shape of the register-fed ke
     (12, 2048, 1536),    # two 8-token MMA tiles, ragged M
     (16, 14336, 4096),   # LLM down projection: the slice bounds the k ranges
     (1, 4096, 1024),
+    (29, 2048, 1024),    # four 8-token MMA tiles, ragged M
 ]
 
 

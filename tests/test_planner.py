@@ -208,14 +208,14 @@ QK0_DECODE_KS = [32, 96, 2048, 4096, 14336, 65536]
 @pytest.mark.parametrize("wtype", [2, 8, 20])
 @pytest.mark.parametrize("sms", [148, 16])
 def test_qk0_decode_plans_are_legal(wtype, sms):
-    """Register-fed opcode 2-4 decode plans (m <= 16): the grid is the tile
+    """Register-fed opcode 2-4 decode plans (m <= 32): the grid is the tile
     groups x k ranges, no range is empty, the activation slice holds the widest
     range, a CTA's shared memory fits (two CTAs per SM within 112 KB each; a
     one-per-SM plan asks for more than half the SM so its CTAs spread)."""
     rings = 16 * 4 * 8 * (272 if wtype == 8 else 144)
-    for m, n, k in itertools.product([1, 4, 8, 9, 16], QK0_DECODE_NS, QK0_DECODE_KS):
+    for m, n, k in itertools.product([1, 4, 8, 9, 16, 17, 32], QK0_DECODE_NS, QK0_DECODE_KS):
         p = htpg.qk0_decode_plan_info(wtype, m, n, k, sms)
-        nt = 1 if m <= 8 else 2
+        nt = 1 if m <= 8 else 2 if m <= 16 else 4
         assert p["ntiles"] == n // 32 and p["ktiles"] == k // 32
         assert p["tiles"] in (16, 8, 4) and p["per_sm"] in (1, 2)
         assert 1 <= p["splits"] <= p["ktiles"]
@@ -233,6 +233,8 @@ def test_qk0_decode_plans_are_legal(wtype, sms):
     (16, 4096, 14336, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
     (4, 14336, 4096, {2: (1, 4), 8: (1, 4), 20: (1, 4)}),
     (16, 14336, 4096, {2: (1, 8), 8: (1, 8), 20: (1, 8)}),
+    (32, 4096, 14336, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
+    (32, 14336, 4096, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
 ])
 def test_qk0_decode_plan_choices(m, k, n, want):
     """On the LLM projections the planner picks the launch shape measured
