@@ -915,7 +915,8 @@ __global__ void __launch_bounds__(kQdThreads, MB) qdec_kernel(const QDecParams P
   const float *all = P.part + static_cast<size_t>(nt) * P.S * TILEF;
   // the lane's elements of every range: QB ranges' loads in flight at a time,
   // added in range order
-  constexpr int QB = NT == 1 ? 4 : NT == 2 ? 2 : 1;
+  // (with up to 128 registers per thread twice as many as with 64)
+  constexpr int QB = (MB == 1 ? 8 : 4) / NT;
 #pragma unroll
   for (int cg = 0; cg < 2; ++cg)
 #pragma unroll
@@ -968,12 +969,13 @@ std::atomic<int> g_qdec_shape{0};
 // life: slice load, ring fill, hand-off; a second wave costs it again), the
 // busiest SM's streaming work (CTAs spread over the SMs first: ceil(grid /
 // SMs) x tiles x k-tiles of a range, in k-tile units of this type's bytes at
-// an SM's share of the HBM bandwidth) and the finishing warp's L2 round trips
-// (ceil(S / QB) batches of partial loads).  The smallest estimate wins; ties
-// keep one CTA per SM (fewer CTAs, no tile shared between warps) and wider
-// groups.  On the LLM projections (K x N =
-// 4096 x 14336 and 14336 x 4096, m = 1..16, every type) it picks the fastest
-// measured shape or one within 3%.
+// an SM's share of the HBM bandwidth), the finishing warp's L2 round trips
+// (ceil(S / QB) batches of partial loads) and, where warps share a tile, the
+// sum of their parts in shared memory (one round trip's worth per extra part
+// and 8-token tile).  The smallest estimate wins; ties keep one CTA per SM
+// (fewer CTAs) and wider groups.  On the LLM projections (K x N = 4096 x 14336
+// and 14336 x 4096, m = 1..32, every type) it picks the fastest measured
+// shape or one within 4%.
 QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms) {
   QDecPlan best;
   best.grid = 0;
@@ -983,7 +985,6 @@ QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms) {
   // one k-tile of one 32-column tile: four super-blocks; 13 ns per 576 bytes
   // at ~44 GB/s per SM, against ~700 ns per dependent L2 round trip
   const double kt_ns = 4.0 * (qt == kGgmlQ8_0 ? 272 : 144) / 44.0, trip_ns = 700.0, wave_ns = 8000.0;
-  const int qb = nt == 1 ? 4 : nt == 2 ? 2 : 1;  // the finisher's ranges per batch (qdec_kernel's QB)
   const int force = g_qdec_shape.load();
   double best_cost = 0.0;
   // rows 8 words apart in the banks (16 halves of padding): a half-warp's
@@ -996,6 +997,7 @@ QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms) {
     if (rings >= budget) continue;
     const size_t slice_max = budget - rings < kQdMaxSlice ? budget - rings : kQdMaxSlice;
     const int target = per_sm * num_sms;
+    const int qb = (per_sm == 1 ? 8 : 4) / nt;  // the finisher's ranges per batch (qdec_kernel's QB)
     for (int nw = kQdWarps; nw >= 4; nw /= 2) {
       if (force && force != per_sm * 100 + nw) continue;
       const int groups = (ntiles + nw - 1) / nw, parts = kQdWarps / nw;
@@ -1009,7 +1011,8 @@ QDecPlan plan_qdec(int qt, int M, int N, int K, int num_sms) {
       const long long busiest = (grid + num_sms - 1) / num_sms, waves = (grid + target - 1) / target;
       const double cost = static_cast<double>(waves) * wave_ns +
                           static_cast<double>(busiest) * nw * ((ktiles + S - 1) / S) * kt_ns +
-                          static_cast<double>((S + qb - 1) / qb) * trip_ns;
+                          static_cast<double>((S + qb - 1) / qb) * trip_ns +
+                          static_cast<double>((parts - 1) * nt) * trip_ns;
       if (best.grid == 0 || cost < best_cost) {
         best_cost = cost;
         best.nt = nt;

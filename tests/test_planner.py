@@ -231,14 +231,14 @@ def test_qk0_decode_plans_are_legal(wtype, sms):
 @pytest.mark.parametrize("m,k,n,want", [
     (1, 4096, 14336, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
     (16, 4096, 14336, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
-    (4, 14336, 4096, {2: (1, 4), 8: (1, 4), 20: (1, 4)}),
-    (16, 14336, 4096, {2: (1, 8), 8: (1, 8), 20: (1, 8)}),
+    (4, 14336, 4096, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
+    (16, 14336, 4096, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
     (32, 4096, 14336, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
     (32, 14336, 4096, {2: (1, 16), 8: (1, 16), 20: (1, 16)}),
 ])
 def test_qk0_decode_plan_choices(m, k, n, want):
     """On the LLM projections the planner picks the launch shape measured
-    fastest (back to back on a B200) or one within 3% of it; a forced shape
+    fastest (back to back on a B200) or one within 4% of it; a forced shape
     overrides it until reset."""
     for wtype, (per_sm, tiles) in want.items():
         p = htpg.qk0_decode_plan_info(wtype, m, n, k)
