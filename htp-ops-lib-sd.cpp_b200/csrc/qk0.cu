@@ -687,21 +687,25 @@ struct QdWords {
   uint32_t q[4][4];  // [super-block][column 4g + c]
 };
 
+// Plain loads (the compiler may schedule them; the ring's cp.async wait,
+// which clobbers memory, keeps them after the stage has landed).
 template <int QT>
-__device__ __forceinline__ void qd_load(QdWords &w, uint32_t tile, int g, int t) {
+__device__ __forceinline__ void qd_load(QdWords &w, const uint8_t *tile, int g, int t) {
   constexpr int BLK = QT == kGgmlQ8_0 ? 272 : 144;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const uint32_t sb = tile + j * BLK;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w.sc[j]) : "r"(sb + 4 * t));
+    const uint8_t *sb = tile + j * BLK;
+    w.sc[j] = *reinterpret_cast<const uint32_t *>(sb + 4 * t);
     if constexpr (QT == kGgmlQ8_0) {
-      asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w.q[j][0]), "=r"(w.q[j][2]) : "r"(sb + 16 + 8 * g + 64 * t));
-      w.q[j][1] = w.q[j][0];
-      w.q[j][3] = w.q[j][2];
+      const uint2 q = *reinterpret_cast<const uint2 *>(sb + 16 + 8 * g + 64 * t);
+      w.q[j][0] = w.q[j][1] = q.x;
+      w.q[j][2] = w.q[j][3] = q.y;
     } else {
-      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(w.q[j][0]), "=r"(w.q[j][1]), "=r"(w.q[j][2]), "=r"(w.q[j][3])
-                   : "r"(sb + 16 + 16 * g));
+      const uint4 q = *reinterpret_cast<const uint4 *>(sb + 16 + 16 * g);
+      w.q[j][0] = q.x;
+      w.q[j][1] = q.y;
+      w.q[j][2] = q.z;
+      w.q[j][3] = q.w;
     }
   }
 }
@@ -829,7 +833,7 @@ __global__ void __launch_bounds__(kQdThreads, MB) qdec_kernel(const QDecParams P
   for (int i = 0; i < npairs; ++i) {
     asm volatile("cp.async.wait_group %0;" ::"n"(kQdStages - 1) : "memory");  // pair i has landed
     __syncwarp();
-    const uint32_t stage = ring + static_cast<uint32_t>((i % kQdStages) * PAIR);
+    const uint8_t *stage = reinterpret_cast<const uint8_t *>(qd_smem) + (warp * kQdStages + i % kQdStages) * PAIR;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int kt = 2 * (pp0 + i) + e;
