@@ -635,7 +635,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
   }
 }
 
-// ============================================= register-fed decode (M <= 16)
+// ============================================= register-fed decode (M <= 32)
 // Each CTA owns NW (16, 8 or 4) 32-column weight tiles and one range of
 // 32-deep k-tiles; 16 / NW warps share a tile, each a part of the range, and
 // add their FP32 sums in shared memory in a fixed order.  It first rounds its
@@ -644,7 +644,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
 // own shared-memory ring with cp.async (a k-tile pair of one tile is 8
 // consecutive super-blocks, 1152 or 2176 bytes; four pairs in flight), decodes
 // only the FP16 pairs its MMA fragments hold, with dq_decode's arithmetic, and
-// accumulates with mma.sync m16n8k16 (FP16 x FP16 -> FP32).  Fragment layout:
+// accumulates with mma.sync m16n8k16 (FP16 x FP16 -> FP32), NT = 1, 2 or 4
+// 8-token MMA tiles (M <= 8, 16, 32).  Fragment layout:
 // lane (g, t) holds tile columns 4g .. 4g+3 (MMA rows g / g+8 of column group
 // cg are columns 4g + 2cg / 4g + 2cg + 1, so a lane's codes of one super-block
 // are adjacent in shared memory), pair t of super-blocks 2s and 2s+1 (k = 16s
